@@ -1,0 +1,400 @@
+"""Benchmark: Qwen3-VL-4B-shaped FP8 prefill (T=320) + choice scoring on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload 4B-fp8-T320]
+
+One step = one request: prefill of T=320 tokens (256 visual rows on a 16x16 merged grid +
+64 text ids) through all 36 layers and the 4-choice scoring, replayed from one CUDA graph.
+`value` = whole-job prefill tokens/s with inputs resident in HBM (device-timed with CUDA
+events, max over ranks); `e2e` = the same metric through `Accelerator.prefill_score`
+with the request in pinned host memory (H2D of ids/visual/deepstack rows and the D2H of
+the logits inside the timed region).  Weights (3.6 GB FP8) exceed the 126 MB L2, so no
+flush is needed between steps.  N > 1 (torchrun): one independent replica per GPU, no
+collective on the data path ("replicas only"; requests are independent).
+
+`--impl reference` times the reference's arithmetic on the host CPU: the oracle's
+restatement of the reference path (the reference itself is Triton/CUDA-only and has no
+CPU path), a bounded sample of whole decoder layers scaled to the full model.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "prefill tok/s (Qwen3-VL-4B FP8, T=320 prefill + 4-choice scoring); p50 latency in ms_per_step"
+UNIT = "tok/s"
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=50)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    p.add_argument("--workload", default="4B-fp8-T320")
+    p.add_argument("--cpu-layers", type=int, default=2, help="decoder layers in the CPU sample")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    return p.parse_args()
+
+
+def read_peaks():
+    f = ROOT / "MEASURED_PEAKS.json"
+    if f.exists():
+        d = json.loads(f.read_text())
+        return dict(hbm=d["hbm_gbs"], bf16=d["bf16_tflops"], bf16_sustained=d.get("bf16_tflops_sustained"),
+                    src="measured")
+    return dict(hbm=6650.0, bf16=1590.0, bf16_sustained=1400.0, src="fallback")
+
+
+class Clocks:
+    """nvidia-smi sampling during the timed region."""
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        rows = []
+        try:
+            for line in Path(self.path).read_text().splitlines():
+                f = [x.strip() for x in line.split(",")]
+                if len(f) >= 9:
+                    rows.append(f)
+        except Exception:
+            pass
+        if not rows:
+            return dict(sm_mhz=None, sm_max_mhz=None, reasons=["unsampled"], samples=0)
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            for n, v in zip(names, r[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return dict(sm_mhz=statistics.median(sm) if sm else None, sm_max_mhz=float(rows[0][2]),
+                    reasons=sorted(reasons), samples=len(rows))
+
+
+# ---------------------------------------------------------------------------- CPU side
+
+class CpuSample:
+    """The oracle (the reference path's arithmetic restated on the CPU) on the workload's
+    model: built once, then timed one decoder layer (or the tail) at a time."""
+
+    def __init__(self, dims, layout, threads, n_layers=1):
+        import torch
+        import oracle
+        from fastforward_b200.synthetic import make_model_bf16, make_request
+        from fastforward_b200.mrope import position_ids
+        torch.set_num_threads(threads)
+        self.o = oracle
+        self.dims, self.layout = dims, layout
+        src = make_model_bf16(dims, seed=0, device="cpu", layers=n_layers + 1)
+        self.om = oracle.quantized_model(dims, src, "rowwise")
+        self.req = make_request(dims, layout, seed=1)
+        T = layout.bucket
+        pos = position_ids(T, layout.image_start, layout.grid_h, layout.grid_w)
+        self.cos, self.sin = oracle.mrope_cos_sin(pos, dims.d, dims.theta)
+        self.h = oracle.embed_rows(self.om["embed"], self.req["ids"][:T], self.req["visual"], layout.image_start)
+        self.n_layers = n_layers
+
+    def layer(self, j=0):
+        t0 = time.perf_counter()
+        self.o.decoder_layer(self.om["layers"][j], self.h, self.cos, self.sin, self.om["dims"], "rowwise",
+                             self.req["deep"][0], self.layout.image_start, self.layout.nv)
+        return time.perf_counter() - t0
+
+    def tail(self):
+        t0 = time.perf_counter()
+        om = self.om
+        self.o.tail(om["layers"][self.n_layers], self.h, self.cos, self.sin, om["dims"], "rowwise",
+                    self.req["pick"], om["final_norm"], om["head"], self.req["k"])
+        return time.perf_counter() - t0
+
+    def full_request_seconds(self, t_layer, t_tail):
+        return t_layer * (self.dims.layers - 1) + t_tail
+
+
+def run_reference(args):
+    import torch
+    from fastforward_b200.config import MODELS, WORKLOADS
+    name, layout, mode = WORKLOADS[args.workload]
+    dims = MODELS[name]
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    cs = CpuSample(dims, layout, threads)
+    t_tail = cs.tail()
+    times = []
+    for i in range(args.warmup + args.steps):
+        t = cs.layer()
+        if i >= args.warmup:
+            times.append(cs.full_request_seconds(t, t_tail))
+    T = layout.bucket
+    per_req = statistics.median(times)
+    value = T / per_req
+    line = dict(metric=METRIC, value=value, unit=UNIT, n_gpus=args.gpus, steps=args.steps, warmup=args.warmup,
+                ms_per_step=per_req * 1e3, higher_is_better=True, scaling="weak", vs_baseline=None, dtype="fp8-e4m3",
+                data="synthetic", impl="reference",
+                config=dict(workload=args.workload, model=f"Qwen3-VL-{name}-shaped", global_batch=1, seq_len=T,
+                            parallelism="cpu"),
+                cpu_baseline=dict(value=value, unit=UNIT, cores=threads, kind="port",
+                                  sample=f"1 decoder layer per step (tail timed once, {t_tail:.2f}s), scaled to "
+                                         f"{dims.layers - 1} layers + tail"),
+                e2e=dict(value=value, unit=UNIT, h2d_bytes_per_step=0, d2h_bytes_per_step=0))
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------- GPU side
+
+def gemm_roofline(eng, T, peaks, reps=20):
+    """Times each GEMM role of the forward standalone (same shapes and plans as inside the
+    graph) with CUDA events; returns per-role stats and the dominant role."""
+    import torch
+    from fastforward_b200 import _lib as L
+    m = eng.m
+    d = eng.d
+    b = eng.buffers_for(T)
+    pl = eng._plans(T)
+    lay = m.layers[0]
+    s = torch.cuda.current_stream()
+    eng._s = s.cuda_stream
+    roles = {"qkv": (b.x8, b.xs, b.qkv), "o": (b.o8, b.os, b.lin_out), "gateup": (b.post8, b.posts, b.act),
+             "down": (b.act8, b.acts, b.lin_out)}
+    out = {}
+    for role, (a8, sc, o) in roles.items():
+        p = pl[("full", role)]
+        for _ in range(3):
+            eng._gemm(p, a8, sc, lay.lin[role], o, b.ws, True)
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+        ev[0].record(s)
+        for i in range(reps):
+            eng._gemm(p, a8, sc, m.layers[i % m.depth].lin[role], o, b.ws, True)
+        ev[1].record(s)
+        torch.cuda.synchronize()
+        dt = ev[0].elapsed_time(ev[1]) / reps * 1e-3
+        flops = 2.0 * p.m * p.n * p.k
+        wbytes = p.n * p.k
+        out[role] = dict(m=p.m, n=p.n, k=p.k, bn=p.bn, splits=p.splits, us=dt * 1e6, tflops=flops / dt / 1e12,
+                         weight_gbs=wbytes / dt / 1e9)
+    return out
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+    from fastforward_b200.config import MODELS, WORKLOADS
+    from fastforward_b200.engine import Engine, PackedModel
+    from fastforward_b200.synthetic import make_model_bf16, make_request
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+    name, layout, mode = WORKLOADS[args.workload]
+    dims = MODELS[name]
+    T = layout.bucket
+    peaks = read_peaks()
+
+    with torch.no_grad():
+        src = make_model_bf16(dims, seed=0, device=dev)
+        pm = PackedModel(dims, src, mode=mode, device=dev, free_source=True)
+        del src
+        torch.cuda.empty_cache()
+        eng = Engine(pm)
+        # requests: a pool of distinct synthetic requests in pinned host memory
+        n_pool = 8
+        reqs = []
+        for i in range(n_pool):
+            r = make_request(dims, layout, seed=1000 * rank + i)
+            reqs.append(dict(ids=r["ids"][:layout.n_tokens].pin_memory(), visual=r["visual"].pin_memory(),
+                             deep=[x.pin_memory() for x in r["deep"]], pick=r["pick"], k=r["k"]))
+        entry = eng.capture(T, layout.image_start, layout.nv, layout.grid_h, layout.grid_w, layout.k, dims.deepstack)
+        dev_reqs = [dict(ids=r["ids"].to(dev), visual=r["visual"].to(dev), deep=[x.to(dev) for x in r["deep"]],
+                         pick=r["pick"]) for r in reqs]
+        torch.cuda.synchronize()
+
+        # ---- value: graph replays, inputs resident in HBM
+        def stage_dev(r):
+            b = entry["buffers"]
+            b.ids[:r["ids"].shape[0]].copy_(r["ids"])
+            entry["visual"][:layout.nv].copy_(r["visual"])
+            for dst, src_ in zip(entry["deep"], r["deep"]):
+                dst.copy_(src_)
+            b.pick.fill_(r["pick"])
+
+        for i in range(args.warmup):
+            stage_dev(dev_reqs[i % n_pool])
+            entry["graph"].replay()
+        torch.cuda.synchronize()
+        s = torch.cuda.current_stream()
+        starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+        ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+        # stage all inputs for the timed steps ahead: each step's request already in HBM
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        with Clocks(local) as clk:
+            t_all0 = torch.cuda.Event(enable_timing=True)
+            t_all1 = torch.cuda.Event(enable_timing=True)
+            t_all0.record(s)
+            for i in range(args.steps):
+                starts[i].record(s)
+                entry["graph"].replay()
+                ends[i].record(s)
+            t_all1.record(s)
+            torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        total_s = t_all0.elapsed_time(t_all1) * 1e-3
+        lat = sorted(a.elapsed_time(b_) for a, b_ in zip(starts, ends))
+        p50 = lat[len(lat) // 2]
+        p99 = lat[min(len(lat) - 1, int(round(0.99 * (len(lat) - 1))))]
+        if world > 1:
+            t = torch.tensor([total_s], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            total_s = t.item()
+        value = world * args.steps * T / total_s
+
+        # ---- e2e: through the public entry with host (pinned) buffers, H2D + D2H per step
+        from fastforward_b200.api import Accelerator
+
+        class _Bound(Accelerator):
+            def __init__(self, engine, dims_, buckets):
+                import threading
+                self.engine = engine
+                self.dims = dims_
+                self.device = dev
+                self.lock = threading.RLock()
+                self.buckets = buckets
+        from fastforward_b200.config import BUCKETS
+        acc = _Bound(eng, dims, BUCKETS)
+        for i in range(args.warmup):
+            r = reqs[i % n_pool]
+            acc.prefill_score(r["ids"], r["visual"], r["deep"], r["k"], layout.image_start, layout.grid_h,
+                              layout.grid_w)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        w0 = time.perf_counter()
+        for i in range(args.steps):
+            r = reqs[i % n_pool]
+            acc.prefill_score(r["ids"], r["visual"], r["deep"], r["k"], layout.image_start, layout.grid_h,
+                              layout.grid_w)
+        e1.record(s)
+        torch.cuda.synchronize()
+        wall = time.perf_counter() - w0
+        e2e_s = max(e0.elapsed_time(e1) * 1e-3, 0.0)
+        if world > 1:
+            t = torch.tensor([e2e_s], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            e2e_s = t.item()
+        e2e_value = world * args.steps * T / e2e_s
+        r0 = reqs[0]
+        h2d = (r0["ids"].numel() * 8 + r0["visual"].numel() * 2 + sum(x.numel() * 2 for x in r0["deep"]) + 8)
+        d2h = 2 * layout.k * 4
+
+        # ---- roofline of the dominant kernel (the FP8 GEMM), standalone event timing
+        roles = gemm_roofline(eng, T, peaks)
+        fp8_peak = 2.0 * peaks["bf16"]
+        dom = max(roles, key=lambda k: roles[k]["us"])
+        dr = roles[dom]
+        roofline = dict(bound="tensor", achieved=dr["tflops"], peak=fp8_peak, unit="TFLOP/s",
+                        frac=dr["tflops"] / fp8_peak, traffic=None, kernel=f"fp8_gemm_kernel ({dom})",
+                        peak_note=f"FP8 dense = 2 x {peaks['src']} cuBLAS bf16 {peaks['bf16']} TFLOP/s",
+                        weight_stream_gbs=dr["weight_gbs"], hbm_peak_gbs=peaks["hbm"],
+                        per_role={k: {kk: (round(vv, 3) if isinstance(vv, float) else vv) for kk, vv in v.items()}
+                                  for k, v in roles.items()})
+        gemm_us = sum(v["us"] for v in roles.values()) * (dims.layers - 1)
+        # whole-forward algorithmic roofline: max(FLOPs / FP8 peak, weight bytes / HBM)
+        P = dims.params_per_layer() * dims.layers
+        flops = 2.0 * T * P + 4.0 * (T * (T + 1) / 2) * dims.d * dims.hq * dims.layers
+        t_roof = max(flops / (fp8_peak * 1e12), P / (peaks["hbm"] * 1e9))
+
+        cpu = None
+        if rank == 0 and world == 1 and not args.no_cpu_baseline:
+            threads = os.cpu_count() or 1
+            cs = CpuSample(dims, layout, threads)
+            t_layers = [cs.layer() for _ in range(args.cpu_layers)]
+            t_tail = cs.tail()
+            full = cs.full_request_seconds(statistics.median(t_layers), t_tail)
+            cpu = dict(value=T / full, unit=UNIT, cores=threads, kind="port",
+                       sample=f"{args.cpu_layers} timed decoder layers (median {statistics.median(t_layers):.2f}s) "
+                              f"+ tail ({t_tail:.2f}s) of the {name} model at T={T}, scaled to "
+                              f"{dims.layers - 1} layers + tail")
+
+    clk_sum = clk.summary()
+    if rank == 0:
+        line = dict(metric=METRIC, value=value, unit=UNIT, n_gpus=world, steps=args.steps, warmup=args.warmup,
+                    ms_per_step=p50, higher_is_better=True, scaling="weak", vs_baseline=None, dtype="fp8-e4m3",
+                    data="synthetic (seeded N(0,0.02) weights, N(0,1) visual/deepstack rows, uniform text ids)",
+                    config=dict(workload=args.workload, model=f"Qwen3-VL-{name}-shaped", global_batch=world,
+                                seq_len=T, parallelism=f"replicas{world}", quant=mode,
+                                l2="weights (3.6 GB) exceed L2; no flush needed", tokens_per_step=T),
+                    latency_ms=dict(p50=p50, p99=p99, mean=total_s / args.steps * 1e3),
+                    requests_per_s=world * args.steps / total_s,
+                    roofline=roofline,
+                    forward_roofline=dict(flops=flops, weight_bytes=P, t_roofline_ms=t_roof * 1e3,
+                                          frac=t_roof * 1e3 / p50, note="max(FLOPs/FP8 peak, weights/HBM) / p50"),
+                    gemm_share_est=gemm_us * 1e-3 / p50,
+                    e2e=dict(value=e2e_value, unit=UNIT, h2d_bytes_per_step=h2d, d2h_bytes_per_step=d2h,
+                             wall_s=wall, api="Accelerator.prefill_score"),
+                    gpu_launches=eng.launches_per_forward() * args.steps,
+                    clocks=clk_sum, cpu_baseline=cpu)
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        del entry
+        eng.graphs.clear()
+        dist.destroy_process_group()
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,116 @@
+"""ctypes binding of libffb200.so (the C ABI declared in include/ffb200.h).
+
+The library is loaded from this package directory.  There is no fallback: if the
+shared library is missing or no CUDA device is present, every op raises.
+"""
+import ctypes
+from ctypes import c_float, c_int, c_int64, c_size_t, c_uint32, c_void_p, c_char_p
+from pathlib import Path
+
+import torch
+
+LIB_PATH = Path(__file__).resolve().with_name("libffb200.so")
+
+OK, EINVAL, EUNSUPPORTED, ECUDA, ETIMEOUT = 0, -1, -2, -3, -4
+QUANT_NONE, QUANT_STATIC, QUANT_ROWWISE = 0, 1, 2
+EPI_BF16, EPI_F32_PARTIAL, EPI_SWIGLU = 0, 1, 2
+
+P, I, F = c_void_p, c_int, c_float
+
+# name -> argtypes, in the order of include/ffb200.h
+SIGNATURES = {
+    "ffb_version": [],
+    "ffb_set_pdl": [I],
+    "ffb_last_error": [c_char_p, c_size_t],
+    "ffb_device_error": [P, I],
+    "ffb_embed_gather": [P, P, c_int64, P, I, I, P, I, I, P],
+    "ffb_rmsnorm": [P, P, F, P, I, F, P, P, I, I, P],
+    "ffb_add_rmsnorm": [P, P, P, I, P, I, I, P, F, P, P, I, F, P, P, I, I, P],
+    "ffb_qk_norm_rope": [P, P, I, I, P, P, F, P, P, P, P, P, I, I, I, P],
+    "ffb_attention": [P, P, P, P, I, P, I, I, I, I, F, P],
+    "ffb_gather_rows": [P, P, P, I, I, P],
+    "ffb_quantize_fp8": [P, I, F, P, P, I, I, P],
+    "ffb_quantize_weight_fp8": [P, I, P, P, P, I, I, P],
+    "ffb_fp8_gemm": [P, P, I, P, P, I, I, P, P, I, I, I, I, I, P],
+    "ffb_pack_gateup": [P, P, I, I, I, P],
+    "ffb_swiglu": [P, P, I, P, I, I, P],
+    "ffb_readout": [P, P, P, I, P, F, P, I, I, P, P, I, P],
+    "ffb_pack_int4": [P, P, P, I, I, P],
+    "ffb_w4a16_gemm": [P, P, P, I, P, P, I, I, I, I, I, P],
+}
+
+
+class FFBError(RuntimeError):
+    """A libffb200 call failed (CUDA error or device-side timeout)."""
+
+
+class FFBUnsupported(FFBError, NotImplementedError):
+    """The kernels do not implement the requested configuration."""
+
+
+_lib = None
+
+
+def lib():
+    """The loaded library (loaded on first use)."""
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise FFBError(f"{LIB_PATH.name} is not built; run `python -m fastforward_b200.build`")
+        handle = ctypes.CDLL(str(LIB_PATH))
+        for name, args in SIGNATURES.items():
+            fn = getattr(handle, name)
+            fn.argtypes = args
+            fn.restype = c_char_p if name == "ffb_version" else c_int
+        _lib = handle
+    return _lib
+
+
+def last_error():
+    buf = ctypes.create_string_buffer(512)
+    lib().ffb_last_error(buf, 512)
+    return buf.value.decode(errors="replace")
+
+
+def check(rc):
+    if rc == OK:
+        return
+    msg = last_error()
+    if rc == EINVAL:
+        raise ValueError(msg)
+    if rc == EUNSUPPORTED:
+        raise FFBUnsupported(msg)
+    raise FFBError(f"[{rc}] {msg}")
+
+
+def call(name, *args):
+    """Calls `name` and raises on a non-zero return code."""
+    check(getattr(lib(), name)(*args))
+
+
+def ptr(t):
+    """Device pointer of a tensor, or None (NULL) for None."""
+    if t is None:
+        return None
+    if not t.is_cuda:
+        raise ValueError("libffb200 ops take CUDA tensors only (no CPU fallback)")
+    return t.data_ptr()
+
+
+def stream_ptr(device=None):
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def device_error(clear=False):
+    w = c_uint32(0)
+    call("ffb_device_error", ctypes.addressof(w), int(clear))
+    return w.value
+
+
+def set_pdl(enable):
+    return lib().ffb_set_pdl(int(enable))
+
+
+def require_cuda():
+    if not torch.cuda.is_available():
+        raise FFBError("a CUDA device is required: this path has no CPU fallback")

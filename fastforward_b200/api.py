@@ -1,0 +1,194 @@
+"""Public surface, mirroring FastForward's `fastforward_accel.api` (api.py:1-99).
+
+`Accelerator(bundle, *, backend="fast")`, `.predict(image, question, candidates, item_id,
+*, backend=None)`, `.warmup(requests)`, `.activate_fast()`, `validate_request`,
+`response` keep the reference's names, argument meaning, return dict and errors
+(ValueError for schema/backend/choices/sha problems, FileNotFoundError for missing
+files, RuntimeError for device problems and non-finite outputs; one RLock per instance
+serialises calls).  Behind them the B200 engine runs the prefill + scoring path.
+
+What lies before the path in the reference -- image decode, resize, vision tower,
+tokenizer (`_family/depth_runtime.py:54-82`) -- is outside this package: `predict` takes
+it from an `encoder(image, question, candidates) -> Request` callable.  Bundles with a
+`synthetic` block (seeded random weights, no checkpoint files) get a deterministic
+synthetic encoder so the whole surface runs without model assets.  `prefill_score` is the
+internal entry that `predict` calls after the encoder; benchmarks call it directly.
+"""
+import hashlib
+import json
+import math
+import threading
+from dataclasses import dataclass, field
+from pathlib import Path
+
+BACKENDS = ("fast",)
+
+
+def sha256(path):
+    h = hashlib.sha256()
+    with open(path, "rb") as f:
+        for block in iter(lambda: f.read(1024 * 1024), b""):
+            h.update(block)
+    return h.hexdigest()
+
+
+def validate_request(image, question, candidates):
+    """Same checks and errors as the reference (`api.py:17-25`)."""
+    if not Path(image).is_file():
+        raise FileNotFoundError(image)
+    if not isinstance(question, str) or not question.strip():
+        raise ValueError("A nonempty question is required")
+    if not isinstance(candidates, (list, tuple)) or not 2 <= len(candidates) <= 8:
+        raise ValueError("Provide two to eight choices")
+    if any(not isinstance(x, str) or not x.strip() for x in candidates):
+        raise ValueError("Choices must be nonempty strings")
+
+
+def response(logits, candidates, item_id, logprobs=None):
+    """Argmax (first maximum wins) + softmax probabilities, as the reference (`api.py:28-34`).
+    `logprobs` (the GPU log-softmax) is added when given."""
+    if len(logits) != len(candidates) or not all(math.isfinite(x) for x in logits):
+        raise RuntimeError("Invalid model output")
+    prediction = max(range(len(logits)), key=lambda i: logits[i])
+    exps = [math.exp(x - max(logits)) for x in logits]
+    out = dict(id=item_id, answer=dict(letter=chr(65 + prediction), text=candidates[prediction]),
+               logits=logits, probabilities=[x / sum(exps) for x in exps])
+    if logprobs is not None:
+        out["logprobs"] = logprobs
+    return out
+
+
+@dataclass
+class Request:
+    """What the path consumes for one request (the encoder's output)."""
+    ids: "object"                 # [n] int64 token ids (image positions hold any id)
+    visual: "object"              # [nv, H] bf16 visual-merger rows
+    deep: list = field(default_factory=list)   # deepstack rows, each [nv, H]
+    image_start: int = 0
+    grid_h: int = 32              # patch grid before the 2x2 merge
+    grid_w: int = 32
+    k: int = 4
+
+    @property
+    def pick(self):
+        return int(self.ids.shape[0]) - 1
+
+
+class SyntheticEncoder:
+    """Deterministic stand-in for image decode + vision tower + tokenizer: the request's
+    bytes seed the synthetic visual rows and text ids of the bundle's layout."""
+
+    def __init__(self, dims, layout):
+        self.dims = dims
+        self.layout = layout
+
+    def __call__(self, image, question, candidates):
+        import torch
+        from .synthetic import make_request
+        h = hashlib.sha256(Path(image).read_bytes() + question.encode() + "\x00".join(candidates).encode())
+        seed = int.from_bytes(h.digest()[:8], "little") & ((1 << 62) - 1)
+        lay = self.layout
+        r = make_request(self.dims, lay, seed=seed)
+        n = lay.n_tokens
+        return Request(ids=r["ids"][:n], visual=r["visual"], deep=r["deep"], image_start=lay.image_start,
+                       grid_h=lay.grid_h, grid_w=lay.grid_w, k=len(candidates))
+
+
+class Accelerator:
+    """Load one supported model and run its prefill + choice scoring on one B200.
+
+    The caller owns the CUDA device (`device`, default the current one).  Graph capture
+    happens on the first request of each geometry.  Calls are serialised by an RLock;
+    graph buffers are private to the instance.
+    """
+
+    def __init__(self, bundle, *, backend="fast", device=None, encoder=None):
+        self.bundle = Path(bundle).resolve()
+        c = json.loads(self.bundle.read_text())
+        if c.get("schema_version") != 1 or c.get("task") != "visual_choice":
+            raise ValueError("Unsupported adaptation bundle schema or task")
+        if backend not in BACKENDS:
+            raise ValueError("Unknown backend")
+        synthetic = c.get("synthetic")
+        if synthetic is None:
+            for key in ("model", "checkpoint"):
+                if not Path(c[key]).exists():
+                    raise FileNotFoundError(c[key])
+            if sha256(c["checkpoint"]) != c["checkpoint_sha256"]:
+                raise ValueError("Recovery checkpoint SHA256 mismatch")
+            raise ValueError("Checkpoint loading is not part of this package; use a synthetic bundle")
+        import torch
+        if not torch.cuda.is_available():
+            raise RuntimeError("A CUDA GPU is required; CPU fallback is disabled")
+        dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+        if torch.cuda.get_device_capability(dev)[0] != 10:
+            raise RuntimeError("This backend requires a B200 (sm_100a)")
+        if c.get("architecture") != "qwen3_vl_family":
+            raise ValueError("No adapter registered for this architecture")
+        from .config import MODELS, Layout, BUCKETS
+        from .engine import Engine, PackedModel
+        from .synthetic import make_model_bf16
+        self.config = c
+        self.backend = backend
+        self.lock = threading.RLock()
+        self.device = dev
+        self.dims = MODELS[synthetic["model"]]
+        self.buckets = tuple(c.get("buckets", BUCKETS))
+        mode = synthetic.get("mode", "rowwise")
+        layers = synthetic.get("layers")
+        with torch.cuda.device(dev), torch.no_grad():
+            src = make_model_bf16(self.dims, seed=int(synthetic.get("seed", 0)), device=dev, layers=layers)
+            self.model = PackedModel(self.dims, src, mode=mode, device=dev, free_source=True)
+            del src
+            torch.cuda.empty_cache()
+            self.engine = Engine(self.model)
+        lay = synthetic.get("layout", {})
+        self.layout = Layout(int(lay.get("image_start", 0)), int(lay.get("grid_h", 32)), int(lay.get("grid_w", 32)),
+                             int(lay.get("n_text", 64)))
+        self.encoder = encoder or SyntheticEncoder(self.dims, self.layout)
+        self._staging = {}
+
+    # ------------------------------------------------------------------ path entry
+    def prefill_score(self, ids, visual, deep, k, image_start=0, grid_h=32, grid_w=32, pick=None):
+        """Prefill + choice scoring of one request; returns (logits [k], logprobs [k]) lists.
+
+        ids [n] int64, visual [nv, H] bf16, deep list of [nv, H] bf16 -- host (pinned or
+        pageable) or device tensors.  n is padded with id 0 to the first bucket >= n."""
+        import torch
+        n = int(ids.shape[0])
+        if not 2 <= k <= 8:
+            raise ValueError("Provide two to eight choices")
+        bucket = next((b for b in self.buckets if b >= n), None)
+        if bucket is None:
+            raise ValueError(f"{n} tokens exceed the largest bucket {self.buckets[-1]} (no truncation)")
+        nv = int(visual.shape[0]) if visual is not None else 0
+        if nv != (grid_h // 2) * (grid_w // 2):
+            raise ValueError("visual rows must match the merged image grid")
+        pick = n - 1 if pick is None else int(pick)
+        with self.lock, torch.no_grad(), torch.cuda.device(self.device):
+            entry = self.engine.capture(bucket, image_start, nv, grid_h, grid_w, k, len(deep or []))
+            z, lp = self.engine.replay(entry, ids.to(self.device, non_blocking=True),
+                                       visual.to(self.device, non_blocking=True) if nv else None,
+                                       [x.to(self.device, non_blocking=True) for x in (deep or [])], pick)
+            out = torch.stack([z, lp]).cpu()  # one device->host read, synchronises the stream
+        return out[0].tolist(), out[1].tolist()
+
+    def predict(self, image, question, candidates, item_id="request", *, backend=None):
+        validate_request(image, question, candidates)
+        mode = self.backend if backend is None else backend
+        if mode not in BACKENDS:
+            raise ValueError("Unknown backend")
+        with self.lock:
+            r = self.encoder(str(image), question, list(candidates))
+            z, lp = self.prefill_score(r.ids, r.visual, r.deep, len(candidates), r.image_start, r.grid_h,
+                                       r.grid_w)
+        return response(z, candidates, item_id, logprobs=lp)
+
+    def warmup(self, requests):
+        for r in requests:
+            self.predict(r["image_path"], r["instruction"], r["candidates"], r.get("item_id", "warmup"))
+
+    def activate_fast(self):
+        """The packed FP8/int4 weights are built at construction; kept for API parity."""
+        with self.lock:
+            self.backend = "fast"

@@ -1,0 +1,95 @@
+"""Model shapes and request layouts of the Qwen3-VL language decoders this path serves.
+
+The four families are the ones FastForward ships bundles for (`configs/{2B,4B,8B,32B}.json`,
+`expected_dimensions` = (layers, hidden, vision blocks)); the remaining dimensions are the
+published Qwen3-VL text-config values.  Buckets follow the reference bundles: 64..2048 in
+steps of 16 (`configs/*.json` "buckets").
+"""
+from dataclasses import dataclass, field, asdict
+
+BUCKETS = tuple(range(64, 2049, 16))
+VOCAB = 151936
+# Eight fixed token ids standing in for the tokens of " A" .. " H"
+# (`scaled_qwen_runtime.py:70-72` reads them from the tokenizer, which is absent here).
+OPTION_IDS = (362, 425, 356, 422, 468, 434, 479, 472)
+
+
+@dataclass(frozen=True)
+class Dims:
+    name: str
+    layers: int
+    hidden: int
+    hq: int
+    hk: int
+    inter: int
+    d: int = 128
+    vocab: int = VOCAB
+    tied: bool = True
+    eps: float = 1e-6
+    theta: float = 5_000_000.0
+    sections: tuple = (24, 20, 20)
+    deepstack: int = 3
+
+    @property
+    def qkv_out(self):
+        return (self.hq + 2 * self.hk) * self.d
+
+    def as_dict(self):
+        return asdict(self)
+
+    def params_per_layer(self):
+        h, i = self.hidden, self.inter
+        return self.qkv_out * h + h * self.hq * self.d + 2 * i * h + h * i
+
+
+MODELS = {
+    "2B": Dims("2B", 28, 2048, 16, 8, 6144, tied=True),
+    "4B": Dims("4B", 36, 2560, 32, 8, 9728, tied=True),
+    "8B": Dims("8B", 36, 4096, 32, 8, 12288, tied=False),
+    "32B": Dims("32B", 64, 5120, 64, 8, 25600, tied=False),
+}
+
+
+@dataclass
+class Layout:
+    """Token layout of one request: [prefix text][image grid][suffix text] + bucket padding.
+
+    `grid_h`/`grid_w` are patch-grid sizes before the 2x2 merge (as `image_grid_thw`),
+    so the image contributes (grid_h/2)*(grid_w/2) visual tokens.
+    """
+    image_start: int
+    grid_h: int
+    grid_w: int
+    n_text: int
+    k: int = 4
+    extra: dict = field(default_factory=dict)
+
+    @property
+    def nv(self):
+        return (self.grid_h // 2) * (self.grid_w // 2)
+
+    @property
+    def n_tokens(self):
+        return self.image_start + self.nv + self.n_text
+
+    @property
+    def bucket(self):
+        n = self.n_tokens
+        return next(b for b in BUCKETS if b >= n)
+
+    @property
+    def pick(self):
+        return self.n_tokens - 1
+
+
+# The benchmark configurations (synthetic stand-ins for the reference's VQA suites).
+WORKLOADS = {
+    # 2B-shaped, 256 visual tokens on a 16x16 LLM grid + 64 text, 4 choices
+    "2B-fp8-T320": ("2B", Layout(0, 32, 32, 64, k=4), "rowwise"),
+    # north-star: 4B-shaped FP8 prefill of 320 tokens + choice scoring
+    "4B-fp8-T320": ("4B", Layout(0, 32, 32, 64, k=4), "rowwise"),
+    # 4B-shaped W4A16, 512 visual tokens on a 16x32 grid + 64 text, 8 choices
+    "4B-w4a16-T576": ("4B", Layout(0, 32, 64, 64, k=8), "int4"),
+    # 32B-shaped FP8, 960 visual tokens on a 30x32 grid + 64 text, 4 choices
+    "32B-fp8-T1024": ("32B", Layout(0, 60, 64, 64, k=4), "rowwise"),
+}

@@ -1,0 +1,107 @@
+// Library-wide host plumbing: thread-local error messages, the per-device error word,
+// and TMA descriptor encoding through the driver entry point (no link against libcuda).
+#include "common.cuh"
+
+#include <stdarg.h>
+#include <string.h>
+#include <mutex>
+
+__device__ uint32_t ffb_device_error_word = 0;
+
+namespace ffb {
+
+int g_use_pdl = 1;
+
+static thread_local char g_last_error[512] = "";
+
+void set_error(const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+  va_end(ap);
+}
+
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int check_launch(const char* what) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(FFB_ECUDA, "%s: launch failed: %s", what, cudaGetErrorString(e));
+  return FFB_OK;
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+int make_tmap_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t row_bytes,
+                 uint32_t box_rows, uint32_t box_cols, int elem_bytes) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(FFB_ECUDA, "cuTensorMapEncodeTiled is unavailable from the driver");
+  if (!aligned(base, 16)) return fail(FFB_EINVAL, "TMA base address must be 16-byte aligned");
+  if (row_bytes % 16 != 0) return fail(FFB_EINVAL, "TMA row pitch (%llu bytes) must be a multiple of 16",
+                                       (unsigned long long)row_bytes);
+  if ((uint64_t)box_cols * elem_bytes != 128)
+    return fail(FFB_EINVAL, "TMA box inner extent must be 128 bytes for the 128-byte swizzle");
+  CUtensorMapDataType dt = elem_bytes == 1 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {row_bytes};
+  cuuint32_t box[2] = {box_cols, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(FFB_ECUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return FFB_OK;
+}
+
+}  // namespace ffb
+
+extern "C" {
+
+const char* ffb_version(void) { return "ffb200 0.1.0 sm_100a"; }
+
+int ffb_set_pdl(int enable) {
+  const int old = ffb::g_use_pdl;
+  ffb::g_use_pdl = enable ? 1 : 0;
+  return old;
+}
+
+int ffb_last_error(char* buf, size_t len) {
+  if (!buf || len == 0) return FFB_EINVAL;
+  strncpy(buf, ffb::g_last_error, len - 1);
+  buf[len - 1] = 0;
+  return FFB_OK;
+}
+
+int ffb_device_error(uint32_t* word, int clear) {
+  if (!word) return ffb::fail(FFB_EINVAL, "ffb_device_error: word is NULL");
+  cudaError_t e = cudaMemcpyFromSymbol(word, ffb_device_error_word, sizeof(uint32_t));
+  if (e != cudaSuccess) return ffb::fail(FFB_ECUDA, "ffb_device_error: %s", cudaGetErrorString(e));
+  if (clear) {
+    uint32_t zero = 0;
+    e = cudaMemcpyToSymbol(ffb_device_error_word, &zero, sizeof(uint32_t));
+    if (e != cudaSuccess) return ffb::fail(FFB_ECUDA, "ffb_device_error: %s", cudaGetErrorString(e));
+  }
+  return FFB_OK;
+}
+
+}  // extern "C"

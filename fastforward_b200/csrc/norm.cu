@@ -1,0 +1,237 @@
+// RMSNorm and residual-add + RMSNorm, each optionally emitting the FP8 copy of its
+// output that the next linear consumes (so the quantiser needs no launch of its own).
+//
+// Rounding follows the reference kernels: x = bf16(a + b) (and bf16(x + deep) on the
+// deepstack rows), y = bf16(bf16(x * inv) * w) (_legacy/lower_kernels.py:7-21,
+// _legacy/sub10_runtime.py:31-36), with inv = 1/sqrt(sum(x^2)/H + eps) computed from an
+// exact float64 sum of squares and IEEE sqrt/divide (order-independent, so the result is
+// reproducible bit for bit; the reference's fp32 tree sum + hardware rsqrt is not).  One CTA per row,
+// 128-bit vector loads, the row held in registers between the reduction and the store.
+// HBM traffic per row: read a, b (or the split-K partials), w; write residual, out, q8.
+#include "common.cuh"
+#include "pdl.cuh"
+
+namespace {
+
+constexpr int NT = 256;   // threads per row
+constexpr int MAXV = 4;   // 8-element vectors per thread -> H <= 8192
+
+__device__ __forceinline__ double block_sum_d(double v, double* red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  v = warp_sum_d(v);
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  double r = (lane < NT / 32) ? red[lane] : 0.0;
+  if (warp == 0) {
+    r = warp_sum_d(r);
+    if (lane == 0) red[NT / 32] = r;
+  }
+  __syncthreads();
+  r = red[NT / 32];
+  __syncthreads();
+  return r;
+}
+
+__device__ __forceinline__ float block_reduce(float v, float* red, bool is_max) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  v = is_max ? warp_max(v) : warp_sum(v);
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float r = (lane < NT / 32) ? red[lane] : (is_max ? 0.f : 0.f);
+  if (warp == 0) {
+    r = is_max ? warp_max(r) : warp_sum(r);
+    if (lane == 0) red[NT / 32] = r;
+  }
+  __syncthreads();
+  r = red[NT / 32];
+  __syncthreads();
+  return r;
+}
+
+__device__ __forceinline__ void load8(const uint16_t* p, float (&f)[8]) {
+  uint4 u = *reinterpret_cast<const uint4*>(p);
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    f[2 * i] = __uint_as_float(w[i] << 16);
+    f[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+  }
+}
+__device__ __forceinline__ void store8(uint16_t* p, const float (&f)[8]) {
+  uint32_t w[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) w[i] = (uint32_t)f2bf(f[2 * i]) | ((uint32_t)f2bf(f[2 * i + 1]) << 16);
+  *reinterpret_cast<uint4*>(p) = make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+struct NormArgs {
+  const uint16_t* a;
+  const uint16_t* b;
+  const float* b32;
+  int splits;
+  const uint16_t* deep;
+  int start, nv;
+  const uint16_t* w;
+  float eps;
+  uint16_t* residual;
+  uint16_t* out;
+  int quant_mode;
+  float inv_scale;
+  uint8_t* q8;
+  float* qscale;
+  int T, H;
+  int add;  // 0: plain RMSNorm of a
+};
+
+__global__ void __launch_bounds__(NT) add_rmsnorm_kernel(const NormArgs p) {
+  __shared__ float red[NT / 32 + 1];
+  __shared__ double redd[NT / 32 + 1];
+  pdl_wait();
+  const int row = blockIdx.x;
+  const int nvec = p.H / 8;
+  const size_t base = (size_t)row * p.H;
+  const bool deep_row = p.deep && row >= p.start && row < p.start + p.nv;
+  float x[MAXV][8];
+  double ss = 0.0;
+#pragma unroll
+  for (int i = 0; i < MAXV; ++i) {
+    const int v = threadIdx.x + i * NT;
+    if (v < nvec) {
+      load8(p.a + base + v * 8, x[i]);
+      if (p.add) {
+        float b[8];
+        if (p.b) {
+          load8(p.b + base + v * 8, b);
+        } else {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) b[e] = 0.f;
+          for (int s = 0; s < p.splits; ++s) {
+            const float4* src = reinterpret_cast<const float4*>(p.b32 + (size_t)s * p.T * p.H + base + v * 8);
+            const float4 lo = src[0], hi = src[1];
+            b[0] += lo.x; b[1] += lo.y; b[2] += lo.z; b[3] += lo.w;
+            b[4] += hi.x; b[5] += hi.y; b[6] += hi.z; b[7] += hi.w;
+          }
+#pragma unroll
+          for (int e = 0; e < 8; ++e) b[e] = round_bf(b[e]);  // the linear's bf16 output
+        }
+#pragma unroll
+        for (int e = 0; e < 8; ++e) x[i][e] = round_bf(x[i][e] + b[e]);
+        if (deep_row) {
+          float d[8];
+          load8(p.deep + (size_t)(row - p.start) * p.H + v * 8, d);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) x[i][e] = round_bf(x[i][e] + d[e]);
+        }
+        if (p.residual) store8(p.residual + base + v * 8, x[i]);
+      }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) ss += (double)(x[i][e] * x[i][e]);  // x*x exact in fp32
+    }
+  }
+  const float inv = inv_rms_from_ss(block_sum_d(ss, redd), p.H, p.eps);
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < MAXV; ++i) {
+    const int v = threadIdx.x + i * NT;
+    if (v < nvec) {
+      float w[8];
+      load8(p.w + v * 8, w);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        x[i][e] = round_bf(round_bf(x[i][e] * inv) * w[e]);
+        amax = fmaxf(amax, fabsf(x[i][e]));
+      }
+      if (p.out) store8(p.out + base + v * 8, x[i]);
+    }
+  }
+  pdl_launch();
+  if (p.quant_mode == FFB_QUANT_NONE) return;
+  float mul = p.inv_scale, scale = 0.f;
+  if (p.quant_mode == FFB_QUANT_ROWWISE) {
+    amax = block_reduce(amax, red, true);
+    scale = fmaxf(amax, 1e-12f) / 448.f;
+    if (threadIdx.x == 0) p.qscale[row] = scale;
+  }
+#pragma unroll
+  for (int i = 0; i < MAXV; ++i) {
+    const int v = threadIdx.x + i * NT;
+    if (v < nvec) {
+      uint32_t lo = 0, hi = 0;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float qv = p.quant_mode == FFB_QUANT_ROWWISE ? __fdiv_rn(x[i][e], scale) : x[i][e] * mul;
+        const uint32_t b = f2e4m3(clamp448(qv));
+        if (e < 4) lo |= b << (8 * e);
+        else hi |= b << (8 * (e - 4));
+      }
+      *reinterpret_cast<uint2*>(p.q8 + base + v * 8) = make_uint2(lo, hi);
+    }
+  }
+}
+
+int run(const NormArgs& p, const char* who, void* stream) {
+  FFB_REQUIRE(p.a && p.w, "%s: NULL input", who);
+  FFB_REQUIRE(p.T > 0 && p.H > 0 && p.H % 8 == 0 && p.H <= NT * MAXV * 8, "%s: H=%d must be a multiple of 8 and <= %d",
+              who, p.H, NT * MAXV * 8);
+  FFB_REQUIRE(p.quant_mode >= 0 && p.quant_mode <= 2, "%s: bad quant_mode %d", who, p.quant_mode);
+  FFB_REQUIRE(p.quant_mode == FFB_QUANT_NONE || p.q8, "%s: quant_mode needs q8", who);
+  FFB_REQUIRE(p.quant_mode != FFB_QUANT_ROWWISE || p.qscale, "%s: ROWWISE needs qscale", who);
+  FFB_REQUIRE(p.out || p.quant_mode != FFB_QUANT_NONE, "%s: nothing to write", who);
+  FFB_REQUIRE(ffb::aligned(p.a, 16) && ffb::aligned(p.w, 16) && (!p.out || ffb::aligned(p.out, 16)),
+              "%s: bf16 rows must be 16-byte aligned", who);
+  FFB_REQUIRE(!p.q8 || ffb::aligned(p.q8, 8), "%s: q8 must be 8-byte aligned", who);
+  cudaError_t e = ffb::launch(add_rmsnorm_kernel, dim3(p.T), dim3(NT), 0, (cudaStream_t)stream, p);
+  if (e != cudaSuccess) return ffb::fail(FFB_ECUDA, "%s: launch: %s", who, cudaGetErrorString(e));
+  return FFB_OK;
+}
+
+}  // namespace
+
+extern "C" int ffb_rmsnorm(const uint16_t* x, const uint16_t* w, float eps, uint16_t* out, int quant_mode,
+                           float inv_scale, uint8_t* q8, float* qscale, int T, int H, void* stream) {
+  NormArgs p = {};
+  p.a = x;
+  p.w = w;
+  p.eps = eps;
+  p.out = out;
+  p.quant_mode = quant_mode;
+  p.inv_scale = inv_scale;
+  p.q8 = q8;
+  p.qscale = qscale;
+  p.T = T;
+  p.H = H;
+  p.add = 0;
+  return run(p, "ffb_rmsnorm", stream);
+}
+
+extern "C" int ffb_add_rmsnorm(const uint16_t* a, const uint16_t* b, const float* b32, int splits,
+                               const uint16_t* deep, int start, int nv, const uint16_t* w, float eps,
+                               uint16_t* residual, uint16_t* out, int quant_mode, float inv_scale, uint8_t* q8,
+                               float* qscale, int T, int H, void* stream) {
+  FFB_REQUIRE(b || (b32 && splits >= 1), "ffb_add_rmsnorm: need b or (b32, splits >= 1)");
+  FFB_REQUIRE(!b32 || ffb::aligned(b32, 16), "ffb_add_rmsnorm: b32 must be 16-byte aligned");
+  FFB_REQUIRE(!b || ffb::aligned(b, 16), "ffb_add_rmsnorm: b must be 16-byte aligned");
+  FFB_REQUIRE(!deep || (start >= 0 && nv >= 0 && start + nv <= T && ffb::aligned(deep, 16)),
+              "ffb_add_rmsnorm: bad deepstack window start=%d nv=%d T=%d", start, nv, T);
+  FFB_REQUIRE(residual != nullptr, "ffb_add_rmsnorm: residual is NULL");
+  NormArgs p = {};
+  p.a = a;
+  p.b = b;
+  p.b32 = b ? nullptr : b32;
+  p.splits = splits;
+  p.deep = deep;
+  p.start = start;
+  p.nv = deep ? nv : 0;
+  p.w = w;
+  p.eps = eps;
+  p.residual = residual;
+  p.out = out;
+  p.quant_mode = quant_mode;
+  p.inv_scale = inv_scale;
+  p.q8 = q8;
+  p.qscale = qscale;
+  p.T = T;
+  p.H = H;
+  p.add = 1;
+  return run(p, "ffb_add_rmsnorm", stream);
+}

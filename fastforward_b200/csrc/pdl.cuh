@@ -1,0 +1,30 @@
+// Programmatic dependent launch helpers.  Every kernel of the library calls pdl_wait()
+// before its first global-memory access (read or write), so launching it with the
+// programmatic-serialization attribute only overlaps its launch and prologue with the
+// tail of the previous kernel on the stream; without the attribute both calls are no-ops.
+#pragma once
+#include <cuda_runtime.h>
+
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+namespace ffb {
+// Process-wide switch (set through ffb_set_pdl); read when a kernel is launched.
+extern int g_use_pdl;
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                          Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = g_use_pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+}  // namespace ffb

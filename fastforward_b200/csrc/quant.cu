@@ -1,0 +1,161 @@
+// FP8 quantisers: activations (static per-tensor scale or per-token dynamic scale),
+// set-up-time weights (per-tensor or per-output-channel absmax), and the gate/up row
+// interleave used by the fused SwiGLU GEMM epilogue.
+//
+// Static:   q = e4m3(clamp(x * inv, +-448))              _family/depth_fp8.py:8-12
+// Rowwise:  s = max(max|x|, 1e-12)/448, q = e4m3(x / s)    _legacy/fp8_private.py:11-18
+// Weights:  s = max(max|W|, 1e-12)/448, W8 = e4m3(W / s)   _legacy/limit_kernels.py:122-127
+//                                       (per row: _legacy/fp8_private.py:22-27)
+// All divisions are IEEE round-to-nearest (__fdiv_rn), all conversions RNE, so the bytes
+// are reproducible on any IEEE implementation.
+#include "common.cuh"
+#include "pdl.cuh"
+
+namespace {
+
+constexpr int NT = 256;
+
+__device__ __forceinline__ float block_max(float v, float* red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  v = warp_max(v);
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  if (warp == 0) {
+    float r = lane < NT / 32 ? red[lane] : 0.f;
+    r = warp_max(r);
+    if (lane == 0) red[NT / 32] = r;
+  }
+  __syncthreads();
+  const float r = red[NT / 32];
+  __syncthreads();
+  return r;
+}
+
+// One CTA per row: absmax (ROWWISE only), then quantise.  Works for any K (scalar tail).
+__global__ void __launch_bounds__(NT) quant_rows_kernel(const uint16_t* __restrict__ x, int mode, float inv,
+                                                        uint8_t* __restrict__ q8, float* __restrict__ qscale,
+                                                        int K) {
+  __shared__ float red[NT / 32 + 1];
+  pdl_wait();
+  const int row = blockIdx.x;
+  const uint16_t* xr = x + (size_t)row * K;
+  uint8_t* qr = q8 + (size_t)row * K;
+  float scale = 0.f;
+  if (mode == FFB_QUANT_ROWWISE) {
+    float amax = 0.f;
+    for (int k = threadIdx.x; k < K; k += NT) amax = fmaxf(amax, fabsf(bf2f(xr[k])));
+    amax = block_max(amax, red);
+    scale = fmaxf(amax, 1e-12f) / 448.f;
+    if (threadIdx.x == 0) qscale[row] = scale;
+  }
+  pdl_launch();
+  for (int k = threadIdx.x; k < K; k += NT) {
+    const float v = bf2f(xr[k]);
+    const float qv = mode == FFB_QUANT_ROWWISE ? __fdiv_rn(v, scale) : v * inv;
+    qr[k] = f2e4m3(clamp448(qv));
+  }
+}
+
+// Weight absmax per row into ws (fp32), or the global max when `reduce_rows` > 0.
+__global__ void __launch_bounds__(NT) row_absmax_kernel(const uint16_t* __restrict__ w, float* __restrict__ out,
+                                                        int K) {
+  __shared__ float red[NT / 32 + 1];
+  pdl_wait();
+  const uint16_t* wr = w + (size_t)blockIdx.x * K;
+  float amax = 0.f;
+  for (int k = threadIdx.x; k < K; k += NT) amax = fmaxf(amax, fabsf(bf2f(wr[k])));
+  amax = block_max(amax, red);
+  if (threadIdx.x == 0) out[blockIdx.x] = amax;
+}
+
+__global__ void __launch_bounds__(NT) global_scale_kernel(const float* __restrict__ rowmax, int N,
+                                                          float* __restrict__ scale) {
+  __shared__ float red[NT / 32 + 1];
+  pdl_wait();
+  float m = 0.f;
+  for (int i = threadIdx.x; i < N; i += NT) m = fmaxf(m, rowmax[i]);
+  m = block_max(m, red);
+  if (threadIdx.x == 0) scale[0] = fmaxf(m, 1e-12f) / 448.f;
+}
+
+// W8[n,k] = e4m3(clamp(W / s)), s = scale[per_channel ? n : 0]; per-channel scales are
+// produced here from rowmax.
+__global__ void __launch_bounds__(NT) weight_quant_kernel(const uint16_t* __restrict__ w,
+                                                          const float* __restrict__ rowmax, int per_channel,
+                                                          float* __restrict__ scale, uint8_t* __restrict__ w8,
+                                                          int K) {
+  pdl_wait();
+  const int n = blockIdx.x;
+  float s;
+  if (per_channel) {
+    s = fmaxf(rowmax[n], 1e-12f) / 448.f;
+    if (threadIdx.x == 0) scale[n] = s;
+  } else {
+    s = scale[0];
+  }
+  const uint16_t* wr = w + (size_t)n * K;
+  uint8_t* qr = w8 + (size_t)n * K;
+  for (int k = threadIdx.x; k < K; k += NT) qr[k] = f2e4m3(clamp448(__fdiv_rn(bf2f(wr[k]), s)));
+}
+
+// Row permutation for the SwiGLU epilogue: dst tile t = src gate rows [64t, 64t+64) then
+// src up rows [I + 64t, I + 64t + 64).  One CTA per destination row.
+__global__ void pack_gateup_kernel(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst, int I,
+                                   size_t row_bytes) {
+  pdl_wait();
+  const int r = blockIdx.x;
+  const int t = r / 128, j = r % 128;
+  const int s = j < 64 ? 64 * t + j : I + 64 * t + (j - 64);
+  const uint8_t* a = src + (size_t)s * row_bytes;
+  uint8_t* b = dst + (size_t)r * row_bytes;
+  if (row_bytes % 16 == 0) {
+    for (size_t i = threadIdx.x; i < row_bytes / 16; i += blockDim.x)
+      reinterpret_cast<uint4*>(b)[i] = reinterpret_cast<const uint4*>(a)[i];
+  } else {
+    for (size_t i = threadIdx.x; i < row_bytes; i += blockDim.x) b[i] = a[i];
+  }
+}
+
+}  // namespace
+
+extern "C" int ffb_quantize_fp8(const uint16_t* x, int quant_mode, float inv_scale, uint8_t* q8, float* qscale,
+                                int M, int K, void* stream) {
+  FFB_REQUIRE(x && q8, "ffb_quantize_fp8: NULL pointer");
+  FFB_REQUIRE(M > 0 && K > 0, "ffb_quantize_fp8: bad shape M=%d K=%d", M, K);
+  FFB_REQUIRE(quant_mode == FFB_QUANT_STATIC || quant_mode == FFB_QUANT_ROWWISE, "ffb_quantize_fp8: bad mode %d",
+              quant_mode);
+  FFB_REQUIRE(quant_mode != FFB_QUANT_ROWWISE || qscale, "ffb_quantize_fp8: ROWWISE needs qscale");
+  cudaError_t e = ffb::launch(quant_rows_kernel, dim3(M), dim3(NT), 0, (cudaStream_t)stream, x, quant_mode,
+                              inv_scale, q8, qscale, K);
+  if (e != cudaSuccess) return ffb::fail(FFB_ECUDA, "ffb_quantize_fp8: %s", cudaGetErrorString(e));
+  return FFB_OK;
+}
+
+extern "C" int ffb_quantize_weight_fp8(const uint16_t* w, int per_channel, uint8_t* w8, float* scale, void* ws,
+                                       int N, int K, void* stream) {
+  FFB_REQUIRE(w && w8 && scale && ws, "ffb_quantize_weight_fp8: NULL pointer");
+  FFB_REQUIRE(N > 0 && K > 0, "ffb_quantize_weight_fp8: bad shape N=%d K=%d", N, K);
+  cudaStream_t s = (cudaStream_t)stream;
+  float* rowmax = reinterpret_cast<float*>(ws);
+  cudaError_t e = ffb::launch(row_absmax_kernel, dim3(N), dim3(NT), 0, s, w, rowmax, K);
+  if (e == cudaSuccess && !per_channel)
+    e = ffb::launch(global_scale_kernel, dim3(1), dim3(NT), 0, s, (const float*)rowmax, N, scale);
+  if (e == cudaSuccess)
+    e = ffb::launch(weight_quant_kernel, dim3(N), dim3(NT), 0, s, w, (const float*)rowmax, per_channel, scale, w8, K);
+  if (e != cudaSuccess) return ffb::fail(FFB_ECUDA, "ffb_quantize_weight_fp8: %s", cudaGetErrorString(e));
+  return FFB_OK;
+}
+
+extern "C" int ffb_pack_gateup(const void* src, void* dst, int I, int K, int elem_bytes, void* stream) {
+  FFB_REQUIRE(src && dst && src != dst, "ffb_pack_gateup: bad pointers");
+  FFB_REQUIRE(I > 0 && I % 64 == 0, "ffb_pack_gateup: I=%d must be a multiple of 64", I);
+  FFB_REQUIRE(elem_bytes == 1 || elem_bytes == 2 || elem_bytes == 4, "ffb_pack_gateup: elem_bytes %d", elem_bytes);
+  FFB_REQUIRE(K > 0, "ffb_pack_gateup: K=%d", K);
+  const size_t row_bytes = (size_t)K * elem_bytes;
+  FFB_REQUIRE(row_bytes % 16 != 0 || (ffb::aligned(src, 16) && ffb::aligned(dst, 16)),
+              "ffb_pack_gateup: rows must be 16-byte aligned");
+  cudaError_t e = ffb::launch(pack_gateup_kernel, dim3(2 * I), dim3(128), 0, (cudaStream_t)stream,
+                              (const uint8_t*)src, (uint8_t*)dst, I, row_bytes);
+  if (e != cudaSuccess) return ffb::fail(FFB_ECUDA, "ffb_pack_gateup: %s", cudaGetErrorString(e));
+  return FFB_OK;
+}

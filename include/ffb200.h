@@ -1,0 +1,182 @@
+/*
+ * ffb200.h - C ABI of libffb200.so, the B200 (sm_100a) kernels behind FastForward's
+ * Qwen3-VL language-decoder prefill + choice-scoring path.
+ *
+ * Every entry point replaces one fused op of the reference (FastForward 0.2.4.post1,
+ * paths relative to src/fastforward_accel/), cited beside it.  Conventions:
+ *   - all tensor arguments are caller-owned device pointers; bf16 tensors are passed
+ *     as raw 16-bit words (uint16_t), FP8 e4m3 as uint8_t, row-major unless stated;
+ *   - `stream` is a cudaStream_t passed as void*; work is enqueued on it and the call
+ *     returns without synchronising; no entry point allocates device memory, except
+ *     ffb_quantize_weight_fp8 which is a set-up call (it synchronises nothing either);
+ *     scratch space is always passed in (`ws`);
+ *   - return value 0 on success, a negative FFB_E* code otherwise; the message of the
+ *     last failure on the calling thread is available from ffb_last_error();
+ *   - reentrant: the only mutable global state is a per-device error word that kernels
+ *     set when a bounded device-side wait gives up (read with ffb_device_error()).
+ */
+#ifndef FFB200_H
+#define FFB200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define FFB_OK 0
+#define FFB_EINVAL (-1)        /* bad shape / pointer / alignment / argument        */
+#define FFB_EUNSUPPORTED (-2)  /* a configuration the kernels do not implement      */
+#define FFB_ECUDA (-3)         /* a CUDA runtime / driver call failed               */
+#define FFB_ETIMEOUT (-4)      /* a kernel's bounded wait gave up (device error word) */
+
+/* Activation quantisation modes of the FP8 path. */
+#define FFB_QUANT_NONE 0       /* no FP8 output                                           */
+#define FFB_QUANT_STATIC 1     /* q = e4m3(clamp(x * inv, +-448)); depth_fp8.py:8-12       */
+#define FFB_QUANT_ROWWISE 2    /* s = max|x_row|/448, q = e4m3(x / s); fp8_private.py:11-18 */
+
+/* GEMM epilogues. */
+#define FFB_EPI_BF16 0         /* out[m,n] = bf16(acc * sa * sw)                           */
+#define FFB_EPI_F32_PARTIAL 1  /* ws[split][m][n] = acc * sa * sw (fp32), reduced by the consumer */
+#define FFB_EPI_SWIGLU 2       /* gate/up rows interleaved per 64; out[m,c] = bf16(bf16(silu(g)) * u) */
+
+/* Library identification: returns a static string ("ffb200 <version> sm_100a"). */
+const char* ffb_version(void);
+
+/* Enables (1) or disables (0) programmatic dependent launch for every kernel launched
+ * afterwards (default on): each kernel then overlaps its launch and prologue with the
+ * previous kernel on the stream and waits on the device before touching memory.
+ * Returns the previous setting.  Process-wide; not a per-call argument. */
+int ffb_set_pdl(int enable);
+
+/* Copies the calling thread's last error message into buf (always NUL-terminated). */
+int ffb_last_error(char* buf, size_t len);
+
+/* Reads (and with clear != 0, resets) the current device's error word: 0 = no error,
+ * else a bit set per kernel family whose bounded wait timed out.  Synchronous. */
+int ffb_device_error(uint32_t* word, int clear);
+
+/* Embedding gather + visual-row scatter.
+ * Replaces scaled_qwen_runtime.py:145 `embed_tokens(ids).index_copy(1, vi, visual)`.
+ * h[t] = table[ids[t]] for t outside [image_start, image_start+nv), visual[t-image_start] inside. */
+int ffb_embed_gather(const int64_t* ids, const uint16_t* table, int64_t vocab,
+                     const uint16_t* visual, int image_start, int nv,
+                     uint16_t* h, int T, int H, void* stream);
+
+/* Plain RMSNorm (+ optional fused FP8 quantisation of the output).
+ * Replaces _legacy/sub10_runtime.py:31-41 (`rms_one` / `fast_norm`); the fused quant
+ * replaces the quantiser launched by the next linear (_family/depth_fp8.py:15-19 or
+ * _legacy/fp8_private.py:11-18).  out may be NULL when only the FP8 copy is wanted.
+ * q8 [T,H] e4m3 and qscale [T] fp32 (ROWWISE) are written when quant_mode != NONE. */
+int ffb_rmsnorm(const uint16_t* x, const uint16_t* w, float eps, uint16_t* out,
+                int quant_mode, float inv_scale, uint8_t* q8, float* qscale,
+                int T, int H, void* stream);
+
+/* Residual add (+ deepstack rows) + RMSNorm (+ optional fused FP8 quant).
+ * Replaces _legacy/lower_kernels.py:7-32 (`_add_rms` / `add_rms`).
+ * b is the bf16 [T,H] branch output, or (b == NULL) the sum over `splits` fp32 partial
+ * tiles b32[splits][T][H] that a split-K GEMM left (rounded to bf16 before the add).
+ * deep [nv,H] is added to rows [start, start+nv) (NULL for none). */
+int ffb_add_rmsnorm(const uint16_t* a, const uint16_t* b, const float* b32, int splits,
+                    const uint16_t* deep, int start, int nv,
+                    const uint16_t* w, float eps, uint16_t* residual, uint16_t* out,
+                    int quant_mode, float inv_scale, uint8_t* q8, float* qscale,
+                    int T, int H, void* stream);
+
+/* Per-head QK RMSNorm + interleaved-M-RoPE rotation (rotate-half with bf16 cos/sin).
+ * Replaces _legacy/broad_kernels.py:63-74 (`qk_pair`) -> lower_kernels.py:66-98.
+ * Input: the packed qkv rows [T, (HQ+2HK)*128] as bf16 (qkv) or as `splits` fp32
+ * partials (qkv == NULL, qkv32[splits][T][row_stride]).  Output head-major:
+ * yq [HQ,T,128], yk [HK,T,128] and the V copy yv [HK,T,128] (yv may be NULL). */
+int ffb_qk_norm_rope(const uint16_t* qkv, const float* qkv32, int splits, int row_stride,
+                     const uint16_t* q_norm, const uint16_t* k_norm, float eps,
+                     const uint16_t* cos, const uint16_t* sin,
+                     uint16_t* yq, uint16_t* yk, uint16_t* yv,
+                     int T, int HQ, int HK, void* stream);
+
+/* Causal GQA attention, head_dim 128.
+ * Replaces _legacy/limit_kernels.py:36-45 (`attention_direct`, triangular, or SELECTED
+ * with `positions`).  k/v [HK,T,128] (head-major, contiguous); positions [S] int64 or
+ * NULL (= 0..S-1).  q is [HQ,S,128], or with q_gather != 0 (needs positions) the full
+ * [HQ,T,128] projection from which query row s is q[:, positions[s]] (the tail's
+ * `q.index_select(2, pick)`, _family/night_runtime.py:100).  out [S, HQ*128] bf16. */
+int ffb_attention(const uint16_t* q, const uint16_t* k, const uint16_t* v,
+                  const int64_t* positions, int q_gather, uint16_t* out,
+                  int S, int T, int HQ, int HK, float scale, void* stream);
+
+/* Copies rows index[i] of src [*, row_bytes] to dst [n, row_bytes] (index on device;
+ * the tail's `h.index_select(1, pick)`, _family/night_runtime.py:103). */
+int ffb_gather_rows(const void* src, const int64_t* index, void* dst, int n, int row_bytes,
+                    void* stream);
+
+/* Activation FP8 quantisation of a bf16 [M,K] matrix.
+ * STATIC replaces _family/depth_fp8.py:8-19 (`_runtime_scale`); ROWWISE replaces
+ * _legacy/fp8_private.py:11-18 (`quantize_rows`).  q8 [M,K]; qscale [M] (ROWWISE). */
+int ffb_quantize_fp8(const uint16_t* x, int quant_mode, float inv_scale,
+                     uint8_t* q8, float* qscale, int M, int K, void* stream);
+
+/* Set-up-time weight quantisation W [N,K] bf16 -> W8 [N,K] e4m3 + fp32 scale.
+ * per_channel = 0: one scale (_legacy/limit_kernels.py:122-127, StaticFP8Linear);
+ * per_channel = 1: scale[N] (_legacy/fp8_private.py:22-27, FP8Linear).
+ * ws: >= 4*N bytes of scratch. */
+int ffb_quantize_weight_fp8(const uint16_t* w, int per_channel, uint8_t* w8, float* scale,
+                            void* ws, int N, int K, void* stream);
+
+/* FP8 e4m3 W8A8 GEMM on tcgen05 (kind::f8f6f4), fp32 accumulation in tensor memory.
+ * Replaces _family/depth_fp8.py:22-26 (`RuntimeScaleLinear.__call__` -> torch._scaled_mm)
+ * and _legacy/fp8_private.py:29-38.  a8 [M,K] activations, w8 [N,K] weights (K-major);
+ * a_scale is [M] (a_per_row) or [1]; w_scale is [N] (w_per_col) or [1].
+ * epilogue FFB_EPI_BF16: out [M,N] bf16; FFB_EPI_F32_PARTIAL: ws [splits][M][N] fp32
+ * (the consumer sums the splits); FFB_EPI_SWIGLU: out [M,N/2] bf16 with w8 rows packed
+ * as 64 gate rows then the matching 64 up rows per 128-row tile (ffb_pack_gateup order).
+ * splits = K-split count (1 unless FFB_EPI_F32_PARTIAL); token_tile = 0 picks one. */
+int ffb_fp8_gemm(const uint8_t* a8, const float* a_scale, int a_per_row,
+                 const uint8_t* w8, const float* w_scale, int w_per_col,
+                 int epilogue, uint16_t* out, float* ws, int splits, int token_tile,
+                 int M, int N, int K, void* stream);
+
+/* Reorders the rows of a [2I,K] gate/up weight (gate rows 0..I-1, up rows I..2I-1) into
+ * the FFB_EPI_SWIGLU tile order: tile t = gate rows 64t..64t+63 then up rows 64t..64t+63.
+ * Works on any 1- or 2-byte element type of width `elem_bytes` (bf16 or e4m3), and on
+ * the matching [2I] per-channel scale vector when elem_bytes == 4. */
+int ffb_pack_gateup(const void* src, void* dst, int I, int K, int elem_bytes, void* stream);
+
+/* SwiGLU on strided gate/up views: y[m,i] = bf16(bf16(g/(1+exp(-g))) * u).
+ * Replaces _legacy/search_kernels.py:8-23 (`swiglu`).  gate/up rows have stride
+ * `row_stride` elements; y is [M, I] contiguous. */
+int ffb_swiglu(const uint16_t* gate, const uint16_t* up, int row_stride, uint16_t* y,
+               int M, int I, void* stream);
+
+/* Final tail readout: chosen = bf16(residual + mlp), final RMSNorm, dot with the n
+ * option rows, then log-softmax over the first k.
+ * Replaces _legacy/limit_kernels.py:48-66 (`lm_readout`) + the `residual[0] + mlp`
+ * add of _family/night_runtime.py:104.  mlp is a bf16 row, or (mlp == NULL) the sum of
+ * `splits` fp32 partial rows mlp32[splits][H] (rounded to bf16), or absent when both
+ * are NULL.  logits [n] fp32 (bf16-rounded dots as in the reference), logprobs [k] fp32
+ * (may be NULL). */
+int ffb_readout(const uint16_t* residual, const uint16_t* mlp, const float* mlp32, int splits,
+                const uint16_t* norm_w, float eps, const uint16_t* head, int n, int k,
+                float* logits, float* logprobs, int H, void* stream);
+
+/* Symmetric int4 group-128 weight packing for the W4A16 path:
+ * s = bf16(max|W_g|/7), q = clamp(rne(W/s), -8, 7), two nibbles per byte along K
+ * (low nibble = even k).  packed [N, K/2] uint8, scales [N, K/128] bf16.
+ * Replaces the packing of _family/night_runtime.py:15-26 (`Int4.__init__`) with the
+ * symmetric g128 scheme. */
+int ffb_pack_int4(const uint16_t* w, uint8_t* packed, uint16_t* scales, int N, int K,
+                  void* stream);
+
+/* W4A16 GEMM: out[m,n] = bf16( sum_k x[m,k] * bf16(q[n,k] * s[n,k/128]) ), weights
+ * dequantised to bf16 in shared memory and multiplied on tcgen05 (kind::f16).
+ * Replaces _family/night_runtime.py:31-33 (`Int4.__call__` -> _weight_int4pack_mm).
+ * x [M,K] bf16; epilogue FFB_EPI_BF16 / FFB_EPI_F32_PARTIAL / FFB_EPI_SWIGLU as above. */
+int ffb_w4a16_gemm(const uint16_t* x, const uint8_t* packed, const uint16_t* scales,
+                   int epilogue, uint16_t* out, float* ws, int splits, int token_tile,
+                   int M, int N, int K, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FFB200_H */

@@ -1,0 +1,531 @@
+"""CPU restatement of the reference's prefill + choice-scoring arithmetic.
+
+TEST INFRASTRUCTURE ONLY (see the package docstring): nothing in the product
+package imports this module.
+
+Every function names the reference file:line it restates (paths relative to the
+FastForward project root, `src/fastforward_accel/...`).  Rounding points are
+reproduced exactly: wherever the reference casts an fp32 intermediate to bf16
+(`.to(R.dtype.element_ty)` in its Triton kernels, or a bf16 store) this code does
+`_bf(...)`, which is fp32 -> bf16 round-to-nearest-even -> fp32.
+
+Known, documented differences from the GPU reference that are NOT modelled:
+  * RMSNorm statistics: the reference sums x^2 in fp32 (kernel order) and applies the
+    hardware `tl.rsqrt`; here (and in the CUDA kernels) the sum is exact (float64) and
+    the reciprocal square root is IEEE (see `_inv_rms`).  `tl.exp` is likewise replaced
+    by the correctly rounded exponential.
+  * fp32 dot-product reductions (attention, readout) have a different summation order.
+  * FP8 GEMMs accumulate in float64 here (exact for e4m3 x e4m3 products), so the
+    oracle is the "true" value that the GPU fp32 accumulation approximates.
+"""
+import math
+
+import torch
+
+BF16 = torch.bfloat16
+E4M3 = torch.float8_e4m3fn
+FP8_MAX = 448.0
+
+__all__ = [
+    "rms_one", "add_rms", "qk_pair", "attention_direct", "quantize_static",
+    "quantize_rows", "quantize_weight_tensor", "quantize_weight_channel",
+    "fp8_linear_static", "fp8_linear_rowwise", "swiglu", "lm_readout",
+    "log_softmax", "int4_sym_quantize", "int4_sym_dequantize", "int4_sym_pack",
+    "int4_asym_quantize", "mrope_position_ids", "mrope_cos_sin", "embed_rows",
+    "prefill_score", "decoder_layer", "tail", "response_argmax", "quantized_model",
+]
+
+
+def _bf(x):
+    """fp32 -> bf16 (round to nearest even) -> fp32."""
+    return x.float().to(BF16).float()
+
+
+def _f32(v):
+    """A Python float as the fp32 scalar a Triton constexpr becomes."""
+    return torch.tensor(v, dtype=torch.float32)
+
+
+def _inv_rms(x, eps):
+    """1 / sqrt(sum(x^2)/n + eps) for fp32 rows of bf16 values.
+
+    The reference sums x^2 in fp32 in its kernel's reduction order and uses the hardware
+    rsqrt; both are unspecified orders/approximations.  This restatement (and the CUDA
+    kernels) sum the squares -- exact in fp32, since x is bf16 -- in float64, which is exact
+    here and therefore order-independent, round the sum to fp32, divide by n in fp32 and
+    take an IEEE square root and IEEE reciprocal.  Every rounding after that follows the
+    reference.  Returns [..., 1] fp32."""
+    n = x.shape[-1]
+    ss = (x.double() * x.double()).sum(-1, keepdim=True).float()
+    var = ss / _f32(n)
+    return _f32(1.0) / torch.sqrt(var + _f32(eps))
+
+
+# ----------------------------------------------------------------------------- norms
+
+def rms_one(x, weight, eps):
+    """Plain RMSNorm, `_legacy/sub10_runtime.py:31-36` (`rms_one`).
+
+    variance = sum(x^2)/H (fp32); y = bf16( bf16(x * rsqrt(variance + eps)) * w ).
+    x: [..., H] bf16, weight: [H] bf16 -> [..., H] bf16.
+    """
+    xf = x.float()
+    n = _bf(xf * _inv_rms(xf, eps))
+    return (n * weight.float()).to(BF16)
+
+
+def add_rms(a, b, deep, weight, eps, start=0, nv=0):
+    """Residual add (+ deepstack rows) + RMSNorm, `_legacy/lower_kernels.py:7-21`.
+
+    x = bf16(a + b); rows in [start, start+nv) additionally x = bf16(x + deep[row-start]);
+    returns (residual = x, out = bf16(bf16(x * rsqrt(mean(x^2) + eps)) * w)).
+    a, b: [T, H] bf16; deep: [nv, H] bf16 or None.
+    """
+    x = _bf(a.float() + b.float())
+    if deep is not None and nv > 0:
+        x = x.clone()
+        x[start:start + nv] = _bf(x[start:start + nv] + deep.float())
+    n = _bf(x * _inv_rms(x, eps))
+    return x.to(BF16), (n * weight.float()).to(BF16)
+
+
+# ----------------------------------------------------------------------------- QK norm + RoPE
+
+def _rope_rows(x, w, cos, sin, eps):
+    """One (token, head) row set, `_legacy/lower_kernels.py:66-86` (`_rope_rows`).
+
+    x: [T, Hh, D] fp32 (bf16 values); cos/sin: [T, D] fp32 (bf16 values).
+    """
+    d = x.shape[-1]
+    half = d // 2
+    r = torch.cat((x[..., half:], x[..., :half]), -1)          # other = i +/- D/2
+    wf = w.float()
+    wr = torch.cat((wf[half:], wf[:half]))
+    inv = _inv_rms(x, eps)
+    xn = _bf(_bf(x * inv) * wf)
+    rn = _bf(_bf(r * inv) * wr)
+    sign = torch.cat((-torch.ones(half), torch.ones(half)))
+    rn = rn * sign
+    c = cos[:, None, :]
+    s = sin[:, None, :]
+    left = _bf(xn * c)
+    right = _bf(rn * s)
+    return (left + right).to(BF16)                                # store rounds to bf16
+
+
+def qk_pair(q, k, q_norm, k_norm, cos, sin, eps_q=1e-6, eps_k=1e-6):
+    """Per-head RMSNorm then rotate-half RoPE for Q and K.
+
+    Restates `_legacy/broad_kernels.py:63-74` (`qk_pair`, half=False) which launches
+    `_legacy/lower_kernels.py:89-98` (`_pair_rows`) -> `:66-86` (`_rope_rows`).
+    q: [T, HQ, D], k: [T, HK, D] bf16; cos/sin: [T, D] bf16.
+    Returns yq [HQ, T, D], yk [HK, T, D] bf16 (head-major).
+    """
+    c = cos.float()
+    s = sin.float()
+    yq = _rope_rows(q.float(), q_norm, c, s, eps_q).transpose(0, 1).contiguous()
+    yk = _rope_rows(k.float(), k_norm, c, s, eps_k).transpose(0, 1).contiguous()
+    return yq, yk
+
+
+# ----------------------------------------------------------------------------- attention
+
+def attention_direct(q, k, v, scale, positions=None, block_n=64):
+    """Causal GQA attention with the reference's blocked online softmax.
+
+    Restates `_legacy/limit_kernels.py:8-33` (`_attention_direct`):
+      score = (q . k) * SCALE (fp32), masked to keys n <= position (and n < T);
+      running max / denominator per key block of `block_n`; p = exp(score - max),
+      cast to bf16 before the P.V product; out = bf16(acc / den).
+    Key blocks past the diagonal are fully masked and therefore no-ops, so
+    `TRIANGULAR` (which skips them) needs no separate branch here.
+    q: [HQ, S, D], k, v: [HK, T, D] bf16; positions: [S] int64 or None (= arange(S)).
+    Returns [S, HQ, D] bf16.
+    """
+    hq, s_len, d = q.shape
+    hk, t_len, _ = k.shape
+    group = hq // hk
+    pos = torch.arange(s_len) if positions is None else positions.long()
+    sc = _f32(scale)
+    qf = q.float()
+    kf = k.float().repeat_interleave(group, 0)
+    vf = v.float().repeat_interleave(group, 0)
+    mx = torch.full((hq, s_len), float("-inf"))
+    den = torch.zeros(hq, s_len)
+    acc = torch.zeros(hq, s_len, d)
+    for start in range(0, t_len, block_n):
+        n = torch.arange(start, min(start + block_n, t_len))
+        score = torch.matmul(qf.double(), kf[:, n].double().transpose(1, 2)).float() * sc
+        mask = pos[:, None] >= n[None, :]
+        score = score.masked_fill(~mask[None], float("-inf"))
+        new = torch.maximum(mx, score.amax(-1))
+        alpha = torch.exp(mx - new)
+        p = torch.exp(score - new[..., None])
+        den = den * alpha + p.sum(-1)
+        pv = torch.matmul(_bf(p).double(), vf[:, n].double()).float()
+        acc = acc * alpha[..., None] + pv
+        mx = new
+    out = (acc / den[..., None]).to(BF16)
+    return out.transpose(0, 1).contiguous()
+
+
+# ----------------------------------------------------------------------------- FP8
+
+def quantize_static(x, inverse_scale):
+    """Static per-tensor activation quant, `_family/depth_fp8.py:8-19` (`_runtime_scale`)
+    = `_legacy/limit_kernels.py:110-114` (`_static_fp8`).
+
+    q = e4m3(clamp(x * INV, -448, 448)), rows padded with zeros to a multiple of 16.
+    Returns q [pad16(M), K] float8_e4m3fn.
+    """
+    x = x.reshape(-1, x.shape[-1]).float()
+    m, k = x.shape
+    pad = (m + 15) // 16 * 16
+    v = (x * _f32(inverse_scale)).clamp(-FP8_MAX, FP8_MAX)
+    q = torch.zeros(pad, k, dtype=E4M3)
+    q[:m] = v.to(E4M3)
+    return q
+
+
+def quantize_rows(x):
+    """Per-token dynamic activation quant, `_legacy/fp8_private.py:11-18` (`quantize_rows`).
+
+    scale = max(max|x_row|, 1e-12) / 448 (fp32); q = e4m3(clamp(x / scale, +-448)).
+    Rows padded with zeros to a multiple of 16 (their scale is 1e-12/448).
+    Returns (q [pad16(M), K] e4m3, scale [pad16(M)] fp32).
+    """
+    x = x.reshape(-1, x.shape[-1]).float()
+    m, k = x.shape
+    pad = (m + 15) // 16 * 16
+    xp = torch.zeros(pad, k)
+    xp[:m] = x
+    scale = torch.clamp(xp.abs().amax(-1), min=1e-12) / _f32(FP8_MAX)
+    q = (xp / scale[:, None]).clamp(-FP8_MAX, FP8_MAX).to(E4M3)
+    return q, scale
+
+
+def quantize_weight_tensor(w):
+    """Per-tensor weight quant, `_legacy/limit_kernels.py:122-127` (`StaticFP8Linear.__init__`).
+
+    scale = max(max|W|, 1e-12) / 448; W8 = e4m3(clamp(W / scale, +-448)).
+    Returns (W8 [N, K] e4m3, scale [1] fp32).
+    """
+    wf = w.float()
+    scale = wf.abs().amax().clamp_min(1e-12) / _f32(FP8_MAX)
+    w8 = (wf / scale).clamp(-FP8_MAX, FP8_MAX).to(E4M3)
+    return w8, scale.reshape(1)
+
+
+def quantize_weight_channel(w):
+    """Per-output-channel weight quant, `_legacy/fp8_private.py:22-27` (`FP8Linear.__init__`).
+
+    scale[n] = max(max|W[n,:]|, 1e-12) / 448; W8 = e4m3(clamp(W / scale, +-448)).
+    Returns (W8 [N, K] e4m3, scale [N] fp32).
+    """
+    wf = w.float()
+    scale = wf.abs().amax(dim=1, keepdim=True).clamp_min(1e-12) / _f32(FP8_MAX)
+    w8 = (wf / scale).clamp(-FP8_MAX, FP8_MAX).to(E4M3)
+    return w8, scale.reshape(-1)
+
+
+def _fp8_dot(q, w8):
+    """Exact e4m3 x e4m3 dot products (float64 accumulation), [M, N] fp64."""
+    return torch.matmul(q.float().double(), w8.float().double().t())
+
+
+def fp8_linear_static(x, w8, w_scale, inverse_scale):
+    """`RuntimeScaleLinear.__call__`, `_family/depth_fp8.py:22-26` (+ `torch._scaled_mm`).
+
+    y = bf16( (q . W8^T) * (1/INV) * w_scale ), q = quantize_static(x), sliced to M rows.
+    The activation scale is the fp32 value 1/INV held in `input_scale`
+    (`_legacy/limit_kernels.py:129`).
+    """
+    m = x.reshape(-1, x.shape[-1]).shape[0]
+    q = quantize_static(x, inverse_scale)
+    acc = _fp8_dot(q, w8).float()
+    a_scale = (torch.tensor([1.0], dtype=torch.float64) / inverse_scale).float()
+    y = acc * a_scale * w_scale.float().reshape(1, -1)
+    return y[:m].to(BF16)
+
+
+def fp8_linear_rowwise(x, w8, w_scale):
+    """`FP8Linear.__call__`, `_legacy/fp8_private.py:29-38`: per-token x per-channel scales.
+
+    y = bf16( (q . W8^T) * a_scale[row] * w_scale[col] ).
+    """
+    m = x.reshape(-1, x.shape[-1]).shape[0]
+    q, a_scale = quantize_rows(x)
+    acc = _fp8_dot(q, w8).float()
+    y = acc * a_scale[:, None] * w_scale.float().reshape(1, -1)
+    return y[:m].to(BF16)
+
+
+# ----------------------------------------------------------------------------- MLP / readout
+
+def swiglu(gate, up):
+    """`_legacy/search_kernels.py:8-15` (`_swiglu`): y = bf16( bf16(g / (1 + exp(-g))) * u )."""
+    g = gate.float()
+    u = up.float()
+    act = _bf(g / (1.0 + torch.exp(-g)))
+    return (act * u).to(BF16)
+
+
+def lm_readout(x, norm_weight, head, eps):
+    """Final norm of the chosen row + option-row dots, `_legacy/limit_kernels.py:48-57`.
+
+    xn = bf16(bf16(x * rsqrt(mean(x^2)+eps)) * w); out[o] = bf16( sum(xn * head[o]) ) as fp32.
+    x: [H] bf16; head: [n, H] bf16 -> [n] fp32.
+    """
+    xf = x.float().reshape(-1)
+    inv = _inv_rms(xf, eps)
+    xn = _bf(_bf(xf * inv) * norm_weight.float())
+    dots = torch.matmul(head.float().double(), xn.double()).float()
+    return _bf(dots)
+
+
+def log_softmax(logits):
+    """Log-softmax over the k option logits (fp32), the BASELINE scoring output."""
+    z = logits.float()
+    m = z.max()
+    return z - m - torch.log(torch.exp(z - m).sum())
+
+
+def response_argmax(logits):
+    """Argmax with the lowest index winning ties, `_family/family_api.py:41`."""
+    vals = [float(v) for v in logits]
+    return max(range(len(vals)), key=lambda i: (vals[i], -i))
+
+
+# ----------------------------------------------------------------------------- int4
+
+def int4_sym_quantize(w, group=128):
+    """Symmetric int4, group 128, bf16 scales (the W4A16 scheme of the BASELINE config).
+
+    s = bf16(max|W_g| / 7) (floored at 1e-8 before rounding); q = clamp(rne(W / s), -8, 7).
+    Returns (q [N, K] int8 in [-8, 7], scales [N, K/group] bf16).
+    """
+    n, k = w.shape
+    wf = w.float().reshape(n, k // group, group)
+    s = (wf.abs().amax(-1).clamp_min(1e-8) / _f32(7.0)).to(BF16)
+    q = torch.round(wf / s.float()[..., None]).clamp(-8, 7).to(torch.int8)
+    return q.reshape(n, k), s
+
+
+def int4_sym_dequantize(q, scales, group=128):
+    """W ~= bf16(q * s): the bf16 weight tile the W4A16 GEMM dequantises into shared
+    memory before its bf16 tensor-core product (q * s needs up to 11 mantissa bits,
+    so the bf16 rounding is part of the scheme).  Returns [N, K] fp32 (bf16 values)."""
+    n, k = q.shape
+    w = q.float().reshape(n, k // group, group) * scales.float()[..., None]
+    return _bf(w).reshape(n, k)
+
+
+def int4_sym_pack(q):
+    """Pack int4 values two per byte along K: byte = (q[2j] & 0xF) | (q[2j+1] & 0xF) << 4.
+
+    Returns [N, K/2] uint8 (low nibble = even k).
+    """
+    u = (q.to(torch.int16) & 0xF).to(torch.uint8)
+    return (u[:, 0::2] | (u[:, 1::2] << 4)).contiguous()
+
+
+def int4_asym_quantize(w, group=32):
+    """The reference's asymmetric int4 (`_family/night_runtime.py:18-30`, `Int4`).
+
+    scale = clamp((max-min)/15, 1e-6); q = clamp(round((W-min)/scale), 0, 15);
+    zero = min + 8*scale; (scale, zero) stored in bf16; deq = (q-8)*s + z with the
+    bf16-rounded s and z (`night_runtime.py:29-30`).
+    Returns (q [N,K] uint8, scale [N,K/g] bf16, zero [N,K/g] bf16, deq [N,K] fp32).
+    """
+    n, k = w.shape
+    x = w.float().reshape(n, -1, group)
+    low = x.amin(-1, keepdim=True)
+    high = x.amax(-1, keepdim=True)
+    scale = ((high - low) / 15).clamp_min(1e-6)
+    q = ((x - low) / scale).round().clamp(0, 15).to(torch.uint8)
+    zeros = low + scale * 8
+    s = scale.squeeze(-1).to(BF16)
+    z = zeros.squeeze(-1).to(BF16)
+    deq = ((q.float() - 8) * s.float()[..., None] + z.float()[..., None]).reshape(n, k)
+    return q.reshape(n, k), s, z, deq
+
+
+# ----------------------------------------------------------------------------- M-RoPE
+
+def mrope_position_ids(n_tokens, image_start, grid_h, grid_w, spatial_merge=2):
+    """3-axis position ids for text + one image, as Qwen3-VL `get_rope_index` computes them
+    (transformers `modeling_qwen3_vl.py` get_rope_index / get_vision_position_ids; called by
+    `scaled_qwen_runtime.py:92` and `_family/depth_runtime.py:173`).
+
+    Text tokens before the image: 0..image_start-1 on all three axes.  Image tokens
+    (gh = grid_h/merge rows x gw = grid_w/merge cols, row-major): t = s, h = s + row,
+    w = s + col with s = image_start.  Text after the image resumes at s + max(gh, gw).
+    `grid_h`/`grid_w` are patch-grid sizes before the 2x2 spatial merge.
+    Returns [3, n_tokens] int64.
+    """
+    gh, gw = grid_h // spatial_merge, grid_w // spatial_merge
+    nv = gh * gw
+    assert image_start + nv <= n_tokens
+    pos = torch.zeros(3, n_tokens, dtype=torch.long)
+    pre = torch.arange(image_start)
+    pos[:, :image_start] = pre
+    s = image_start
+    rows = torch.arange(gh).repeat_interleave(gw)
+    cols = torch.arange(gw).repeat(gh)
+    pos[0, s:s + nv] = s
+    pos[1, s:s + nv] = s + rows
+    pos[2, s:s + nv] = s + cols
+    nxt = s + max(gh, gw)
+    tail = n_tokens - (s + nv)
+    pos[:, s + nv:] = nxt + torch.arange(tail)
+    return pos
+
+
+def mrope_cos_sin(position_ids, head_dim=128, theta=5_000_000.0, sections=(24, 20, 20)):
+    """Interleaved M-RoPE cos/sin tables (transformers `Qwen3VLTextRotaryEmbedding.forward`
+    + `apply_interleaved_mrope`, used at `scaled_qwen_runtime.py:145`).
+
+    inv_freq[i] = 1 / theta^(2i/D) (fp32); freqs[a, t, i] = pos[a, t] * inv_freq[i];
+    frequency i takes axis H when i % 3 == 1 and i < 3*sections[1], axis W when
+    i % 3 == 2 and i < 3*sections[2], else axis T; emb = cat(f, f); cos/sin in fp32
+    then bf16.  position_ids: [3, T] int64 -> (cos, sin) [T, D] bf16.
+    """
+    half = head_dim // 2
+    inv_freq = 1.0 / (theta ** (torch.arange(0, head_dim, 2, dtype=torch.int64).float() / head_dim))
+    freqs = position_ids.float()[:, :, None] * inv_freq[None, None, :]      # [3, T, half]
+    f = freqs[0].clone()
+    for axis, offset in ((1, 1), (2, 2)):
+        length = sections[axis] * 3
+        idx = torch.arange(offset, length, 3)
+        f[:, idx] = freqs[axis][:, idx]
+    assert f.shape[-1] == half
+    emb = torch.cat((f, f), -1)
+    return emb.cos().to(BF16), emb.sin().to(BF16)
+
+
+# ----------------------------------------------------------------------------- whole path
+
+def embed_rows(embed, ids, visual, image_start):
+    """`scaled_qwen_runtime.py:145`: h = embed_tokens(ids) with rows [s, s+nv) replaced
+    by the visual embeddings (`index_copy`).  ids [T] int64, visual [nv, H] bf16."""
+    h = embed[ids.long()].clone()
+    if visual is not None and visual.shape[0] > 0:
+        h[image_start:image_start + visual.shape[0]] = visual
+    return h
+
+
+def _linear(x, lin, mode):
+    if mode == "rowwise":
+        return fp8_linear_rowwise(x, lin["w8"], lin["w_scale"])
+    if mode == "static":
+        return fp8_linear_static(x, lin["w8"], lin["w_scale"], lin["inv"])
+    if mode == "bf16":
+        return (x.float() @ lin["w"].float().t()).to(BF16)
+    if mode == "int4":
+        w = int4_sym_dequantize(lin["q"], lin["s"])
+        return torch.matmul(x.float().double(), w.double().t()).float().to(BF16)
+    raise ValueError(mode)
+
+
+def _attention_block(layer, x, cos, sin, dims, mode, pick=None):
+    hq, hk, d = dims["hq"], dims["hk"], dims["d"]
+    t = x.shape[0]
+    qkv = _linear(x, layer["qkv"], mode)
+    q = qkv[:, :hq * d].reshape(t, hq, d)
+    k = qkv[:, hq * d:(hq + hk) * d].reshape(t, hk, d)
+    v = qkv[:, (hq + hk) * d:].reshape(t, hk, d).transpose(0, 1).contiguous()
+    yq, yk = qk_pair(q, k, layer["q_norm"], layer["k_norm"], cos, sin, dims["eps"], dims["eps"])
+    scale = d ** -0.5
+    if pick is None:
+        out = attention_direct(yq, yk, v, scale)
+    else:
+        sel = torch.tensor([pick])
+        out = attention_direct(yq[:, sel], yk, v, scale, positions=sel)
+    return _linear(out.reshape(out.shape[0], hq * d), layer["o"], mode)
+
+
+def _mlp(layer, x, mode, inter):
+    gu = _linear(x, layer["gateup"], mode)
+    return _linear(swiglu(gu[:, :inter], gu[:, inter:]), layer["down"], mode)
+
+
+def decoder_layer(layer, h, cos, sin, dims, mode, deep=None, image_start=0, nv=0):
+    """One non-final decoder layer on residual `h` [T, H] (`scaled_qwen_runtime.py:152-162`):
+    normalized = rms(h, in_norm); residual, post = add_rms(h, attention(normalized));
+    h' = residual + mlp(post) (+ deepstack rows).  Returns h' [T, H] bf16."""
+    eps = dims["eps"]
+    normalized = rms_one(h, layer["in_norm"], eps)
+    attn = _attention_block(layer, normalized, cos, sin, dims, mode)
+    residual, post = add_rms(h, attn, None, layer["post_norm"], eps)
+    value = _mlp(layer, post, mode, dims["inter"])
+    out, _ = add_rms(residual, value, deep, layer["in_norm"], eps, image_start, nv)
+    return out
+
+
+def tail(layer, h, cos, sin, dims, mode, pick, final_norm, head, k):
+    """The final layer on the pick row + readout (`_family/night_runtime.py:92-105`).
+    Returns (logits [k], logprobs [k])."""
+    eps = dims["eps"]
+    x = rms_one(h, layer["in_norm"], eps)
+    attn = _attention_block(layer, x, cos, sin, dims, mode, pick=pick)
+    residual, post = add_rms(h[pick:pick + 1], attn, None, layer["post_norm"], eps)
+    chosen = (residual.float() + _mlp(layer, post, mode, dims["inter"]).float()).to(BF16)
+    z = lm_readout(chosen[0], final_norm, head, eps)[:k]
+    return z, log_softmax(z)
+
+
+def prefill_score(model, ids, visual, deepstack, position_ids, pick, k, mode="rowwise",
+                  image_start=0, layers=None, trace=None):
+    """Whole prefill + option scoring for one request.
+
+    Layer order and deepstack placement: `scaled_qwen_runtime.py:143-163` (`prefix`);
+    the last layer runs as the pick-row tail `_family/night_runtime.py:92-105`
+    (`tail`: K/V over all rows, Q/o_proj/MLP on the pick row only) followed by
+    `lm_readout` and the `[:k]` slice (`night_runtime.py:125`).  Returns
+    (logits [k] fp32, logprobs [k] fp32).  `trace`, when a list, receives the residual
+    stream entering each layer.
+
+    `model`: dict with "dims" and per-layer quantised weights (see
+    `fastforward_b200.synthetic`); `mode` selects the linear arithmetic
+    ("rowwise" FP8 per-token x per-channel, "static" FP8 per-tensor, "int4", "bf16").
+    """
+    dims = model["dims"]
+    cos, sin = mrope_cos_sin(position_ids, dims["d"], dims["theta"])
+    h = embed_rows(model["embed"], ids, visual, image_start)
+    nv = visual.shape[0] if visual is not None else 0
+    all_layers = model["layers"] if layers is None else [model["layers"][j] for j in layers]
+    depth = len(all_layers)
+    for j in range(depth - 1):
+        if trace is not None:
+            trace.append(h)
+        deep = deepstack[j] if (deepstack is not None and j < len(deepstack)) else None
+        h = decoder_layer(all_layers[j], h, cos, sin, dims, mode, deep, image_start, nv)
+    if trace is not None:
+        trace.append(h)
+    return tail(all_layers[depth - 1], h, cos, sin, dims, mode, pick, model["final_norm"], model["head"], k)
+
+
+def quantized_model(dims, src, mode="rowwise", inv=None):
+    """The oracle's view of a bf16 source model (`fastforward_b200.synthetic` layout, gate
+    rows then up rows): weights quantised here, on the CPU, with the reference's formulas.
+    For mode "static", `inv[j][role]` are the calibrated inverse activation scales."""
+    layers = []
+    for j, lay in enumerate(src["layers"]):
+        d = {n: lay[n].cpu() for n in ("in_norm", "post_norm", "q_norm", "k_norm")}
+        for role in ("qkv", "o", "gateup", "down"):
+            w = lay[role].cpu()
+            if mode == "rowwise":
+                w8, sc = quantize_weight_channel(w)
+                d[role] = dict(w8=w8, w_scale=sc)
+            elif mode == "static":
+                w8, sc = quantize_weight_tensor(w)
+                d[role] = dict(w8=w8, w_scale=sc, inv=inv[j][role])
+            elif mode == "int4":
+                q, sc = int4_sym_quantize(w)
+                d[role] = dict(q=q, s=sc)
+            else:
+                d[role] = dict(w=w)
+        layers.append(d)
+    dims_d = dict(hq=dims.hq, hk=dims.hk, d=dims.d, eps=dims.eps, theta=dims.theta, inter=dims.inter)
+    return dict(dims=dims_d, embed=src["embed"].cpu(), head=src["head"].cpu(), final_norm=src["final_norm"].cpu(),
+                layers=layers)

@@ -1,0 +1,319 @@
+"""Per-kernel parity of libffb200 (called through its C ABI) against the CPU oracle.
+
+Bars: FP8 quantisation and int4 packing bit-exact; norm / RoPE / readout kernels within
+1 bf16 ulp on a small fraction of elements (the GPU's rsqrt/exp are hardware
+approximations, the oracle's are correctly rounded); GEMM outputs within one bf16
+rounding of the oracle's exact FP8 dot products; attention within bf16 tolerance.
+"""
+import math
+
+import pytest
+import torch
+
+import oracle
+from fastforward_b200 import _lib as L
+from fastforward_b200 import ops
+from fastforward_b200._lib import call, ptr
+from tests._util import assert_bf16_near, assert_bytes_equal
+
+pytestmark = pytest.mark.gpu
+BF16 = torch.bfloat16
+E4M3 = torch.float8_e4m3fn
+DEV = "cuda"
+
+
+def _g(seed):
+    return torch.Generator().manual_seed(seed)
+
+
+def _randn(shape, seed, std=1.0):
+    return (torch.randn(shape, generator=_g(seed)) * std).to(BF16)
+
+
+def _sp():
+    return torch.cuda.current_stream().cuda_stream
+
+
+_ALIVE = []
+
+
+def _keep(t):
+    """Holds a device temporary until the test's kernels are done (a tensor created inline in
+    an argument list would be freed, and its memory handed to the next argument, before the
+    call runs)."""
+    _ALIVE.append(t)
+    return t
+
+
+@pytest.fixture(autouse=True)
+def _release_temporaries():
+    yield
+    torch.cuda.synchronize()
+    _ALIVE.clear()
+
+
+class Norm:
+    def __init__(self, w, eps=1e-6):
+        self.weight = w
+        self.variance_epsilon = eps
+
+
+# ---------------------------------------------------------------------------- norms
+
+@pytest.mark.parametrize("T,H", [(1, 2048), (64, 2560), (333, 4096), (17, 5120)])
+def test_rmsnorm(T, H):
+    x = _randn((T, H), 1)
+    w = (1 + 0.1 * torch.randn(H, generator=_g(2))).to(BF16)
+    got = ops.fast_norm(x.to(DEV), Norm(w.to(DEV)))
+    # order-independent statistics (exact fp64 sum of squares, IEEE sqrt/divide): bit-exact
+    assert_bytes_equal(got, oracle.rms_one(x, w, 1e-6), "rmsnorm")
+
+
+@pytest.mark.parametrize("T,H,start,nv", [(64, 2048, 8, 16), (320, 2560, 0, 256), (5, 5120, 0, 0)])
+def test_add_rmsnorm_deep(T, H, start, nv):
+    a, b = _randn((T, H), 3), _randn((T, H), 4)
+    deep = _randn((nv, H), 5) if nv else None
+    w = (1 + 0.1 * torch.randn(H, generator=_g(6))).to(BF16)
+    r, y = ops.add_rms(a.to(DEV), b.to(DEV), deep.to(DEV) if deep is not None else None, Norm(w.to(DEV)),
+                       start, nv)
+    rr, yy = oracle.add_rms(a, b, deep, w, 1e-6, start, nv)
+    assert_bytes_equal(r, rr, "residual")          # pure adds: bit-exact
+    assert_bytes_equal(y, yy, "normed")
+
+
+@pytest.mark.parametrize("mode", [L.QUANT_ROWWISE, L.QUANT_STATIC])
+def test_add_rmsnorm_partials_and_fused_quant(mode):
+    T, H, S = 40, 2560, 3
+    a = _randn((T, H), 7)
+    parts = torch.randn((S, T, H), generator=_g(8)) * 0.5
+    w = torch.ones(H, dtype=BF16)
+    a_d, p_d, w_d = a.to(DEV), parts.to(DEV), w.to(DEV)
+    res = torch.empty((T, H), device=DEV, dtype=BF16)
+    out = torch.empty((T, H), device=DEV, dtype=BF16)
+    q8 = torch.empty((T, H), device=DEV, dtype=E4M3)
+    qs = torch.empty(T, device=DEV, dtype=torch.float32)
+    inv = 37.5
+    call("ffb_add_rmsnorm", ptr(a_d), None, ptr(p_d), S, None, 0, 0, ptr(w_d), 1e-6, ptr(res), ptr(out), mode, inv,
+         ptr(q8), ptr(qs), T, H, _sp())
+    b = parts.sum(0).to(BF16)  # fixed-order fp32 sum, rounded like the linear's bf16 output
+    rr, yy = oracle.add_rms(a, b, None, w, 1e-6)
+    assert_bf16_near(res, rr, max_frac=0.002, what="residual from partials")
+    # normalisation of the kernel's own residual is bit-exact
+    assert_bytes_equal(out, oracle.rms_one(res.cpu(), w, 1e-6), "normed")
+    # the fused quantiser must be bit-exact on the kernel's own bf16 output
+    if mode == L.QUANT_ROWWISE:
+        q_ref, s_ref = oracle.quantize_rows(out.cpu())
+        assert_bytes_equal(q8, q_ref[:T], "fused rowwise q8")
+        assert torch.equal(qs.cpu(), s_ref[:T])
+    else:
+        assert_bytes_equal(q8, oracle.quantize_static(out.cpu(), inv)[:T], "fused static q8")
+
+
+# ---------------------------------------------------------------------------- FP8 quantisers
+
+@pytest.mark.parametrize("M,K", [(1, 2048), (320, 2560), (77, 9728)])
+def test_quantize_activation_bit_exact(M, K):
+    x = _randn((M, K), 9, std=3.0)
+    q, s = ops.quantize_activation(x.to(DEV), L.QUANT_ROWWISE)
+    q_ref, s_ref = oracle.quantize_rows(x)
+    assert_bytes_equal(q, q_ref, "rowwise q8")
+    assert torch.equal(s.cpu(), s_ref)
+    inv = 448.0 / 9.3
+    q, _ = ops.quantize_activation(x.to(DEV), L.QUANT_STATIC, inv)
+    assert_bytes_equal(q, oracle.quantize_static(x, inv), "static q8")
+
+
+@pytest.mark.parametrize("N,K", [(256, 2048), (6144, 2560), (128, 9728)])
+def test_quantize_weight_bit_exact(N, K):
+    w = _randn((N, K), 10, std=0.02)
+    w8, s = ops.quantize_weight(w.to(DEV), per_channel=True)
+    w8r, sr = oracle.quantize_weight_channel(w)
+    assert_bytes_equal(w8, w8r, "per-channel W8")
+    assert torch.equal(s.cpu(), sr)
+    w8, s = ops.quantize_weight(w.to(DEV), per_channel=False)
+    w8r, sr = oracle.quantize_weight_tensor(w)
+    assert_bytes_equal(w8, w8r, "per-tensor W8")
+    assert torch.equal(s.cpu(), sr)
+
+
+# ---------------------------------------------------------------------------- GEMM
+
+def _gemm_case(M, N, K, seed):
+    x = _randn((M, K), seed)
+    w = _randn((N, K), seed + 1, std=0.02)
+    q, sa = oracle.quantize_rows(x)
+    w8, sw = oracle.quantize_weight_channel(w)
+    acc = torch.matmul(q.float().double(), w8.float().double().t())[:M]
+    ref32 = (acc.float() * sa[:M, None] * sw[None, :])
+    return q, sa, w8, sw, ref32
+
+
+@pytest.mark.parametrize("M,N,K,bn", [
+    (320, 6144, 2560, 0), (320, 2560, 4096, 160), (1, 2560, 9728, 16), (16, 256, 256, 16),
+    (100, 384, 1024, 0), (576, 1280, 2560, 192), (64, 128, 128, 64), (333, 512, 2048, 128),
+    (1024, 256, 512, 256), (33, 256, 2048, 32), (200, 256, 768, 224), (90, 256, 640, 96)])
+def test_fp8_gemm_bf16(M, N, K, bn):
+    q, sa, w8, sw, ref32 = _gemm_case(M, N, K, 11)
+    out = torch.empty((M, N), device=DEV, dtype=BF16)
+    call("ffb_fp8_gemm", ptr(_keep(q.to(DEV))), ptr(_keep(sa.to(DEV))), 1, ptr(_keep(w8.to(DEV))), ptr(_keep(sw.to(DEV))), 1, L.EPI_BF16,
+         ptr(out), None, 1, bn, M, N, K, _sp())
+    torch.cuda.synchronize()
+    # one bf16 rounding of the exact FP8 dot products; near-zero outputs (cancellation) are
+    # held to fp32-accumulation accuracy relative to the output scale instead
+    amax = ref32.abs().max().item()
+    assert_bf16_near(out, ref32.to(BF16), max_ulp=1, max_frac=0.02, what=f"gemm {M}x{N}x{K}", atol=2e-5 * amax)
+
+
+@pytest.mark.parametrize("M,N,K,splits", [(320, 2560, 9728, 4), (1, 2560, 4096, 7), (320, 6144, 2560, 3)])
+def test_fp8_gemm_split_k(M, N, K, splits):
+    q, sa, w8, sw, ref32 = _gemm_case(M, N, K, 12)
+    ws = torch.empty((splits, M, N), device=DEV, dtype=torch.float32)
+    call("ffb_fp8_gemm", ptr(_keep(q.to(DEV))), ptr(_keep(sa.to(DEV))), 1, ptr(_keep(w8.to(DEV))), ptr(_keep(sw.to(DEV))), 1,
+         L.EPI_F32_PARTIAL, None, ptr(ws), splits, 0, M, N, K, _sp())
+    got = ws.sum(0).cpu()
+    torch.testing.assert_close(got, ref32, rtol=1e-4, atol=1e-4 * ref32.abs().max().item())
+
+
+def test_fp8_gemm_static_scales():
+    M, N, K = 96, 768, 2048
+    x = _randn((M, K), 13)
+    w = _randn((N, K), 14, std=0.02)
+    inv = 448.0 / x.float().abs().max().item()
+    w8, ws_ = oracle.quantize_weight_tensor(w)
+    want = oracle.fp8_linear_static(x, w8, ws_, inv)
+    lin = ops.RuntimeScaleLinear.__new__(ops.RuntimeScaleLinear)
+    lin.weight, lin.weight_scale = w8.to(DEV), ws_.to(DEV)
+    lin.inverse_scale = inv
+    lin.input_scale = torch.tensor([1.0 / inv], device=DEV)
+    got = lin(x.to(DEV))
+    assert_bf16_near(got, want, max_ulp=1, max_frac=0.02, what="static fp8 linear")
+
+
+@pytest.mark.parametrize("M", [320, 1, 57])
+def test_fp8_gemm_swiglu_epilogue(M):
+    I, K = 512, 2560
+    x = _randn((M, K), 15)
+    w = _randn((2 * I, K), 16, std=0.02)
+    q, sa = oracle.quantize_rows(x)
+    w8, sw = oracle.quantize_weight_channel(w)
+    gu = oracle.fp8_linear_rowwise(x, w8, sw)
+    want = oracle.swiglu(gu[:, :I], gu[:, I:])
+    w_d = w.to(DEV)
+    packed = torch.empty_like(w_d)
+    call("ffb_pack_gateup", ptr(w_d), ptr(packed), I, K, 2, _sp())
+    w8p, swp = ops.quantize_weight(packed, per_channel=True)
+    out = torch.empty((M, I), device=DEV, dtype=BF16)
+    call("ffb_fp8_gemm", ptr(_keep(q.to(DEV))), ptr(_keep(sa.to(DEV))), 1, ptr(w8p), ptr(swp), 1, L.EPI_SWIGLU, ptr(out), None, 1,
+         0, M, 2 * I, K, _sp())
+    assert_bf16_near(out, want, max_ulp=3, max_frac=0.05, what="swiglu epilogue", atol=1e-3 * want.float().abs().max().item())
+
+
+# ---------------------------------------------------------------------------- QK norm + RoPE, attention
+
+def _rope_inputs(T, HQ, HK, seed):
+    from fastforward_b200.mrope import position_ids, cos_sin
+    qkv = _randn((T, (HQ + 2 * HK) * 128), seed)
+    grid = 16 if T >= 64 else 4
+    pos = position_ids(T, 0, grid, grid)
+    cos, sin = cos_sin(pos)
+    qn = (1 + 0.1 * torch.randn(128, generator=_g(seed + 1))).to(BF16)
+    kn = (1 + 0.1 * torch.randn(128, generator=_g(seed + 2))).to(BF16)
+    return qkv, cos, sin, qn, kn
+
+
+@pytest.mark.parametrize("T,HQ,HK", [(320, 32, 8), (7, 16, 8), (1024, 64, 8)])
+def test_qk_norm_rope(T, HQ, HK):
+    qkv, cos, sin, qn, kn = _rope_inputs(T, HQ, HK, 20)
+    yq = torch.empty((HQ, T, 128), device=DEV, dtype=BF16)
+    yk = torch.empty((HK, T, 128), device=DEV, dtype=BF16)
+    yv = torch.empty((HK, T, 128), device=DEV, dtype=BF16)
+    call("ffb_qk_norm_rope", ptr(_keep(qkv.to(DEV))), None, 0, qkv.shape[1], ptr(_keep(qn.to(DEV))), ptr(_keep(kn.to(DEV))), 1e-6,
+         ptr(_keep(cos.to(DEV))), ptr(_keep(sin.to(DEV))), ptr(yq), ptr(yk), ptr(yv), T, HQ, HK, _sp())
+    q = qkv[:, :HQ * 128].reshape(T, HQ, 128)
+    k = qkv[:, HQ * 128:(HQ + HK) * 128].reshape(T, HK, 128)
+    rq, rk = oracle.qk_pair(q, k, qn, kn, cos, sin)
+    assert_bytes_equal(yq, rq, "Q")
+    assert_bytes_equal(yk, rk, "K")
+    assert_bytes_equal(yv, qkv[:, (HQ + HK) * 128:].reshape(T, HK, 128).transpose(0, 1), "V copy")
+
+
+def test_qk_pair_mirror_signature():
+    T, HQ, HK = 64, 16, 8
+    qkv, cos, sin, qn, kn = _rope_inputs(T, HQ, HK, 21)
+    x = qkv.to(DEV)[None]
+    q = x[..., :HQ * 128].view(1, T, HQ, 128)
+    k = x[..., HQ * 128:(HQ + HK) * 128].view(1, T, HK, 128)
+    yq, yk = ops.qk_pair(q, k, Norm(qn.to(DEV)), Norm(kn.to(DEV)), cos.to(DEV)[None], sin.to(DEV)[None], 4, 4, False)
+    rq, rk = oracle.qk_pair(qkv[:, :HQ * 128].reshape(T, HQ, 128), qkv[:, HQ * 128:(HQ + HK) * 128].reshape(T, HK, 128),
+                            qn, kn, cos, sin)
+    assert yq.shape == (1, HQ, T, 128) and yk.shape == (1, HK, T, 128)
+    assert_bytes_equal(yq[0], rq, "Q")
+    assert_bytes_equal(yk[0], rk, "K")
+
+
+@pytest.mark.parametrize("T,HQ,HK", [(320, 32, 8), (100, 16, 8), (1024, 64, 8), (13, 8, 8)])
+def test_attention_causal(T, HQ, HK):
+    q, k, v = _randn((HQ, T, 128), 30), _randn((HK, T, 128), 31), _randn((HK, T, 128), 32)
+    got = ops.attention_direct(q.to(DEV)[None], k.to(DEV)[None], v.to(DEV)[None], 128 ** -0.5)
+    want = oracle.attention_direct(q, k, v, 128 ** -0.5)
+    torch.testing.assert_close(got[0].cpu().float(), want.float(), atol=2e-2, rtol=2e-2)
+
+
+@pytest.mark.parametrize("T,pick", [(320, 319), (320, 200), (77, 0)])
+def test_attention_selected_gather(T, pick):
+    HQ, HK = 32, 8
+    q, k, v = _randn((HQ, T, 128), 33), _randn((HK, T, 128), 34), _randn((HK, T, 128), 35)
+    pos = torch.tensor([pick], dtype=torch.long)
+    out = torch.empty((1, HQ * 128), device=DEV, dtype=BF16)
+    call("ffb_attention", ptr(_keep(q.to(DEV))), ptr(_keep(k.to(DEV))), ptr(_keep(v.to(DEV))), ptr(_keep(pos.to(DEV))), 1, ptr(out), 1, T, HQ, HK,
+         128 ** -0.5, _sp())
+    want = oracle.attention_direct(q[:, pick:pick + 1], k, v, 128 ** -0.5, positions=pos)
+    torch.testing.assert_close(out.cpu().float().reshape(1, HQ, 128), want.float(), atol=2e-2, rtol=2e-2)
+
+
+# ---------------------------------------------------------------------------- misc
+
+def test_swiglu_standalone():
+    M, I = 64, 1536
+    gu = _randn((M, 2 * I), 40, std=2.0)
+    g, u = gu.to(DEV).chunk(2, -1)
+    got = ops.swiglu(g, u)
+    assert_bf16_near(got, oracle.swiglu(gu[:, :I], gu[:, I:]), what="swiglu")
+
+
+@pytest.mark.parametrize("H,k", [(2560, 4), (5120, 8), (2048, 2)])
+def test_readout_logsoftmax(H, k):
+    res, mlp = _randn((H,), 41), _randn((H,), 42)
+    w = (1 + 0.1 * torch.randn(H, generator=_g(43))).to(BF16)
+    head = _randn((8, H), 44, std=0.02)
+    z = torch.empty(8, device=DEV)
+    lp = torch.empty(8, device=DEV)
+    call("ffb_readout", ptr(_keep(res.to(DEV))), ptr(_keep(mlp.to(DEV))), None, 0, ptr(_keep(w.to(DEV))), 1e-6, ptr(_keep(head.to(DEV))), 8, k,
+         ptr(z), ptr(lp), H, _sp())
+    chosen = (res.float() + mlp.float()).to(BF16)
+    zr = oracle.lm_readout(chosen, w, head, 1e-6)
+    assert torch.equal(z.cpu(), zr), (z.cpu(), zr)
+    torch.testing.assert_close(lp[:k].cpu(), oracle.log_softmax(z[:k].cpu()), atol=1e-5, rtol=1e-5)
+
+
+def test_embed_gather_exact():
+    V, H, T = 1000, 2048, 96
+    table = _randn((V, H), 50, std=0.02)
+    ids = torch.randint(0, V, (T,), generator=_g(51))
+    vis = _randn((36, H), 52)
+    h = torch.empty((T, H), device=DEV, dtype=BF16)
+    call("ffb_embed_gather", ptr(_keep(ids.to(DEV))), ptr(_keep(table.to(DEV))), V, ptr(_keep(vis.to(DEV))), 10, 36, ptr(h), T, H, _sp())
+    assert_bytes_equal(h, oracle.embed_rows(table, ids, vis, 10), "embed")
+
+
+@pytest.mark.parametrize("N,K", [(256, 2560), (128, 9728)])
+def test_pack_int4_bit_exact(N, K):
+    w = _randn((N, K), 60, std=0.02)
+    packed, scales = ops.pack_int4(w.to(DEV))
+    q, s = oracle.int4_sym_quantize(w)
+    assert_bytes_equal(scales, s, "int4 scales")
+    assert_bytes_equal(packed, oracle.int4_sym_pack(q), "int4 nibbles")
+
+
+def test_device_error_word_clear():
+    assert L.device_error(clear=True) == 0
