@@ -90,6 +90,8 @@ __global__ void __launch_bounds__(128) attention_kernel(const AttnArgs p) {
   const int q0 = blockIdx.x * BMQ;
 
   pdl_wait();
+
+  pdl_launch();
   // positions of this thread's two rows and the key range the block needs
   const int ra = q0 + warp * 16 + g, rb = ra + 8;
   auto pos_of = [&](int r) -> int {
@@ -238,8 +240,7 @@ __global__ void __launch_bounds__(128) attention_kernel(const AttnArgs p) {
     __syncthreads();
   }
   cp_wait<0>();
-  pdl_launch();
-
+  
   la += __shfl_xor_sync(0xffffffffu, la, 1);
   la += __shfl_xor_sync(0xffffffffu, la, 2);
   lb += __shfl_xor_sync(0xffffffffu, lb, 1);

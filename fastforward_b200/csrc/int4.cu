@@ -13,6 +13,7 @@ namespace {
 __global__ void __launch_bounds__(256) pack_int4_kernel(const uint16_t* __restrict__ w, uint8_t* __restrict__ packed,
                                                         uint16_t* __restrict__ scales, int N, int K) {
   pdl_wait();
+  pdl_launch();
   const int lane = threadIdx.x & 31;
   const long long item = (long long)blockIdx.x * 8 + (threadIdx.x >> 5);
   const int groups = K / 128;

@@ -13,6 +13,7 @@ __global__ void __launch_bounds__(NT) embed_kernel(const int64_t* __restrict__ i
                                                    int64_t vocab, const uint16_t* __restrict__ visual, int s, int nv,
                                                    uint16_t* __restrict__ h, int H) {
   pdl_wait();
+  pdl_launch();
   const int t = blockIdx.x;
   const uint16_t* src;
   if (visual && t >= s && t < s + nv) {
@@ -31,6 +32,7 @@ __global__ void __launch_bounds__(NT) embed_kernel(const int64_t* __restrict__ i
 __global__ void __launch_bounds__(NT) swiglu_kernel(const uint16_t* __restrict__ gate, const uint16_t* __restrict__ up,
                                                     int stride, uint16_t* __restrict__ y, int M, int I) {
   pdl_wait();
+  pdl_launch();
   const size_t n = (size_t)M * I;
   for (size_t i = blockIdx.x * (size_t)NT + threadIdx.x; i < n; i += (size_t)gridDim.x * NT) {
     const size_t m = i / I, c = i % I;
@@ -73,8 +75,8 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
   return r;
 }
 
-// One CTA: chosen = bf16(res + mlp); xn = bf16(bf16(x*rsqrt(mean(x^2)+eps))*w);
-// logits[o] = bf16(xn . head[o]); logprobs = log_softmax(logits[:k]).
+// One CTA: chosen = bf16(res + mlp); xn = bf16(bf16(x*inv)*w); logits[o] = bf16(xn . head[o])
+// (warp o computes option o); logprobs = log_softmax(logits[:k]).
 // (_legacy/limit_kernels.py:48-57 + _family/night_runtime.py:104-105)
 __global__ void __launch_bounds__(NT) readout_kernel(const uint16_t* __restrict__ res, const uint16_t* __restrict__ mlp,
                                                      const float* __restrict__ mlp32, int splits,
@@ -85,6 +87,7 @@ __global__ void __launch_bounds__(NT) readout_kernel(const uint16_t* __restrict_
   __shared__ float z[8];
   extern __shared__ float xn[];  // H floats
   pdl_wait();
+  pdl_launch();
   double ss = 0.0;
   for (int i = threadIdx.x; i < H; i += NT) {
     float x = bf2f(res[i]);
@@ -101,15 +104,17 @@ __global__ void __launch_bounds__(NT) readout_kernel(const uint16_t* __restrict_
   const float inv = inv_rms_from_ss(block_sum_d(ss, redd), H, eps);
   for (int i = threadIdx.x; i < H; i += NT) xn[i] = round_bf(round_bf(xn[i] * inv) * bf2f(w[i]));
   __syncthreads();
-  for (int o = 0; o < n; ++o) {
-    // the products of two bf16 values are exact in fp32; their float64 sum is (nearly
-    // always) exact, so the bf16-rounded logit does not depend on the reduction order
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (warp < n) {
+    // bf16 x bf16 products are exact in fp32; their float64 sum is (nearly always) exact,
+    // so the bf16-rounded logit does not depend on the reduction order
+    const uint16_t* hr = head + (size_t)warp * H;
     double d = 0.0;
-    for (int i = threadIdx.x; i < H; i += NT) d += (double)(xn[i] * bf2f(head[(size_t)o * H + i]));
-    d = block_sum_d(d, redd);
-    if (threadIdx.x == 0) {
-      z[o] = round_bf((float)d);
-      logits[o] = z[o];
+    for (int i = lane; i < H; i += 32) d += (double)(xn[i] * bf2f(hr[i]));
+    d = warp_sum_d(d);
+    if (lane == 0) {
+      z[warp] = round_bf((float)d);
+      logits[warp] = z[warp];
     }
   }
   __syncthreads();
@@ -170,6 +175,7 @@ namespace {
 __global__ void gather_rows_kernel(const uint8_t* __restrict__ src, const int64_t* __restrict__ index,
                                    uint8_t* __restrict__ dst, int row_bytes) {
   pdl_wait();
+  pdl_launch();
   const int64_t r = index[blockIdx.x];
   const uint8_t* a = src + (size_t)r * row_bytes;
   uint8_t* b = dst + (size_t)blockIdx.x * row_bytes;

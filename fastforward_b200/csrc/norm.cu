@@ -5,16 +5,17 @@
 // deepstack rows), y = bf16(bf16(x * inv) * w) (_legacy/lower_kernels.py:7-21,
 // _legacy/sub10_runtime.py:31-36), with inv = 1/sqrt(sum(x^2)/H + eps) computed from an
 // exact float64 sum of squares and IEEE sqrt/divide (order-independent, so the result is
-// reproducible bit for bit; the reference's fp32 tree sum + hardware rsqrt is not).  One CTA per row,
-// 128-bit vector loads, the row held in registers between the reduction and the store.
+// reproducible bit for bit; the reference's fp32 tree sum + hardware rsqrt is not).  One
+// 64-thread CTA per row (every row of a prefill resident at once), 128-bit vector loads,
+// the row held in registers between the reduction and the stores.
 // HBM traffic per row: read a, b (or the split-K partials), w; write residual, out, q8.
 #include "common.cuh"
 #include "pdl.cuh"
 
 namespace {
 
-constexpr int NT = 256;   // threads per row
-constexpr int MAXV = 4;   // 8-element vectors per thread -> H <= 8192
+constexpr int NT = 64;    // threads per row: two warps, so all rows of a prefill run in one wave
+constexpr int MAXV = 16;  // 8-element vectors per thread -> H <= 8192
 
 __device__ __forceinline__ double block_sum_d(double v, double* red) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -83,18 +84,20 @@ struct NormArgs {
   int add;  // 0: plain RMSNorm of a
 };
 
+template <int V>
 __global__ void __launch_bounds__(NT) add_rmsnorm_kernel(const NormArgs p) {
   __shared__ float red[NT / 32 + 1];
   __shared__ double redd[NT / 32 + 1];
   pdl_wait();
+  pdl_launch();
   const int row = blockIdx.x;
   const int nvec = p.H / 8;
   const size_t base = (size_t)row * p.H;
   const bool deep_row = p.deep && row >= p.start && row < p.start + p.nv;
-  float x[MAXV][8];
+  float x[V][8];
   double ss = 0.0;
 #pragma unroll
-  for (int i = 0; i < MAXV; ++i) {
+  for (int i = 0; i < V; ++i) {
     const int v = threadIdx.x + i * NT;
     if (v < nvec) {
       load8(p.a + base + v * 8, x[i]);
@@ -131,7 +134,7 @@ __global__ void __launch_bounds__(NT) add_rmsnorm_kernel(const NormArgs p) {
   const float inv = inv_rms_from_ss(block_sum_d(ss, redd), p.H, p.eps);
   float amax = 0.f;
 #pragma unroll
-  for (int i = 0; i < MAXV; ++i) {
+  for (int i = 0; i < V; ++i) {
     const int v = threadIdx.x + i * NT;
     if (v < nvec) {
       float w[8];
@@ -144,8 +147,7 @@ __global__ void __launch_bounds__(NT) add_rmsnorm_kernel(const NormArgs p) {
       if (p.out) store8(p.out + base + v * 8, x[i]);
     }
   }
-  pdl_launch();
-  if (p.quant_mode == FFB_QUANT_NONE) return;
+    if (p.quant_mode == FFB_QUANT_NONE) return;
   float mul = p.inv_scale, scale = 0.f;
   if (p.quant_mode == FFB_QUANT_ROWWISE) {
     amax = block_reduce(amax, red, true);
@@ -153,7 +155,7 @@ __global__ void __launch_bounds__(NT) add_rmsnorm_kernel(const NormArgs p) {
     if (threadIdx.x == 0) p.qscale[row] = scale;
   }
 #pragma unroll
-  for (int i = 0; i < MAXV; ++i) {
+  for (int i = 0; i < V; ++i) {
     const int v = threadIdx.x + i * NT;
     if (v < nvec) {
       uint32_t lo = 0, hi = 0;
@@ -180,7 +182,13 @@ int run(const NormArgs& p, const char* who, void* stream) {
   FFB_REQUIRE(ffb::aligned(p.a, 16) && ffb::aligned(p.w, 16) && (!p.out || ffb::aligned(p.out, 16)),
               "%s: bf16 rows must be 16-byte aligned", who);
   FFB_REQUIRE(!p.q8 || ffb::aligned(p.q8, 8), "%s: q8 must be 8-byte aligned", who);
-  cudaError_t e = ffb::launch(add_rmsnorm_kernel, dim3(p.T), dim3(NT), 0, (cudaStream_t)stream, p);
+  const int v = (p.H / 8 + NT - 1) / NT;  // vectors per thread
+  cudaError_t e;
+  if (v <= 4) e = ffb::launch(add_rmsnorm_kernel<4>, dim3(p.T), dim3(NT), 0, (cudaStream_t)stream, p);
+  else if (v <= 5) e = ffb::launch(add_rmsnorm_kernel<5>, dim3(p.T), dim3(NT), 0, (cudaStream_t)stream, p);
+  else if (v <= 8) e = ffb::launch(add_rmsnorm_kernel<8>, dim3(p.T), dim3(NT), 0, (cudaStream_t)stream, p);
+  else if (v <= 10) e = ffb::launch(add_rmsnorm_kernel<10>, dim3(p.T), dim3(NT), 0, (cudaStream_t)stream, p);
+  else e = ffb::launch(add_rmsnorm_kernel<16>, dim3(p.T), dim3(NT), 0, (cudaStream_t)stream, p);
   if (e != cudaSuccess) return ffb::fail(FFB_ECUDA, "%s: launch: %s", who, cudaGetErrorString(e));
   return FFB_OK;
 }

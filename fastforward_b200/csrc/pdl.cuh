@@ -1,7 +1,9 @@
 // Programmatic dependent launch helpers.  Every kernel of the library calls pdl_wait()
-// before its first global-memory access (read or write), so launching it with the
-// programmatic-serialization attribute only overlaps its launch and prologue with the
-// tail of the previous kernel on the stream; without the attribute both calls are no-ops.
+// before its first access to memory another kernel writes (the GEMM may stream its
+// constant weights before it), and triggers its dependents right after: the next kernel
+// on the stream may then be scheduled and run its prologue while this one works, and its
+// own pdl_wait() still waits for this grid's completion and memory flush.  Without the
+// launch attribute both calls are no-ops.
 #pragma once
 #include <cuda_runtime.h>
 

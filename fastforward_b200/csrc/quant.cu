@@ -37,6 +37,7 @@ __global__ void __launch_bounds__(NT) quant_rows_kernel(const uint16_t* __restri
                                                         int K) {
   __shared__ float red[NT / 32 + 1];
   pdl_wait();
+  pdl_launch();
   const int row = blockIdx.x;
   const uint16_t* xr = x + (size_t)row * K;
   uint8_t* qr = q8 + (size_t)row * K;
@@ -48,7 +49,6 @@ __global__ void __launch_bounds__(NT) quant_rows_kernel(const uint16_t* __restri
     scale = fmaxf(amax, 1e-12f) / 448.f;
     if (threadIdx.x == 0) qscale[row] = scale;
   }
-  pdl_launch();
   for (int k = threadIdx.x; k < K; k += NT) {
     const float v = bf2f(xr[k]);
     const float qv = mode == FFB_QUANT_ROWWISE ? __fdiv_rn(v, scale) : v * inv;
@@ -61,6 +61,7 @@ __global__ void __launch_bounds__(NT) row_absmax_kernel(const uint16_t* __restri
                                                         int K) {
   __shared__ float red[NT / 32 + 1];
   pdl_wait();
+  pdl_launch();
   const uint16_t* wr = w + (size_t)blockIdx.x * K;
   float amax = 0.f;
   for (int k = threadIdx.x; k < K; k += NT) amax = fmaxf(amax, fabsf(bf2f(wr[k])));
@@ -72,6 +73,7 @@ __global__ void __launch_bounds__(NT) global_scale_kernel(const float* __restric
                                                           float* __restrict__ scale) {
   __shared__ float red[NT / 32 + 1];
   pdl_wait();
+  pdl_launch();
   float m = 0.f;
   for (int i = threadIdx.x; i < N; i += NT) m = fmaxf(m, rowmax[i]);
   m = block_max(m, red);
@@ -85,6 +87,7 @@ __global__ void __launch_bounds__(NT) weight_quant_kernel(const uint16_t* __rest
                                                           float* __restrict__ scale, uint8_t* __restrict__ w8,
                                                           int K) {
   pdl_wait();
+  pdl_launch();
   const int n = blockIdx.x;
   float s;
   if (per_channel) {
@@ -103,6 +106,7 @@ __global__ void __launch_bounds__(NT) weight_quant_kernel(const uint16_t* __rest
 __global__ void pack_gateup_kernel(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst, int I,
                                    size_t row_bytes) {
   pdl_wait();
+  pdl_launch();
   const int r = blockIdx.x;
   const int t = r / 128, j = r % 128;
   const int s = j < 64 ? 64 * t + j : I + 64 * t + (j - 64);

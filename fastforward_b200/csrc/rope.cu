@@ -56,6 +56,7 @@ __device__ __forceinline__ void store4(uint16_t* dst, const float (&y)[4]) {
 
 __global__ void __launch_bounds__(WARPS * 32) qk_norm_rope_kernel(const RopeArgs p) {
   pdl_wait();
+  pdl_launch();
   const int lane = threadIdx.x & 31;
   const int item = blockIdx.x * WARPS + (threadIdx.x >> 5);
   const int heads = p.HQ + 2 * p.HK;

@@ -194,7 +194,7 @@ class Buffers:
 class Engine:
     """Runs prefill + choice scoring for one packed model on one device."""
 
-    def __init__(self, model: PackedModel, pdl=True):
+    def __init__(self, model: PackedModel, pdl=True, autotune=True):
         L.require_cuda()
         self.m = model
         self.d = model.dims
@@ -203,6 +203,8 @@ class Engine:
         self.tables = {}
         self.buffers = {}
         self.plans = {}
+        self.autotune_enabled = autotune and model.mode != "int4"
+        self.tuned = {}
         L.set_pdl(pdl)
 
     # ------------------------------------------------------------------ plans / buffers
@@ -227,10 +229,50 @@ class Engine:
     def buffers_for(self, T):
         if T not in self.buffers:
             pl = self._plans(T)
-            ws = max(p.splits * p.m * p.n for p in pl.values() if p.epilogue == L.EPI_F32_PARTIAL) \
-                if any(p.epilogue == L.EPI_F32_PARTIAL for p in pl.values()) else 1
+            # workspace sized for any split count the tuner may pick (<= MAX_SPLITS)
+            ws = max(self.MAX_SPLITS * p.m * p.n for p in pl.values())
             self.buffers[T] = Buffers(self.d, T, ws, self.device, self.m.mode)
+            if self.autotune_enabled:
+                self._autotune(T)
         return self.buffers[T]
+
+    MAX_SPLITS = 8
+
+    def _autotune(self, T, reps=5):
+        """Times candidate (token tile, K-split) choices of every GEMM of the forward on this
+        device (zero-filled inputs, the layer-0 weights) and keeps the fastest.  Runs once per
+        T, outside any timed region; every candidate computes the same result."""
+        b = self.buffers[T]
+        pl = self.plans[T]
+        lay = self.m.layers[0]
+        s = torch.cuda.current_stream(self.device)
+        self._s = s.cuda_stream
+        ins = {"qkv": (b.x8, b.xs, b.qkv), "o": (b.o8, b.os, b.lin_out), "gateup": (b.post8, b.posts, b.act),
+               "down": (b.act8, b.acts, b.lin_out)}
+        for key, p in list(pl.items()):
+            tag, role = key
+            a8, sc, out = ins[role]
+            nkb = math.ceil(p.k / 128)
+            bns = sorted({p.bn, 128, 96, 64} if p.m > 64 else {p.bn})
+            splits = [1] if p.epilogue == L.EPI_SWIGLU else [x for x in (1, 2, 3, 4, 6, 8) if x <= min(nkb, self.MAX_SPLITS)]
+            best = None
+            for bn in bns:
+                for sp in splits:
+                    epi = p.epilogue if p.epilogue == L.EPI_SWIGLU else (L.EPI_F32_PARTIAL if sp > 1 else L.EPI_BF16)
+                    cand = GemmPlan(p.m, p.n, p.k, bn, sp, epi)
+                    for _ in range(2):
+                        self._gemm(cand, a8, sc, lay.lin[role], out, b.ws, self.m.mode == "rowwise")
+                    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    e0.record(s)
+                    for _ in range(reps):
+                        self._gemm(cand, a8, sc, lay.lin[role], out, b.ws, self.m.mode == "rowwise")
+                    e1.record(s)
+                    e1.synchronize()
+                    us = e0.elapsed_time(e1) / reps * 1e3
+                    if best is None or us < best[0]:
+                        best = (us, cand)
+            pl[key] = best[1]
+            self.tuned[(T,) + key] = dict(us=best[0], bn=best[1].bn, splits=best[1].splits)
 
     def rope_tables(self, T, image_start, grid_h, grid_w):
         key = (T, image_start, grid_h, grid_w)
