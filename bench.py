@@ -194,14 +194,22 @@ def gemm_roofline(eng, T, peaks, reps=20):
     roles = {"qkv": (b.x8, b.xs, b.qkv), "o": (b.o8, b.os, b.lin_out), "gateup": (b.post8, b.posts, b.act),
              "down": (b.act8, b.acts, b.lin_out)}
     out = {}
+    cos, sin = next(iter(eng.tables.values()))
     for role, (a8, sc, o) in roles.items():
         p = pl[("full", role)]
-        for _ in range(3):
-            eng._gemm(p, a8, sc, lay.lin[role], o, b.ws, True)
+
+        def one(i):
+            lay_i = m.layers[i % m.depth]
+            if role == "qkv":  # fused qkv GEMM + QK-norm + RoPE epilogue
+                eng._qkv(p, b, lay_i, cos, sin, T, False, True)
+            else:
+                eng._gemm(p, a8, sc, lay_i.lin[role], o, b.ws, True)
+        for i in range(3):
+            one(i)
         ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
         ev[0].record(s)
         for i in range(reps):
-            eng._gemm(p, a8, sc, m.layers[i % m.depth].lin[role], o, b.ws, True)
+            one(i)
         ev[1].record(s)
         torch.cuda.synchronize()
         dt = ev[0].elapsed_time(ev[1]) / reps * 1e-3

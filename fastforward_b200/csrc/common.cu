@@ -73,6 +73,26 @@ int make_tmap_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t col
   return FFB_OK;
 }
 
+int make_tmap_out(CUtensorMap* map, const void* base, int elem_bytes, uint64_t inner, uint64_t rows,
+                  uint64_t depth, uint64_t row_bytes, uint64_t depth_bytes, uint32_t box_inner, uint32_t box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(FFB_ECUDA, "cuTensorMapEncodeTiled is unavailable from the driver");
+  if (!aligned(base, 16)) return fail(FFB_EINVAL, "TMA base address must be 16-byte aligned");
+  if (row_bytes % 16 != 0 || depth_bytes % 16 != 0)
+    return fail(FFB_EINVAL, "TMA strides (%llu, %llu bytes) must be multiples of 16", (unsigned long long)row_bytes,
+                (unsigned long long)depth_bytes);
+  if ((uint64_t)box_inner * elem_bytes != 64) return fail(FFB_EINVAL, "store box must be 64 bytes wide");
+  const CUtensorMapDataType dt = elem_bytes == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  cuuint64_t dims[3] = {inner, rows, depth};
+  cuuint64_t strides[2] = {row_bytes, depth_bytes};
+  cuuint32_t box[3] = {box_inner, box_rows, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, dt, 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(FFB_ECUDA, "cuTensorMapEncodeTiled (store) failed (%d)", (int)r);
+  return FFB_OK;
+}
+
 }  // namespace ffb
 
 extern "C" {

@@ -135,6 +135,24 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
       "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "l"(policy)
       : "memory");
 }
+// Shared -> global tile store (bulk async group); rows/columns outside the tensor are
+// clipped by the hardware.  x * element size must be a multiple of 16 bytes.
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void* src, int x, int y, int z) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_u32(src)), "r"(x), "r"(y), "r"(z)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {  // the last N groups may still be pending
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+// Orders this thread's prior shared-memory writes before later async-proxy (TMA) reads.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
@@ -254,4 +272,9 @@ namespace ffb {
 // box_cols elements of `elem_bytes`, 128-byte swizzle, zero fill out of bounds.
 int make_tmap_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t row_bytes,
                  uint32_t box_rows, uint32_t box_cols, int elem_bytes);
+// 3-D store map [depth][rows][inner] (bf16 or fp32), box {64 bytes, box_rows, 1}, 64-byte
+// swizzle: the staging tile in shared memory holds row r's 16-byte chunk c at
+// r*64 + ((c ^ ((r >> 1) & 3)) << 4), in a buffer aligned to 512 bytes.
+int make_tmap_out(CUtensorMap* map, const void* base, int elem_bytes, uint64_t inner, uint64_t rows,
+                  uint64_t depth, uint64_t row_bytes, uint64_t depth_bytes, uint32_t box_inner, uint32_t box_rows);
 }  // namespace ffb

@@ -6,45 +6,36 @@
 // _legacy/sub10_runtime.py:31-36), with inv = 1/sqrt(sum(x^2)/H + eps) computed from an
 // exact float64 sum of squares and IEEE sqrt/divide (order-independent, so the result is
 // reproducible bit for bit; the reference's fp32 tree sum + hardware rsqrt is not).  One
-// 64-thread CTA per row (every row of a prefill resident at once), 128-bit vector loads,
-// the row held in registers between the reduction and the stores.
+// CTA per row with H/16 threads (two 128-bit vectors each: enough warps in flight to hide
+// the memory latency), the row held in registers between the reduction and the stores.
 // HBM traffic per row: read a, b (or the split-K partials), w; write residual, out, q8.
 #include "common.cuh"
 #include "pdl.cuh"
 
 namespace {
 
-constexpr int NT = 64;    // threads per row: two warps, so all rows of a prefill run in one wave
-constexpr int MAXV = 16;  // 8-element vectors per thread -> H <= 8192
+constexpr int MAXT = 512;   // threads per row: H/16 rounded up to a warp (two 8-element vectors each)
+constexpr int MAXV = 2;     // 8-element vectors per thread -> H <= 8192
 
+// Block-wide sum (float64) and max (float) over blockDim.x threads; every thread gets it.
 __device__ __forceinline__ double block_sum_d(double v, double* red) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
   v = warp_sum_d(v);
   if (lane == 0) red[warp] = v;
   __syncthreads();
-  double r = (lane < NT / 32) ? red[lane] : 0.0;
-  if (warp == 0) {
-    r = warp_sum_d(r);
-    if (lane == 0) red[NT / 32] = r;
-  }
-  __syncthreads();
-  r = red[NT / 32];
+  double r = 0.0;
+  for (int i = 0; i < nw; ++i) r += red[i];  // fixed order: identical in every thread
   __syncthreads();
   return r;
 }
 
-__device__ __forceinline__ float block_reduce(float v, float* red, bool is_max) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  v = is_max ? warp_max(v) : warp_sum(v);
+__device__ __forceinline__ float block_max(float v, float* red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  v = warp_max(v);
   if (lane == 0) red[warp] = v;
   __syncthreads();
-  float r = (lane < NT / 32) ? red[lane] : (is_max ? 0.f : 0.f);
-  if (warp == 0) {
-    r = is_max ? warp_max(r) : warp_sum(r);
-    if (lane == 0) red[NT / 32] = r;
-  }
-  __syncthreads();
-  r = red[NT / 32];
+  float r = 0.f;
+  for (int i = 0; i < nw; ++i) r = fmaxf(r, red[i]);
   __syncthreads();
   return r;
 }
@@ -85,9 +76,10 @@ struct NormArgs {
 };
 
 template <int V>
-__global__ void __launch_bounds__(NT) add_rmsnorm_kernel(const NormArgs p) {
-  __shared__ float red[NT / 32 + 1];
-  __shared__ double redd[NT / 32 + 1];
+__global__ void __launch_bounds__(MAXT) add_rmsnorm_kernel(const NormArgs p) {
+  __shared__ float red[MAXT / 32];
+  __shared__ double redd[MAXT / 32];
+  const int NT = blockDim.x;
   pdl_wait();
   pdl_launch();
   const int row = blockIdx.x;
@@ -150,7 +142,7 @@ __global__ void __launch_bounds__(NT) add_rmsnorm_kernel(const NormArgs p) {
     if (p.quant_mode == FFB_QUANT_NONE) return;
   float mul = p.inv_scale, scale = 0.f;
   if (p.quant_mode == FFB_QUANT_ROWWISE) {
-    amax = block_reduce(amax, red, true);
+    amax = block_max(amax, red);
     scale = fmaxf(amax, 1e-12f) / 448.f;
     if (threadIdx.x == 0) p.qscale[row] = scale;
   }
@@ -173,8 +165,8 @@ __global__ void __launch_bounds__(NT) add_rmsnorm_kernel(const NormArgs p) {
 
 int run(const NormArgs& p, const char* who, void* stream) {
   FFB_REQUIRE(p.a && p.w, "%s: NULL input", who);
-  FFB_REQUIRE(p.T > 0 && p.H > 0 && p.H % 8 == 0 && p.H <= NT * MAXV * 8, "%s: H=%d must be a multiple of 8 and <= %d",
-              who, p.H, NT * MAXV * 8);
+  FFB_REQUIRE(p.T > 0 && p.H > 0 && p.H % 8 == 0 && p.H <= MAXT * MAXV * 8,
+              "%s: H=%d must be a multiple of 8 and <= %d", who, p.H, MAXT * MAXV * 8);
   FFB_REQUIRE(p.quant_mode >= 0 && p.quant_mode <= 2, "%s: bad quant_mode %d", who, p.quant_mode);
   FFB_REQUIRE(p.quant_mode == FFB_QUANT_NONE || p.q8, "%s: quant_mode needs q8", who);
   FFB_REQUIRE(p.quant_mode != FFB_QUANT_ROWWISE || p.qscale, "%s: ROWWISE needs qscale", who);
@@ -182,13 +174,10 @@ int run(const NormArgs& p, const char* who, void* stream) {
   FFB_REQUIRE(ffb::aligned(p.a, 16) && ffb::aligned(p.w, 16) && (!p.out || ffb::aligned(p.out, 16)),
               "%s: bf16 rows must be 16-byte aligned", who);
   FFB_REQUIRE(!p.q8 || ffb::aligned(p.q8, 8), "%s: q8 must be 8-byte aligned", who);
-  const int v = (p.H / 8 + NT - 1) / NT;  // vectors per thread
-  cudaError_t e;
-  if (v <= 4) e = ffb::launch(add_rmsnorm_kernel<4>, dim3(p.T), dim3(NT), 0, (cudaStream_t)stream, p);
-  else if (v <= 5) e = ffb::launch(add_rmsnorm_kernel<5>, dim3(p.T), dim3(NT), 0, (cudaStream_t)stream, p);
-  else if (v <= 8) e = ffb::launch(add_rmsnorm_kernel<8>, dim3(p.T), dim3(NT), 0, (cudaStream_t)stream, p);
-  else if (v <= 10) e = ffb::launch(add_rmsnorm_kernel<10>, dim3(p.T), dim3(NT), 0, (cudaStream_t)stream, p);
-  else e = ffb::launch(add_rmsnorm_kernel<16>, dim3(p.T), dim3(NT), 0, (cudaStream_t)stream, p);
+  const int nvec = p.H / 8;
+  int nt = (nvec + 1) / 2;     // two vectors per thread
+  nt = (nt + 31) / 32 * 32;    // whole warps
+  cudaError_t e = ffb::launch(add_rmsnorm_kernel<MAXV>, dim3(p.T), dim3(nt), 0, (cudaStream_t)stream, p);
   if (e != cudaSuccess) return ffb::fail(FFB_ECUDA, "%s: launch: %s", who, cudaGetErrorString(e));
   return FFB_OK;
 }

@@ -31,7 +31,70 @@ __device__ __forceinline__ float block_max(float v, float* red) {
   return r;
 }
 
-// One CTA per row: absmax (ROWWISE only), then quantise.  Works for any K (scalar tail).
+__device__ __forceinline__ float block_max_any(float v, float* red) {  // blockDim.x threads
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  v = warp_max(v);
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float r = 0.f;
+  for (int i = 0; i < nw; ++i) r = fmaxf(r, red[i]);
+  __syncthreads();
+  return r;
+}
+
+// One CTA per row, the row held in registers as 8-element vectors (QV per thread):
+// absmax (ROWWISE only), then quantise with 8-byte stores.  K % 8 == 0.
+constexpr int QV = 4;
+__global__ void __launch_bounds__(1024) quant_rows_vec_kernel(const uint16_t* __restrict__ x, int mode, float inv,
+                                                             uint8_t* __restrict__ q8, float* __restrict__ qscale,
+                                                             int K) {
+  __shared__ float red[32];
+  pdl_wait();
+  pdl_launch();
+  const int row = blockIdx.x, nvec = K / 8;
+  const uint16_t* xr = x + (size_t)row * K;
+  uint8_t* qr = q8 + (size_t)row * K;
+  float v[QV][8];
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < QV; ++i) {
+    const int vi = threadIdx.x + i * blockDim.x;
+    if (vi < nvec) {
+      const uint4 u = *reinterpret_cast<const uint4*>(xr + vi * 8);
+      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        v[i][2 * e] = __uint_as_float(w[e] << 16);
+        v[i][2 * e + 1] = __uint_as_float(w[e] & 0xffff0000u);
+      }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) amax = fmaxf(amax, fabsf(v[i][e]));
+    }
+  }
+  float scale = 0.f;
+  if (mode == FFB_QUANT_ROWWISE) {
+    amax = block_max_any(amax, red);
+    scale = fmaxf(amax, 1e-12f) / 448.f;
+    if (threadIdx.x == 0) qscale[row] = scale;
+  }
+#pragma unroll
+  for (int i = 0; i < QV; ++i) {
+    const int vi = threadIdx.x + i * blockDim.x;
+    if (vi < nvec) {
+      uint32_t lo = 0, hi = 0;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float qv = mode == FFB_QUANT_ROWWISE ? __fdiv_rn(v[i][e], scale) : v[i][e] * inv;
+        const uint32_t b = f2e4m3(clamp448(qv));
+        if (e < 4) lo |= b << (8 * e);
+        else hi |= b << (8 * (e - 4));
+      }
+      *reinterpret_cast<uint2*>(qr + vi * 8) = make_uint2(lo, hi);
+    }
+  }
+}
+
+// Scalar fallback for any K: absmax pass, then quantise.
 __global__ void __launch_bounds__(NT) quant_rows_kernel(const uint16_t* __restrict__ x, int mode, float inv,
                                                         uint8_t* __restrict__ q8, float* __restrict__ qscale,
                                                         int K) {
@@ -101,15 +164,15 @@ __global__ void __launch_bounds__(NT) weight_quant_kernel(const uint16_t* __rest
   for (int k = threadIdx.x; k < K; k += NT) qr[k] = f2e4m3(clamp448(__fdiv_rn(bf2f(wr[k]), s)));
 }
 
-// Row permutation for the SwiGLU epilogue: dst tile t = src gate rows [64t, 64t+64) then
-// src up rows [I + 64t, I + 64t + 64).  One CTA per destination row.
+// Row permutation for the SwiGLU epilogue: dst tile t = src gate rows [128t, 128t+128)
+// then src up rows [I + 128t, I + 128t + 128).  One CTA per destination row.
 __global__ void pack_gateup_kernel(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst, int I,
                                    size_t row_bytes) {
   pdl_wait();
   pdl_launch();
   const int r = blockIdx.x;
-  const int t = r / 128, j = r % 128;
-  const int s = j < 64 ? 64 * t + j : I + 64 * t + (j - 64);
+  const int t = r / 256, j = r % 256;
+  const int s = j < 128 ? 128 * t + j : I + 128 * t + (j - 128);
   const uint8_t* a = src + (size_t)s * row_bytes;
   uint8_t* b = dst + (size_t)r * row_bytes;
   if (row_bytes % 16 == 0) {
@@ -129,8 +192,17 @@ extern "C" int ffb_quantize_fp8(const uint16_t* x, int quant_mode, float inv_sca
   FFB_REQUIRE(quant_mode == FFB_QUANT_STATIC || quant_mode == FFB_QUANT_ROWWISE, "ffb_quantize_fp8: bad mode %d",
               quant_mode);
   FFB_REQUIRE(quant_mode != FFB_QUANT_ROWWISE || qscale, "ffb_quantize_fp8: ROWWISE needs qscale");
-  cudaError_t e = ffb::launch(quant_rows_kernel, dim3(M), dim3(NT), 0, (cudaStream_t)stream, x, quant_mode,
-                              inv_scale, q8, qscale, K);
+  cudaError_t e;
+  const int nvec = K / 8;
+  if (K % 8 == 0 && ffb::aligned(x, 16) && ffb::aligned(q8, 8) && nvec <= 1024 * QV) {
+    int nt = (nvec + QV - 1) / QV;
+    nt = (nt + 31) / 32 * 32;
+    e = ffb::launch(quant_rows_vec_kernel, dim3(M), dim3(nt), 0, (cudaStream_t)stream, x, quant_mode, inv_scale, q8,
+                    qscale, K);
+  } else {
+    e = ffb::launch(quant_rows_kernel, dim3(M), dim3(NT), 0, (cudaStream_t)stream, x, quant_mode, inv_scale, q8,
+                    qscale, K);
+  }
   if (e != cudaSuccess) return ffb::fail(FFB_ECUDA, "ffb_quantize_fp8: %s", cudaGetErrorString(e));
   return FFB_OK;
 }
@@ -152,7 +224,7 @@ extern "C" int ffb_quantize_weight_fp8(const uint16_t* w, int per_channel, uint8
 
 extern "C" int ffb_pack_gateup(const void* src, void* dst, int I, int K, int elem_bytes, void* stream) {
   FFB_REQUIRE(src && dst && src != dst, "ffb_pack_gateup: bad pointers");
-  FFB_REQUIRE(I > 0 && I % 64 == 0, "ffb_pack_gateup: I=%d must be a multiple of 64", I);
+  FFB_REQUIRE(I > 0 && I % 128 == 0, "ffb_pack_gateup: I=%d must be a multiple of 128", I);
   FFB_REQUIRE(elem_bytes == 1 || elem_bytes == 2 || elem_bytes == 4, "ffb_pack_gateup: elem_bytes %d", elem_bytes);
   FFB_REQUIRE(K > 0, "ffb_pack_gateup: K=%d", K);
   const size_t row_bytes = (size_t)K * elem_bytes;

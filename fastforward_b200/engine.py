@@ -120,20 +120,16 @@ class PackedModel:
 
 # ---------------------------------------------------------------------------- planning
 
-def pick_token_tile(m):
-    """Same rule as the library default: fewest tiles of <= 256 tokens (multiple of 32)."""
-    if m <= 16:
-        return 16
-    nt = (m + 255) // 256
-    bn = (m + nt - 1) // nt
-    return min(256, (bn + 31) // 32 * 32)
+def pick_feature_tile(n):
+    """Output features per GEMM tile: 256 (the MMA's cost is nearly flat in N) when N allows."""
+    return 256 if n % 256 == 0 else 128
 
 
 def plan_splits(m, n, k, bn=None, allow_split=True, sms=SMS):
     """K-split count that minimises (waves x k-blocks per CTA) plus a small per-split cost
     for the fp32 partial tiles the consumer has to read back."""
-    bn = bn or pick_token_tile(m)
-    base = (n // 128) * math.ceil(m / bn)
+    bn = bn or pick_feature_tile(n)
+    base = (n // bn) * math.ceil(m / 128)
     nkb = math.ceil(k / 128)
     if not allow_split:
         return 1
@@ -218,9 +214,9 @@ class Engine:
                                ("gateup", 2 * d.inter, d.hidden), ("down", d.hidden, d.inter)):
                 if tag == "tail" and role == "qkv":
                     continue
-                bn = pick_token_tile(m)
                 swiglu = role == "gateup"
-                s = plan_splits(m, n, k, bn, allow_split=not swiglu)
+                bn = 128 if role == "qkv" else (256 if swiglu else pick_feature_tile(n))
+                s = plan_splits(m, n, k, bn, allow_split=not swiglu and role != "qkv")
                 epi = L.EPI_SWIGLU if swiglu else (L.EPI_F32_PARTIAL if s > 1 else L.EPI_BF16)
                 pl[(tag, role)] = GemmPlan(m, n, k, bn, s, epi)
         self.plans[T] = pl
@@ -251,10 +247,12 @@ class Engine:
                "down": (b.act8, b.acts, b.lin_out)}
         for key, p in list(pl.items()):
             tag, role = key
+            if role == "qkv" or p.epilogue == L.EPI_SWIGLU:
+                continue  # fixed tiles: one head per tile / gate-up pairs per tile
             a8, sc, out = ins[role]
             nkb = math.ceil(p.k / 128)
-            bns = sorted({p.bn, 128, 96, 64} if p.m > 64 else {p.bn})
-            splits = [1] if p.epilogue == L.EPI_SWIGLU else [x for x in (1, 2, 3, 4, 6, 8) if x <= min(nkb, self.MAX_SPLITS)]
+            bns = [x for x in (256, 128) if p.n % x == 0]
+            splits = [x for x in (1, 2, 3, 4, 6, 8) if x <= min(nkb, self.MAX_SPLITS)]
             best = None
             for bn in bns:
                 for sp in splits:
@@ -294,6 +292,20 @@ class Engine:
              ptr(out) if plan.epilogue != L.EPI_F32_PARTIAL else None,
              ptr(ws) if plan.epilogue == L.EPI_F32_PARTIAL else None, plan.splits, plan.bn, plan.m, plan.n, plan.k,
              self._s)
+
+    def _qkv(self, plan, b, lay, cos, sin, T, int4, rowwise):
+        """qkv projection + per-head QK-norm + M-RoPE -> head-major Q/K/V in b.yq/yk/yv."""
+        d = self.d
+        if int4:
+            self._w4(plan, b.xb, lay.lin["qkv"], b.qkv, b.ws)
+            qb, q32, qs = self._split_args(plan, b.qkv, b.ws)
+            call("ffb_qk_norm_rope", qb, q32, qs, d.qkv_out, ptr(lay.q_norm), ptr(lay.k_norm), float(d.eps),
+                 ptr(cos), ptr(sin), ptr(b.yq), ptr(b.yk), ptr(b.yv), T, d.hq, d.hk, self._s)
+            return
+        lin = lay.lin["qkv"]
+        call("ffb_fp8_gemm_qk_rope", ptr(b.x8), ptr(b.xs), int(rowwise), ptr(lin["w8"]), ptr(lin["scale"]),
+             int(lin["scale"].numel() > 1), ptr(lay.q_norm), ptr(lay.k_norm), float(d.eps), ptr(cos), ptr(sin),
+             ptr(b.yq), ptr(b.yk), ptr(b.yv), T, d.hq, d.hk, d.hidden, self._s)
 
     def _split_args(self, plan, bf16_out, ws):
         """(b, b32, splits) arguments of a consumer of this GEMM's output."""
@@ -338,14 +350,7 @@ class Engine:
             lay = m.layers[j]
             nxt = m.layers[j + 1]
             # ---- attention block
-            p = pl[("full", "qkv")]
-            if int4:
-                self._w4(p, b.xb, lay.lin["qkv"], b.qkv, b.ws)
-            else:
-                self._gemm(p, b.x8, b.xs, lay.lin["qkv"], b.qkv, b.ws, rowwise)
-            qb, q32, qs = self._split_args(p, b.qkv, b.ws)
-            call("ffb_qk_norm_rope", qb, q32, qs, d.qkv_out, ptr(lay.q_norm), ptr(lay.k_norm), eps, ptr(cos),
-                 ptr(sin), ptr(b.yq), ptr(b.yk), ptr(b.yv), T, HQ, HK, self._s)
+            self._qkv(pl[("full", "qkv")], b, lay, cos, sin, T, int4, rowwise)
             call("ffb_attention", ptr(b.yq), ptr(b.yk), ptr(b.yv), None, 0, ptr(b.attn), T, T, HQ, HK, scale,
                  self._s)
             p = pl[("full", "o")]
@@ -388,14 +393,7 @@ class Engine:
         if on_layer is not None:
             on_layer(depth - 1, h_cur)
         lay = m.layers[depth - 1]
-        p = pl[("full", "qkv")]
-        if int4:
-            self._w4(p, b.xb, lay.lin["qkv"], b.qkv, b.ws)
-        else:
-            self._gemm(p, b.x8, b.xs, lay.lin["qkv"], b.qkv, b.ws, rowwise)
-        qb, q32, qs = self._split_args(p, b.qkv, b.ws)
-        call("ffb_qk_norm_rope", qb, q32, qs, d.qkv_out, ptr(lay.q_norm), ptr(lay.k_norm), eps, ptr(cos), ptr(sin),
-             ptr(b.yq), ptr(b.yk), ptr(b.yv), T, HQ, HK, self._s)
+        self._qkv(pl[("full", "qkv")], b, lay, cos, sin, T, int4, rowwise)
         call("ffb_attention", ptr(b.yq), ptr(b.yk), ptr(b.yv), ptr(b.pick), 1, ptr(b.attn), 1, T, HQ, HK, scale,
              self._s)
         p = pl[("tail", "o")]
@@ -430,8 +428,8 @@ class Engine:
 
     def launches_per_forward(self):
         """Kernel launches `enqueue` issues (for the bench's gpu_launches count)."""
-        per_layer = 10 if self.m.mode != "int4" else 8
-        tail = 11 if self.m.mode != "int4" else 9
+        per_layer = 9 if self.m.mode != "int4" else 8
+        tail = 10 if self.m.mode != "int4" else 9
         return 2 + per_layer * (self.m.depth - 1) + tail
 
     # ------------------------------------------------------------------ request I/O

@@ -39,7 +39,7 @@ extern "C" {
 /* GEMM epilogues. */
 #define FFB_EPI_BF16 0         /* out[m,n] = bf16(acc * sa * sw)                           */
 #define FFB_EPI_F32_PARTIAL 1  /* ws[split][m][n] = acc * sa * sw (fp32), reduced by the consumer */
-#define FFB_EPI_SWIGLU 2       /* gate/up rows interleaved per 64; out[m,c] = bf16(bf16(silu(g)) * u) */
+#define FFB_EPI_SWIGLU 2       /* gate/up rows interleaved per 128; out[m,c] = bf16(bf16(silu(g)) * u) */
 
 /* Library identification: returns a static string ("ffb200 <version> sm_100a"). */
 const char* ffb_version(void);
@@ -126,20 +126,34 @@ int ffb_quantize_weight_fp8(const uint16_t* w, int per_channel, uint8_t* w8, flo
 /* FP8 e4m3 W8A8 GEMM on tcgen05 (kind::f8f6f4), fp32 accumulation in tensor memory.
  * Replaces _family/depth_fp8.py:22-26 (`RuntimeScaleLinear.__call__` -> torch._scaled_mm)
  * and _legacy/fp8_private.py:29-38.  a8 [M,K] activations, w8 [N,K] weights (K-major);
- * a_scale is [M] (a_per_row) or [1]; w_scale is [N] (w_per_col) or [1].
+ * a_scale is [M] (a_per_row) or [1]; w_scale is [N] (w_per_col) or [1];
+ * out = (a8 . w8^T) * a_scale[m] * w_scale[n].
  * epilogue FFB_EPI_BF16: out [M,N] bf16; FFB_EPI_F32_PARTIAL: ws [splits][M][N] fp32
- * (the consumer sums the splits); FFB_EPI_SWIGLU: out [M,N/2] bf16 with w8 rows packed
- * as 64 gate rows then the matching 64 up rows per 128-row tile (ffb_pack_gateup order).
- * splits = K-split count (1 unless FFB_EPI_F32_PARTIAL); token_tile = 0 picks one. */
+ * (K split `splits` ways; the consumer sums the splits); FFB_EPI_SWIGLU: out [M,N/2] bf16
+ * with w8 rows (and a per-channel w_scale) in ffb_pack_gateup order.
+ * feature_tile: 128 or 256 output features per tile (0 = 256 when N allows). */
 int ffb_fp8_gemm(const uint8_t* a8, const float* a_scale, int a_per_row,
                  const uint8_t* w8, const float* w_scale, int w_per_col,
-                 int epilogue, uint16_t* out, float* ws, int splits, int token_tile,
+                 int epilogue, uint16_t* out, float* ws, int splits, int feature_tile,
                  int M, int N, int K, void* stream);
 
+/* The qkv projection fused with per-head QK RMSNorm + interleaved-M-RoPE rotation.
+ * Replaces the qkv `RuntimeScaleLinear` (_family/depth_fp8.py:22-26) followed by
+ * `qk_pair` (_legacy/broad_kernels.py:63-74, rounding of lower_kernels.py:66-86): each
+ * 128-feature tile is one head; its bf16 output row is normalised and rotated in the GEMM
+ * epilogue.  w8 [(HQ+2HK)*128, K] packed q|k|v rows; q_norm/k_norm [128]; cos/sin [T,128];
+ * outputs head-major yq [HQ,T,128], yk [HK,T,128], yv [HK,T,128] (V unrotated). */
+int ffb_fp8_gemm_qk_rope(const uint8_t* a8, const float* a_scale, int a_per_row,
+                         const uint8_t* w8, const float* w_scale, int w_per_col,
+                         const uint16_t* q_norm, const uint16_t* k_norm, float eps,
+                         const uint16_t* cos, const uint16_t* sin,
+                         uint16_t* yq, uint16_t* yk, uint16_t* yv,
+                         int T, int HQ, int HK, int K, void* stream);
+
 /* Reorders the rows of a [2I,K] gate/up weight (gate rows 0..I-1, up rows I..2I-1) into
- * the FFB_EPI_SWIGLU tile order: tile t = gate rows 64t..64t+63 then up rows 64t..64t+63.
- * Works on any 1- or 2-byte element type of width `elem_bytes` (bf16 or e4m3), and on
- * the matching [2I] per-channel scale vector when elem_bytes == 4. */
+ * the FFB_EPI_SWIGLU tile order: tile t = gate rows 128t..128t+127 then up rows
+ * 128t..128t+127 (I must be a multiple of 128).  Works on rows of `elem_bytes`*K bytes:
+ * bf16 / e4m3 weights, or a per-channel fp32 scale vector with K = 1, elem_bytes = 4. */
 int ffb_pack_gateup(const void* src, void* dst, int I, int K, int elem_bytes, void* stream);
 
 /* SwiGLU on strided gate/up views: y[m,i] = bf16(bf16(g/(1+exp(-g))) * u).

@@ -22,9 +22,12 @@ def _has_b200():
 
 
 def pytest_collection_modifyitems(config, items):
-    if _has_b200():
-        return
-    skip = pytest.mark.skip(reason="no B200 (sm_100a) device visible")
+    run_slow = os.environ.get("FFB_SLOW") == "1"
+    has_gpu = _has_b200()
+    skip_gpu = pytest.mark.skip(reason="no B200 (sm_100a) device visible")
+    skip_slow = pytest.mark.skip(reason="long-running; set FFB_SLOW=1")
     for item in items:
-        if "gpu" in item.keywords:
-            item.add_marker(skip)
+        if "gpu" in item.keywords and not has_gpu:
+            item.add_marker(skip_gpu)
+        elif "slow" in item.keywords and not run_slow:
+            item.add_marker(skip_slow)

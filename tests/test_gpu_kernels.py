@@ -138,40 +138,43 @@ def test_quantize_weight_bit_exact(N, K):
 
 # ---------------------------------------------------------------------------- GEMM
 
-def _gemm_case(M, N, K, seed):
+def _gemm_case(M, N, K, seed, splits=1):
+    """Inputs and the oracle's fp32 result under its tensor-core accumulation model."""
     x = _randn((M, K), seed)
     w = _randn((N, K), seed + 1, std=0.02)
     q, sa = oracle.quantize_rows(x)
     w8, sw = oracle.quantize_weight_channel(w)
-    acc = torch.matmul(q.float().double(), w8.float().double().t())[:M]
-    ref32 = (acc.float() * sa[:M, None] * sw[None, :])
+    ref32 = oracle.qwen_path._fp8_linear(q, sa, w8, sw, splits)[:M]
     return q, sa, w8, sw, ref32
 
 
 @pytest.mark.parametrize("M,N,K,bn", [
-    (320, 6144, 2560, 0), (320, 2560, 4096, 160), (1, 2560, 9728, 16), (16, 256, 256, 16),
-    (100, 384, 1024, 0), (576, 1280, 2560, 192), (64, 128, 128, 64), (333, 512, 2048, 128),
-    (1024, 256, 512, 256), (33, 256, 2048, 32), (200, 256, 768, 224), (90, 256, 640, 96)])
+    (320, 6144, 2560, 0), (320, 2560, 4096, 128), (1, 2560, 9728, 256), (16, 256, 256, 128),
+    (100, 384, 1024, 0), (576, 1280, 2560, 256), (64, 128, 128, 0), (333, 512, 2048, 128),
+    (1024, 256, 512, 256), (33, 256, 2048, 128), (200, 256, 768, 256), (90, 256, 640, 0)])
 def test_fp8_gemm_bf16(M, N, K, bn):
     q, sa, w8, sw, ref32 = _gemm_case(M, N, K, 11)
     out = torch.empty((M, N), device=DEV, dtype=BF16)
     call("ffb_fp8_gemm", ptr(_keep(q.to(DEV))), ptr(_keep(sa.to(DEV))), 1, ptr(_keep(w8.to(DEV))), ptr(_keep(sw.to(DEV))), 1, L.EPI_BF16,
          ptr(out), None, 1, bn, M, N, K, _sp())
     torch.cuda.synchronize()
-    # one bf16 rounding of the exact FP8 dot products; near-zero outputs (cancellation) are
-    # held to fp32-accumulation accuracy relative to the output scale instead
-    amax = ref32.abs().max().item()
-    assert_bf16_near(out, ref32.to(BF16), max_ulp=1, max_frac=0.02, what=f"gemm {M}x{N}x{K}", atol=2e-5 * amax)
+    # the oracle's tensor-core accumulation model (fp32 sum of exact K=32 partial dots) makes
+    # the bf16 output bit-exact
+    assert_bytes_equal(out, ref32.to(BF16), f"gemm {M}x{N}x{K}")
 
 
-@pytest.mark.parametrize("M,N,K,splits", [(320, 2560, 9728, 4), (1, 2560, 4096, 7), (320, 6144, 2560, 3)])
+@pytest.mark.parametrize("M,N,K,splits", [(320, 2560, 9728, 4), (1, 2560, 4096, 7), (320, 6144, 2560, 3),
+                                          (129, 1280, 1024, 8)])
 def test_fp8_gemm_split_k(M, N, K, splits):
-    q, sa, w8, sw, ref32 = _gemm_case(M, N, K, 12)
+    q, sa, w8, sw, ref32 = _gemm_case(M, N, K, 12, splits)
     ws = torch.empty((splits, M, N), device=DEV, dtype=torch.float32)
     call("ffb_fp8_gemm", ptr(_keep(q.to(DEV))), ptr(_keep(sa.to(DEV))), 1, ptr(_keep(w8.to(DEV))), ptr(_keep(sw.to(DEV))), 1,
          L.EPI_F32_PARTIAL, None, ptr(ws), splits, 0, M, N, K, _sp())
-    got = ws.sum(0).cpu()
-    torch.testing.assert_close(got, ref32, rtol=1e-4, atol=1e-4 * ref32.abs().max().item())
+    parts = ws.cpu()
+    got = parts[0].clone()
+    for s_ in range(1, splits):  # the consumers add the splits in order
+        got = got + parts[s_]
+    assert torch.equal(got, ref32), (got - ref32).abs().max()
 
 
 def test_fp8_gemm_static_scales():
@@ -186,12 +189,12 @@ def test_fp8_gemm_static_scales():
     lin.inverse_scale = inv
     lin.input_scale = torch.tensor([1.0 / inv], device=DEV)
     got = lin(x.to(DEV))
-    assert_bf16_near(got, want, max_ulp=1, max_frac=0.02, what="static fp8 linear")
+    assert_bytes_equal(got, want, "static fp8 linear")
 
 
-@pytest.mark.parametrize("M", [320, 1, 57])
-def test_fp8_gemm_swiglu_epilogue(M):
-    I, K = 512, 2560
+@pytest.mark.parametrize("M,I", [(320, 512), (1, 768), (57, 512), (300, 9728)])
+def test_fp8_gemm_swiglu_epilogue(M, I):
+    K = 2560
     x = _randn((M, K), 15)
     w = _randn((2 * I, K), 16, std=0.02)
     q, sa = oracle.quantize_rows(x)
@@ -205,7 +208,37 @@ def test_fp8_gemm_swiglu_epilogue(M):
     out = torch.empty((M, I), device=DEV, dtype=BF16)
     call("ffb_fp8_gemm", ptr(_keep(q.to(DEV))), ptr(_keep(sa.to(DEV))), 1, ptr(w8p), ptr(swp), 1, L.EPI_SWIGLU, ptr(out), None, 1,
          0, M, 2 * I, K, _sp())
-    assert_bf16_near(out, want, max_ulp=3, max_frac=0.05, what="swiglu epilogue", atol=1e-3 * want.float().abs().max().item())
+    assert_bytes_equal(out, want, "swiglu epilogue")
+
+
+@pytest.mark.parametrize("T,HQ,HK,K", [(320, 32, 8, 2560), (77, 16, 8, 2048), (1, 8, 8, 512)])
+def test_fp8_gemm_qk_rope_fused(T, HQ, HK, K):
+    """qkv projection with the per-head norm + RoPE in its epilogue, against the oracle's
+    FP8 linear (tensor-core accumulation model) rounded to bf16 followed by `qk_pair`:
+    bit-exact."""
+    from fastforward_b200.mrope import position_ids, cos_sin
+    x = _randn((T, K), 70)
+    w = _randn(((HQ + 2 * HK) * 128, K), 71, std=0.02)
+    q8, sa = oracle.quantize_rows(x)
+    w8, sw = oracle.quantize_weight_channel(w)
+    pos = position_ids(max(T, 64), 0, 8, 8)[:, :T] if T < 64 else position_ids(T, 0, 16, 16)
+    cos, sin = cos_sin(pos)
+    qn = (1 + 0.1 * torch.randn(128, generator=_g(72))).to(BF16)
+    kn = (1 + 0.1 * torch.randn(128, generator=_g(73))).to(BF16)
+    yq = torch.empty((HQ, T, 128), device=DEV, dtype=BF16)
+    yk = torch.empty((HK, T, 128), device=DEV, dtype=BF16)
+    yv = torch.empty((HK, T, 128), device=DEV, dtype=BF16)
+    call("ffb_fp8_gemm_qk_rope", ptr(_keep(q8.to(DEV))), ptr(_keep(sa.to(DEV))), 1, ptr(_keep(w8.to(DEV))),
+         ptr(_keep(sw.to(DEV))), 1, ptr(_keep(qn.to(DEV))), ptr(_keep(kn.to(DEV))), 1e-6,
+         ptr(_keep(cos.contiguous().to(DEV))), ptr(_keep(sin.contiguous().to(DEV))), ptr(yq), ptr(yk), ptr(yv),
+         T, HQ, HK, K, _sp())
+    torch.cuda.synchronize()
+    qkv = oracle.fp8_linear_rowwise(x, w8, sw)
+    rq, rk = oracle.qk_pair(qkv[:, :HQ * 128].reshape(T, HQ, 128), qkv[:, HQ * 128:(HQ + HK) * 128].reshape(T, HK, 128),
+                            qn, kn, cos, sin)
+    assert_bytes_equal(yq, rq, "Q")
+    assert_bytes_equal(yk, rk, "K")
+    assert_bytes_equal(yv, qkv[:, (HQ + HK) * 128:].reshape(T, HK, 128).transpose(0, 1), "V")
 
 
 # ---------------------------------------------------------------------------- QK norm + RoPE, attention
