@@ -27,7 +27,7 @@ E4M3 = torch.float8_e4m3fn
 FP8_MAX = 448.0
 
 __all__ = [
-    "rms_one", "add_rms", "qk_pair", "attention_direct", "quantize_static",
+    "rms_one", "add_rms", "qk_pair", "attention_direct", "set_attention_block", "quantize_static",
     "quantize_rows", "quantize_weight_tensor", "quantize_weight_channel",
     "fp8_linear_static", "fp8_linear_rowwise", "swiglu", "lm_readout",
     "log_softmax", "int4_sym_quantize", "int4_sym_dequantize", "int4_sym_pack",
@@ -467,6 +467,20 @@ def _linear(x, lin, mode, tail=False):
     raise ValueError(mode)
 
 
+# Key-block width of the oracle's online softmax in the decoder layers (the reference
+# kernel's BLOCK_N = 64).  Tests re-run the oracle with another width: the two results differ
+# only by attention's rounding, which measures the noise floor an FP8 network amplifies.
+ATTENTION_BLOCK_N = 64
+
+
+def set_attention_block(n):
+    """Sets the decoder layers' softmax key-block width; returns the previous one."""
+    global ATTENTION_BLOCK_N
+    assert n > 0
+    old, ATTENTION_BLOCK_N = ATTENTION_BLOCK_N, int(n)
+    return old
+
+
 def _attention_block(layer, x, cos, sin, dims, mode, pick=None):
     hq, hk, d = dims["hq"], dims["hk"], dims["d"]
     t = x.shape[0]
@@ -477,10 +491,10 @@ def _attention_block(layer, x, cos, sin, dims, mode, pick=None):
     yq, yk = qk_pair(q, k, layer["q_norm"], layer["k_norm"], cos, sin, dims["eps"], dims["eps"])
     scale = d ** -0.5
     if pick is None:
-        out = attention_direct(yq, yk, v, scale)
+        out = attention_direct(yq, yk, v, scale, block_n=ATTENTION_BLOCK_N)
     else:
         sel = torch.tensor([pick])
-        out = attention_direct(yq[:, sel], yk, v, scale, positions=sel)
+        out = attention_direct(yq[:, sel], yk, v, scale, positions=sel, block_n=ATTENTION_BLOCK_N)
     return _linear(out.reshape(out.shape[0], hq * d), layer["o"], mode, tail=pick is not None)
 
 

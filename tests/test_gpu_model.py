@@ -63,16 +63,30 @@ def test_tail_only_matches_oracle(name):
     torch.testing.assert_close(lp, oracle.log_softmax(z), atol=1e-5, rtol=1e-5)
 
 
+def _with_attention_block(n, fn, *args, **kw):
+    old = oracle.set_attention_block(n)
+    try:
+        return fn(*args, **kw)
+    finally:
+        oracle.set_attention_block(old)
+
+
 @pytest.mark.parametrize("name,n_layers", [("2B", 3), ("4B", 2)])
 def test_prefill_free_running_matches_oracle(name, n_layers):
-    """A few whole layers without teacher forcing: the oracle accumulates its FP8 GEMMs as the
-    tensor cores do (and with the engine's K splits), so only attention's exp/ordering
-    differences remain between the two."""
+    """A few whole layers without teacher forcing.  The oracle accumulates its FP8 GEMMs as
+    the tensor cores do (with the engine's K splits) and its norms bit-exactly, so only
+    attention's rounding (exp, summation order) separates the two, and an FP8 network
+    amplifies it.  Its size is measured as the oracle's own change when its softmax runs
+    over 32-key blocks instead of 64: the engine must stay within TOL or that floor, i.e. no
+    farther from the oracle than an equally valid blocking of the oracle itself."""
     dims, src, req, layout = small_case(MODELS[name], n_layers, vocab=4096)
     eng, z, _ = _run_engine(dims, src, req, layout)
-    zr, _ = _oracle(dims, src, req, layout, splits=_splits(eng, layout.bucket))
-    err = _check_logits(z, zr)
-    print(f"\n{name} {n_layers} layers free-running |dz| = {err:.3g}")
+    sp = _splits(eng, layout.bucket)
+    zr, _ = _oracle(dims, src, req, layout, splits=sp)
+    zr32, _ = _with_attention_block(32, _oracle, dims, src, req, layout, splits=sp)
+    floor = (zr - zr32).abs().max().item()
+    err = _check_logits(z, zr, max(TOL, floor))
+    print(f"\n{name} {n_layers} layers free-running |dz| = {err:.3g} (oracle noise floor {floor:.3g})")
 
 
 @pytest.mark.parametrize("name", ["2B", "4B"])
@@ -165,11 +179,14 @@ def _teacher_forced(name, n_layers, vocab=4096, layout=None):
     stats = []
     for j in range(len(hs) - 1):
         deep = req["deep"][j] if j < len(req["deep"]) else None
-        want = oracle.decoder_layer(om["layers"][j], hs[j], cos, sin, om["dims"], "rowwise", deep,
-                                    layout.image_start, nv).float()
+        args = (om["layers"][j], hs[j], cos, sin, om["dims"], "rowwise", deep, layout.image_start, nv)
+        want = oracle.decoder_layer(*args).float()
+        alt = _with_attention_block(32, oracle.decoder_layer, *args).float()  # attention noise floor
         got = hs[j + 1].float()
-        err = (got - want).abs()
-        stats.append((j, err.max().item() / want.abs().max().item(), err.mean().item() / want.abs().mean().item()))
+        scale_max, scale_mean = want.abs().max().item(), want.abs().mean().item()
+        err, flo = (got - want).abs(), (alt - want).abs()
+        stats.append((j, err.max().item() / scale_max, err.mean().item() / scale_mean,
+                      flo.max().item() / scale_max, flo.mean().item() / scale_mean))
     zr, _ = oracle.tail(om["layers"][-1], hs[-1], cos, sin, om["dims"], "rowwise", req["pick"], om["final_norm"],
                         om["head"], req["k"])
     return stats, z.cpu(), zr
@@ -177,12 +194,14 @@ def _teacher_forced(name, n_layers, vocab=4096, layout=None):
 
 @pytest.mark.parametrize("name,n_layers", [("2B", 4), ("4B", 3)])
 def test_layers_teacher_forced(name, n_layers):
-    """Whole layers on the engine's own inputs: only attention's ordering differences remain,
-    so the per-layer deviation is tiny (max 2% of the layer output's max, mean 0.1%)."""
+    """Whole layers on the engine's own inputs: only attention's rounding differs, so each
+    layer's deviation stays within 2% of the output's max (0.1% on average) or within the
+    oracle's own change under a different softmax blocking, whichever is larger."""
     stats, z, zr = _teacher_forced(name, n_layers)
-    print(f"\n{name} per-layer (max rel, mean rel):", stats, "tail", (z - zr).abs().max().item())
-    for j, max_rel, mean_rel in stats:
-        assert max_rel <= 0.02 and mean_rel <= 1e-3, (j, max_rel, mean_rel)
+    print(f"\n{name} per-layer (max rel, mean rel, floor max, floor mean):", stats, "tail",
+          (z - zr).abs().max().item())
+    for j, max_rel, mean_rel, fmax, fmean in stats:
+        assert max_rel <= max(0.02, fmax) and mean_rel <= max(1e-3, fmean), stats[j]
     _check_logits(z, zr)
 
 
@@ -212,7 +231,8 @@ def test_full_depth_2b_teacher_forced():
     """All 28 layers of the 2B shape at T=320, each checked against the oracle on the
     engine's own input, and the tail's logits/argmax against the oracle's tail."""
     stats, z, zr = _teacher_forced("2B", None, vocab=8192)
-    print("\n2B full depth per-layer (max rel, mean rel):", stats, "tail", (z - zr).abs().max().item())
-    for j, max_rel, mean_rel in stats:
-        assert max_rel <= 0.02 and mean_rel <= 1e-3, (j, max_rel, mean_rel)
+    print("\n2B full depth per-layer (max rel, mean rel, floor max, floor mean):", stats, "tail",
+          (z - zr).abs().max().item())
+    for j, max_rel, mean_rel, fmax, fmean in stats:
+        assert max_rel <= max(0.02, fmax) and mean_rel <= max(1e-3, fmean), stats[j]
     _check_logits(z, zr)
