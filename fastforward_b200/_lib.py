@@ -31,6 +31,7 @@ SIGNATURES = {
     "ffb_gather_rows": [P, P, P, I, I, P],
     "ffb_quantize_fp8": [P, I, F, P, P, I, I, P],
     "ffb_quantize_weight_fp8": [P, I, P, P, P, I, I, P],
+    "ffb_quantize_weight_fp8_noalloc": [P, I, P, P, I, I, P],
     "ffb_fp8_gemm": [P, P, I, P, P, I, I, P, P, I, I, I, I, I, P],
     "ffb_fp8_gemm_qk_rope": [P, P, I, P, P, I, P, P, F, P, P, P, P, P, I, I, I, I, P],
     "ffb_pack_gateup": [P, P, I, I, I, P],

@@ -11,6 +11,8 @@
 #include "common.cuh"
 #include "pdl.cuh"
 
+#include <atomic>
+
 namespace {
 
 constexpr int NT = 256;
@@ -219,6 +221,46 @@ extern "C" int ffb_quantize_weight_fp8(const uint16_t* w, int per_channel, uint8
   if (e == cudaSuccess)
     e = ffb::launch(weight_quant_kernel, dim3(N), dim3(NT), 0, s, w, (const float*)rowmax, per_channel, scale, w8, K);
   if (e != cudaSuccess) return ffb::fail(FFB_ECUDA, "ffb_quantize_weight_fp8: %s", cudaGetErrorString(e));
+  return FFB_OK;
+}
+
+// Fixed scratch of ffb_quantize_weight_fp8_noalloc: the weight's per-row |max|, one fp32
+// per row.  No entry needs a starting value: row_absmax_kernel writes rows [0, N) before
+// global_scale_kernel / weight_quant_kernel read them, in stream order.
+static __device__ __align__(256) float g_noalloc_rowmax[FFB_QW_NOALLOC_MAX_N];
+
+namespace {
+constexpr int kMaxDevices = 64;
+std::atomic<float*> g_noalloc_rowmax_ptr[kMaxDevices];  // per device, looked up once
+}  // namespace
+
+extern "C" int ffb_quantize_weight_fp8_noalloc(const uint16_t* w, int per_channel, uint8_t* w8, float* scale,
+                                               int N, int K, void* stream) {
+  FFB_REQUIRE(w && w8 && scale, "ffb_quantize_weight_fp8_noalloc: NULL pointer");
+  FFB_REQUIRE(N > 0 && K > 0, "ffb_quantize_weight_fp8_noalloc: bad shape N=%d K=%d", N, K);
+  FFB_REQUIRE(N <= FFB_QW_NOALLOC_MAX_N,
+              "ffb_quantize_weight_fp8_noalloc: N=%d rows exceed the fixed scratch of %d rows "
+              "(use ffb_quantize_weight_fp8 with caller scratch)", N, FFB_QW_NOALLOC_MAX_N);
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return ffb::fail(FFB_ECUDA, "ffb_quantize_weight_fp8_noalloc: cudaGetDevice: %s",
+                                         cudaGetErrorString(e));
+  FFB_REQUIRE(dev >= 0 && dev < kMaxDevices, "ffb_quantize_weight_fp8_noalloc: device %d out of range", dev);
+  float* rowmax = g_noalloc_rowmax_ptr[dev].load(std::memory_order_acquire);
+  if (rowmax == nullptr) {
+    // with `dev` current; concurrent first calls all store the same address
+    e = cudaGetSymbolAddress(reinterpret_cast<void**>(&rowmax), g_noalloc_rowmax);
+    if (e != cudaSuccess)
+      return ffb::fail(FFB_ECUDA, "ffb_quantize_weight_fp8_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+    g_noalloc_rowmax_ptr[dev].store(rowmax, std::memory_order_release);
+  }
+  cudaStream_t s = (cudaStream_t)stream;
+  e = ffb::launch(row_absmax_kernel, dim3(N), dim3(NT), 0, s, w, rowmax, K);
+  if (e == cudaSuccess && !per_channel)
+    e = ffb::launch(global_scale_kernel, dim3(1), dim3(NT), 0, s, (const float*)rowmax, N, scale);
+  if (e == cudaSuccess)
+    e = ffb::launch(weight_quant_kernel, dim3(N), dim3(NT), 0, s, w, (const float*)rowmax, per_channel, scale, w8, K);
+  if (e != cudaSuccess) return ffb::fail(FFB_ECUDA, "ffb_quantize_weight_fp8_noalloc: %s", cudaGetErrorString(e));
   return FFB_OK;
 }
 

@@ -7,9 +7,9 @@
  *   - all tensor arguments are caller-owned device pointers; bf16 tensors are passed
  *     as raw 16-bit words (uint16_t), FP8 e4m3 as uint8_t, row-major unless stated;
  *   - `stream` is a cudaStream_t passed as void*; work is enqueued on it and the call
- *     returns without synchronising; no entry point allocates device memory, except
- *     ffb_quantize_weight_fp8 which is a set-up call (it synchronises nothing either);
- *     scratch space is always passed in (`ws`);
+ *     returns without synchronising; no entry point allocates device memory: scratch
+ *     space is passed in (`ws`), except for ffb_quantize_weight_fp8_noalloc, which uses
+ *     a fixed array inside the library;
  *   - return value 0 on success, a negative FFB_E* code otherwise; the message of the
  *     last failure on the calling thread is available from ffb_last_error();
  *   - reentrant: the only mutable global state is a per-device error word that kernels
@@ -122,6 +122,26 @@ int ffb_quantize_fp8(const uint16_t* x, int quant_mode, float inv_scale,
  * ws: >= 4*N bytes of scratch. */
 int ffb_quantize_weight_fp8(const uint16_t* w, int per_channel, uint8_t* w8, float* scale,
                             void* ws, int N, int K, void* stream);
+
+/* ffb_quantize_weight_fp8 without caller scratch.  This entry point has no counterpart in
+ * the reference.  The per-row maxima live in a fixed device array inside the library
+ * (FFB_QW_NOALLOC_MAX_N fp32 entries, 256 KiB per device), so a caller that cannot
+ * allocate device memory - a C host that owns only the weight and its outputs, or a
+ * process already at its device-memory cap - can still quantise weights.
+ *   - allocates nothing: no cudaMalloc/cudaFree and no allocating library call;
+ *   - N > FFB_QW_NOALLOC_MAX_N is rejected with FFB_EINVAL (use ffb_quantize_weight_fp8);
+ *   - the first call on each device looks the array up with cudaGetSymbolAddress, with
+ *     that device current (this may load the library's device code); make that first
+ *     call before any stream capture;
+ *   - nothing in the array has to start at zero: a call writes every entry it reads;
+ *   - one array per device, shared by every call on it: calls whose execution overlaps
+ *     (different streams, different host threads) race on it; calls on one stream are
+ *     ordered and safe;
+ *   - `stream` must belong to the current device.
+ * Arguments and results are those of ffb_quantize_weight_fp8 without `ws`. */
+#define FFB_QW_NOALLOC_MAX_N 65536
+int ffb_quantize_weight_fp8_noalloc(const uint16_t* w, int per_channel, uint8_t* w8, float* scale,
+                                    int N, int K, void* stream);
 
 /* FP8 e4m3 W8A8 GEMM on tcgen05 (kind::f8f6f4), fp32 accumulation in tensor memory.
  * Replaces _family/depth_fp8.py:22-26 (`RuntimeScaleLinear.__call__` -> torch._scaled_mm)
