@@ -42,6 +42,11 @@ def parse():
     p.add_argument("--workload", default="4B-fp8-T320")
     p.add_argument("--cpu-layers", type=int, default=2, help="decoder layers in the CPU sample")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--layers", type=int, default=None,
+                   help="build only this many decoder layers (same shapes; for small profiler captures)")
+    p.add_argument("--ncu-range", action="store_true",
+                   help="after set-up, replay one forward inside a cudaProfilerStart/Stop range and exit "
+                        "(for `ncu --profile-from-start off`); prints no bench line")
     return p.parse_args()
 
 
@@ -118,6 +123,9 @@ class CpuSample:
         from fastforward_b200.synthetic import make_model_bf16, make_request
         from fastforward_b200.mrope import position_ids
         torch.set_num_threads(threads)
+        # a CPU implementation times ordinary fp32 GEMMs of the e4m3 values (as CPU
+        # torch._scaled_mm computes them), not the oracle's bit-level tensor-core model
+        oracle.set_accumulation("fp32")
         self.o = oracle
         self.dims, self.layout = dims, layout
         src = make_model_bf16(dims, seed=0, device="cpu", layers=n_layers + 1)
@@ -172,12 +180,25 @@ def run_reference(args):
                             parallelism="cpu"),
                 cpu_baseline=dict(value=value, unit=UNIT, cores=threads, kind="port",
                                   sample=f"1 decoder layer per step (tail timed once, {t_tail:.2f}s), scaled to "
-                                         f"{dims.layers - 1} layers + tail"),
+                                         f"{dims.layers - 1} layers + tail; fp32 GEMMs of the e4m3 values"),
                 e2e=dict(value=value, unit=UNIT, h2d_bytes_per_step=0, d2h_bytes_per_step=0))
     print(json.dumps(line), flush=True)
 
 
 # ---------------------------------------------------------------------------- GPU side
+
+PROFILE_GATEUP = ROOT / "profiles" / "fp8_gemm_gateup_4B_T320.md"
+
+
+def ncu_traffic(workload, role):
+    """DRAM bytes (read + write) per launch of the dominant GEMM, from the committed ncu
+    summary of that kernel on this workload (None when there is no such summary)."""
+    import re
+    if workload != "4B-fp8-T320" or role != "gateup" or not PROFILE_GATEUP.exists():
+        return None
+    m = re.search(r"dram_bytes_per_launch:\s*(\d+)", PROFILE_GATEUP.read_text())
+    return int(m.group(1)) if m else None
+
 
 def gemm_roofline(eng, T, peaks, reps=20):
     """Times each GEMM role of the forward standalone (same shapes and plans as inside the
@@ -241,7 +262,7 @@ def run_ours(args):
     peaks = read_peaks()
 
     with torch.no_grad():
-        src = make_model_bf16(dims, seed=0, device=dev)
+        src = make_model_bf16(dims, seed=0, device=dev, layers=args.layers)
         pm = PackedModel(dims, src, mode=mode, device=dev, free_source=True)
         del src
         torch.cuda.empty_cache()
@@ -271,6 +292,15 @@ def run_ours(args):
             stage_dev(dev_reqs[i % n_pool])
             entry["graph"].replay()
         torch.cuda.synchronize()
+        if args.ncu_range:
+            torch.cuda.profiler.start()
+            entry["graph"].replay()
+            torch.cuda.synchronize()
+            torch.cuda.profiler.stop()
+            if rank == 0:
+                print(json.dumps(dict(ncu_range="one graph replay", workload=args.workload, layers=pm.depth,
+                                      launches=eng.launches_per_forward())), flush=True)
+            return
         s = torch.cuda.current_stream()
         starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
         ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
@@ -347,7 +377,10 @@ def run_ours(args):
         dom = max(roles, key=lambda k: roles[k]["us"])
         dr = roles[dom]
         roofline = dict(bound="tensor", achieved=dr["tflops"], peak=fp8_peak, unit="TFLOP/s",
-                        frac=dr["tflops"] / fp8_peak, traffic=None, kernel=f"fp8_gemm_kernel ({dom})",
+                        frac=dr["tflops"] / fp8_peak, traffic=ncu_traffic(args.workload, dom),
+                        traffic_note="ncu dram__bytes_read.sum + dram__bytes_write.sum per launch; "
+                                     "algorithmic weight bytes per launch = %d" % (dr["n"] * dr["k"]),
+                        kernel=f"fp8_gemm_kernel ({dom})",
                         peak_note=f"FP8 dense = 2 x {peaks['src']} cuBLAS bf16 {peaks['bf16']} TFLOP/s",
                         weight_stream_gbs=dr["weight_gbs"], hbm_peak_gbs=peaks["hbm"],
                         per_role={k: {kk: (round(vv, 3) if isinstance(vv, float) else vv) for kk, vv in v.items()}
@@ -368,7 +401,7 @@ def run_ours(args):
             cpu = dict(value=T / full, unit=UNIT, cores=threads, kind="port",
                        sample=f"{args.cpu_layers} timed decoder layers (median {statistics.median(t_layers):.2f}s) "
                               f"+ tail ({t_tail:.2f}s) of the {name} model at T={T}, scaled to "
-                              f"{dims.layers - 1} layers + tail")
+                              f"{dims.layers - 1} layers + tail; fp32 GEMMs of the e4m3 values")
 
     clk_sum = clk.summary()
     if rank == 0:

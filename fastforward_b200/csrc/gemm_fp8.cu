@@ -91,24 +91,21 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
 }
 __device__ __forceinline__ float lo_bf(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float hi_bf(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
-__device__ __forceinline__ float wsc(const GemmArgs& a, int n) { return a.w_per_col ? a.w_scale[n] : a.w_scale[0]; }
 
-// Per-head RMSNorm + rotate-half RoPE of one token's 128-wide head held as packed bf16
-// pairs x[64] (elements 2i, 2i+1 in the low/high halves of x[i]); writes the 128 outputs
-// to dst.  Rounding as _legacy/lower_kernels.py:66-86, statistics as inv_rms_from_ss.
-__device__ __forceinline__ void qk_rope_row(const uint32_t (&x)[64], const uint16_t* __restrict__ wn,
-                                            const uint16_t* __restrict__ cosr, const uint16_t* __restrict__ sinr,
-                                            float eps, uint16_t* __restrict__ dst) {
-  double ss = 0.0;
-#pragma unroll
-  for (int i = 0; i < 64; ++i) {
-    const float a = lo_bf(x[i]), b = hi_bf(x[i]);
-    ss += (double)(a * a) + (double)(b * b);
-  }
-  const float inv = inv_rms_from_ss(ss, 128, eps);
+// Rotate-half RoPE of one token's normalised head, the half owned by this thread.
+// xk holds packed bf16 pairs (elements 2i, 2i+1 in the low/high halves of a word) of head
+// elements [32*PART, 32*PART + 32) in xk[0..16) and of their rotate-half partners
+// [64 + 32*PART, 96 + 32*PART) in xk[16..32); inv = 1/rms of the whole head.  Writes
+// those 64 outputs to dst (the 128-wide head row).  Rounding as
+// _legacy/lower_kernels.py:66-86.
+template <int PART>
+__device__ __forceinline__ void qk_rope_half(const uint32_t (&xk)[32], float inv, const uint16_t* __restrict__ wn,
+                                             const uint16_t* __restrict__ cosr, const uint16_t* __restrict__ sinr,
+                                             uint16_t* __restrict__ dst) {
   // elements e and e+64 are rotate-half partners: handle 8 of each per step
 #pragma unroll
-  for (int e0 = 0; e0 < 64; e0 += 8) {
+  for (int r0 = 0; r0 < 32; r0 += 8) {
+    const int e0 = 32 * PART + r0;
     const uint4 w0 = *reinterpret_cast<const uint4*>(wn + e0);
     const uint4 w1 = *reinterpret_cast<const uint4*>(wn + e0 + 64);
     const uint4 c0 = *reinterpret_cast<const uint4*>(cosr + e0);
@@ -121,8 +118,7 @@ __device__ __forceinline__ void qk_rope_row(const uint32_t (&x)[64], const uint1
     uint32_t ya[4], yb[4];
 #pragma unroll
     for (int p = 0; p < 4; ++p) {
-      const int i = (e0 >> 1) + p;  // packed index of elements e0+2p, e0+2p+1
-      const uint32_t xa = x[i], xb = x[i + 32];
+      const uint32_t xa = xk[(r0 >> 1) + p], xb = xk[16 + (r0 >> 1) + p];
       float out_a[2], out_b[2];
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
@@ -143,10 +139,12 @@ __device__ __forceinline__ void qk_rope_row(const uint32_t (&x)[64], const uint1
   }
 }
 
-template <int BN>
+template <int BN, int EPI>
 __global__ void __launch_bounds__(THREADS, 1)
     fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_w,
                     const __grid_constant__ CUtensorMap tmap_o, const GemmArgs args) {
+  static_assert(EPI != EPI_QKROPE || BN == 128, "one head per tile");
+  static_assert(EPI != FFB_EPI_SWIGLU || BN == 256, "gate/up pairs of 128 channels per tile");
   using C = Cfg<BN>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -176,7 +174,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmap_a);
     tma_prefetch_desc(&tmap_w);
-    if (args.epilogue != EPI_QKROPE) tma_prefetch_desc(&tmap_o);
+    if (EPI != EPI_QKROPE) tma_prefetch_desc(&tmap_o);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, C::TMEM_COLS);
@@ -285,43 +283,75 @@ __global__ void __launch_bounds__(THREADS, 1)
       int tt, ks, ft;
       tile_coords(args, t, tt, ks, ft);
       const int buf = lt & 1;
+      const int m = tt * BM + q * 32 + lane;  // this thread's token
+      const bool row_ok = m < args.M;
+      const int n0 = ft * BN;
+      // the tile's scales come from HBM: request them while its MMAs run
+      if (args.w_per_col && lane < BN / 32) prefetch_l1(args.w_scale + n0 + lane * 32);
+      if (args.a_per_row && row_ok) prefetch_l1(args.a_scale + m);
       // each epilogue warp waits on its own; a timeout makes every one of them stop
       if (!(mbar_wait_bounded(&tfull[buf], (uint32_t)(lt >> 1) & 1u, abort_flag) && !*abort_flag)) {
         *abort_flag = 1;
         break;
       }
       tc_fence_after();
-      const int m = tt * BM + q * 32 + lane;  // this thread's token
-      const bool row_ok = m < args.M;
       const float sa = args.a_per_row ? (row_ok ? args.a_scale[m] : 0.f) : args.a_scale[0];
       const uint32_t acc = tmem + (uint32_t)(buf * BN) + ((uint32_t)(q * 32) << 16);
-      const int n0 = ft * BN;
+      // per-feature scales of tile columns [c, c + 8)
+      auto scales8 = [&](int c, float (&w)[8]) {
+        if (args.w_per_col) {
+          ldg8(args.w_scale + n0 + c, w);
+        } else {
+          const float w0 = args.w_scale[0];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) w[j] = w0;
+        }
+      };
 
-      if (args.epilogue == EPI_QKROPE) {
-        // one head per tile (BN == 128); the first four warps own the whole row
-        if (half == 0) {
-          uint32_t x[64];
+      if constexpr (EPI == EPI_QKROPE) {
+        // One head per tile (BN == 128).  Both column halves read the token's whole head
+        // (its RMSNorm needs all 128 values, summed exactly in element order); half h
+        // keeps and writes elements [32h, 32h + 32) and their partners [64 + 32h, 96 + 32h).
+        uint32_t xk[32];
+        double ss = 0.0;
 #pragma unroll
-          for (int c = 0; c < 128; c += 16) {
-            float v[16];
-            tmem_ld16(acc + (uint32_t)c, v);
+        for (int c = 0; c < 128; c += 16) {
+          uint32_t r[16];
+          tmem_ld16_async(acc + (uint32_t)c, r);
+          float w0[8], w1[8];
+          scales8(c, w0);
+          scales8(c + 8, w1);
+          tmem_wait_ld();
+          reg_fence(r);
+          const bool mine = ((c >> 5) & 1) == half;
+          const int k0 = (c >> 6) * 16 + ((c & 31) >> 1);  // slot of element c in xk
 #pragma unroll
-            for (int j = 0; j < 16; j += 2)  // the linear's bf16 output
-              x[(c + j) >> 1] = pack2(v[j] * sa * wsc(args, n0 + c + j), v[j + 1] * sa * wsc(args, n0 + c + j + 1));
+          for (int j = 0; j < 16; j += 2) {
+            const float* w = j < 8 ? w0 : w1;
+            const uint32_t x2 = pack2(__uint_as_float(r[j]) * sa * w[j & 7], __uint_as_float(r[j + 1]) * sa * w[(j & 7) + 1]);
+            const float a = lo_bf(x2), b = hi_bf(x2);
+            ss += (double)(a * a) + (double)(b * b);  // x*x is exact in fp32 for bf16 x
+            if (mine) xk[k0 + (j >> 1)] = x2;
           }
-          if (row_ok) {
-            const RopeSide& r = args.rope;
-            const size_t T = (size_t)args.M;
-            if (ft < r.HQ + r.HK) {
-              const bool is_q = ft < r.HQ;
-              uint16_t* dst = is_q ? r.yq + ((size_t)ft * T + m) * 128 : r.yk + ((size_t)(ft - r.HQ) * T + m) * 128;
-              qk_rope_row(x, is_q ? r.q_norm : r.k_norm, r.cos + (size_t)m * 128, r.sin + (size_t)m * 128, r.eps,
-                          dst);
-            } else {
-              uint16_t* dst = r.yv + ((size_t)(ft - r.HQ - r.HK) * T + m) * 128;
+        }
+        if (row_ok) {
+          const RopeSide& r = args.rope;
+          const size_t T = (size_t)args.M;
+          if (ft < r.HQ + r.HK) {
+            const bool is_q = ft < r.HQ;
+            uint16_t* dst = is_q ? r.yq + ((size_t)ft * T + m) * 128 : r.yk + ((size_t)(ft - r.HQ) * T + m) * 128;
+            const uint16_t* wn = is_q ? r.q_norm : r.k_norm;
+            const float inv = inv_rms_from_ss(ss, 128, r.eps);
+            if (half == 0)
+              qk_rope_half<0>(xk, inv, wn, r.cos + (size_t)m * 128, r.sin + (size_t)m * 128, dst);
+            else
+              qk_rope_half<1>(xk, inv, wn, r.cos + (size_t)m * 128, r.sin + (size_t)m * 128, dst);
+          } else {  // v heads: copied through
+            uint16_t* dst = r.yv + ((size_t)(ft - r.HQ - r.HK) * T + m) * 128 + half * 32;
 #pragma unroll
-              for (int i = 0; i < 64; i += 4)
-                *reinterpret_cast<uint4*>(dst + 2 * i) = make_uint4(x[i], x[i + 1], x[i + 2], x[i + 3]);
+            for (int i = 0; i < 16; i += 4) {
+              *reinterpret_cast<uint4*>(dst + 2 * i) = make_uint4(xk[i], xk[i + 1], xk[i + 2], xk[i + 3]);
+              *reinterpret_cast<uint4*>(dst + 64 + 2 * i) = make_uint4(xk[16 + i], xk[17 + i], xk[18 + i], xk[19 + i]);
             }
           }
         }
@@ -344,51 +374,88 @@ __global__ void __launch_bounds__(THREADS, 1)
           }
           ++sc;
         };
-        if (args.epilogue == FFB_EPI_SWIGLU) {
-          // columns [0, BN/2) are gate channels ft*BN/2 + j, [BN/2, BN) the matching up rows
+        if constexpr (EPI == FFB_EPI_SWIGLU) {
+          // columns [0, BN/2) are gate channels ft*BN/2 + j, [BN/2, BN) the matching up rows;
+          // 8 channels at a time, the next group's TMEM loads in flight during the math
           constexpr int HALFC = BN / 2;
+          const int cb = half * (HALFC / 2);
 #pragma unroll 1
-          for (int c = half * (HALFC / 2); c < (half + 1) * (HALFC / 2); c += 32) {
+          for (int c0 = cb; c0 < cb + HALFC / 2; c0 += 32) {
             uint32_t o[16];
+            uint32_t g[2][8], u[2][8];
+            tmem_ld8_async(acc + (uint32_t)c0, g[0]);
+            tmem_ld8_async(acc + (uint32_t)(HALFC + c0), u[0]);
+            tmem_wait_ld();
+            reg_fence(g[0]);
+            reg_fence(u[0]);
 #pragma unroll
-            for (int sub = 0; sub < 32; sub += 16) {
-              float g[16], u[16];
-              tmem_ld16(acc + (uint32_t)(c + sub), g);
-              tmem_ld16(acc + (uint32_t)(HALFC + c + sub), u);
+            for (int grp = 0; grp < 4; ++grp) {
+              const int c = c0 + grp * 8, cur = grp & 1;
+              if (grp < 3) {
+                tmem_ld8_async(acc + (uint32_t)(c + 8), g[cur ^ 1]);
+                tmem_ld8_async(acc + (uint32_t)(HALFC + c + 8), u[cur ^ 1]);
+              }
+              float wg[8], wu[8];
+              scales8(c, wg);
+              scales8(HALFC + c, wu);
 #pragma unroll
-              for (int j = 0; j < 16; j += 2) {
+              for (int j = 0; j < 8; j += 2) {
                 float y2[2];
 #pragma unroll
                 for (int h = 0; h < 2; ++h) {
-                  const int jj = sub + j + h;
-                  const float gv = round_bf(g[j + h] * sa * wsc(args, n0 + c + jj));          // bf16 gate
-                  const float uv = round_bf(u[j + h] * sa * wsc(args, n0 + HALFC + c + jj));  // bf16 up
+                  const float gv = round_bf(__uint_as_float(g[cur][j + h]) * sa * wg[j + h]);  // bf16 gate
+                  const float uv = round_bf(__uint_as_float(u[cur][j + h]) * sa * wu[j + h]);  // bf16 up
                   y2[h] = round_bf(__fdiv_rn(gv, 1.f + expf(-gv))) * uv;
                 }
-                o[(sub + j) >> 1] = pack2(y2[0], y2[1]);
+                o[grp * 4 + (j >> 1)] = pack2(y2[0], y2[1]);
+              }
+              if (grp < 3) {
+                tmem_wait_ld();
+                reg_fence(g[cur ^ 1]);
+                reg_fence(u[cur ^ 1]);
               }
             }
-            staged_store(o, ft * HALFC + c, 0);
+            staged_store(o, ft * HALFC + c0, 0);
           }
-        } else if (args.epilogue == FFB_EPI_F32_PARTIAL) {
+        } else if constexpr (EPI == FFB_EPI_F32_PARTIAL) {
 #pragma unroll 1
           for (int c = half * (BN / 2); c < (half + 1) * (BN / 2); c += 16) {
-            float v[16];
-            tmem_ld16(acc + (uint32_t)c, v);
+            uint32_t r[16];
+            tmem_ld16_async(acc + (uint32_t)c, r);
+            float w0[8], w1[8];
+            scales8(c, w0);
+            scales8(c + 8, w1);
+            tmem_wait_ld();
+            reg_fence(r);
             uint32_t o[16];
 #pragma unroll
-            for (int j = 0; j < 16; ++j) o[j] = __float_as_uint(v[j] * sa * wsc(args, n0 + c + j));
+            for (int j = 0; j < 8; ++j) {
+              o[j] = __float_as_uint(__uint_as_float(r[j]) * sa * w0[j]);
+              o[8 + j] = __float_as_uint(__uint_as_float(r[8 + j]) * sa * w1[j]);
+            }
             staged_store(o, n0 + c, ks);
           }
         } else {
 #pragma unroll 1
           for (int c = half * (BN / 2); c < (half + 1) * (BN / 2); c += 32) {
-            float v[32];
-            tmem_ld32(acc + (uint32_t)c, v);
+            uint32_t r0[16], r1[16];
+            tmem_ld16_async(acc + (uint32_t)c, r0);
+            tmem_ld16_async(acc + (uint32_t)(c + 16), r1);
+            tmem_wait_ld();
+            reg_fence(r0);
+            reg_fence(r1);
             uint32_t o[16];
 #pragma unroll
-            for (int j = 0; j < 32; j += 2)
-              o[j >> 1] = pack2(v[j] * sa * wsc(args, n0 + c + j), v[j + 1] * sa * wsc(args, n0 + c + j + 1));
+            for (int g = 0; g < 4; ++g) {
+              float w[8];
+              scales8(c + 8 * g, w);
+              const uint32_t* r = g < 2 ? r0 : r1;
+#pragma unroll
+              for (int j = 0; j < 8; j += 2) {
+                const int k = (g & 1) * 8 + j;
+                o[g * 4 + (j >> 1)] = pack2(__uint_as_float(r[k]) * sa * w[j], __uint_as_float(r[k + 1]) * sa * w[j + 1]);
+              }
+            }
             staged_store(o, n0 + c, 0);
           }
         }
@@ -428,9 +495,21 @@ int num_sms() {
   return sms;
 }
 
+template <int BN, int EPI>
+cudaError_t launch_instance(const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap& to, const GemmArgs& ga,
+                            int grid, cudaStream_t stream) {
+  using C = Cfg<BN>;
+  static bool attr_set = false;  // the attribute is per function (one device per process here)
+  if (!attr_set) {
+    cudaError_t e = cudaFuncSetAttribute(fp8_gemm_kernel<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+    if (e != cudaSuccess) return e;
+    attr_set = true;
+  }
+  return ffb::launch(fp8_gemm_kernel<BN, EPI>, dim3(grid), dim3(THREADS), C::SMEM, stream, ta, tw, to, ga);
+}
+
 template <int BN>
 int launch_bn(const uint8_t* a8, const uint8_t* w8, GemmArgs& ga, cudaStream_t stream) {
-  using C = Cfg<BN>;
   CUtensorMap ta, tw, to;
   memset(&to, 0, sizeof(to));
   int rc = ffb::make_tmap_2d(&ta, a8, (uint64_t)ga.M, (uint64_t)ga.K, (uint64_t)ga.K, BM, BK, 1);
@@ -443,16 +522,19 @@ int launch_bn(const uint8_t* a8, const uint8_t* w8, GemmArgs& ga, cudaStream_t s
     rc = ffb::make_tmap_out(&to, ga.ws, 4, ga.N, ga.M, ga.splits, (uint64_t)ga.N * 4, (uint64_t)ga.N * ga.M * 4, 16,
                             32);
   if (rc) return rc;
-  static bool attr_set = false;  // the attribute is per function (one device per process here)
-  if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(fp8_gemm_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
-    if (e != cudaSuccess) return ffb::fail(FFB_ECUDA, "ffb_fp8_gemm: smem attribute: %s", cudaGetErrorString(e));
-    attr_set = true;
-  }
   ga.n_ttiles = (ga.M + BM - 1) / BM;
   ga.n_tiles = (ga.N / BN) * ga.splits * ga.n_ttiles;
   const int grid = ga.n_tiles < num_sms() ? ga.n_tiles : num_sms();
-  cudaError_t e = ffb::launch(fp8_gemm_kernel<BN>, dim3(grid), dim3(THREADS), C::SMEM, stream, ta, tw, to, ga);
+  cudaError_t e = cudaErrorInvalidValue;
+  if constexpr (BN == 128) {
+    if (ga.epilogue == EPI_QKROPE) e = launch_instance<128, EPI_QKROPE>(ta, tw, to, ga, grid, stream);
+    else if (ga.epilogue == FFB_EPI_BF16) e = launch_instance<128, FFB_EPI_BF16>(ta, tw, to, ga, grid, stream);
+    else if (ga.epilogue == FFB_EPI_F32_PARTIAL) e = launch_instance<128, FFB_EPI_F32_PARTIAL>(ta, tw, to, ga, grid, stream);
+  } else {
+    if (ga.epilogue == FFB_EPI_SWIGLU) e = launch_instance<256, FFB_EPI_SWIGLU>(ta, tw, to, ga, grid, stream);
+    else if (ga.epilogue == FFB_EPI_BF16) e = launch_instance<256, FFB_EPI_BF16>(ta, tw, to, ga, grid, stream);
+    else if (ga.epilogue == FFB_EPI_F32_PARTIAL) e = launch_instance<256, FFB_EPI_F32_PARTIAL>(ta, tw, to, ga, grid, stream);
+  }
   if (e != cudaSuccess) return ffb::fail(FFB_ECUDA, "ffb_fp8_gemm: launch: %s", cudaGetErrorString(e));
   return FFB_OK;
 }
@@ -464,6 +546,7 @@ int check_common(const uint8_t* a8, const float* a_scale, const uint8_t* w8, con
   FFB_REQUIRE(N % 128 == 0, "ffb_fp8_gemm: N=%d must be a multiple of 128", N);
   FFB_REQUIRE(K % 16 == 0, "ffb_fp8_gemm: K=%d must be a multiple of 16", K);
   FFB_REQUIRE(ffb::aligned(a8, 16) && ffb::aligned(w8, 16), "ffb_fp8_gemm: operands must be 16-byte aligned");
+  FFB_REQUIRE(ffb::aligned(w_scale, 16), "ffb_fp8_gemm: w_scale must be 16-byte aligned");
   return FFB_OK;
 }
 

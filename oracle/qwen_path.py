@@ -236,13 +236,15 @@ def quantize_weight_channel(w):
 # one accumulator per split; the splits' scaled fp32 partials are summed in split order.
 # "exact": float64 accumulation, the ideal that any fp32 hardware approximates (the
 # reference's cuBLAS FP8 GEMM accumulates in its own unspecified order).
+# "fp32": an ordinary fp32 GEMM of the e4m3 values (what CPU torch._scaled_mm does); the
+# fast mode the CPU timing legs use, not a parity reference.
 ACCUMULATION = "tcgen05"
 
 
 def set_accumulation(mode):
-    """Selects the FP8 accumulation model ("tcgen05" or "exact"); returns the previous one."""
+    """Selects the FP8 accumulation model ("tcgen05", "exact" or "fp32"); returns the previous one."""
     global ACCUMULATION
-    assert mode in ("tcgen05", "exact")
+    assert mode in ("tcgen05", "exact", "fp32")
     old, ACCUMULATION = ACCUMULATION, mode
     return old
 
@@ -252,6 +254,8 @@ def _fp8_acc(q, w8, k0=0, k1=None):
     k1 = q.shape[1] if k1 is None else k1
     if ACCUMULATION == "exact":
         return torch.matmul(q[:, k0:k1].float().double(), w8[:, k0:k1].float().double().t()).float()
+    if ACCUMULATION == "fp32":
+        return torch.matmul(q[:, k0:k1].float(), w8[:, k0:k1].float().t())
     from . import _tc
     return _tc.acc(q, w8, k0, k1)
 
