@@ -73,6 +73,26 @@ int make_tmap_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t col
   return FFB_OK;
 }
 
+int make_tmap_2d_bytes(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t row_bytes,
+                       uint32_t box_rows, uint32_t box_cols) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(FFB_ECUDA, "cuTensorMapEncodeTiled is unavailable from the driver");
+  if (!aligned(base, 16)) return fail(FFB_EINVAL, "TMA base address must be 16-byte aligned");
+  if (row_bytes % 16 != 0) return fail(FFB_EINVAL, "TMA row pitch (%llu bytes) must be a multiple of 16",
+                                       (unsigned long long)row_bytes);
+  if (box_cols % 16 != 0 || box_cols > 256 || box_rows > 256)
+    return fail(FFB_EINVAL, "TMA byte box %u x %u: inner extent a multiple of 16, both <= 256", box_cols, box_rows);
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {row_bytes};
+  cuuint32_t box[2] = {box_cols, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(FFB_ECUDA, "cuTensorMapEncodeTiled (bytes) failed (%d)", (int)r);
+  return FFB_OK;
+}
+
 int make_tmap_out(CUtensorMap* map, const void* base, int elem_bytes, uint64_t inner, uint64_t rows,
                   uint64_t depth, uint64_t row_bytes, uint64_t depth_bytes, uint32_t box_inner, uint32_t box_rows) {
   EncodeTiledFn fn = encode_fn();

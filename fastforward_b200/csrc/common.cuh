@@ -302,6 +302,10 @@ namespace ffb {
 // box_cols elements of `elem_bytes`, 128-byte swizzle, zero fill out of bounds.
 int make_tmap_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t row_bytes,
                  uint32_t box_rows, uint32_t box_cols, int elem_bytes);
+// 2-D byte map without swizzle: rows x cols bytes, box box_rows x box_cols (box_cols a
+// multiple of 16), zero fill out of bounds; the tile lands row after row in shared memory.
+int make_tmap_2d_bytes(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t row_bytes,
+                       uint32_t box_rows, uint32_t box_cols);
 // 3-D store map [depth][rows][inner] (bf16 or fp32), box {64 bytes, box_rows, 1}, 64-byte
 // swizzle: the staging tile in shared memory holds row r's 16-byte chunk c at
 // r*64 + ((c ^ ((r >> 1) & 3)) << 4), in a buffer aligned to 512 bytes.

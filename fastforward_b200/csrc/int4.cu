@@ -1,4 +1,4 @@
-// W4A16 path: symmetric int4 group-128 weight packing and the W4A16 GEMM.
+// W4A16 path: symmetric int4 group-128 weight packing (the GEMM is gemm_w4a16.cu).
 //
 // Packing (set-up): per group of 128 along K, s = bf16(max|W|/7) (floored at 1e-8),
 // q = clamp(rne(W/s), -8, 7), two nibbles per byte (low nibble = even k).
@@ -52,11 +52,4 @@ extern "C" int ffb_pack_int4(const uint16_t* w, uint8_t* packed, uint16_t* scale
                               w, packed, scales, N, K);
   if (e != cudaSuccess) return ffb::fail(FFB_ECUDA, "ffb_pack_int4: %s", cudaGetErrorString(e));
   return FFB_OK;
-}
-
-extern "C" int ffb_w4a16_gemm(const uint16_t* x, const uint8_t* packed, const uint16_t* scales, int epilogue,
-                              uint16_t* out, float* ws, int splits, int token_tile, int M, int N, int K, void* stream) {
-  (void)x; (void)packed; (void)scales; (void)epilogue; (void)out; (void)ws; (void)splits; (void)token_tile;
-  (void)M; (void)N; (void)K; (void)stream;
-  return ffb::fail(FFB_EUNSUPPORTED, "ffb_w4a16_gemm: not built yet");
 }

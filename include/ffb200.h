@@ -204,9 +204,12 @@ int ffb_pack_int4(const uint16_t* w, uint8_t* packed, uint16_t* scales, int N, i
 /* W4A16 GEMM: out[m,n] = bf16( sum_k x[m,k] * bf16(q[n,k] * s[n,k/128]) ), weights
  * dequantised to bf16 in shared memory and multiplied on tcgen05 (kind::f16).
  * Replaces _family/night_runtime.py:31-33 (`Int4.__call__` -> _weight_int4pack_mm).
- * x [M,K] bf16; epilogue FFB_EPI_BF16 / FFB_EPI_F32_PARTIAL / FFB_EPI_SWIGLU as above. */
+ * x [M,K] bf16 (K a multiple of 128); packed/scales as written by ffb_pack_int4;
+ * epilogue FFB_EPI_BF16 / FFB_EPI_F32_PARTIAL / FFB_EPI_SWIGLU as for ffb_fp8_gemm, without
+ * scales (they are inside the dequantised weights); feature_tile 128 or 256 (0 = 256
+ * when N allows; SwiGLU always 256). */
 int ffb_w4a16_gemm(const uint16_t* x, const uint8_t* packed, const uint16_t* scales,
-                   int epilogue, uint16_t* out, float* ws, int splits, int token_tile,
+                   int epilogue, uint16_t* out, float* ws, int splits, int feature_tile,
                    int M, int N, int K, void* stream);
 
 #ifdef __cplusplus

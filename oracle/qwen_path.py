@@ -275,6 +275,30 @@ def _fp8_linear(q, a_scale, w8, w_scale, splits=1):
     return total
 
 
+def _bf16_acc(a, w, k0, k1):
+    """Accumulated bf16 x bf16 dot products over K in [k0, k1) as fp32 [M, N] (the W4A16
+    GEMM's tcgen05 kind::f16 accumulation under ACCUMULATION "tcgen05")."""
+    if ACCUMULATION == "exact":
+        return torch.matmul(a[:, k0:k1].float().double(), w[:, k0:k1].float().double().t()).float()
+    if ACCUMULATION == "fp32":
+        return torch.matmul(a[:, k0:k1].float(), w[:, k0:k1].float().t())
+    from . import _tc
+    return _tc.acc_bf16(a, w, k0, k1)
+
+
+def _bf16_linear(x, w, splits=1):
+    """fp32 sum_s acc_s of x [M, K] . w [N, K]^T (bf16 values), K split in 64-column
+    blocks as the W4A16 kernel splits it (block range [s*nkb/S, (s+1)*nkb/S))."""
+    k = x.shape[1]
+    nkb = k // 64
+    total = None
+    for s in range(splits):
+        kb0, kb1 = s * nkb // splits, (s + 1) * nkb // splits
+        part = _bf16_acc(x.to(BF16), w.to(BF16), kb0 * 64, kb1 * 64)
+        total = part if total is None else total + part
+    return total
+
+
 def _fp8_dot(q, w8):
     """Accumulated FP8 dot products (fp64 tensor of fp32 values), no K split."""
     return _fp8_acc(q, w8).double()
@@ -465,9 +489,8 @@ def _linear(x, lin, mode, tail=False):
         return fp8_linear_static(x, lin["w8"], lin["w_scale"], lin["inv"], splits)
     if mode == "bf16":
         return (x.float() @ lin["w"].float().t()).to(BF16)
-    if mode == "int4":
-        w = int4_sym_dequantize(lin["q"], lin["s"])
-        return torch.matmul(x.float().double(), w.double().t()).float().to(BF16)
+    if mode == "int4":  # W4A16: x . bf16(q * s) (`_family/night_runtime.py:31-33` semantics)
+        return _bf16_linear(x, int4_sym_dequantize(lin["q"], lin["s"]), splits).to(BF16)
     raise ValueError(mode)
 
 

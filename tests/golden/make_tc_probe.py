@@ -3,6 +3,9 @@ and a GPU): raw fp32 accumulators of ffb_fp8_gemm (F32_PARTIAL epilogue, unit sc
 the oracle's accumulation model (oracle/tcgemm.c) must reproduce bit for bit.
 
 - tc_acc_probe.pt: seeded large-magnitude e4m3 inputs, whole K = 2560.
+- tc_bf16_probe.pt: the W4A16 GEMM (ffb_w4a16_gemm, kind::f16, bf16 x bf16) on a
+  moderate and a wide-exponent-range input (rows scaled by 2^-6 .. 2^6); the first 8 tokens
+  x 32 features of each are kept.
 - tc_acc_split.pt: the decoder's own operand distributions (per-token quantised bf16
   activations x per-channel quantised weights, std 0.02) through split-K = 3 (the first
   K split, [0, 768), is kept).  The kept tokens and features are those of the 50
@@ -74,6 +77,28 @@ def main():
                     tokens=torch.tensor(ms), features=torch.tensor(ns), k_range=(0, k1),
                     note="raw fp32 accumulators of the first K split of ffb_fp8_gemm (splits=3) on a B200"),
                HERE / "tc_acc_split.pt")
+    # kind::f16 (bf16) accumulation through the W4A16 GEMM, unit scales inside the weights
+    from fastforward_b200 import ops
+    probe = {}
+    for name, seed, xs, wsd in (("normal", 7, 1.0, 0.02), ("wide", 8, 50.0, 3.0)):
+        g = torch.Generator().manual_seed(seed)
+        M, N, K = 64, 256, 2560
+        x = torch.randn(M, K, generator=g) * xs
+        if name == "wide":
+            x = x * torch.pow(2.0, torch.randint(-6, 7, (M, K), generator=g).float())
+        x = x.to(torch.bfloat16)
+        w = (torch.randn(N, K, generator=g) * wsd).to(torch.bfloat16)
+        packed, scales = ops.pack_int4(w.to(dev))
+        q, s = oracle.int4_sym_quantize(w)
+        deq = oracle.int4_sym_dequantize(q, s).to(torch.bfloat16)
+        acc = torch.empty(1, M, N, device=dev)
+        xd = x.to(dev)
+        call("ffb_w4a16_gemm", ptr(xd), ptr(packed), ptr(scales), L.EPI_F32_PARTIAL, None, ptr(acc), 1, 256, M, N, K,
+             torch.cuda.current_stream().cuda_stream)
+        torch.cuda.synchronize()
+        probe[name] = dict(x=x[:8].clone(), w=deq[:32].clone(), acc=acc[0, :8, :32].cpu().clone())
+    probe["note"] = "raw fp32 accumulators of ffb_w4a16_gemm (F32_PARTIAL, one split) on a B200"
+    torch.save(probe, HERE / "tc_bf16_probe.pt")
     print(HERE)
 
 

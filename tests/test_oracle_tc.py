@@ -45,3 +45,11 @@ def test_k_split_ranges_match_whole_k_per_chunk_boundaries():
     # by the fp32 summation of two accumulators
     two = _tc.acc(d["a8"], d["w8"], 0, k // 2) + _tc.acc(d["a8"], d["w8"], k // 2, k)
     assert torch.allclose(two.double(), whole.double(), rtol=1e-5, atol=1e-2)
+
+
+def test_bf16_model_reproduces_gpu_accumulators():
+    # kind::f16 (bf16 x bf16) through the W4A16 GEMM: moderate and wide exponent ranges
+    d = torch.load(Path(__file__).resolve().parent / "golden" / "tc_bf16_probe.pt")
+    for name in ("normal", "wide"):
+        got = _tc.acc_bf16(d[name]["x"], d[name]["w"], 0, d[name]["x"].shape[1])
+        assert torch.equal(got, d[name]["acc"]), f"{name}: {(got != d[name]['acc']).sum().item()} differ"
