@@ -33,6 +33,17 @@ METRIC = "prefill tok/s (Qwen3-VL-4B FP8, T=320 prefill + 4-choice scoring); p50
 UNIT = "tok/s"
 
 
+def metric_for(workload):
+    """The headline metric for the default workload; the same wording for the others."""
+    if workload == "4B-fp8-T320":
+        return METRIC
+    from fastforward_b200.config import WORKLOADS
+    name, layout, mode = WORKLOADS[workload]
+    quant = "W4A16" if mode == "int4" else "FP8"
+    return (f"prefill tok/s (Qwen3-VL-{name} {quant}, T={layout.bucket} prefill + {layout.k}-choice scoring); "
+            "p50 latency in ms_per_step")
+
+
 def parse():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
@@ -117,7 +128,7 @@ class CpuSample:
     """The oracle (the reference path's arithmetic restated on the CPU) on the workload's
     model: built once, then timed one decoder layer (or the tail) at a time."""
 
-    def __init__(self, dims, layout, threads, n_layers=1):
+    def __init__(self, dims, layout, threads, n_layers=1, mode="rowwise"):
         import torch
         import oracle
         from fastforward_b200.synthetic import make_model_bf16, make_request
@@ -129,7 +140,8 @@ class CpuSample:
         self.o = oracle
         self.dims, self.layout = dims, layout
         src = make_model_bf16(dims, seed=0, device="cpu", layers=n_layers + 1)
-        self.om = oracle.quantized_model(dims, src, "rowwise")
+        self.mode = mode
+        self.om = oracle.quantized_model(dims, src, mode)
         self.req = make_request(dims, layout, seed=1)
         T = layout.bucket
         pos = position_ids(T, layout.image_start, layout.grid_h, layout.grid_w)
@@ -139,14 +151,14 @@ class CpuSample:
 
     def layer(self, j=0):
         t0 = time.perf_counter()
-        self.o.decoder_layer(self.om["layers"][j], self.h, self.cos, self.sin, self.om["dims"], "rowwise",
+        self.o.decoder_layer(self.om["layers"][j], self.h, self.cos, self.sin, self.om["dims"], self.mode,
                              self.req["deep"][0], self.layout.image_start, self.layout.nv)
         return time.perf_counter() - t0
 
     def tail(self):
         t0 = time.perf_counter()
         om = self.om
-        self.o.tail(om["layers"][self.n_layers], self.h, self.cos, self.sin, om["dims"], "rowwise",
+        self.o.tail(om["layers"][self.n_layers], self.h, self.cos, self.sin, om["dims"], self.mode,
                     self.req["pick"], om["final_norm"], om["head"], self.req["k"])
         return time.perf_counter() - t0
 
@@ -163,7 +175,7 @@ def run_reference(args):
     if rank != 0:
         return
     threads = os.cpu_count() or 1
-    cs = CpuSample(dims, layout, threads)
+    cs = CpuSample(dims, layout, threads, mode=mode)
     t_tail = cs.tail()
     times = []
     for i in range(args.warmup + args.steps):
@@ -173,14 +185,14 @@ def run_reference(args):
     T = layout.bucket
     per_req = statistics.median(times)
     value = T / per_req
-    line = dict(metric=METRIC, value=value, unit=UNIT, n_gpus=args.gpus, steps=args.steps, warmup=args.warmup,
-                ms_per_step=per_req * 1e3, higher_is_better=True, scaling="weak", vs_baseline=None, dtype="fp8-e4m3",
+    line = dict(metric=metric_for(args.workload), value=value, unit=UNIT, n_gpus=args.gpus, steps=args.steps, warmup=args.warmup,
+                ms_per_step=per_req * 1e3, higher_is_better=True, scaling="weak", vs_baseline=None, dtype="int4-bf16" if mode == "int4" else "fp8-e4m3",
                 data="synthetic", impl="reference",
                 config=dict(workload=args.workload, model=f"Qwen3-VL-{name}-shaped", global_batch=1, seq_len=T,
                             parallelism="cpu"),
                 cpu_baseline=dict(value=value, unit=UNIT, cores=threads, kind="port",
                                   sample=f"1 decoder layer per step (tail timed once, {t_tail:.2f}s), scaled to "
-                                         f"{dims.layers - 1} layers + tail; fp32 GEMMs of the e4m3 values"),
+                                         f"{dims.layers - 1} layers + tail; fp32 GEMMs of the quantised weights"),
                 e2e=dict(value=value, unit=UNIT, h2d_bytes_per_step=0, d2h_bytes_per_step=0))
     print(json.dumps(line), flush=True)
 
@@ -204,27 +216,31 @@ def gemm_roofline(eng, T, peaks, reps=20):
     """Times each GEMM role of the forward standalone (same shapes and plans as inside the
     graph) with CUDA events; returns per-role stats and the dominant role."""
     import torch
-    from fastforward_b200 import _lib as L
     m = eng.m
-    d = eng.d
     b = eng.buffers_for(T)
     pl = eng._plans(T)
-    lay = m.layers[0]
     s = torch.cuda.current_stream()
     eng._s = s.cuda_stream
-    roles = {"qkv": (b.x8, b.xs, b.qkv), "o": (b.o8, b.os, b.lin_out), "gateup": (b.post8, b.posts, b.act),
-             "down": (b.act8, b.acts, b.lin_out)}
+    int4 = m.mode == "int4"
+    if int4:  # bf16 GEMM inputs
+        roles = {"qkv": (b.xb, None, b.qkv), "o": (b.attn, None, b.lin_out), "gateup": (b.postb, None, b.act),
+                 "down": (b.act, None, b.lin_out)}
+    else:
+        roles = {"qkv": (b.x8, b.xs, b.qkv), "o": (b.o8, b.os, b.lin_out), "gateup": (b.post8, b.posts, b.act),
+                 "down": (b.act8, b.acts, b.lin_out)}
     out = {}
     cos, sin = next(iter(eng.tables.values()))
-    for role, (a8, sc, o) in roles.items():
+    for role, (a, sc, o) in roles.items():
         p = pl[("full", role)]
 
         def one(i):
             lay_i = m.layers[i % m.depth]
-            if role == "qkv":  # fused qkv GEMM + QK-norm + RoPE epilogue
-                eng._qkv(p, b, lay_i, cos, sin, T, False, True)
+            if role == "qkv":  # qkv GEMM (+ the fused QK-norm + RoPE epilogue in FP8 mode)
+                eng._qkv(p, b, lay_i, cos, sin, T, int4, True)
+            elif int4:
+                eng._w4(p, a, lay_i.lin[role], o, b.ws)
             else:
-                eng._gemm(p, a8, sc, lay_i.lin[role], o, b.ws, True)
+                eng._gemm(p, a, sc, lay_i.lin[role], o, b.ws, True)
         for i in range(3):
             one(i)
         ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
@@ -235,7 +251,7 @@ def gemm_roofline(eng, T, peaks, reps=20):
         torch.cuda.synchronize()
         dt = ev[0].elapsed_time(ev[1]) / reps * 1e-3
         flops = 2.0 * p.m * p.n * p.k
-        wbytes = p.n * p.k
+        wbytes = p.n * p.k * (0.5 + 2 / 128 if int4 else 1)
         out[role] = dict(m=p.m, n=p.n, k=p.k, bn=p.bn, splits=p.splits, us=dt * 1e6, tflops=flops / dt / 1e12,
                          weight_gbs=wbytes / dt / 1e9)
     return out
@@ -371,51 +387,60 @@ def run_ours(args):
         h2d = (r0["ids"].numel() * 8 + r0["visual"].numel() * 2 + sum(x.numel() * 2 for x in r0["deep"]) + 8)
         d2h = 2 * layout.k * 4
 
-        # ---- roofline of the dominant kernel (the FP8 GEMM), standalone event timing
+        # ---- roofline of the dominant kernel (the GEMM), standalone event timing
         roles = gemm_roofline(eng, T, peaks)
-        fp8_peak = 2.0 * peaks["bf16"]
+        int4 = mode == "int4"
+        tc_peak = peaks["bf16"] if int4 else 2.0 * peaks["bf16"]
+        wfac = 0.5 + 2 / 128 if int4 else 1.0  # weight bytes per parameter
         dom = max(roles, key=lambda k: roles[k]["us"])
         dr = roles[dom]
-        roofline = dict(bound="tensor", achieved=dr["tflops"], peak=fp8_peak, unit="TFLOP/s",
-                        frac=dr["tflops"] / fp8_peak, traffic=ncu_traffic(args.workload, dom),
+        if int4:
+            peak_note = f"bf16 dense = {peaks['src']} cuBLAS bf16 {peaks['bf16']} TFLOP/s"
+        else:
+            peak_note = f"FP8 dense = 2 x {peaks['src']} cuBLAS bf16 {peaks['bf16']} TFLOP/s"
+        roofline = dict(bound="tensor", achieved=dr["tflops"], peak=tc_peak, unit="TFLOP/s",
+                        frac=dr["tflops"] / tc_peak, traffic=ncu_traffic(args.workload, dom),
                         traffic_note="ncu dram__bytes_read.sum + dram__bytes_write.sum per launch; "
-                                     "algorithmic weight bytes per launch = %d" % (dr["n"] * dr["k"]),
-                        kernel=f"fp8_gemm_kernel ({dom})",
-                        peak_note=f"FP8 dense = 2 x {peaks['src']} cuBLAS bf16 {peaks['bf16']} TFLOP/s",
+                                     "algorithmic weight bytes per launch = %d" % int(dr["n"] * dr["k"] * wfac),
+                        kernel=f"{'w4a16' if int4 else 'fp8'}_gemm_kernel ({dom})",
+                        peak_note=peak_note,
                         weight_stream_gbs=dr["weight_gbs"], hbm_peak_gbs=peaks["hbm"],
                         per_role={k: {kk: (round(vv, 3) if isinstance(vv, float) else vv) for kk, vv in v.items()}
                                   for k, v in roles.items()})
         gemm_us = sum(v["us"] for v in roles.values()) * (dims.layers - 1)
-        # whole-forward algorithmic roofline: max(FLOPs / FP8 peak, weight bytes / HBM)
+        # whole-forward algorithmic roofline: max(FLOPs / tensor peak, weight bytes / HBM)
         P = dims.params_per_layer() * dims.layers
         flops = 2.0 * T * P + 4.0 * (T * (T + 1) / 2) * dims.d * dims.hq * dims.layers
-        t_roof = max(flops / (fp8_peak * 1e12), P / (peaks["hbm"] * 1e9))
+        weight_bytes = P * wfac
+        t_roof = max(flops / (tc_peak * 1e12), weight_bytes / (peaks["hbm"] * 1e9))
 
         cpu = None
         if rank == 0 and world == 1 and not args.no_cpu_baseline:
             threads = os.cpu_count() or 1
-            cs = CpuSample(dims, layout, threads)
+            cs = CpuSample(dims, layout, threads, mode=mode)
             t_layers = [cs.layer() for _ in range(args.cpu_layers)]
             t_tail = cs.tail()
             full = cs.full_request_seconds(statistics.median(t_layers), t_tail)
             cpu = dict(value=T / full, unit=UNIT, cores=threads, kind="port",
                        sample=f"{args.cpu_layers} timed decoder layers (median {statistics.median(t_layers):.2f}s) "
                               f"+ tail ({t_tail:.2f}s) of the {name} model at T={T}, scaled to "
-                              f"{dims.layers - 1} layers + tail; fp32 GEMMs of the e4m3 values")
+                              f"{dims.layers - 1} layers + tail; fp32 GEMMs of the quantised weights")
 
     clk_sum = clk.summary()
     if rank == 0:
-        line = dict(metric=METRIC, value=value, unit=UNIT, n_gpus=world, steps=args.steps, warmup=args.warmup,
-                    ms_per_step=p50, higher_is_better=True, scaling="weak", vs_baseline=None, dtype="fp8-e4m3",
-                    data="synthetic (seeded N(0,0.02) weights, N(0,1) visual/deepstack rows, uniform text ids)",
+        line = dict(metric=metric_for(args.workload), value=value, unit=UNIT, n_gpus=world, steps=args.steps, warmup=args.warmup,
+                    ms_per_step=p50, higher_is_better=True, scaling="weak", vs_baseline=None,
+                    dtype="int4-bf16" if int4 else "fp8-e4m3", data="synthetic (seeded N(0,0.02) weights, N(0,1) visual/deepstack rows, uniform text ids)",
                     config=dict(workload=args.workload, model=f"Qwen3-VL-{name}-shaped", global_batch=world,
                                 seq_len=T, parallelism=f"replicas{world}", quant=mode,
-                                l2="weights (3.6 GB) exceed L2; no flush needed", tokens_per_step=T),
+                                l2=f"weights ({weight_bytes / 1e9:.1f} GB) exceed L2; no flush needed",
+                                tokens_per_step=T),
                     latency_ms=dict(p50=p50, p99=p99, mean=total_s / args.steps * 1e3),
                     requests_per_s=world * args.steps / total_s,
                     roofline=roofline,
-                    forward_roofline=dict(flops=flops, weight_bytes=P, t_roofline_ms=t_roof * 1e3,
-                                          frac=t_roof * 1e3 / p50, note="max(FLOPs/FP8 peak, weights/HBM) / p50"),
+                    forward_roofline=dict(flops=flops, weight_bytes=weight_bytes, t_roofline_ms=t_roof * 1e3,
+                                          frac=t_roof * 1e3 / p50,
+                                          note="max(FLOPs/tensor peak, weights/HBM) / p50"),
                     gemm_share_est=gemm_us * 1e-3 / p50,
                     e2e=dict(value=e2e_value, unit=UNIT, h2d_bytes_per_step=h2d, d2h_bytes_per_step=d2h,
                              wall_s=wall, api="Accelerator.prefill_score"),
