@@ -276,18 +276,22 @@ def run_ours(args):
     dims = MODELS[name]
     T = layout.bucket
     peaks = read_peaks()
+    # the 32B model is tensor-parallel over the ranks (one request stream shared by all of
+    # them); the smaller models run one independent replica per rank
+    tp_mode = name == "32B" and world > 1
 
     with torch.no_grad():
         src = make_model_bf16(dims, seed=0, device=dev, layers=args.layers)
-        pm = PackedModel(dims, src, mode=mode, device=dev, free_source=True)
+        pm = PackedModel(dims, src, mode=mode, device=dev, free_source=True, tp=(rank, world) if tp_mode else None)
         del src
         torch.cuda.empty_cache()
-        eng = Engine(pm)
-        # requests: a pool of distinct synthetic requests in pinned host memory
+        eng = Engine(pm, tp_group=dist.group.WORLD if tp_mode else None)
+        # requests: a pool of distinct synthetic requests in pinned host memory (the same
+        # requests on every rank of a tensor-parallel group)
         n_pool = 8
         reqs = []
         for i in range(n_pool):
-            r = make_request(dims, layout, seed=1000 * rank + i)
+            r = make_request(dims, layout, seed=(0 if tp_mode else 1000 * rank) + i)
             reqs.append(dict(ids=r["ids"][:layout.n_tokens].pin_memory(), visual=r["visual"].pin_memory(),
                              deep=[x.pin_memory() for x in r["deep"]], pick=r["pick"], k=r["k"]))
         entry = eng.capture(T, layout.image_start, layout.nv, layout.grid_h, layout.grid_w, layout.k, dims.deepstack)
@@ -344,7 +348,8 @@ def run_ours(args):
             t = torch.tensor([total_s], device=dev)
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             total_s = t.item()
-        value = world * args.steps * T / total_s
+        streams = 1 if tp_mode else world  # independent request streams
+        value = streams * args.steps * T / total_s
 
         # ---- e2e: through the public entry with host (pinned) buffers, H2D + D2H per step
         from fastforward_b200.api import Accelerator
@@ -382,7 +387,7 @@ def run_ours(args):
             t = torch.tensor([e2e_s], device=dev)
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             e2e_s = t.item()
-        e2e_value = world * args.steps * T / e2e_s
+        e2e_value = streams * args.steps * T / e2e_s
         r0 = reqs[0]
         h2d = (r0["ids"].numel() * 8 + r0["visual"].numel() * 2 + sum(x.numel() * 2 for x in r0["deep"]) + 8)
         d2h = 2 * layout.k * 4
@@ -412,7 +417,9 @@ def run_ours(args):
         P = dims.params_per_layer() * dims.layers
         flops = 2.0 * T * P + 4.0 * (T * (T + 1) / 2) * dims.d * dims.hq * dims.layers
         weight_bytes = P * wfac
-        t_roof = max(flops / (tc_peak * 1e12), weight_bytes / (peaks["hbm"] * 1e9))
+        # a tensor-parallel group shares one request: its roofline has `world` GPUs' peaks
+        gpus_per_stream = world if tp_mode else 1
+        t_roof = max(flops / (tc_peak * 1e12), weight_bytes / (peaks["hbm"] * 1e9)) / gpus_per_stream
 
         cpu = None
         if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -429,18 +436,19 @@ def run_ours(args):
     clk_sum = clk.summary()
     if rank == 0:
         line = dict(metric=metric_for(args.workload), value=value, unit=UNIT, n_gpus=world, steps=args.steps, warmup=args.warmup,
-                    ms_per_step=p50, higher_is_better=True, scaling="weak", vs_baseline=None,
+                    ms_per_step=p50, higher_is_better=True, scaling="strong" if tp_mode else "weak",
+                    vs_baseline=None,
                     dtype="int4-bf16" if int4 else "fp8-e4m3", data="synthetic (seeded N(0,0.02) weights, N(0,1) visual/deepstack rows, uniform text ids)",
-                    config=dict(workload=args.workload, model=f"Qwen3-VL-{name}-shaped", global_batch=world,
-                                seq_len=T, parallelism=f"replicas{world}", quant=mode,
+                    config=dict(workload=args.workload, model=f"Qwen3-VL-{name}-shaped", global_batch=streams,
+                                seq_len=T, parallelism=f"tp{world}" if tp_mode else f"replicas{world}", quant=mode,
                                 l2=f"weights ({weight_bytes / 1e9:.1f} GB) exceed L2; no flush needed",
                                 tokens_per_step=T),
                     latency_ms=dict(p50=p50, p99=p99, mean=total_s / args.steps * 1e3),
-                    requests_per_s=world * args.steps / total_s,
+                    requests_per_s=streams * args.steps / total_s,
                     roofline=roofline,
                     forward_roofline=dict(flops=flops, weight_bytes=weight_bytes, t_roofline_ms=t_roof * 1e3,
                                           frac=t_roof * 1e3 / p50,
-                                          note="max(FLOPs/tensor peak, weights/HBM) / p50"),
+                                          note="max(FLOPs/tensor peak, weights/HBM) / GPUs per request / p50"),
                     gemm_share_est=gemm_us * 1e-3 / p50,
                     e2e=dict(value=e2e_value, unit=UNIT, h2d_bytes_per_step=h2d, d2h_bytes_per_step=d2h,
                              wall_s=wall, api="Accelerator.prefill_score"),

@@ -68,13 +68,20 @@ class PackedModel:
     scales (the BASELINE scheme, `_legacy/fp8_private.py`); "static": per-tensor weight
     scale + static per-tensor activation scale (`_family/depth_fp8.py`, the reference's
     shipped scheme; inverse scales from `calibrate`); "int4": W4A16 symmetric group 128.
-    The gate/up weight rows (and their scales) are stored interleaved per 64 channels for
+    The gate/up weight rows (and their scales) are stored interleaved per 128 channels for
     the fused SwiGLU epilogue.
+
+    tp = (rank, world) keeps only this rank's tensor-parallel shard of every linear
+    (`fastforward_b200.tp`): each weight is packed whole, then sliced, and `dims` becomes the
+    per-rank shape (heads and SwiGLU channels divided by the world size).
     """
 
-    def __init__(self, dims, bf16_model, mode="rowwise", device="cuda", free_source=False):
+    def __init__(self, dims, bf16_model, mode="rowwise", device="cuda", free_source=False, tp=None):
         assert mode in ("rowwise", "static", "int4")
-        self.dims = dims
+        from . import tp as tpmod
+        self.full_dims = dims
+        self.tp = tp
+        self.dims = tpmod.local_dims(dims, tp[1]) if tp else dims
         self.mode = mode
         self.device = torch.device(device)
         self.embed = bf16_model["embed"].to(self.device, BF16).contiguous()
@@ -99,6 +106,8 @@ class PackedModel:
                 else:
                     w8, scale = _pack_fp8(w, per_channel=(mode == "rowwise"))
                     lay.lin[role] = dict(w8=w8, scale=scale)
+                if tp:
+                    lay.lin[role] = tpmod.shard_packed(role, lay.lin[role], dims, tp[0], tp[1])
                 lay.inv[role] = 1.0
                 del w
             self.layers.append(lay)
@@ -190,10 +199,16 @@ class Buffers:
 class Engine:
     """Runs prefill + choice scoring for one packed model on one device."""
 
-    def __init__(self, model: PackedModel, pdl=True, autotune=True):
+    def __init__(self, model: PackedModel, pdl=True, autotune=True, tp_group=None):
+        """tp_group: the torch.distributed (NCCL) group of a tensor-parallel model
+        (`PackedModel(tp=...)`); o_proj and down_proj partial sums are all-reduced in it."""
         L.require_cuda()
         self.m = model
         self.d = model.dims
+        self.world = model.tp[1] if model.tp else 1
+        self.group = tp_group
+        if self.world > 1 and tp_group is None:
+            raise ValueError("a tensor-parallel model needs its process group")
         self.device = model.device
         self.graphs = {}
         self.tables = {}
@@ -218,6 +233,8 @@ class Engine:
                 bn = 128 if role == "qkv" else (256 if swiglu else pick_feature_tile(n))
                 s = plan_splits(m, n, k, bn, allow_split=not swiglu and role != "qkv")
                 epi = L.EPI_SWIGLU if swiglu else (L.EPI_F32_PARTIAL if s > 1 else L.EPI_BF16)
+                if self.world > 1 and role in ("o", "down"):  # fp32 partial for the all-reduce
+                    s, epi = 1, L.EPI_F32_PARTIAL
                 pl[(tag, role)] = GemmPlan(m, n, k, bn, s, epi)
         self.plans[T] = pl
         return pl
@@ -249,6 +266,8 @@ class Engine:
             tag, role = key
             if role == "qkv" or p.epilogue == L.EPI_SWIGLU:
                 continue  # fixed tiles: one head per tile / gate-up pairs per tile
+            if self.world > 1 and role in ("o", "down"):
+                continue  # one fp32 partial per rank, all-reduced
             a8, sc, out = ins[role]
             nkb = math.ceil(p.k / 128)
             bns = [x for x in (256, 128) if p.n % x == 0]
@@ -307,6 +326,13 @@ class Engine:
              int(lin["scale"].numel() > 1), ptr(lay.q_norm), ptr(lay.k_norm), float(d.eps), ptr(cos), ptr(sin),
              ptr(b.yq), ptr(b.yk), ptr(b.yv), T, d.hq, d.hk, d.hidden, self._s)
 
+    def _tp_reduce(self, plan, ws):
+        """Sums this rank's fp32 partial [m, n] (in ws) over the tensor-parallel group, in
+        place, on the current stream (captured into the graph with the kernels)."""
+        if self.world > 1:
+            import torch.distributed as dist
+            dist.all_reduce(ws[:plan.m * plan.n], group=self.group)
+
     def _split_args(self, plan, bf16_out, ws):
         """(b, b32, splits) arguments of a consumer of this GEMM's output."""
         if plan.epilogue == L.EPI_F32_PARTIAL:
@@ -360,6 +386,7 @@ class Engine:
                 call("ffb_quantize_fp8", ptr(b.attn), qmode, lay.inv["o"], ptr(b.o8), ptr(b.os), T, HQ * D,
                      self._s)
                 self._gemm(p, b.o8, b.os, lay.lin["o"], b.lin_out, b.ws, rowwise)
+            self._tp_reduce(p, b.ws)
             ob, o32, os_ = self._split_args(p, b.lin_out, b.ws)
             if int4:
                 call("ffb_add_rmsnorm", ptr(h_cur), ob, o32, os_, None, 0, 0, ptr(lay.post_norm), eps, ptr(h_mid),
@@ -380,6 +407,7 @@ class Engine:
                 call("ffb_quantize_fp8", ptr(b.act), qmode, lay.inv["down"], ptr(b.act8), ptr(b.acts), T, I,
                      self._s)
                 self._gemm(p, b.act8, b.acts, lay.lin["down"], b.lin_out, b.ws, rowwise)
+            self._tp_reduce(p, b.ws)
             db, d32, ds = self._split_args(p, b.lin_out, b.ws)
             dp = deep[j] if (deep is not None and j < len(deep)) else None
             if int4:
@@ -402,6 +430,7 @@ class Engine:
         else:
             call("ffb_quantize_fp8", ptr(b.attn), qmode, lay.inv["o"], ptr(b.o8), ptr(b.os), 1, HQ * D, self._s)
             self._gemm(p, b.o8, b.os, lay.lin["o"], b.lin_out, b.ws, rowwise)
+        self._tp_reduce(p, b.ws)
         ob, o32, os_ = self._split_args(p, b.lin_out, b.ws)
         call("ffb_gather_rows", ptr(h_cur), ptr(b.pick), ptr(b.hp), 1, H * 2, self._s)
         if int4:
@@ -421,6 +450,7 @@ class Engine:
         else:
             call("ffb_quantize_fp8", ptr(b.act), qmode, lay.inv["down"], ptr(b.act8), ptr(b.acts), 1, I, self._s)
             self._gemm(p, b.act8, b.acts, lay.lin["down"], b.mlp1, b.ws, rowwise)
+        self._tp_reduce(p, b.ws)
         mb, m32, ms = self._split_args(p, b.mlp1, b.ws)
         call("ffb_readout", ptr(b.res1), mb, m32, ms, ptr(m.final_norm), eps, ptr(m.head), m.head.shape[0], int(k),
              ptr(b.logits), ptr(b.logprobs), H, self._s)

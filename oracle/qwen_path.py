@@ -481,7 +481,36 @@ def embed_rows(embed, ids, visual, image_start):
     return h
 
 
+def _tp_linear(x, lin, mode, world):
+    """A K-split (row-parallel) linear over `world` tensor-parallel ranks: rank r holds
+    input columns [r*K/world, (r+1)*K/world) of x and of the weight, quantises its slice
+    of each row on its own (per-token scales over the slice) and produces an fp32 partial;
+    the partials are summed in rank order (the all-reduce) and rounded once to bf16."""
+    x = x.reshape(-1, x.shape[-1])
+    m, k = x.shape
+    w = k // world
+    total = None
+    for r in range(world):
+        xs = x[:, r * w:(r + 1) * w]
+        if mode == "rowwise":
+            q, sa = quantize_rows(xs)
+            part = _fp8_linear(q, sa, lin["w8"][:, r * w:(r + 1) * w].contiguous(), lin["w_scale"], 1)[:m]
+        elif mode == "static":
+            q = quantize_static(xs, lin["inv"])
+            sa = (torch.tensor([1.0], dtype=torch.float64) / lin["inv"]).float()
+            part = _fp8_linear(q, sa, lin["w8"][:, r * w:(r + 1) * w].contiguous(), lin["w_scale"], 1)[:m]
+        elif mode == "int4":
+            deq = int4_sym_dequantize(lin["q"][:, r * w:(r + 1) * w], lin["s"][:, r * w // 128:(r + 1) * w // 128])
+            part = _bf16_linear(xs, deq, 1)
+        else:
+            raise ValueError(mode)
+        total = part if total is None else total + part
+    return total.to(BF16)
+
+
 def _linear(x, lin, mode, tail=False):
+    if lin.get("tp_world", 1) > 1:
+        return _tp_linear(x, lin, mode, lin["tp_world"])
     splits = lin.get("splits_tail" if tail else "splits", 1)
     if mode == "rowwise":
         return fp8_linear_rowwise(x, lin["w8"], lin["w_scale"], splits)
@@ -586,11 +615,13 @@ def prefill_score(model, ids, visual, deepstack, position_ids, pick, k, mode="ro
     return tail(all_layers[depth - 1], h, cos, sin, dims, mode, pick, model["final_norm"], model["head"], k)
 
 
-def quantized_model(dims, src, mode="rowwise", inv=None, splits=None):
+def quantized_model(dims, src, mode="rowwise", inv=None, splits=None, tp=1):
     """The oracle's view of a bf16 source model (`fastforward_b200.synthetic` layout, gate
     rows then up rows): weights quantised here, on the CPU, with the reference's formulas.
     For mode "static", `inv[j][role]` are the calibrated inverse activation scales;
-    `splits` maps (tag, role) -> K-split count of the GPU plan ("full"/"tail")."""
+    `splits` maps (tag, role) -> K-split count of the GPU plan ("full"/"tail");
+    `tp` > 1 computes o_proj and down_proj as `tp` tensor-parallel partial sums
+    (`_tp_linear`); every other op is the same on every rank."""
     layers = []
     for j, lay in enumerate(src["layers"]):
         d = {n: lay[n].cpu() for n in ("in_norm", "post_norm", "q_norm", "k_norm")}
@@ -610,6 +641,8 @@ def quantized_model(dims, src, mode="rowwise", inv=None, splits=None):
             if splits:
                 d[role]["splits"] = splits.get(("full", role), 1)
                 d[role]["splits_tail"] = splits.get(("tail", role), 1)
+            if tp > 1 and role in ("o", "down"):
+                d[role]["tp_world"] = tp
         layers.append(d)
     dims_d = dict(hq=dims.hq, hk=dims.hk, d=dims.d, eps=dims.eps, theta=dims.theta, inter=dims.inter)
     return dict(dims=dims_d, embed=src["embed"].cpu(), head=src["head"].cpu(), final_norm=src["final_norm"].cpu(),
