@@ -1,4 +1,6 @@
-// Causal GQA attention for head_dim 128 (prefill and the pick-row tail).
+// Causal GQA attention for head_dim 128: the pick-row tail (selected query rows) and
+// prefill with unaligned outputs here; the full causal prefill goes to the tcgen05 kernel
+// of attention_tc.cu.
 //
 // Semantics of the reference kernel (_legacy/limit_kernels.py:8-33): scores in fp32,
 // scaled by 1/sqrt(128); online softmax over key blocks (running max, rescaled
@@ -262,6 +264,9 @@ __global__ void __launch_bounds__(128) attention_kernel(const AttnArgs p) {
 
 }  // namespace
 
+int ffb_attention_tc(const uint16_t* q, const uint16_t* k, const uint16_t* v, uint16_t* out, int T, int HQ, int HK,
+                     float scale, cudaStream_t stream);
+
 extern "C" int ffb_attention(const uint16_t* q, const uint16_t* k, const uint16_t* v, const int64_t* positions,
                              int q_gather, uint16_t* out, int S, int T, int HQ, int HK, float scale, void* stream) {
   FFB_REQUIRE(q && k && v && out, "ffb_attention: NULL pointer");
@@ -271,6 +276,8 @@ extern "C" int ffb_attention(const uint16_t* q, const uint16_t* k, const uint16_
   FFB_REQUIRE(!q_gather || positions, "ffb_attention: q_gather needs positions");
   FFB_REQUIRE(ffb::aligned(q, 16) && ffb::aligned(k, 16) && ffb::aligned(v, 16) && ffb::aligned(out, 4),
               "ffb_attention: alignment");
+  if (!positions && S == T && ffb::aligned(out, 16))  // causal prefill: the tcgen05 kernel
+    return ffb_attention_tc(q, k, v, out, T, HQ, HK, scale, (cudaStream_t)stream);
   static bool attr = false;
   if (!attr) {
     cudaError_t e = cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);

@@ -1,0 +1,337 @@
+// Causal GQA prefill attention (head_dim 128) on the sm_100a tensor cores: TMA-fed
+// tcgen05 MMAs with the score and output tiles in tensor memory.
+//
+// Semantics of the reference kernel (_legacy/limit_kernels.py:8-33, BLOCK_N = 64): scores
+// in fp32 scaled by 1/sqrt(128); online softmax over 64-key blocks (running max m,
+// denominator l = l * alpha + sum(p), accumulator acc = acc * alpha + P.V with
+// alpha = exp(m_old - m_new)); P cast to bf16 before its product with V; output
+// bf16(acc / l).  Keys past the query's position (and past T) are masked.
+//
+// One CTA = 128 query rows of one head (the M of the MMA); 320 threads:
+//   warp 0     TMA producer: the Q tile once ([128 x 128] as two 64-column swizzled
+//              halves), K and V blocks of 64 keys into a ring of KV_STAGES slots;
+//   warp 1     TMEM allocator + single-thread MMA issuer:
+//                S_j = Q . K_j^T  (M 128, N 64, 8 x K16, both operands K-major) -> TMEM;
+//                O_j = P_j . V_j  (M 128, N 128, 4 x K16; V read MN-major straight from
+//                                  its row-major [key][d] tile) -> TMEM;
+//   warps 2..9 softmax, two threads per query row (TMEM lane quarter = warp % 4; warps w
+//              and w + 4 share a quarter): each reads 32 of the block's 64 scores, the two
+//              exchange their row maxima through shared memory, each writes its half of
+//              the bf16 P row into a swizzled [128 x 64] tile, keeps its own part of the
+//              denominator (same alpha) and folds its 64 columns of the previous block's O
+//              into an fp32 accumulator in registers (o = o * alpha + O, one block late).
+// S, P and O are double-buffered: the MMA warp issues S_{j+2} as soon as the softmax has
+// read S_j and P_j . V_j as soon as P_j is written, so the tensor core works on the next
+// blocks while the softmax runs.  Barriers: q_full, kv_full/kv_empty[stage],
+// s_full/s_free[2], p_full[2], o_full[2].  Every wait is bounded; a timeout sets the
+// abort flag and the device error word, and TMEM is released.
+#include "common.cuh"
+#include "pdl.cuh"
+
+namespace {
+
+constexpr int D = 128;
+constexpr int BM = 128;             // query rows per CTA (UMMA M)
+constexpr int BN = 64;              // keys per block (the reference's BLOCK_N)
+constexpr int KV_STAGES = 3;
+constexpr int Q_HALF = BM * 128;    // one 64-column half of the Q tile: 16 KB
+constexpr int KV_HALF = BN * 128;   // one 64-column half of a K or V block: 8 KB
+constexpr int STAGE = 4 * KV_HALF;  // K (2 halves) + V (2 halves)
+constexpr int P_BYTES = BM * 128;   // [128 x 64] bf16
+constexpr int THREADS = 320;
+constexpr int XCH_BYTES = 2 * 2 * BM * 4;  // row-max exchange [2 buffers][2 halves][128 rows]
+constexpr int SMEM = 2 * Q_HALF + KV_STAGES * STAGE + 2 * P_BYTES + XCH_BYTES + 256 + 1024;
+constexpr int TMEM_COLS = 512;      // S[b] at column 64b (64 wide), O[b] at 128 + 128b (128 wide)
+
+struct TcArgs {
+  uint16_t* out;
+  int T, HQ, HK;
+  float scale_log2;  // scale * log2(e)
+};
+
+__global__ void __launch_bounds__(THREADS, 1)
+    attention_tc_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_k,
+                        const __grid_constant__ CUtensorMap tmap_v, const TcArgs args) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sq = smem;                          // [2][128 x 128 B]
+  uint8_t* skv = sq + 2 * Q_HALF;              // [KV_STAGES][K0 K1 V0 V1]
+  uint8_t* sp = skv + KV_STAGES * STAGE;       // P tiles [2]
+  float* xch = reinterpret_cast<float*>(sp + 2 * P_BYTES);
+  uint64_t* q_full = reinterpret_cast<uint64_t*>(sp + 2 * P_BYTES + XCH_BYTES);
+  uint64_t* kv_full = q_full + 1;
+  uint64_t* kv_empty = kv_full + KV_STAGES;
+  uint64_t* s_full = kv_empty + KV_STAGES;  // [2]
+  uint64_t* s_free = s_full + 2;            // [2]
+  uint64_t* p_full = s_free + 2;            // [2]
+  uint64_t* o_full = p_full + 2;            // [2]
+  uint64_t* x_bar = o_full + 2;             // [4]: one per lane quarter, two arrivals
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(x_bar + 4);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int qt = gridDim.x - 1 - blockIdx.x;  // heaviest (latest) query tiles first
+  const int h = blockIdx.y, kvh = h / (args.HQ / args.HK);
+  const int q0 = qt * BM;
+  const int kend = min(args.T, q0 + BM);      // keys any row of this tile can see
+  const int nb = (kend + BN - 1) / BN;
+
+  if (tid == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < KV_STAGES; ++s) {
+      mbar_init(&kv_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&s_full[b], 1);
+      mbar_init(&s_free[b], 8);
+      mbar_init(&p_full[b], 8);
+      mbar_init(&o_full[b], 1);
+    }
+    for (int q = 0; q < 4; ++q) mbar_init(&x_bar[q], 2);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmap_q);
+    tma_prefetch_desc(&tmap_k);
+    tma_prefetch_desc(&tmap_v);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  pdl_wait();
+  if (tid == 0) pdl_launch();
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      const uint64_t pol = policy_evict_last();
+      mbar_arrive_expect_tx(q_full, 2 * Q_HALF);
+      tma_load_3d(sq, &tmap_q, q_full, 0, q0, h, pol);
+      tma_load_3d(sq + Q_HALF, &tmap_q, q_full, 64, q0, h, pol);
+      int issued = 0;
+      for (int j = 0; j < nb && !*abort_flag; ++j, ++issued) {
+        const int s = j % KV_STAGES;
+        if (j >= KV_STAGES &&
+            !mbar_wait_bounded(&kv_empty[s], ((uint32_t)(j / KV_STAGES) & 1u) ^ 1u, abort_flag)) {
+          *abort_flag = 1;
+          break;
+        }
+        uint8_t* st = skv + s * STAGE;
+        mbar_arrive_expect_tx(&kv_full[s], STAGE);
+        tma_load_3d(st, &tmap_k, &kv_full[s], 0, j * BN, kvh, pol);
+        tma_load_3d(st + KV_HALF, &tmap_k, &kv_full[s], 64, j * BN, kvh, pol);
+        tma_load_3d(st + 2 * KV_HALF, &tmap_v, &kv_full[s], 0, j * BN, kvh, pol);
+        tma_load_3d(st + 3 * KV_HALF, &tmap_v, &kv_full[s], 64, j * BN, kvh, pol);
+      }
+      if (*abort_flag) {  // copies in flight must land before the CTA exits
+        volatile int never = 0;
+        mbar_wait_bounded(q_full, 0, &never, 200000000ull);
+        for (int j = (issued > KV_STAGES ? issued - KV_STAGES : 0); j < issued; ++j)
+          mbar_wait_bounded(&kv_full[j % KV_STAGES], (uint32_t)(j / KV_STAGES) & 1u, &never, 200000000ull);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc_s = idesc_bf16(BM, BN);
+      constexpr uint32_t idesc_o = idesc_bf16(BM, D) | (1u << 16);  // B (= V) MN-major
+      const uint32_t qa = smem_u32(sq);
+      // S_j = Q . K_j^T into S[j & 1]
+      auto issue_s = [&](int j) -> bool {
+        const int st = j % KV_STAGES;
+        if (!mbar_wait_bounded(&kv_full[st], (uint32_t)(j / KV_STAGES) & 1u, abort_flag)) return false;
+        tc_fence_after();
+        const uint32_t kb = smem_u32(skv + st * STAGE);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk)  // K = head dim: 4 steps of 32 bytes in each half
+          umma_f16(tmem + 64 * (j & 1), umma_desc_sw128(qa + (kk >> 2) * Q_HALF + (kk & 3) * 32),
+                   umma_desc_sw128(kb + (kk >> 2) * KV_HALF + (kk & 3) * 32), idesc_s, kk > 0 ? 1u : 0u);
+        umma_commit(&s_full[j & 1]);
+        return true;
+      };
+      bool ok = mbar_wait_bounded(q_full, 0, abort_flag);
+      for (int j = 0; j < 2 && j < nb && ok; ++j) ok = issue_s(j);
+      for (int j = 0; j < nb && ok; ++j) {
+        const int b = j & 1, st = j % KV_STAGES;
+        ok = mbar_wait_bounded(&p_full[b], (uint32_t)(j >> 1) & 1u, abort_flag);
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t pa = smem_u32(sp + b * P_BYTES), vb = smem_u32(skv + st * STAGE + 2 * KV_HALF);
+#pragma unroll
+        for (int kk = 0; kk < BN / 16; ++kk)  // K = keys: 16 per step (32 B of P, 2 KB of V)
+          umma_f16(tmem + 128 + 128 * b, umma_desc_sw128(pa + kk * 32), umma_desc_sw128_mn(vb + kk * 2048, KV_HALF),
+                   idesc_o, kk > 0 ? 1u : 0u);
+        umma_commit(&o_full[b]);
+        umma_commit(&kv_empty[st]);
+        if (j + 2 < nb) {  // S[b] is free once the softmax has read S_j
+          ok = mbar_wait_bounded(&s_free[b], (uint32_t)(j >> 1) & 1u, abort_flag);
+          if (ok) ok = issue_s(j + 2);
+        }
+      }
+      if (!ok) *abort_flag = 1;
+    }
+  } else {
+    // ------------------------------------------------------------------ softmax
+    const int quarter = warp & 3;
+    const int hc = (warp - 2) >> 2;     // which half: keys [32hc, 32hc+32), columns [64hc, 64hc+64)
+    const int r = quarter * 32 + lane;  // this thread's query row in the tile
+    const int qpos = q0 + r;
+    const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
+    float o[D / 2];
+#pragma unroll
+    for (int i = 0; i < D / 2; ++i) o[i] = 0.f;
+    float m = -INFINITY, l = 0.f, alpha_prev = 0.f;
+    int xph = 0;  // phases of this quarter's exchange barrier used so far
+    // The partner thread's value of the row (written to xch[buffer][half][row] by both).
+    auto exchange = [&](float mine) -> float {
+      float* slot = xch + (xph & 1) * 2 * BM;
+      slot[hc * BM + r] = mine;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&x_bar[quarter]);
+      float other = 0.f;
+      if (mbar_wait_bounded(&x_bar[quarter], (uint32_t)xph & 1u, abort_flag)) other = slot[(hc ^ 1) * BM + r];
+      else *abort_flag = 1;
+      ++xph;
+      return other;
+    };
+    // o = o * alpha + O_j for this thread's 64 columns (the fold of block j's P.V)
+    auto fold = [&](int j, float alpha) -> bool {
+      if (!(mbar_wait_bounded(&o_full[j & 1], (uint32_t)(j >> 1) & 1u, abort_flag) && !*abort_flag)) return false;
+      tc_fence_after();
+#pragma unroll
+      for (int c = 0; c < D / 2; c += 16) {
+        uint32_t t16[16];
+        tmem_ld16_async(tmem + lane_addr + 128 + 128 * (j & 1) + 64 * hc + (uint32_t)c, t16);
+        tmem_wait_ld();
+        reg_fence(t16);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) o[c + i] = o[c + i] * alpha + __uint_as_float(t16[i]);
+      }
+      tc_fence_before();
+      return true;
+    };
+    bool ok = true;
+    for (int j = 0; j < nb && ok; ++j) {
+      const int b = j & 1;
+      if (!(mbar_wait_bounded(&s_full[b], (uint32_t)(j >> 1) & 1u, abort_flag) && !*abort_flag)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      uint32_t sr[32];
+      asm volatile("tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+                   : "=r"(sr[0]), "=r"(sr[1]), "=r"(sr[2]), "=r"(sr[3]), "=r"(sr[4]), "=r"(sr[5]), "=r"(sr[6]), "=r"(sr[7]), "=r"(sr[8]), "=r"(sr[9]), "=r"(sr[10]), "=r"(sr[11]), "=r"(sr[12]), "=r"(sr[13]), "=r"(sr[14]), "=r"(sr[15]), "=r"(sr[16]), "=r"(sr[17]), "=r"(sr[18]), "=r"(sr[19]), "=r"(sr[20]), "=r"(sr[21]), "=r"(sr[22]), "=r"(sr[23]), "=r"(sr[24]), "=r"(sr[25]), "=r"(sr[26]), "=r"(sr[27]), "=r"(sr[28]), "=r"(sr[29]), "=r"(sr[30]), "=r"(sr[31])
+                   : "r"(tmem + lane_addr + 64 * b + 32 * hc));
+      tmem_wait_ld();
+      reg_fence(sr);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s_free[b]);  // the MMA warp may overwrite S[b]
+      // mask + online softmax in base 2 (score * scale * log2 e), in place
+      float bmax = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 32; ++c) {
+        const int key = j * BN + 32 * hc + c;
+        const float x = (key > qpos || key >= args.T) ? -INFINITY : __uint_as_float(sr[c]) * args.scale_log2;
+        sr[c] = __float_as_uint(x);
+        bmax = fmaxf(bmax, x);
+      }
+      bmax = fmaxf(bmax, exchange(bmax));  // the row's maximum over all 64 keys
+      if (*abort_flag) {
+        ok = false;
+        break;
+      }
+      const float nm = fmaxf(m, bmax);
+      const float base = nm == -INFINITY ? 0.f : nm;
+      const float alpha = exp2f(m - base);
+      m = nm;
+      float psum = 0.f;
+      // this half of P_j row r into P[b]: 4 chunks of 16 bytes, 128-byte swizzle.  P[b] was
+      // last read by P_{j-2} . V_{j-2}, whose completion the fold of block j-2 waited for.
+      uint8_t* prow = sp + b * P_BYTES + r * 128;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t w[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float p0 = exp2f(__uint_as_float(sr[8 * c + 2 * e]) - base);
+          const float p1 = exp2f(__uint_as_float(sr[8 * c + 2 * e + 1]) - base);
+          psum += p0 + p1;
+          w[e] = (uint32_t)f2bf(p0) | ((uint32_t)f2bf(p1) << 16);
+        }
+        const int chunk = 4 * hc + c;
+        *reinterpret_cast<uint4*>(prow + ((chunk ^ (r & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+      l = l * alpha + psum;  // this half's part of the denominator
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[b]);
+      if (j > 0) ok = fold(j - 1, alpha_prev);  // block j-1's P.V ran while this softmax did
+      alpha_prev = alpha;
+    }
+    if (ok && nb > 0) ok = fold(nb - 1, alpha_prev);
+    if (ok) {
+      l += exchange(l);  // both halves' parts of the denominator
+      ok = !*abort_flag;
+    }
+    if (!ok) {
+      *abort_flag = 1;
+    } else if (qpos < args.T) {
+      uint16_t* dst = args.out + ((size_t)qpos * args.HQ + h) * D + 64 * hc;
+#pragma unroll
+      for (int i = 0; i < D / 2; i += 8) {
+        uint32_t w[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          w[e] = (uint32_t)f2bf(__fdiv_rn(o[i + 2 * e], l)) | ((uint32_t)f2bf(__fdiv_rn(o[i + 2 * e + 1], l)) << 16);
+        *reinterpret_cast<uint4*>(dst + i) = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+    }
+  }
+
+  if (warp == 1 && lane == 0 && *abort_flag) {
+    // MMAs already issued must finish before TMEM and shared memory are released
+    volatile int never = 0;
+    mbar_wait_bounded(&o_full[0], 0, &never, 100000000ull);
+    mbar_wait_bounded(&o_full[1], 0, &never, 100000000ull);
+  }
+  if (tid == 0 && *abort_flag) atomicOr(&ffb_device_error_word, ffb::ERR_ATTN_TIMEOUT);
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, TMEM_COLS);
+  }
+}
+
+}  // namespace
+
+// Causal self-attention over all T rows (q, k, v head-major [H, T, 128] bf16, out
+// [T, HQ*128]); called by ffb_attention for positions == NULL.
+int ffb_attention_tc(const uint16_t* q, const uint16_t* k, const uint16_t* v, uint16_t* out, int T, int HQ, int HK,
+                     float scale, cudaStream_t stream) {
+  CUtensorMap tq, tk, tv;
+  int rc = ffb::make_tmap_3d_bf16(&tq, q, D, (uint64_t)T, (uint64_t)HQ, 64, BM);
+  if (!rc) rc = ffb::make_tmap_3d_bf16(&tk, k, D, (uint64_t)T, (uint64_t)HK, 64, BN);
+  if (!rc) rc = ffb::make_tmap_3d_bf16(&tv, v, D, (uint64_t)T, (uint64_t)HK, 64, BN);
+  if (rc) return rc;
+  static bool attr = false;
+  if (!attr) {
+    cudaError_t e = cudaFuncSetAttribute(attention_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
+    if (e != cudaSuccess) return ffb::fail(FFB_ECUDA, "ffb_attention: %s", cudaGetErrorString(e));
+    attr = true;
+  }
+  TcArgs a = {out, T, HQ, HK, scale * 1.4426950408889634f};
+  cudaError_t e = ffb::launch(attention_tc_kernel, dim3((T + BM - 1) / BM, HQ), dim3(THREADS), SMEM, stream, tq, tk, tv,
+                              a);
+  if (e != cudaSuccess) return ffb::fail(FFB_ECUDA, "ffb_attention: %s", cudaGetErrorString(e));
+  return FFB_OK;
+}

@@ -73,6 +73,24 @@ int make_tmap_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t col
   return FFB_OK;
 }
 
+int make_tmap_3d_bf16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t rows, uint64_t depth,
+                      uint32_t box_inner, uint32_t box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(FFB_ECUDA, "cuTensorMapEncodeTiled is unavailable from the driver");
+  if (!aligned(base, 16)) return fail(FFB_EINVAL, "TMA base address must be 16-byte aligned");
+  if ((inner * 2) % 16 != 0) return fail(FFB_EINVAL, "TMA row pitch must be a multiple of 16 bytes");
+  if (box_inner * 2 != 128) return fail(FFB_EINVAL, "TMA box inner extent must be 128 bytes for the 128-byte swizzle");
+  cuuint64_t dims[3] = {inner, rows, depth};
+  cuuint64_t strides[2] = {inner * 2, inner * 2 * rows};
+  cuuint32_t box[3] = {box_inner, box_rows, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(FFB_ECUDA, "cuTensorMapEncodeTiled (3d) failed (%d)", (int)r);
+  return FFB_OK;
+}
+
 int make_tmap_2d_bytes(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t row_bytes,
                        uint32_t box_rows, uint32_t box_cols) {
   EncodeTiledFn fn = encode_fn();

@@ -135,6 +135,14 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
       "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "l"(policy)
       : "memory");
 }
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y, int z,
+                                            uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%3, %4, %5}], [%2], %6;" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z), "l"(policy)
+      : "memory");
+}
 // Shared -> global tile store (bulk async group); rows/columns outside the tensor are
 // clipped by the hardware.  x * element size must be a multiple of 16 bytes.
 __device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void* src, int x, int y, int z) {
@@ -289,6 +297,18 @@ __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t smem_addr) {
 }
 
 // Instruction descriptors (dense, f32 accumulate, both operands K-major).
+// UMMA shared-memory descriptor for an MN-major operand staged with the 128-byte swizzle:
+// 64 MN elements (128 bytes) per line, 8 K lines per 1024-byte atom (SBO = 1024 between
+// K groups of 8), MN chunks of 64 elements `lbo_bytes` apart.
+__device__ __forceinline__ uint64_t umma_desc_sw128_mn(uint32_t smem_addr, uint32_t lbo_bytes) {
+  uint64_t d = 0;
+  d |= (uint64_t)((smem_addr & 0x3FFFFu) >> 4);
+  d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)(1024 >> 4) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;
+  return d;
+}
 __host__ __device__ constexpr uint32_t idesc_e4m3(int M, int N) {
   return (1u << 4) | (0u << 7) | (0u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
@@ -302,6 +322,10 @@ namespace ffb {
 // box_cols elements of `elem_bytes`, 128-byte swizzle, zero fill out of bounds.
 int make_tmap_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t row_bytes,
                  uint32_t box_rows, uint32_t box_cols, int elem_bytes);
+// 3-D bf16 load map [depth][rows][inner] (contiguous), box box_inner (= 64, 128 bytes) x
+// box_rows x 1, 128-byte swizzle; rows past `rows` of a depth slice are zero filled.
+int make_tmap_3d_bf16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t rows, uint64_t depth,
+                      uint32_t box_inner, uint32_t box_rows);
 // 2-D byte map without swizzle: rows x cols bytes, box box_rows x box_cols (box_cols a
 // multiple of 16), zero fill out of bounds; the tile lands row after row in shared memory.
 int make_tmap_2d_bytes(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t row_bytes,
