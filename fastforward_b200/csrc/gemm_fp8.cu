@@ -19,7 +19,8 @@
 //               launch wait (weights do not depend on the previous kernel);
 //   warp 1      TMEM allocator + single-thread MMA issuer; two accumulator buffers so the
 //               MMAs of tile i+1 overlap the epilogue of tile i (tfull[b] / tempty[b]);
-//   warps 2..9  epilogue: warp w reads TMEM lanes 32*(w%4).. (its 32 tokens) and half of
+//   warps 2..   epilogue (8 warps; 16 for SwiGLU, whose per-output math is the heaviest):
+//               warp w reads TMEM lanes 32*(w%4).. (its 32 tokens) and its share of
 //               the columns, applies per-token x per-feature scales and writes:
 //               bf16 rows / fp32 split-K partial rows / SwiGLU rows / (qkv) per-head
 //               RMSNorm + rotate-half RoPE rows, head-major.
@@ -36,8 +37,9 @@ constexpr int BM = 128;      // tokens per tile (UMMA M)
 constexpr int BK = 128;      // K bytes per stage (one 128-byte swizzle atom row)
 constexpr int UMMA_K = 32;   // K per tcgen05.mma for 8-bit operands
 constexpr int A_TILE_BYTES = BM * BK;
-constexpr int EPI_WARPS = 8;
-constexpr int THREADS = 64 + EPI_WARPS * 32;
+// Epilogue warps per instance: two or four per TMEM lane quarter.
+__host__ __device__ constexpr int epi_warps(int epi) { return epi == FFB_EPI_SWIGLU ? 16 : 8; }
+__host__ __device__ constexpr int threads_of(int epi) { return 64 + epi_warps(epi) * 32; }
 constexpr int SMEM_LIMIT = 232448;
 constexpr int EPI_QKROPE = 100;  // internal epilogue code of ffb_fp8_gemm_qk_rope
 
@@ -45,7 +47,7 @@ template <int BN>
 struct Cfg {
   static constexpr int B_TILE_BYTES = BN * BK;
   static constexpr int STAGE_BYTES = A_TILE_BYTES + B_TILE_BYTES;
-  static constexpr int STG_BYTES = EPI_WARPS * 2 * 2048;  // per warp: 2 x [32 rows x 64 B] store staging
+  static constexpr int STG_BYTES = 16 * 2048;  // 16 x [32 rows x 64 B] store staging buffers
   static constexpr int FIXED = STG_BYTES + 256 + 1024;    // staging, barriers, alignment slack
   static constexpr int FIT = (SMEM_LIMIT - FIXED) / STAGE_BYTES;
   static constexpr int STAGES = FIT > 8 ? 8 : FIT;
@@ -140,11 +142,13 @@ __device__ __forceinline__ void qk_rope_half(const uint32_t (&xk)[32], float inv
 }
 
 template <int BN, int EPI>
-__global__ void __launch_bounds__(THREADS, 1)
+__global__ void __launch_bounds__(threads_of(EPI), 1)
     fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_w,
                     const __grid_constant__ CUtensorMap tmap_o, const GemmArgs args) {
   static_assert(EPI != EPI_QKROPE || BN == 128, "one head per tile");
   static_assert(EPI != FFB_EPI_SWIGLU || BN == 256, "gate/up pairs of 128 channels per tile");
+  constexpr int EPI_WARPS = epi_warps(EPI);
+  constexpr int BUFS = 16 / EPI_WARPS;  // staging buffers per epilogue warp
   using C = Cfg<BN>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -276,7 +280,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     pdl_wait();
     if (warp == 2 && lane == 0) pdl_launch();
     const int q = warp & 3;            // TMEM lane quarter = this warp's 32 tokens
-    const int half = (warp - 2) >> 2;  // which half of the tile's columns
+    const int half = (warp - 2) >> 2;  // which share of the tile's columns (0 .. EPI_WARPS/4 - 1)
     int lt = 0;
     uint32_t sc = 0;                   // staged-store counter (selects the staging buffer)
     for (int t = blockIdx.x; t < args.n_tiles; t += gridDim.x, ++lt) {
@@ -359,8 +363,11 @@ __global__ void __launch_bounds__(THREADS, 1)
         // Staged stores: the warp writes its [32 tokens x 64 B] chunk into one of its two
         // swizzled staging buffers and lane 0 issues a TMA store (rows >= M are clipped).
         auto staged_store = [&](const uint32_t (&w16)[16], int x, int z) {
-          uint8_t* sb = stg_all + ((warp - 2) * 2 + (sc & 1)) * 2048;
-          if (lane == 0) bulk_wait_read<1>();  // the store that used this buffer has read it
+          uint8_t* sb = stg_all + ((warp - 2) * BUFS + (int)(sc % BUFS)) * 2048;
+          if (lane == 0) {  // the store that last used this buffer has read it
+            if constexpr (BUFS == 2) bulk_wait_read<1>();
+            else bulk_wait_read<0>();
+          }
           __syncwarp();
 #pragma unroll
           for (int c = 0; c < 4; ++c)
@@ -378,9 +385,10 @@ __global__ void __launch_bounds__(THREADS, 1)
           // columns [0, BN/2) are gate channels ft*BN/2 + j, [BN/2, BN) the matching up rows;
           // 8 channels at a time, the next group's TMEM loads in flight during the math
           constexpr int HALFC = BN / 2;
-          const int cb = half * (HALFC / 2);
+          constexpr int PER_WARP = HALFC / (EPI_WARPS / 4);  // gate channels per warp
+          const int cb = half * PER_WARP;
 #pragma unroll 1
-          for (int c0 = cb; c0 < cb + HALFC / 2; c0 += 32) {
+          for (int c0 = cb; c0 < cb + PER_WARP; c0 += 32) {
             uint32_t o[16];
             uint32_t g[2][8], u[2][8];
             tmem_ld8_async(acc + (uint32_t)c0, g[0]);
@@ -505,7 +513,7 @@ cudaError_t launch_instance(const CUtensorMap& ta, const CUtensorMap& tw, const 
     if (e != cudaSuccess) return e;
     attr_set = true;
   }
-  return ffb::launch(fp8_gemm_kernel<BN, EPI>, dim3(grid), dim3(THREADS), C::SMEM, stream, ta, tw, to, ga);
+  return ffb::launch(fp8_gemm_kernel<BN, EPI>, dim3(grid), dim3(threads_of(EPI)), C::SMEM, stream, ta, tw, to, ga);
 }
 
 template <int BN>
