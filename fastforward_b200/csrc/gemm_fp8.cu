@@ -19,7 +19,7 @@
 //               launch wait (weights do not depend on the previous kernel);
 //   warp 1      TMEM allocator + single-thread MMA issuer; two accumulator buffers so the
 //               MMAs of tile i+1 overlap the epilogue of tile i (tfull[b] / tempty[b]);
-//   warps 2..   epilogue (8 warps; 16 for SwiGLU, whose per-output math is the heaviest):
+//   warps 2..   epilogue (16 warps; 8 for the qkv + RoPE epilogue):
 //               warp w reads TMEM lanes 32*(w%4).. (its 32 tokens) and its share of
 //               the columns, applies per-token x per-feature scales and writes:
 //               bf16 rows / fp32 split-K partial rows / SwiGLU rows / (qkv) per-head
@@ -37,11 +37,12 @@ constexpr int BM = 128;      // tokens per tile (UMMA M)
 constexpr int BK = 128;      // K bytes per stage (one 128-byte swizzle atom row)
 constexpr int UMMA_K = 32;   // K per tcgen05.mma for 8-bit operands
 constexpr int A_TILE_BYTES = BM * BK;
-// Epilogue warps per instance: two or four per TMEM lane quarter.
-__host__ __device__ constexpr int epi_warps(int epi) { return epi == FFB_EPI_SWIGLU ? 16 : 8; }
-__host__ __device__ constexpr int threads_of(int epi) { return 64 + epi_warps(epi) * 32; }
 constexpr int SMEM_LIMIT = 232448;
 constexpr int EPI_QKROPE = 100;  // internal epilogue code of ffb_fp8_gemm_qk_rope
+// Epilogue warps per instance: four per TMEM lane quarter (two for the qkv + RoPE epilogue,
+// whose per-thread head row needs more registers than 18 warps leave).
+__host__ __device__ constexpr int epi_warps(int epi) { return epi == EPI_QKROPE ? 8 : 16; }
+__host__ __device__ constexpr int threads_of(int epi) { return 64 + epi_warps(epi) * 32; }
 
 template <int BN>
 struct Cfg {
@@ -426,8 +427,9 @@ __global__ void __launch_bounds__(threads_of(EPI), 1)
             staged_store(o, ft * HALFC + c0, 0);
           }
         } else if constexpr (EPI == FFB_EPI_F32_PARTIAL) {
+          constexpr int SHARE = BN / (EPI_WARPS / 4);  // columns per warp
 #pragma unroll 1
-          for (int c = half * (BN / 2); c < (half + 1) * (BN / 2); c += 16) {
+          for (int c = half * SHARE; c < (half + 1) * SHARE; c += 16) {
             uint32_t r[16];
             tmem_ld16_async(acc + (uint32_t)c, r);
             float w0[8], w1[8];
@@ -444,8 +446,9 @@ __global__ void __launch_bounds__(threads_of(EPI), 1)
             staged_store(o, n0 + c, ks);
           }
         } else {
+          constexpr int SHARE = BN / (EPI_WARPS / 4);  // columns per warp
 #pragma unroll 1
-          for (int c = half * (BN / 2); c < (half + 1) * (BN / 2); c += 32) {
+          for (int c = half * SHARE; c < (half + 1) * SHARE; c += 32) {
             uint32_t r0[16], r1[16];
             tmem_ld16_async(acc + (uint32_t)c, r0);
             tmem_ld16_async(acc + (uint32_t)(c + 16), r1);
