@@ -19,7 +19,7 @@
 //               launch wait (weights do not depend on the previous kernel);
 //   warp 1      TMEM allocator + single-thread MMA issuer; two accumulator buffers so the
 //               MMAs of tile i+1 overlap the epilogue of tile i (tfull[b] / tempty[b]);
-//   warps 2..   epilogue (16 warps; 8 for the qkv + RoPE epilogue):
+//   warps 2..17 epilogue:
 //               warp w reads TMEM lanes 32*(w%4).. (its 32 tokens) and its share of
 //               the columns, applies per-token x per-feature scales and writes:
 //               bf16 rows / fp32 split-K partial rows / SwiGLU rows / (qkv) per-head
@@ -39,9 +39,8 @@ constexpr int UMMA_K = 32;   // K per tcgen05.mma for 8-bit operands
 constexpr int A_TILE_BYTES = BM * BK;
 constexpr int SMEM_LIMIT = 232448;
 constexpr int EPI_QKROPE = 100;  // internal epilogue code of ffb_fp8_gemm_qk_rope
-// Epilogue warps per instance: four per TMEM lane quarter (two for the qkv + RoPE epilogue,
-// whose per-thread head row needs more registers than 18 warps leave).
-__host__ __device__ constexpr int epi_warps(int epi) { return epi == EPI_QKROPE ? 8 : 16; }
+// Epilogue warps per instance: four per TMEM lane quarter.
+__host__ __device__ constexpr int epi_warps(int) { return 16; }
 __host__ __device__ constexpr int threads_of(int epi) { return 64 + epi_warps(epi) * 32; }
 
 template <int BN>
@@ -95,20 +94,19 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
 __device__ __forceinline__ float lo_bf(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float hi_bf(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
 
-// Rotate-half RoPE of one token's normalised head, the half owned by this thread.
+// Rotate-half RoPE of one token's normalised head, the quarter owned by this thread.
 // xk holds packed bf16 pairs (elements 2i, 2i+1 in the low/high halves of a word) of head
-// elements [32*PART, 32*PART + 32) in xk[0..16) and of their rotate-half partners
-// [64 + 32*PART, 96 + 32*PART) in xk[16..32); inv = 1/rms of the whole head.  Writes
-// those 64 outputs to dst (the 128-wide head row).  Rounding as
-// _legacy/lower_kernels.py:66-86.
+// elements [16*PART, 16*PART + 16) in xk[0..8) and of their rotate-half partners
+// [64 + 16*PART, 80 + 16*PART) in xk[8..16); inv = 1/rms of the whole head.  Writes those
+// 32 outputs to dst (the 128-wide head row).  Rounding as _legacy/lower_kernels.py:66-86.
 template <int PART>
-__device__ __forceinline__ void qk_rope_half(const uint32_t (&xk)[32], float inv, const uint16_t* __restrict__ wn,
+__device__ __forceinline__ void qk_rope_part(const uint32_t (&xk)[16], float inv, const uint16_t* __restrict__ wn,
                                              const uint16_t* __restrict__ cosr, const uint16_t* __restrict__ sinr,
                                              uint16_t* __restrict__ dst) {
   // elements e and e+64 are rotate-half partners: handle 8 of each per step
 #pragma unroll
-  for (int r0 = 0; r0 < 32; r0 += 8) {
-    const int e0 = 32 * PART + r0;
+  for (int r0 = 0; r0 < 16; r0 += 8) {
+    const int e0 = 16 * PART + r0;
     const uint4 w0 = *reinterpret_cast<const uint4*>(wn + e0);
     const uint4 w1 = *reinterpret_cast<const uint4*>(wn + e0 + 64);
     const uint4 c0 = *reinterpret_cast<const uint4*>(cosr + e0);
@@ -121,7 +119,7 @@ __device__ __forceinline__ void qk_rope_half(const uint32_t (&xk)[32], float inv
     uint32_t ya[4], yb[4];
 #pragma unroll
     for (int p = 0; p < 4; ++p) {
-      const uint32_t xa = xk[(r0 >> 1) + p], xb = xk[16 + (r0 >> 1) + p];
+      const uint32_t xa = xk[(r0 >> 1) + p], xb = xk[8 + (r0 >> 1) + p];
       float out_a[2], out_b[2];
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
@@ -158,7 +156,8 @@ __global__ void __launch_bounds__(threads_of(EPI), 1)
   uint64_t* empty = full + C::STAGES;
   uint64_t* tfull = empty + C::STAGES;  // [2]
   uint64_t* tempty = tfull + 2;         // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  uint64_t* xbar = tempty + 2;          // [4]: qkv epilogue, per lane quarter, 4 arrivals
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(xbar + 4);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -173,6 +172,7 @@ __global__ void __launch_bounds__(threads_of(EPI), 1)
       mbar_init(&tfull[b], 1);
       mbar_init(&tempty[b], EPI_WARPS);
     }
+    for (int q = 0; q < 4; ++q) mbar_init(&xbar[q], 4);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -291,9 +291,20 @@ __global__ void __launch_bounds__(threads_of(EPI), 1)
       const int m = tt * BM + q * 32 + lane;  // this thread's token
       const bool row_ok = m < args.M;
       const int n0 = ft * BN;
-      // the tile's scales come from HBM: request them while its MMAs run
+      // the tile's scales (and the RoPE tables of this thread's token) come from HBM / L2:
+      // request them while the tile's MMAs run
       if (args.w_per_col && lane < BN / 32) prefetch_l1(args.w_scale + n0 + lane * 32);
       if (args.a_per_row && row_ok) prefetch_l1(args.a_scale + m);
+      if constexpr (EPI == EPI_QKROPE) {
+        const RopeSide& r = args.rope;
+        if (row_ok && ft < r.HQ + r.HK) {
+          prefetch_l1(r.cos + (size_t)m * 128 + 16 * half);  // this thread's 16 + partners
+          prefetch_l1(r.cos + (size_t)m * 128 + 64 + 16 * half);
+          prefetch_l1(r.sin + (size_t)m * 128 + 16 * half);
+          prefetch_l1(r.sin + (size_t)m * 128 + 64 + 16 * half);
+          if (lane < 2) prefetch_l1((ft < r.HQ ? r.q_norm : r.k_norm) + 64 * lane);
+        }
+      }
       // each epilogue warp waits on its own; a timeout makes every one of them stop
       if (!(mbar_wait_bounded(&tfull[buf], (uint32_t)(lt >> 1) & 1u, abort_flag) && !*abort_flag)) {
         *abort_flag = 1;
@@ -314,13 +325,15 @@ __global__ void __launch_bounds__(threads_of(EPI), 1)
       };
 
       if constexpr (EPI == EPI_QKROPE) {
-        // One head per tile (BN == 128).  Both column halves read the token's whole head
-        // (its RMSNorm needs all 128 values, summed exactly in element order); half h
-        // keeps and writes elements [32h, 32h + 32) and their partners [64 + 32h, 96 + 32h).
-        uint32_t xk[32];
-        double ss = 0.0;
+        // One head per tile (BN == 128).  Warp share p of a lane quarter owns elements
+        // [16p, 16p + 16) of each token's head and their rotate-half partners
+        // [64 + 16p, 80 + 16p); the head's sum of squares (its RMSNorm statistic) is the
+        // exact sum of the four shares' float64 partial sums, exchanged through shared memory.
+        uint32_t xk[16];
+        double ssp = 0.0;
 #pragma unroll
-        for (int c = 0; c < 128; c += 16) {
+        for (int g = 0; g < 2; ++g) {
+          const int c = 64 * g + 16 * half;
           uint32_t r[16];
           tmem_ld16_async(acc + (uint32_t)c, r);
           float w0[8], w1[8];
@@ -328,17 +341,27 @@ __global__ void __launch_bounds__(threads_of(EPI), 1)
           scales8(c + 8, w1);
           tmem_wait_ld();
           reg_fence(r);
-          const bool mine = ((c >> 5) & 1) == half;
-          const int k0 = (c >> 6) * 16 + ((c & 31) >> 1);  // slot of element c in xk
 #pragma unroll
           for (int j = 0; j < 16; j += 2) {
             const float* w = j < 8 ? w0 : w1;
             const uint32_t x2 = pack2(__uint_as_float(r[j]) * sa * w[j & 7], __uint_as_float(r[j + 1]) * sa * w[(j & 7) + 1]);
             const float a = lo_bf(x2), b = hi_bf(x2);
-            ss += (double)(a * a) + (double)(b * b);  // x*x is exact in fp32 for bf16 x
-            if (mine) xk[k0 + (j >> 1)] = x2;
+            ssp += (double)(a * a) + (double)(b * b);  // x*x is exact in fp32 for bf16 x
+            xk[8 * g + (j >> 1)] = x2;
           }
         }
+        // the store-staging area is unused by this epilogue: [2 tiles][4 shares][128 rows]
+        double* slots = reinterpret_cast<double*>(stg_all) + (lt & 1) * 4 * BM;
+        slots[half * BM + q * 32 + lane] = ssp;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&xbar[q]);
+        if (!mbar_wait_bounded(&xbar[q], (uint32_t)lt & 1u, abort_flag)) {
+          *abort_flag = 1;
+          break;
+        }
+        double ss = 0.0;
+#pragma unroll
+        for (int p = 0; p < 4; ++p) ss += slots[p * BM + q * 32 + lane];
         if (row_ok) {
           const RopeSide& r = args.rope;
           const size_t T = (size_t)args.M;
@@ -347,17 +370,20 @@ __global__ void __launch_bounds__(threads_of(EPI), 1)
             uint16_t* dst = is_q ? r.yq + ((size_t)ft * T + m) * 128 : r.yk + ((size_t)(ft - r.HQ) * T + m) * 128;
             const uint16_t* wn = is_q ? r.q_norm : r.k_norm;
             const float inv = inv_rms_from_ss(ss, 128, r.eps);
-            if (half == 0)
-              qk_rope_half<0>(xk, inv, wn, r.cos + (size_t)m * 128, r.sin + (size_t)m * 128, dst);
-            else
-              qk_rope_half<1>(xk, inv, wn, r.cos + (size_t)m * 128, r.sin + (size_t)m * 128, dst);
-          } else {  // v heads: copied through
-            uint16_t* dst = r.yv + ((size_t)(ft - r.HQ - r.HK) * T + m) * 128 + half * 32;
-#pragma unroll
-            for (int i = 0; i < 16; i += 4) {
-              *reinterpret_cast<uint4*>(dst + 2 * i) = make_uint4(xk[i], xk[i + 1], xk[i + 2], xk[i + 3]);
-              *reinterpret_cast<uint4*>(dst + 64 + 2 * i) = make_uint4(xk[16 + i], xk[17 + i], xk[18 + i], xk[19 + i]);
+            const uint16_t* cr = r.cos + (size_t)m * 128;
+            const uint16_t* sr = r.sin + (size_t)m * 128;
+            switch (half) {
+              case 0: qk_rope_part<0>(xk, inv, wn, cr, sr, dst); break;
+              case 1: qk_rope_part<1>(xk, inv, wn, cr, sr, dst); break;
+              case 2: qk_rope_part<2>(xk, inv, wn, cr, sr, dst); break;
+              default: qk_rope_part<3>(xk, inv, wn, cr, sr, dst); break;
             }
+          } else {  // v heads: copied through
+            uint16_t* dst = r.yv + ((size_t)(ft - r.HQ - r.HK) * T + m) * 128 + half * 16;
+            *reinterpret_cast<uint4*>(dst) = make_uint4(xk[0], xk[1], xk[2], xk[3]);
+            *reinterpret_cast<uint4*>(dst + 8) = make_uint4(xk[4], xk[5], xk[6], xk[7]);
+            *reinterpret_cast<uint4*>(dst + 64) = make_uint4(xk[8], xk[9], xk[10], xk[11]);
+            *reinterpret_cast<uint4*>(dst + 72) = make_uint4(xk[12], xk[13], xk[14], xk[15]);
           }
         }
       } else {
