@@ -93,3 +93,21 @@ WORKLOADS = {
     # 32B-shaped FP8, 960 visual tokens on a 30x32 grid + 64 text, 4 choices
     "32B-fp8-T1024": ("32B", Layout(0, 60, 64, 64, k=4), "rowwise"),
 }
+
+# Request streams (independent requests of varying geometry): model, FP8 mode, size.
+STREAMS = {
+    # 8B-shaped FP8: visual tokens uniform in {64, 144, 256} on square grids, text length
+    # uniform in [32, 128], choices uniform in 2..8
+    "8B-fp8-stream": ("8B", "rowwise", 256),
+}
+
+
+def stream_layouts(n, seed=1):
+    """The geometries of a synthetic request stream (seeded): list of Layout."""
+    import random
+    rng = random.Random(seed)
+    out = []
+    for _ in range(n):
+        side = rng.choice((8, 12, 16))  # merged grid side: 64 / 144 / 256 visual tokens
+        out.append(Layout(0, 2 * side, 2 * side, rng.randint(32, 128), k=rng.randint(2, 8)))
+    return out
