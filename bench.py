@@ -39,7 +39,7 @@ def metric_for(workload):
         return METRIC
     from fastforward_b200.config import WORKLOADS
     name, layout, mode = WORKLOADS[workload]
-    quant = "W4A16" if mode == "int4" else "FP8"
+    quant = {"int4": "W4A16", "static": "FP8 static-scale"}.get(mode, "FP8")
     return (f"prefill tok/s (Qwen3-VL-{name} {quant}, T={layout.bucket} prefill + {layout.k}-choice scoring); "
             "p50 latency in ms_per_step")
 
@@ -233,14 +233,16 @@ def gemm_roofline(eng, T, peaks, reps=20):
     for role, (a, sc, o) in roles.items():
         p = pl[("full", role)]
 
+        rowwise = m.mode == "rowwise"
+
         def one(i):
             lay_i = m.layers[i % m.depth]
             if role == "qkv":  # qkv GEMM (+ the fused QK-norm + RoPE epilogue in FP8 mode)
-                eng._qkv(p, b, lay_i, cos, sin, T, int4, True)
+                eng._qkv(p, b, lay_i, cos, sin, T, int4, rowwise)
             elif int4:
                 eng._w4(p, a, lay_i.lin[role], o, b.ws)
             else:
-                eng._gemm(p, a, sc, lay_i.lin[role], o, b.ws, True)
+                eng._gemm(p, a, sc if rowwise else lay_i.ascale[role], lay_i.lin[role], o, b.ws, rowwise)
         for i in range(3):
             one(i)
         ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
@@ -282,7 +284,16 @@ def run_ours(args):
 
     with torch.no_grad():
         src = make_model_bf16(dims, seed=0, device=dev, layers=args.layers)
-        pm = PackedModel(dims, src, mode=mode, device=dev, free_source=True, tp=(rank, world) if tp_mode else None)
+        profile = None
+        if mode == "static":  # calibrate the static activation bounds on one request first
+            from fastforward_b200.engine import calibrate_profile
+            r = make_request(dims, layout, seed=999, device=dev)
+            profile, _ = calibrate_profile(
+                dims, src, [dict(ids=r["ids"][:T], visual=r["visual"], deep=r["deep"], pick=r["pick"], k=r["k"],
+                                 image_start=layout.image_start, grid_h=layout.grid_h, grid_w=layout.grid_w, T=T)],
+                device=dev, tp=(rank, world) if tp_mode else None, tp_group=dist.group.WORLD if tp_mode else None)
+        pm = PackedModel(dims, src, mode=mode, device=dev, free_source=True, tp=(rank, world) if tp_mode else None,
+                         profile=profile)
         del src
         torch.cuda.empty_cache()
         eng = Engine(pm, tp_group=dist.group.WORLD if tp_mode else None)

@@ -136,17 +136,56 @@ class Accelerator:
         self.buckets = tuple(c.get("buckets", BUCKETS))
         mode = synthetic.get("mode", "rowwise")
         layers = synthetic.get("layers")
-        with torch.cuda.device(dev), torch.no_grad():
-            src = make_model_bf16(self.dims, seed=int(synthetic.get("seed", 0)), device=dev, layers=layers)
-            self.model = PackedModel(self.dims, src, mode=mode, device=dev, free_source=True)
-            del src
-            torch.cuda.empty_cache()
-            self.engine = Engine(self.model)
         lay = synthetic.get("layout", {})
         self.layout = Layout(int(lay.get("image_start", 0)), int(lay.get("grid_h", 32)), int(lay.get("grid_w", 32)),
                              int(lay.get("n_text", 64)))
+        profile = self._read_profile(c) if mode == "static" else None
+        with torch.cuda.device(dev), torch.no_grad():
+            src = make_model_bf16(self.dims, seed=int(synthetic.get("seed", 0)), device=dev, layers=layers)
+            if mode == "static" and profile is None and synthetic.get("calibrate"):
+                profile = self._calibrate(src, int(synthetic["calibrate"]), float(c.get("fp8_calibration_margin", 1.5)))
+            self.profile = profile
+            self.model = PackedModel(self.dims, src, mode=mode, device=dev, free_source=True, profile=profile)
+            del src
+            torch.cuda.empty_cache()
+            self.engine = Engine(self.model)
         self.encoder = encoder or SyntheticEncoder(self.dims, self.layout)
         self._staging = {}
+
+    # ------------------------------------------------------------------ static FP8 profile
+    @staticmethod
+    def _read_profile(c):
+        """The bundle's calibration profile for mode "static", as the reference's
+        `activate_fast` reads it (`_family/family_api.py:27-31`): `profile_path` (JSON with
+        a "profiles" map of variants) checked against `profile_sha256`, then the bounds of
+        `variant` ("{layer}:{role}" -> bound).  None when the bundle names no profile."""
+        path = c.get("profile_path")
+        if path is None:
+            return None
+        if not Path(path).is_file():
+            raise FileNotFoundError(path)
+        if sha256(path) != c.get("profile_sha256"):
+            raise ValueError("Calibration profile SHA256 mismatch")
+        profiles = json.loads(Path(path).read_text())["profiles"]
+        variant = c.get("variant")
+        if variant not in profiles:
+            raise ValueError(f"Unknown calibration variant {variant!r}")
+        return {key: float(v) for key, v in profiles[variant].items()}
+
+    def _calibrate(self, src, count, margin):
+        """Calibrates static bounds on `count` seeded synthetic requests of the bundle's
+        layout (the reference's `fp8_calibrate` rows, `_legacy/limit_runtime.py:78-97`)."""
+        from .engine import calibrate_profile
+        from .synthetic import make_request
+        lay = self.layout
+        T = next(b for b in self.buckets if b >= lay.n_tokens)
+        reqs = []
+        for i in range(count):
+            r = make_request(self.dims, lay, seed=1000 + i, device=self.device)
+            reqs.append(dict(ids=r["ids"][:T], visual=r["visual"], deep=r["deep"], pick=lay.n_tokens - 1,
+                             k=lay.k, image_start=lay.image_start, grid_h=lay.grid_h, grid_w=lay.grid_w, T=T))
+        profile, _ = calibrate_profile(self.dims, src, reqs, margin, device=self.device)
+        return profile
 
     # ------------------------------------------------------------------ path entry
     def prefill_score(self, ids, visual, deep, k, image_start=0, grid_h=32, grid_w=32, pick=None):

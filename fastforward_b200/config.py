@@ -88,6 +88,9 @@ WORKLOADS = {
     "2B-fp8-T320": ("2B", Layout(0, 32, 32, 64, k=4), "rowwise"),
     # north-star: 4B-shaped FP8 prefill of 320 tokens + choice scoring
     "4B-fp8-T320": ("4B", Layout(0, 32, 32, 64, k=4), "rowwise"),
+    # the same with the reference's shipped FP8 scheme (per-tensor weight scales, static
+    # activation scales from a calibration profile)
+    "4B-fp8static-T320": ("4B", Layout(0, 32, 32, 64, k=4), "static"),
     # 4B-shaped W4A16, 512 visual tokens on a 16x32 grid + 64 text, 8 choices
     "4B-w4a16-T576": ("4B", Layout(0, 32, 64, 64, k=8), "int4"),
     # 32B-shaped FP8, 960 visual tokens on a 30x32 grid + 64 text, 4 choices

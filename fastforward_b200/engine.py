@@ -29,6 +29,22 @@ from .mrope import position_ids, cos_sin
 BF16 = torch.bfloat16
 E4M3 = torch.float8_e4m3fn
 SMS = 148
+ROLES = ("qkv", "o", "gateup", "down")
+# Calibration-profile key of each role: "{layer}:{role}" with the reference's role names
+# (`_family/night_runtime.py:72-76`, `pack_release`).
+PROFILE_ROLE = {"qkv": "qkv", "o": "output", "gateup": "gateup", "down": "down"}
+FP8_MAX = 448.0
+# Static activation bound used when no profile is given: StaticFP8Linear's default
+# inverse scale 16 (`_legacy/limit_kernels.py:120`), i.e. bound 448 / 16.
+DEFAULT_STATIC_BOUND = FP8_MAX / 16.0
+
+
+def static_bound(maximum, margin=1.5):
+    """Calibrated static activation bound from an observed max|x|, as the reference's
+    calibration (`_legacy/limit_runtime.py:88-91`): inverse = 2^floor(log2(448 /
+    (max(maximum, 1e-12) * margin))), bound = 448 / inverse (exact: inverse is a power of two)."""
+    inverse = 2.0 ** math.floor(math.log2(FP8_MAX / (max(float(maximum), 1e-12) * margin)))
+    return FP8_MAX / inverse
 
 
 # ---------------------------------------------------------------------------- packing
@@ -58,7 +74,8 @@ class PackedLayer:
     q_norm: torch.Tensor
     k_norm: torch.Tensor
     lin: dict = field(default_factory=dict)   # role -> dict(w8, scale) | dict(packed, scales)
-    inv: dict = field(default_factory=dict)   # role -> static inverse activation scale
+    inv: dict = field(default_factory=dict)   # role -> static inverse activation scale 448/bound
+    ascale: dict = field(default_factory=dict)  # role -> fp32 [1] device tensor bound/448
 
 
 class PackedModel:
@@ -67,7 +84,13 @@ class PackedModel:
     mode "rowwise": FP8 e4m3 weights with per-output-channel scales, per-token activation
     scales (the BASELINE scheme, `_legacy/fp8_private.py`); "static": per-tensor weight
     scale + static per-tensor activation scale (`_family/depth_fp8.py`, the reference's
-    shipped scheme; inverse scales from `calibrate`); "int4": W4A16 symmetric group 128.
+    shipped scheme); "int4": W4A16 symmetric group 128.
+
+    `profile` (static mode) maps "{layer}:{role}" (roles qkv, output, gateup, down) to the
+    activation bound of that linear, as the reference's calibration profiles do: the
+    activation is quantised with inverse scale 448/bound and the GEMM multiplies by the
+    fp32 input scale bound/448 (`_family/night_runtime.py:48-54`).  Without a profile every
+    bound is 448/16 (StaticFP8Linear's default).  `calibrate_profile` measures one.
     The gate/up weight rows (and their scales) are stored interleaved per 128 channels for
     the fused SwiGLU epilogue.
 
@@ -76,8 +99,10 @@ class PackedModel:
     per-rank shape (heads and SwiGLU channels divided by the world size).
     """
 
-    def __init__(self, dims, bf16_model, mode="rowwise", device="cuda", free_source=False, tp=None):
+    def __init__(self, dims, bf16_model, mode="rowwise", device="cuda", free_source=False, tp=None, profile=None):
         assert mode in ("rowwise", "static", "int4")
+        if profile is not None and mode != "static":
+            raise ValueError("a calibration profile applies to mode 'static' only")
         from . import tp as tpmod
         self.full_dims = dims
         self.tp = tp
@@ -109,11 +134,36 @@ class PackedModel:
                 if tp:
                     lay.lin[role] = tpmod.shard_packed(role, lay.lin[role], dims, tp[0], tp[1])
                 lay.inv[role] = 1.0
+                if mode == "static":
+                    lay.ascale[role] = torch.empty(1, device=self.device, dtype=torch.float32)
                 del w
             self.layers.append(lay)
             if free_source:
                 src_layers[j] = None
+        if mode == "static":
+            self.set_profile(profile)
         torch.cuda.synchronize(self.device)
+
+    def set_profile(self, profile):
+        """Sets every static activation bound from `profile` ("{layer}:{role}" -> bound;
+        None = the default bound), as the reference's `select(variant)` does
+        (`_family/night_runtime.py:48-54`).  Graphs captured before keep the old inverse
+        scales: `Engine.set_profile` drops them."""
+        if self.mode != "static":
+            raise ValueError("a calibration profile applies to mode 'static' only")
+        for j, lay in enumerate(self.layers):
+            for role in ROLES:
+                key = f"{j}:{PROFILE_ROLE[role]}"
+                if profile is None:
+                    bound = DEFAULT_STATIC_BOUND
+                elif key in profile:
+                    bound = float(profile[key])
+                else:
+                    raise ValueError(f"calibration profile has no bound for {key}")
+                if not (math.isfinite(bound) and bound > 0):
+                    raise ValueError(f"bad static activation bound {bound} for {key}")
+                lay.inv[role] = FP8_MAX / bound
+                lay.ascale[role].fill_(bound / FP8_MAX)
 
     @property
     def depth(self):
@@ -269,6 +319,8 @@ class Engine:
             if self.world > 1 and role in ("o", "down"):
                 continue  # one fp32 partial per rank, all-reduced
             a8, sc, out = ins[role]
+            if self.m.mode == "static":
+                sc = lay.ascale[role]
             nkb = math.ceil(p.k / 128)
             bns = [x for x in (256, 128) if p.n % x == 0]
             splits = [x for x in (1, 2, 3, 4, 6, 8) if x <= min(nkb, self.MAX_SPLITS)]
@@ -322,7 +374,7 @@ class Engine:
                  ptr(cos), ptr(sin), ptr(b.yq), ptr(b.yk), ptr(b.yv), T, d.hq, d.hk, self._s)
             return
         lin = lay.lin["qkv"]
-        call("ffb_fp8_gemm_qk_rope", ptr(b.x8), ptr(b.xs), int(rowwise), ptr(lin["w8"]), ptr(lin["scale"]),
+        call("ffb_fp8_gemm_qk_rope", ptr(b.x8), ptr(b.xs if rowwise else lay.ascale["qkv"]), int(rowwise), ptr(lin["w8"]), ptr(lin["scale"]),
              int(lin["scale"].numel() > 1), ptr(lay.q_norm), ptr(lay.k_norm), float(d.eps), ptr(cos), ptr(sin),
              ptr(b.yq), ptr(b.yk), ptr(b.yv), T, d.hq, d.hk, d.hidden, self._s)
 
@@ -339,13 +391,16 @@ class Engine:
             return None, ptr(ws), plan.splits
         return ptr(bf16_out), None, 0
 
-    def enqueue(self, T, image_start, nv, grid_h, grid_w, k, visual, deep, b=None, on_layer=None):
+    def enqueue(self, T, image_start, nv, grid_h, grid_w, k, visual, deep, b=None, on_layer=None, observe=None):
         """Enqueue the whole forward for the request held in the T-row static buffers.
 
         visual: [>= nv, H] bf16 device rows scattered to [image_start, image_start + nv);
         deep: list of [nv, H] bf16 device tensors (deepstack rows added after layers 0..).
         on_layer(j, h): optional hook called with the residual stream entering layer j
         (debug tracing; it must only enqueue stream-ordered work).
+        observe (rowwise mode): fp32 [depth, 4] device tensor that keeps, per layer and role
+        (ROLES order), the largest per-token activation scale max|x|/448 entering that
+        linear (calibration).
         Results land in b.logits [8] / b.logprobs [:k]."""
         d, m = self.d, self.m
         b = b or self.buffers_for(T)
@@ -359,6 +414,16 @@ class Engine:
         qmode = L.QUANT_ROWWISE if rowwise else L.QUANT_STATIC
         scale = D ** -0.5
         lay0 = m.layers[0]
+        if observe is not None and not rowwise:
+            raise ValueError("activation observation needs the rowwise (per-token scale) forward")
+
+        def sa(lay_, role, rowbuf):  # the GEMM's activation scale: per-token or static
+            return rowbuf if rowwise else lay_.ascale[role]
+
+        def obs(j, role, scales, rows):
+            if observe is not None:
+                r = ROLES.index(role)
+                observe[j, r] = torch.maximum(observe[j, r], scales[:rows].amax())
 
         call("ffb_embed_gather", ptr(b.ids), ptr(m.embed), d.vocab, ptr(visual), image_start,
              nv if visual is not None else 0, ptr(b.hA), T, H, self._s)
@@ -368,6 +433,7 @@ class Engine:
         else:
             call("ffb_rmsnorm", ptr(b.hA), ptr(lay0.in_norm), eps, None, qmode, lay0.inv["qkv"], ptr(b.x8),
                  ptr(b.xs), T, H, self._s)
+            obs(0, "qkv", b.xs, T)
         h_cur, h_mid = b.hA, b.hB
         depth = m.depth
         for j in range(depth - 1):
@@ -385,7 +451,8 @@ class Engine:
             else:
                 call("ffb_quantize_fp8", ptr(b.attn), qmode, lay.inv["o"], ptr(b.o8), ptr(b.os), T, HQ * D,
                      self._s)
-                self._gemm(p, b.o8, b.os, lay.lin["o"], b.lin_out, b.ws, rowwise)
+                obs(j, "o", b.os, T)
+                self._gemm(p, b.o8, sa(lay, "o", b.os), lay.lin["o"], b.lin_out, b.ws, rowwise)
             self._tp_reduce(p, b.ws)
             ob, o32, os_ = self._split_args(p, b.lin_out, b.ws)
             if int4:
@@ -394,19 +461,21 @@ class Engine:
             else:
                 call("ffb_add_rmsnorm", ptr(h_cur), ob, o32, os_, None, 0, 0, ptr(lay.post_norm), eps, ptr(h_mid),
                      None, qmode, lay.inv["gateup"], ptr(b.post8), ptr(b.posts), T, H, self._s)
+                obs(j, "gateup", b.posts, T)
             # ---- MLP block
             p = pl[("full", "gateup")]
             if int4:
                 self._w4(p, b.postb, lay.lin["gateup"], b.act, b.ws)
             else:
-                self._gemm(p, b.post8, b.posts, lay.lin["gateup"], b.act, b.ws, rowwise)
+                self._gemm(p, b.post8, sa(lay, "gateup", b.posts), lay.lin["gateup"], b.act, b.ws, rowwise)
             p = pl[("full", "down")]
             if int4:
                 self._w4(p, b.act, lay.lin["down"], b.lin_out, b.ws)
             else:
                 call("ffb_quantize_fp8", ptr(b.act), qmode, lay.inv["down"], ptr(b.act8), ptr(b.acts), T, I,
                      self._s)
-                self._gemm(p, b.act8, b.acts, lay.lin["down"], b.lin_out, b.ws, rowwise)
+                obs(j, "down", b.acts, T)
+                self._gemm(p, b.act8, sa(lay, "down", b.acts), lay.lin["down"], b.lin_out, b.ws, rowwise)
             self._tp_reduce(p, b.ws)
             db, d32, ds = self._split_args(p, b.lin_out, b.ws)
             dp = deep[j] if (deep is not None and j < len(deep)) else None
@@ -417,6 +486,7 @@ class Engine:
                 call("ffb_add_rmsnorm", ptr(h_mid), db, d32, ds, ptr(dp), image_start, nv if dp is not None else 0,
                      ptr(nxt.in_norm), eps, ptr(h_cur), None, qmode, nxt.inv["qkv"], ptr(b.x8), ptr(b.xs), T, H,
                      self._s)
+                obs(j + 1, "qkv", b.xs, T)
         # ---- tail: last layer on the pick row (night_runtime.py:92-105)
         if on_layer is not None:
             on_layer(depth - 1, h_cur)
@@ -429,7 +499,8 @@ class Engine:
             self._w4(p, b.attn, lay.lin["o"], b.lin_out, b.ws)
         else:
             call("ffb_quantize_fp8", ptr(b.attn), qmode, lay.inv["o"], ptr(b.o8), ptr(b.os), 1, HQ * D, self._s)
-            self._gemm(p, b.o8, b.os, lay.lin["o"], b.lin_out, b.ws, rowwise)
+            obs(depth - 1, "o", b.os, 1)
+            self._gemm(p, b.o8, sa(lay, "o", b.os), lay.lin["o"], b.lin_out, b.ws, rowwise)
         self._tp_reduce(p, b.ws)
         ob, o32, os_ = self._split_args(p, b.lin_out, b.ws)
         call("ffb_gather_rows", ptr(h_cur), ptr(b.pick), ptr(b.hp), 1, H * 2, self._s)
@@ -439,17 +510,19 @@ class Engine:
         else:
             call("ffb_add_rmsnorm", ptr(b.hp), ob, o32, os_, None, 0, 0, ptr(lay.post_norm), eps, ptr(b.res1),
                  None, qmode, lay.inv["gateup"], ptr(b.post8), ptr(b.posts), 1, H, self._s)
+            obs(depth - 1, "gateup", b.posts, 1)
         p = pl[("tail", "gateup")]
         if int4:
             self._w4(p, b.postb, lay.lin["gateup"], b.act, b.ws)
         else:
-            self._gemm(p, b.post8, b.posts, lay.lin["gateup"], b.act, b.ws, rowwise)
+            self._gemm(p, b.post8, sa(lay, "gateup", b.posts), lay.lin["gateup"], b.act, b.ws, rowwise)
         p = pl[("tail", "down")]
         if int4:
             self._w4(p, b.act, lay.lin["down"], b.mlp1, b.ws)
         else:
             call("ffb_quantize_fp8", ptr(b.act), qmode, lay.inv["down"], ptr(b.act8), ptr(b.acts), 1, I, self._s)
-            self._gemm(p, b.act8, b.acts, lay.lin["down"], b.mlp1, b.ws, rowwise)
+            obs(depth - 1, "down", b.acts, 1)
+            self._gemm(p, b.act8, sa(lay, "down", b.acts), lay.lin["down"], b.mlp1, b.ws, rowwise)
         self._tp_reduce(p, b.ws)
         mb, m32, ms = self._split_args(p, b.mlp1, b.ws)
         call("ffb_readout", ptr(b.res1), mb, m32, ms, ptr(m.final_norm), eps, ptr(m.head), m.head.shape[0], int(k),
@@ -476,14 +549,58 @@ class Engine:
             b.pick.fill_(int(pick))
         return b
 
-    def forward(self, ids, visual, deep, pick, k, image_start, grid_h, grid_w, T=None):
+    def forward(self, ids, visual, deep, pick, k, image_start, grid_h, grid_w, T=None, observe=None):
         """Eager forward (no graph): returns (logits [k], logprobs [k]) on the device."""
         T = T or ids.shape[0]
         b = self.stage(T, ids, visual, pick)
         vis = visual.contiguous() if visual is not None else None
         nv = visual.shape[0] if visual is not None else 0
-        self.enqueue(T, image_start, nv, grid_h, grid_w, k, vis, deep, b)
+        self.enqueue(T, image_start, nv, grid_h, grid_w, k, vis, deep, b, observe=observe)
         return b.logits[:k], b.logprobs[:k]
+
+    def calibrate(self, requests, margin=1.5):
+        """Static-FP8 calibration profile, by the reference's procedure
+        (`_legacy/limit_runtime.py:78-97`): run the calibration requests, keep the largest
+        |x| entering each linear, and give each linear the bound `static_bound(max, margin)`.
+
+        The observed forward is this engine's rowwise-FP8 forward (mode "rowwise"): each
+        token's scale is max|x_row|/448 in fp32, so 448 x the largest scale, rounded to bf16,
+        is the largest |x| exactly.  (The reference observes its bf16-weight forward; the two
+        activations differ by the FP8 rounding of the weights, which moves a power-of-two
+        bound only when a maximum lies within that rounding of a bound boundary.)  With a
+        tensor-parallel model the maxima are reduced (MAX) over the group, so every rank gets
+        the same profile.
+
+        requests: iterable of dicts with `forward`'s arguments (ids, visual, deep, pick, k,
+        image_start, grid_h, grid_w, T).  Returns (profile {"{layer}:{role}": bound},
+        maxima {"{layer}:{role}": max|x|})."""
+        if self.m.mode != "rowwise":
+            raise ValueError("calibration runs the rowwise-FP8 forward of the model")
+        observe = torch.zeros((self.m.depth, len(ROLES)), device=self.device, dtype=torch.float32)
+        n = 0
+        for r in requests:
+            self.forward(observe=observe, **r)
+            n += 1
+        if n == 0:
+            raise ValueError("calibration needs at least one request")
+        if self.world > 1:
+            import torch.distributed as dist
+            dist.all_reduce(observe, op=dist.ReduceOp.MAX, group=self.group)
+        maxima = (observe.double() * FP8_MAX).to(BF16).float().cpu()
+        profile, seen = {}, {}
+        for j in range(self.m.depth):
+            for r, role in enumerate(ROLES):
+                key = f"{j}:{PROFILE_ROLE[role]}"
+                seen[key] = float(maxima[j, r])
+                profile[key] = static_bound(seen[key], margin)
+        return profile, seen
+
+    def set_profile(self, profile):
+        """New static activation bounds (`PackedModel.set_profile`); drops captured graphs,
+        whose kernels hold the old inverse scales."""
+        torch.cuda.synchronize(self.device)
+        self.m.set_profile(profile)
+        self.graphs.clear()
 
     def trace(self, ids, visual, deep, pick, k, image_start, grid_h, grid_w, T=None):
         """Eager forward that also returns the residual stream entering every layer
@@ -541,3 +658,16 @@ class Engine:
         entry["graph"].replay()
         k = entry["k"]
         return b.logits[:k], b.logprobs[:k]
+
+
+def calibrate_profile(dims, bf16_model, requests, margin=1.5, device="cuda", tp=None, tp_group=None):
+    """Calibration profile of a bf16 source model for mode "static": packs it rowwise
+    (per-channel FP8), runs `Engine.calibrate` over `requests` and frees the packed copy.
+    Returns (profile, maxima) as `Engine.calibrate`."""
+    pm = PackedModel(dims, bf16_model, "rowwise", device, tp=tp)
+    eng = Engine(pm, autotune=False, tp_group=tp_group)
+    try:
+        return eng.calibrate(requests, margin)
+    finally:
+        del eng, pm
+        torch.cuda.empty_cache()

@@ -33,6 +33,7 @@ __all__ = [
     "log_softmax", "int4_sym_quantize", "int4_sym_dequantize", "int4_sym_pack",
     "int4_asym_quantize", "mrope_position_ids", "mrope_cos_sin", "embed_rows",
     "prefill_score", "decoder_layer", "tail", "response_argmax", "quantized_model", "set_accumulation",
+    "static_bound", "calibration_profile",
 ]
 
 
@@ -304,16 +305,18 @@ def _fp8_dot(q, w8):
     return _fp8_acc(q, w8).double()
 
 
-def fp8_linear_static(x, w8, w_scale, inverse_scale, splits=1):
+def fp8_linear_static(x, w8, w_scale, inverse_scale, splits=1, a_scale=None):
     """`RuntimeScaleLinear.__call__`, `_family/depth_fp8.py:22-26` (+ `torch._scaled_mm`).
 
-    y = bf16( (q . W8^T) * (1/INV) * w_scale ), q = quantize_static(x), sliced to M rows.
-    The activation scale is the fp32 value 1/INV held in `input_scale`
-    (`_legacy/limit_kernels.py:129`).
+    y = bf16( (q . W8^T) * a_scale * w_scale ), q = quantize_static(x), sliced to M rows.
+    The activation scale is the fp32 `input_scale`: 1/INV by default
+    (`_legacy/limit_kernels.py:129`), bound/448 when a calibration profile set it
+    (`_family/night_runtime.py:54`, passed here as `a_scale`).
     """
     m = x.reshape(-1, x.shape[-1]).shape[0]
     q = quantize_static(x, inverse_scale)
-    a_scale = (torch.tensor([1.0], dtype=torch.float64) / inverse_scale).float()
+    if a_scale is None:
+        a_scale = (torch.tensor([1.0], dtype=torch.float64) / inverse_scale).float()
     return _fp8_linear(q, a_scale, w8, w_scale, splits)[:m].to(BF16)
 
 
@@ -497,7 +500,9 @@ def _tp_linear(x, lin, mode, world):
             part = _fp8_linear(q, sa, lin["w8"][:, r * w:(r + 1) * w].contiguous(), lin["w_scale"], 1)[:m]
         elif mode == "static":
             q = quantize_static(xs, lin["inv"])
-            sa = (torch.tensor([1.0], dtype=torch.float64) / lin["inv"]).float()
+            sa = lin.get("a_scale")
+            if sa is None:
+                sa = (torch.tensor([1.0], dtype=torch.float64) / lin["inv"]).float()
             part = _fp8_linear(q, sa, lin["w8"][:, r * w:(r + 1) * w].contiguous(), lin["w_scale"], 1)[:m]
         elif mode == "int4":
             deq = int4_sym_dequantize(lin["q"][:, r * w:(r + 1) * w], lin["s"][:, r * w // 128:(r + 1) * w // 128])
@@ -508,14 +513,21 @@ def _tp_linear(x, lin, mode, world):
     return total.to(BF16)
 
 
+# Calibration observer: None, or a dict that `_linear` updates with the largest |x|
+# entering each linear, keyed by the linear's profile key ("{layer}:{role}").
+_OBSERVED = None
+
+
 def _linear(x, lin, mode, tail=False):
+    if _OBSERVED is not None and "key" in lin:  # CalibrationLinear, `_legacy/limit_runtime.py:15-19`
+        _OBSERVED[lin["key"]] = max(_OBSERVED.get(lin["key"], 0.0), float(x.float().abs().amax()))
     if lin.get("tp_world", 1) > 1:
         return _tp_linear(x, lin, mode, lin["tp_world"])
     splits = lin.get("splits_tail" if tail else "splits", 1)
     if mode == "rowwise":
         return fp8_linear_rowwise(x, lin["w8"], lin["w_scale"], splits)
     if mode == "static":
-        return fp8_linear_static(x, lin["w8"], lin["w_scale"], lin["inv"], splits)
+        return fp8_linear_static(x, lin["w8"], lin["w_scale"], lin["inv"], splits, lin.get("a_scale"))
     if mode == "bf16":
         return (x.float() @ lin["w"].float().t()).to(BF16)
     if mode == "int4":  # W4A16: x . bf16(q * s) (`_family/night_runtime.py:31-33` semantics)
@@ -615,24 +627,64 @@ def prefill_score(model, ids, visual, deepstack, position_ids, pick, k, mode="ro
     return tail(all_layers[depth - 1], h, cos, sin, dims, mode, pick, model["final_norm"], model["head"], k)
 
 
-def quantized_model(dims, src, mode="rowwise", inv=None, splits=None, tp=1):
+# Profile key role names of the reference (`_family/night_runtime.py:72-76`).
+PROFILE_ROLE = {"qkv": "qkv", "o": "output", "gateup": "gateup", "down": "down"}
+
+
+def static_bound(maximum, margin=1.5):
+    """The reference's calibration rule (`_legacy/limit_runtime.py:90-91`):
+    inverse = 2^floor(log2(448 / (max(maximum, 1e-12) * margin))); returned as the
+    profile bound 448 / inverse."""
+    inverse = 2.0 ** math.floor(math.log2(FP8_MAX / (max(float(maximum), 1e-12) * margin)))
+    return FP8_MAX / inverse
+
+
+def calibration_profile(model, requests, mode="bf16", margin=1.5):
+    """Calibration as `_legacy/limit_runtime.py:78-97`: run `prefill_score` over the
+    requests with every linear observing the largest |x| it receives
+    (`CalibrationLinear`, `limit_runtime.py:15-19`), then bound = `static_bound`.
+    `model` from `quantized_model(..., mode)`; the reference observes its bf16 forward
+    (mode "bf16").  requests: dicts of `prefill_score`'s arguments.
+    Returns (profile {"{layer}:{role}": bound}, maxima {"{layer}:{role}": max|x|})."""
+    global _OBSERVED
+    seen = {}
+    _OBSERVED = seen
+    try:
+        for r in requests:
+            prefill_score(model, mode=mode, **r)
+    finally:
+        _OBSERVED = None
+    return {key: static_bound(v, margin) for key, v in seen.items()}, seen
+
+
+def quantized_model(dims, src, mode="rowwise", inv=None, splits=None, tp=1, profile=None):
     """The oracle's view of a bf16 source model (`fastforward_b200.synthetic` layout, gate
     rows then up rows): weights quantised here, on the CPU, with the reference's formulas.
-    For mode "static", `inv[j][role]` are the calibrated inverse activation scales;
-    `splits` maps (tag, role) -> K-split count of the GPU plan ("full"/"tail");
-    `tp` > 1 computes o_proj and down_proj as `tp` tensor-parallel partial sums
-    (`_tp_linear`); every other op is the same on every rank."""
+    For mode "static", either `profile` {"{layer}:{role}": bound} (roles qkv, output,
+    gateup, down) sets inverse scale 448/bound and input scale fp32(bound/448)
+    (`_family/night_runtime.py:48-54`), or `inv[j][role]` gives inverse scales directly
+    (input scale 1/inv, `_legacy/limit_kernels.py:129`); neither = inverse scale 16
+    (`limit_kernels.py:120`).  `splits` maps (tag, role) -> K-split count of the GPU plan
+    ("full"/"tail"); `tp` > 1 computes o_proj and down_proj as `tp` tensor-parallel
+    partial sums (`_tp_linear`); every other op is the same on every rank.  Every linear
+    carries its profile key ("key") for `calibration_profile`."""
     layers = []
     for j, lay in enumerate(src["layers"]):
         d = {n: lay[n].cpu() for n in ("in_norm", "post_norm", "q_norm", "k_norm")}
         for role in ("qkv", "o", "gateup", "down"):
             w = lay[role].cpu()
+            key = f"{j}:{PROFILE_ROLE[role]}"
             if mode == "rowwise":
                 w8, sc = quantize_weight_channel(w)
                 d[role] = dict(w8=w8, w_scale=sc)
             elif mode == "static":
                 w8, sc = quantize_weight_tensor(w)
-                d[role] = dict(w8=w8, w_scale=sc, inv=inv[j][role])
+                if profile is not None:
+                    bound = float(profile[key])
+                    d[role] = dict(w8=w8, w_scale=sc, inv=FP8_MAX / bound,
+                                   a_scale=torch.tensor([bound / FP8_MAX], dtype=torch.float32))
+                else:
+                    d[role] = dict(w8=w8, w_scale=sc, inv=inv[j][role] if inv is not None else 16.0)
             elif mode == "int4":
                 q, sc = int4_sym_quantize(w)
                 d[role] = dict(q=q, s=sc)
@@ -643,6 +695,7 @@ def quantized_model(dims, src, mode="rowwise", inv=None, splits=None, tp=1):
                 d[role]["splits_tail"] = splits.get(("tail", role), 1)
             if tp > 1 and role in ("o", "down"):
                 d[role]["tp_world"] = tp
+            d[role]["key"] = key
         layers.append(d)
     dims_d = dict(hq=dims.hq, hk=dims.hk, d=dims.d, eps=dims.eps, theta=dims.theta, inter=dims.inter)
     return dict(dims=dims_d, embed=src["embed"].cpu(), head=src["head"].cpu(), final_norm=src["final_norm"].cpu(),

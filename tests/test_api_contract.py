@@ -60,3 +60,20 @@ def test_accelerator_has_no_cpu_fallback(tmp_path):
         pytest.skip("a GPU is present")
     with pytest.raises(RuntimeError, match="CPU fallback is disabled"):
         Accelerator(_bundle(tmp_path))
+
+
+def test_static_profile_bundle_fields(tmp_path):
+    """Static-FP8 bundles name their calibration profile as the reference's bundles do
+    (`_family/family_api.py:27-31`): path, sha256 and variant."""
+    from fastforward_b200.api import sha256
+    prof = tmp_path / "profile.json"
+    prof.write_text(json.dumps({"profiles": {"v1": {"0:qkv": 3.5, "0:output": 1.75}}}))
+    c = dict(profile_path=str(prof), profile_sha256=sha256(prof), variant="v1")
+    assert Accelerator._read_profile(c) == {"0:qkv": 3.5, "0:output": 1.75}
+    assert Accelerator._read_profile({}) is None
+    with pytest.raises(ValueError):
+        Accelerator._read_profile(dict(c, profile_sha256="0" * 64))
+    with pytest.raises(ValueError):
+        Accelerator._read_profile(dict(c, variant="v2"))
+    with pytest.raises(FileNotFoundError):
+        Accelerator._read_profile(dict(c, profile_path=str(tmp_path / "missing.json")))

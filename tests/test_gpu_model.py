@@ -5,6 +5,8 @@ within 2e-2 max-abs.  Plus the reference runtime's own gates: graph replay equal
 eager path, and bucket-padding rows cannot change the result (`sub10_runtime.py:166-167`:
 pad tokens overwritten with another id must give a bit-identical output).
 """
+import math
+
 import pytest
 import torch
 
@@ -89,16 +91,32 @@ def test_prefill_free_running_matches_oracle(name, n_layers):
     print(f"\n{name} {n_layers} layers free-running |dz| = {err:.3g} (oracle noise floor {floor:.3g})")
 
 
-@pytest.mark.parametrize("name", ["2B", "4B"])
-def test_layer_ops_teacher_forced(name):
+def _profile(dims, src, req, layout):
+    """A calibration profile for a small case: the oracle's bf16 calibration (the
+    reference's procedure) on the case's own request."""
+    from fastforward_b200.mrope import position_ids
+    T = layout.bucket
+    pos = position_ids(T, layout.image_start, layout.grid_h, layout.grid_w)
+    om = oracle.quantized_model(dims, src, "bf16")
+    prof, _ = oracle.calibration_profile(om, [dict(ids=req["ids"][:T], visual=req["visual"], deepstack=req["deep"],
+                                                   position_ids=pos, pick=req["pick"], k=req["k"],
+                                                   image_start=layout.image_start)])
+    return prof
+
+
+@pytest.mark.parametrize("name,mode", [("2B", "rowwise"), ("4B", "rowwise"), ("2B", "static"), ("4B", "static")])
+def test_layer_ops_teacher_forced(name, mode):
     """Every op of a full decoder layer at the model's real shapes (T=320), each checked
     against the oracle fed with the engine's own inputs to that op: quantised bytes and
-    norms bit-exact, GEMM outputs within one bf16 rounding of the exact FP8 products."""
+    norms bit-exact, GEMM outputs within one bf16 rounding of the exact FP8 products.
+    Mode "static" runs the reference's shipped scheme (per-tensor weights, static
+    activation scales from a calibration profile)."""
     from fastforward_b200.engine import GemmPlan
     from fastforward_b200 import _lib as L
     from tests._util import assert_bf16_near, assert_bytes_equal
     dims, src, req, layout = small_case(MODELS[name], 2, vocab=4096)
-    eng = Engine(PackedModel(dims, src, device=DEV), autotune=False)
+    prof = _profile(dims, src, req, layout) if mode == "static" else None
+    eng = Engine(PackedModel(dims, src, mode=mode, device=DEV, profile=prof), autotune=False)
     T = layout.bucket
     eng.buffers_for(T)
     for key, p in eng.plans[T].items():          # keep every GEMM output in its bf16 buffer
@@ -121,17 +139,23 @@ def test_layer_ops_teacher_forced(name):
                 on_layer=grab)
     torch.cuda.synchronize()
     S = {k: v.cpu() for k, v in snap.items()}
-    om = oracle.quantized_model(dims, src, "rowwise")
+    om = oracle.quantized_model(dims, src, mode, profile=prof)
     lay, eps, H, HQ, HK, I = om["layers"][0], dims.eps, dims.hidden, dims.hq, dims.hk, dims.inter
     pos = oracle.mrope_position_ids(T, 0, 32, 32)
     cos, sin = oracle.mrope_cos_sin(pos, dims.d, dims.theta)
 
     def lin(a8, sa, w):  # the oracle's FP8 linear on the engine's own quantised input
-        return oracle.qwen_path._fp8_linear(a8, sa, w["w8"], w["w_scale"], 1)
+        return oracle.qwen_path._fp8_linear(a8, sa if mode == "rowwise" else w["a_scale"], w["w8"], w["w_scale"], 1)
 
-    q, s = oracle.quantize_rows(oracle.rms_one(S["h0"], lay["in_norm"], eps))
+    def quant(x, role, name):  # the oracle's activation quant; returns (bytes, per-token scales)
+        if mode == "rowwise":
+            q, s = oracle.quantize_rows(x)
+            assert torch.equal(S[name], s[:T]), name
+            return q
+        return oracle.quantize_static(x, lay[role]["inv"])
+
+    q = quant(oracle.rms_one(S["h0"], lay["in_norm"], eps), "qkv", "xs")
     assert_bytes_equal(S["x8"], q[:T], "x8")
-    assert torch.equal(S["xs"], s[:T])
     qkv = lin(S["x8"], S["xs"], lay["qkv"]).to(torch.bfloat16)  # fused qkv GEMM + norm + RoPE
     rq, rk = oracle.qk_pair(qkv[:, :HQ * 128].reshape(T, HQ, 128), qkv[:, HQ * 128:(HQ + HK) * 128].reshape(T, HK, 128),
                             lay["q_norm"], lay["k_norm"], cos, sin)
@@ -140,17 +164,17 @@ def test_layer_ops_teacher_forced(name):
     assert_bytes_equal(S["yv"], qkv[:, (HQ + HK) * 128:].reshape(T, HK, 128).transpose(0, 1), "yv")
     att = oracle.attention_direct(S["yq"], S["yk"], S["yv"], 128 ** -0.5).reshape(T, HQ * 128)
     torch.testing.assert_close(S["attn"].float(), att.float(), atol=2e-2, rtol=2e-2)
-    q, s = oracle.quantize_rows(S["attn"])
+    q = quant(S["attn"], "o", "os")
     assert_bytes_equal(S["o8"], q[:T], "o8")
     o = lin(S["o8"], S["os"], lay["o"]).to(torch.bfloat16)
     h_mid = (S["h0"].float() + o.float()).to(torch.bfloat16)
     assert_bytes_equal(S["hB"], h_mid, "residual after attention")
-    q, s = oracle.quantize_rows(oracle.rms_one(S["hB"], lay["post_norm"], eps))
+    q = quant(oracle.rms_one(S["hB"], lay["post_norm"], eps), "gateup", "posts")
     assert_bytes_equal(S["post8"], q[:T], "post8")
     gu = lin(S["post8"], S["posts"], lay["gateup"]).to(torch.bfloat16)
     act = oracle.swiglu(gu[:, :I], gu[:, I:])
     assert_bytes_equal(S["act"], act, "swiglu")
-    q, s = oracle.quantize_rows(S["act"])
+    q = quant(S["act"], "down", "acts")
     assert_bytes_equal(S["act8"], q[:T], "act8")
     dn = lin(S["act8"], S["acts"], lay["down"]).to(torch.bfloat16)
     h1 = (S["hB"].float() + dn.float()).to(torch.bfloat16).float()
@@ -158,20 +182,21 @@ def test_layer_ops_teacher_forced(name):
     assert_bytes_equal(S["hA"], h1.to(torch.bfloat16), "residual after mlp + deepstack")
 
 
-def _teacher_forced(name, n_layers, vocab=4096, layout=None):
+def _teacher_forced(name, n_layers, vocab=4096, layout=None, mode="rowwise"):
     """Run the engine once, capturing the residual stream entering each layer; feed each
     captured input to the oracle's layer and compare with the engine's next input.  The
     errors of one layer then cannot compound through the rest (an FP8 model amplifies any
     last-bit difference: the oracle run with fp32 instead of fp64 accumulation moves its own
     logits by 0.03-0.1 at 2-6 layers on these random weights)."""
     dims, src, req, layout = small_case(MODELS[name], n_layers, vocab=vocab, layout=layout)
-    pm = PackedModel(dims, src, device=DEV)
+    prof = _profile(dims, src, req, layout) if mode == "static" else None
+    pm = PackedModel(dims, src, mode=mode, device=DEV, profile=prof)
     eng = Engine(pm)
     T = layout.bucket
     hs, z, _ = eng.trace(req["ids"][:T].to(DEV), req["visual"].to(DEV), [x.to(DEV) for x in req["deep"]],
                          req["pick"], req["k"], layout.image_start, layout.grid_h, layout.grid_w, T=T)
     hs = [h.cpu() for h in hs]
-    om = oracle.quantized_model(dims, src, "rowwise", splits=_splits(eng, T))
+    om = oracle.quantized_model(dims, src, mode, splits=_splits(eng, T), profile=prof)
     from fastforward_b200.mrope import position_ids
     pos = position_ids(T, layout.image_start, layout.grid_h, layout.grid_w)
     cos, sin = oracle.mrope_cos_sin(pos, dims.d, dims.theta)
@@ -179,7 +204,7 @@ def _teacher_forced(name, n_layers, vocab=4096, layout=None):
     stats = []
     for j in range(len(hs) - 1):
         deep = req["deep"][j] if j < len(req["deep"]) else None
-        args = (om["layers"][j], hs[j], cos, sin, om["dims"], "rowwise", deep, layout.image_start, nv)
+        args = (om["layers"][j], hs[j], cos, sin, om["dims"], mode, deep, layout.image_start, nv)
         want = oracle.decoder_layer(*args).float()
         alt = _with_attention_block(32, oracle.decoder_layer, *args).float()  # attention noise floor
         got = hs[j + 1].float()
@@ -187,17 +212,17 @@ def _teacher_forced(name, n_layers, vocab=4096, layout=None):
         err, flo = (got - want).abs(), (alt - want).abs()
         stats.append((j, err.max().item() / scale_max, err.mean().item() / scale_mean,
                       flo.max().item() / scale_max, flo.mean().item() / scale_mean))
-    zr, _ = oracle.tail(om["layers"][-1], hs[-1], cos, sin, om["dims"], "rowwise", req["pick"], om["final_norm"],
+    zr, _ = oracle.tail(om["layers"][-1], hs[-1], cos, sin, om["dims"], mode, req["pick"], om["final_norm"],
                         om["head"], req["k"])
     return stats, z.cpu(), zr
 
 
-@pytest.mark.parametrize("name,n_layers", [("2B", 4), ("4B", 3)])
-def test_layers_teacher_forced(name, n_layers):
+@pytest.mark.parametrize("name,n_layers,mode", [("2B", 4, "rowwise"), ("4B", 3, "rowwise"), ("4B", 3, "static")])
+def test_layers_teacher_forced(name, n_layers, mode):
     """Whole layers on the engine's own inputs: only attention's rounding differs, so each
     layer's deviation stays within 2% of the output's max (0.1% on average) or within the
     oracle's own change under a different softmax blocking, whichever is larger."""
-    stats, z, zr = _teacher_forced(name, n_layers)
+    stats, z, zr = _teacher_forced(name, n_layers, mode=mode)
     print(f"\n{name} per-layer (max rel, mean rel, floor max, floor mean):", stats, "tail",
           (z - zr).abs().max().item())
     for j, max_rel, mean_rel, fmax, fmean in stats:
@@ -236,3 +261,65 @@ def test_full_depth_2b_teacher_forced():
     for j, max_rel, mean_rel, fmax, fmean in stats:
         assert max_rel <= max(0.02, fmax) and mean_rel <= max(1e-3, fmean), stats[j]
     _check_logits(z, zr)
+
+
+def test_calibration_matches_oracle():
+    """`Engine.calibrate` (the rowwise forward observing every linear's input) against the
+    oracle's calibration of the same forward: the maxima agree within attention's rounding
+    noise (5%) and the power-of-two bounds are equal; against the reference's procedure (the
+    bf16 forward) the bounds are equal wherever the maximum is not within the FP8 weight
+    rounding (5%) of a bound boundary."""
+    from fastforward_b200.engine import calibrate_profile
+    from fastforward_b200.mrope import position_ids
+    from fastforward_b200.synthetic import make_request
+    dims, src, req, layout = small_case(MODELS["2B"], 3, vocab=4096)
+    reqs = [req, make_request(dims, layout, seed=7)]
+    T = layout.bucket
+    pos = position_ids(T, layout.image_start, layout.grid_h, layout.grid_w)
+    dev_reqs = [dict(ids=r["ids"][:T].to(DEV), visual=r["visual"].to(DEV), deep=[x.to(DEV) for x in r["deep"]],
+                     pick=r["pick"], k=r["k"], image_start=layout.image_start, grid_h=layout.grid_h,
+                     grid_w=layout.grid_w, T=T) for r in reqs]
+    prof, seen = calibrate_profile(dims, src, dev_reqs, device=DEV)
+    cpu_reqs = [dict(ids=r["ids"][:T], visual=r["visual"], deepstack=r["deep"], position_ids=pos, pick=r["pick"],
+                     k=r["k"], image_start=layout.image_start) for r in reqs]
+    assert set(prof) == {f"{j}:{r}" for j in range(3) for r in ("qkv", "output", "gateup", "down")}
+    p_row, s_row = oracle.calibration_profile(oracle.quantized_model(dims, src, "rowwise"), cpu_reqs, mode="rowwise")
+    p_bf, s_bf = oracle.calibration_profile(oracle.quantized_model(dims, src, "bf16"), cpu_reqs, mode="bf16")
+    print("\nkey: engine max / oracle rowwise max / oracle bf16 max -> engine bound, bf16 bound")
+    for key in sorted(prof):
+        print(f"  {key}: {seen[key]:.5g} / {s_row[key]:.5g} / {s_bf[key]:.5g} -> {prof[key]:g}, {p_bf[key]:g}")
+        # full-T inputs agree to the bit here; the tail's single pick row carries the whole
+        # prefix's attention-rounding noise (a few bf16 ulps)
+        assert abs(seen[key] - s_row[key]) <= 0.05 * s_row[key], key
+        x = 448.0 / (s_bf[key] * 1.5)  # distance of the bf16 maximum from a boundary
+        near = abs(x / 2.0 ** round(math.log2(x)) - 1.0) < 0.05
+        if not near:
+            assert prof[key] == p_bf[key], key
+            assert prof[key] == p_row[key], key
+
+
+def test_accelerator_static_calibrated_bundle(tmp_path):
+    """A static-FP8 bundle calibrated at construction (`calibrate`: request count), then a
+    `predict` through the public surface; the calibrated profile written to a file and
+    named by path + sha256 + variant gives a bit-identical answer."""
+    import json
+    from fastforward_b200.api import Accelerator, sha256
+    img = tmp_path / "img.png"
+    img.write_bytes(b"\x89PNG synthetic")
+    syn = dict(model="2B", layers=2, seed=0, mode="static", calibrate=2, layout=dict(grid_h=16, grid_w=16, n_text=32))
+    c = dict(schema_version=1, task="visual_choice", architecture="qwen3_vl_family", synthetic=syn)
+    p = tmp_path / "bundle.json"
+    p.write_text(json.dumps(c))
+    acc = Accelerator(p)
+    assert set(acc.profile) == {f"{j}:{r}" for j in range(2) for r in ("qkv", "output", "gateup", "down")}
+    r1 = acc.predict(img, "What is shown?", ["cat", "dog", "bird", "fish"])
+    assert all(math.isfinite(x) for x in r1["logits"])
+    prof = tmp_path / "profile.json"
+    prof.write_text(json.dumps({"profiles": {"v": acc.profile}}))
+    del acc
+    syn2 = dict(syn)
+    del syn2["calibrate"]
+    p.write_text(json.dumps(dict(c, synthetic=syn2, profile_path=str(prof), profile_sha256=sha256(prof),
+                                 variant="v")))
+    r2 = Accelerator(p).predict(img, "What is shown?", ["cat", "dog", "bird", "fish"])
+    assert r2["logits"] == r1["logits"]
