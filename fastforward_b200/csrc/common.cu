@@ -1,12 +1,28 @@
 // Library-wide host plumbing: thread-local error messages, the per-device error word,
 // and TMA descriptor encoding through the driver entry point (no link against libcuda).
 #include "common.cuh"
+#include "pdl.cuh"
 
 #include <stdarg.h>
 #include <string.h>
+#include <atomic>
 #include <mutex>
 
 __device__ uint32_t ffb_device_error_word = 0;
+__device__ uint16_t ffb_silu_table[65536];
+
+namespace {
+
+__global__ void silu_table_kernel() {
+  pdl_wait();  // keeps the programmatic-launch chain transitive for the kernels after it
+  pdl_launch();
+  const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+  ffb_silu_table[i] = f2bf(silu_bf16(bf2f((uint16_t)i)));
+}
+
+std::atomic<int> g_silu_filled[64];
+
+}  // namespace
 
 namespace ffb {
 
@@ -128,6 +144,19 @@ int make_tmap_out(CUtensorMap* map, const void* base, int elem_bytes, uint64_t i
   CUresult r = fn(map, dt, 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                   CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(FFB_ECUDA, "cuTensorMapEncodeTiled (store) failed (%d)", (int)r);
+  return FFB_OK;
+}
+
+int ensure_silu_table(cudaStream_t stream) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail(FFB_ECUDA, "silu table: %s", cudaGetErrorString(e));
+  if (dev >= 0 && dev < 64 && g_silu_filled[dev].load(std::memory_order_acquire)) return FFB_OK;
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  e = cudaStreamIsCapturing(stream, &cap);
+  if (e == cudaSuccess) e = launch(silu_table_kernel, dim3(65536 / 256), dim3(256), 0, stream);
+  if (e != cudaSuccess) return fail(FFB_ECUDA, "silu table: %s", cudaGetErrorString(e));
+  if (cap == cudaStreamCaptureStatusNone && dev >= 0 && dev < 64) g_silu_filled[dev].store(1, std::memory_order_release);
   return FFB_OK;
 }
 

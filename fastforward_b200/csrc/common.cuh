@@ -33,6 +33,11 @@ enum : uint32_t {
   ERR_ATTN_TIMEOUT = 1u << 2,
 };
 
+// Fills ffb_silu_table on this device once (stream-ordered, before the caller's next
+// launch); inside a stream capture the fill is captured as well and the table is marked
+// filled only by an uncaptured call.
+int ensure_silu_table(cudaStream_t stream);
+
 }  // namespace ffb
 
 // One error word per device that loads the library.
@@ -44,6 +49,17 @@ __device__ __forceinline__ uint16_t f2bf(float f) {  // round to nearest even
   return __bfloat16_as_ushort(__float2bfloat16_rn(f));
 }
 __device__ __forceinline__ float round_bf(float f) { return bf2f(f2bf(f)); }
+
+// SiLU of a bf16 value as the reference rounds it, bf16(g / (1 + exp(-g))) with an IEEE
+// divide (_legacy/search_kernels.py:14).
+__device__ __forceinline__ float silu_bf16(float g) { return round_bf(__fdiv_rn(g, 1.f + expf(-g))); }
+
+// silu_bf16 of every bf16 value, indexed by its bits (filled by ffb::ensure_silu_table):
+// the SwiGLU epilogues look the activation up instead of evaluating exp and a division.
+extern __device__ uint16_t ffb_silu_table[65536];
+__device__ __forceinline__ float silu_lookup(float g_bf16) {
+  return bf2f(__ldg(&ffb_silu_table[__float_as_uint(g_bf16) >> 16]));
+}
 // fp32 -> e4m3 with round-to-nearest-even; the callers clamp to +-448 first, so the
 // saturating conversion never sees an out-of-range value.
 __device__ __forceinline__ uint8_t f2e4m3(float f) {

@@ -97,25 +97,24 @@ __device__ __forceinline__ float hi_bf(uint32_t w) { return __uint_as_float(w & 
 // Rotate-half RoPE of one token's normalised head, the quarter owned by this thread.
 // xk holds packed bf16 pairs (elements 2i, 2i+1 in the low/high halves of a word) of head
 // elements [16*PART, 16*PART + 16) in xk[0..8) and of their rotate-half partners
-// [64 + 16*PART, 80 + 16*PART) in xk[8..16); inv = 1/rms of the whole head.  Writes those
-// 32 outputs to dst (the 128-wide head row).  Rounding as _legacy/lower_kernels.py:66-86.
+// [64 + 16*PART, 80 + 16*PART) in xk[8..16); inv = 1/rms of the whole head; cs holds this
+// token's cos (cs[0..2)) and sin (cs[2..4)) at elements [16*PART, 16*PART + 16).  The
+// tables' two halves are equal (rotate-half tables are cat(freqs, freqs)), so those values
+// also serve the partners.  Writes the 32 outputs to dst (the 128-wide head row).
+// Rounding as _legacy/lower_kernels.py:66-86.
 template <int PART>
 __device__ __forceinline__ void qk_rope_part(const uint32_t (&xk)[16], float inv, const uint16_t* __restrict__ wn,
-                                             const uint16_t* __restrict__ cosr, const uint16_t* __restrict__ sinr,
-                                             uint16_t* __restrict__ dst) {
+                                             const uint4 (&cs)[4], uint16_t* __restrict__ dst) {
   // elements e and e+64 are rotate-half partners: handle 8 of each per step
 #pragma unroll
   for (int r0 = 0; r0 < 16; r0 += 8) {
     const int e0 = 16 * PART + r0;
     const uint4 w0 = *reinterpret_cast<const uint4*>(wn + e0);
     const uint4 w1 = *reinterpret_cast<const uint4*>(wn + e0 + 64);
-    const uint4 c0 = *reinterpret_cast<const uint4*>(cosr + e0);
-    const uint4 c1 = *reinterpret_cast<const uint4*>(cosr + e0 + 64);
-    const uint4 s0 = *reinterpret_cast<const uint4*>(sinr + e0);
-    const uint4 s1 = *reinterpret_cast<const uint4*>(sinr + e0 + 64);
+    const uint4 c0 = cs[r0 >> 3], s0 = cs[2 + (r0 >> 3)];
     const uint32_t wa[4] = {w0.x, w0.y, w0.z, w0.w}, wb[4] = {w1.x, w1.y, w1.z, w1.w};
-    const uint32_t ca[4] = {c0.x, c0.y, c0.z, c0.w}, cb[4] = {c1.x, c1.y, c1.z, c1.w};
-    const uint32_t sa[4] = {s0.x, s0.y, s0.z, s0.w}, sb[4] = {s1.x, s1.y, s1.z, s1.w};
+    const uint32_t ca[4] = {c0.x, c0.y, c0.z, c0.w};
+    const uint32_t sa[4] = {s0.x, s0.y, s0.z, s0.w};
     uint32_t ya[4], yb[4];
 #pragma unroll
     for (int p = 0; p < 4; ++p) {
@@ -127,10 +126,10 @@ __device__ __forceinline__ void qk_rope_part(const uint32_t (&xk)[16], float inv
         const float vb = h ? hi_bf(xb) : lo_bf(xb);  // element e + 64
         const float na = round_bf(round_bf(va * inv) * (h ? hi_bf(wa[p]) : lo_bf(wa[p])));
         const float nb = round_bf(round_bf(vb * inv) * (h ? hi_bf(wb[p]) : lo_bf(wb[p])));
-        const float cea = h ? hi_bf(ca[p]) : lo_bf(ca[p]), ceb = h ? hi_bf(cb[p]) : lo_bf(cb[p]);
-        const float sea = h ? hi_bf(sa[p]) : lo_bf(sa[p]), seb = h ? hi_bf(sb[p]) : lo_bf(sb[p]);
-        out_a[h] = round_bf(na * cea) + round_bf(-nb * sea);  // y[e]    = xn[e]*c - xn[e+64]*s
-        out_b[h] = round_bf(nb * ceb) + round_bf(na * seb);   // y[e+64] = xn[e+64]*c + xn[e]*s
+        const float ce = h ? hi_bf(ca[p]) : lo_bf(ca[p]);
+        const float se = h ? hi_bf(sa[p]) : lo_bf(sa[p]);
+        out_a[h] = round_bf(na * ce) + round_bf(-nb * se);  // y[e]    = xn[e]*c - xn[e+64]*s
+        out_b[h] = round_bf(nb * ce) + round_bf(na * se);   // y[e+64] = xn[e+64]*c + xn[e]*s
       }
       ya[p] = pack2(out_a[0], out_a[1]);
       yb[p] = pack2(out_b[0], out_b[1]);
@@ -295,13 +294,15 @@ __global__ void __launch_bounds__(threads_of(EPI), 1)
       // request them while the tile's MMAs run
       if (args.w_per_col && lane < BN / 32) prefetch_l1(args.w_scale + n0 + lane * 32);
       if (args.a_per_row && row_ok) prefetch_l1(args.a_scale + m);
+      uint4 cs[4];  // qkv: this token's cos (loaded now) / sin (after the wait) at its 16 head elements
       if constexpr (EPI == EPI_QKROPE) {
         const RopeSide& r = args.rope;
         if (row_ok && ft < r.HQ + r.HK) {
-          prefetch_l1(r.cos + (size_t)m * 128 + 16 * half);  // this thread's 16 + partners
-          prefetch_l1(r.cos + (size_t)m * 128 + 64 + 16 * half);
-          prefetch_l1(r.sin + (size_t)m * 128 + 16 * half);
-          prefetch_l1(r.sin + (size_t)m * 128 + 64 + 16 * half);
+          const uint4* cr = reinterpret_cast<const uint4*>(r.cos + (size_t)m * 128 + 16 * half);
+          const uint4* sr = reinterpret_cast<const uint4*>(r.sin + (size_t)m * 128 + 16 * half);
+          cs[0] = __ldg(cr);
+          cs[1] = __ldg(cr + 1);
+          prefetch_l1(sr);
           if (lane < 2) prefetch_l1((ft < r.HQ ? r.q_norm : r.k_norm) + 64 * lane);
         }
       }
@@ -329,6 +330,11 @@ __global__ void __launch_bounds__(threads_of(EPI), 1)
         // [16p, 16p + 16) of each token's head and their rotate-half partners
         // [64 + 16p, 80 + 16p); the head's sum of squares (its RMSNorm statistic) is the
         // exact sum of the four shares' float64 partial sums, exchanged through shared memory.
+        if (row_ok && ft < args.rope.HQ + args.rope.HK) {
+          const uint4* sr = reinterpret_cast<const uint4*>(args.rope.sin + (size_t)m * 128 + 16 * half);
+          cs[2] = __ldg(sr);
+          cs[3] = __ldg(sr + 1);
+        }
         uint32_t xk[16];
         double ssp = 0.0;
 #pragma unroll
@@ -336,18 +342,19 @@ __global__ void __launch_bounds__(threads_of(EPI), 1)
           const int c = 64 * g + 16 * half;
           uint32_t r[16];
           tmem_ld16_async(acc + (uint32_t)c, r);
-          float w0[8], w1[8];
-          scales8(c, w0);
-          scales8(c + 8, w1);
           tmem_wait_ld();
           reg_fence(r);
 #pragma unroll
-          for (int j = 0; j < 16; j += 2) {
-            const float* w = j < 8 ? w0 : w1;
-            const uint32_t x2 = pack2(__uint_as_float(r[j]) * sa * w[j & 7], __uint_as_float(r[j + 1]) * sa * w[(j & 7) + 1]);
-            const float a = lo_bf(x2), b = hi_bf(x2);
-            ssp += (double)(a * a) + (double)(b * b);  // x*x is exact in fp32 for bf16 x
-            xk[8 * g + (j >> 1)] = x2;
+          for (int j8 = 0; j8 < 16; j8 += 8) {
+            float w[8];
+            scales8(c + j8, w);
+#pragma unroll
+            for (int j = j8; j < j8 + 8; j += 2) {
+              const uint32_t x2 = pack2(__uint_as_float(r[j]) * sa * w[j - j8], __uint_as_float(r[j + 1]) * sa * w[j - j8 + 1]);
+              const float a = lo_bf(x2), b = hi_bf(x2);
+              ssp += (double)(a * a) + (double)(b * b);  // x*x is exact in fp32 for bf16 x
+              xk[8 * g + (j >> 1)] = x2;
+            }
           }
         }
         // the store-staging area is unused by this epilogue: [2 tiles][4 shares][128 rows]
@@ -370,13 +377,11 @@ __global__ void __launch_bounds__(threads_of(EPI), 1)
             uint16_t* dst = is_q ? r.yq + ((size_t)ft * T + m) * 128 : r.yk + ((size_t)(ft - r.HQ) * T + m) * 128;
             const uint16_t* wn = is_q ? r.q_norm : r.k_norm;
             const float inv = inv_rms_from_ss(ss, 128, r.eps);
-            const uint16_t* cr = r.cos + (size_t)m * 128;
-            const uint16_t* sr = r.sin + (size_t)m * 128;
             switch (half) {
-              case 0: qk_rope_part<0>(xk, inv, wn, cr, sr, dst); break;
-              case 1: qk_rope_part<1>(xk, inv, wn, cr, sr, dst); break;
-              case 2: qk_rope_part<2>(xk, inv, wn, cr, sr, dst); break;
-              default: qk_rope_part<3>(xk, inv, wn, cr, sr, dst); break;
+              case 0: qk_rope_part<0>(xk, inv, wn, cs, dst); break;
+              case 1: qk_rope_part<1>(xk, inv, wn, cs, dst); break;
+              case 2: qk_rope_part<2>(xk, inv, wn, cs, dst); break;
+              default: qk_rope_part<3>(xk, inv, wn, cs, dst); break;
             }
           } else {  // v heads: copied through
             uint16_t* dst = r.yv + ((size_t)(ft - r.HQ - r.HK) * T + m) * 128 + half * 16;
@@ -433,14 +438,16 @@ __global__ void __launch_bounds__(threads_of(EPI), 1)
               float wg[8], wu[8];
               scales8(c, wg);
               scales8(HALFC + c, wu);
+              float act[8];  // bf16 SiLU of the bf16 gate values, looked up
+#pragma unroll
+              for (int j = 0; j < 8; ++j) act[j] = silu_lookup(round_bf(__uint_as_float(g[cur][j]) * sa * wg[j]));
 #pragma unroll
               for (int j = 0; j < 8; j += 2) {
                 float y2[2];
 #pragma unroll
                 for (int h = 0; h < 2; ++h) {
-                  const float gv = round_bf(__uint_as_float(g[cur][j + h]) * sa * wg[j + h]);  // bf16 gate
                   const float uv = round_bf(__uint_as_float(u[cur][j + h]) * sa * wu[j + h]);  // bf16 up
-                  y2[h] = round_bf(__fdiv_rn(gv, 1.f + expf(-gv))) * uv;
+                  y2[h] = act[j + h] * uv;
                 }
                 o[grp * 4 + (j >> 1)] = pack2(y2[0], y2[1]);
               }
@@ -562,6 +569,10 @@ int launch_bn(const uint8_t* a8, const uint8_t* w8, GemmArgs& ga, cudaStream_t s
   ga.n_ttiles = (ga.M + BM - 1) / BM;
   ga.n_tiles = (ga.N / BN) * ga.splits * ga.n_ttiles;
   const int grid = ga.n_tiles < num_sms() ? ga.n_tiles : num_sms();
+  if (ga.epilogue == FFB_EPI_SWIGLU) {
+    rc = ffb::ensure_silu_table(stream);
+    if (rc) return rc;
+  }
   cudaError_t e = cudaErrorInvalidValue;
   if constexpr (BN == 128) {
     if (ga.epilogue == EPI_QKROPE) e = launch_instance<128, EPI_QKROPE>(ta, tw, to, ga, grid, stream);

@@ -332,7 +332,7 @@ __global__ void __launch_bounds__(THREADS, 1)
               for (int h = 0; h < 2; ++h) {
                 const float gv = round_bf(__uint_as_float(g[cur][j + h]));  // bf16 gate
                 const float uv = round_bf(__uint_as_float(u[cur][j + h]));  // bf16 up
-                y2[h] = round_bf(__fdiv_rn(gv, 1.f + expf(-gv))) * uv;
+                y2[h] = silu_lookup(gv) * uv;
               }
               o[grp * 4 + (j >> 1)] = pack2(y2[0], y2[1]);
             }
@@ -436,6 +436,10 @@ int launch_bn(const uint16_t* x, const uint8_t* packed, int epilogue, uint16_t* 
   wa.n_ttiles = (wa.M + BM - 1) / BM;
   wa.n_tiles = (wa.N / BN) * wa.splits * wa.n_ttiles;
   const int grid = wa.n_tiles < num_sms() ? wa.n_tiles : num_sms();
+  if (epilogue == FFB_EPI_SWIGLU) {
+    rc = ffb::ensure_silu_table(stream);
+    if (rc) return rc;
+  }
   cudaError_t e = cudaErrorInvalidValue;
   if constexpr (BN == 256) {
     if (epilogue == FFB_EPI_SWIGLU) e = launch_instance<256, FFB_EPI_SWIGLU>(ta, tw, to, wa, grid, stream);

@@ -38,5 +38,5 @@ def cos_sin(pos, head_dim=128, theta=5_000_000.0, sections=(24, 20, 20)):
     for axis in (1, 2):
         idx = torch.arange(axis, sections[axis] * 3, 3)
         f[:, idx] = freqs[axis][:, idx]
-    emb = torch.cat((f, f), -1)
+    emb = torch.cat((f, f), -1)  # equal halves: the fused qkv epilogue reads columns [0, 64) only
     return emb.cos().to(torch.bfloat16), emb.sin().to(torch.bfloat16)

@@ -161,7 +161,9 @@ int ffb_fp8_gemm(const uint8_t* a8, const float* a_scale, int a_per_row,
  * Replaces the qkv `RuntimeScaleLinear` (_family/depth_fp8.py:22-26) followed by
  * `qk_pair` (_legacy/broad_kernels.py:63-74, rounding of lower_kernels.py:66-86): each
  * 128-feature tile is one head; its bf16 output row is normalised and rotated in the GEMM
- * epilogue.  w8 [(HQ+2HK)*128, K] packed q|k|v rows; q_norm/k_norm [128]; cos/sin [T,128];
+ * epilogue.  w8 [(HQ+2HK)*128, K] packed q|k|v rows; q_norm/k_norm [128]; cos/sin [T,128]
+ * rotate-half tables whose two 64-column halves are equal (cat(freqs, freqs), as every
+ * Qwen3-VL / HF rotary table): only columns [0, 64) are read;
  * outputs head-major yq [HQ,T,128], yk [HK,T,128], yv [HK,T,128] (V unrotated). */
 int ffb_fp8_gemm_qk_rope(const uint8_t* a8, const float* a_scale, int a_per_row,
                          const uint8_t* w8, const float* w_scale, int w_per_col,

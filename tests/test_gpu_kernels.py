@@ -211,6 +211,37 @@ def test_fp8_gemm_swiglu_epilogue(M, I):
     assert_bytes_equal(out, want, "swiglu epilogue")
 
 
+def test_swiglu_epilogue_every_bf16_gate():
+    """The SwiGLU epilogues look the activation bf16(g / (1 + exp(-g))) up by the bf16 gate's
+    bits; the table must equal the formula evaluated on the device (the standalone swiglu
+    kernel: expf + IEEE divide) for every finite bf16 gate.  Each GEMM column computes
+    acc = 1 (one-hot rows) times a per-channel scale equal to the gate value under test."""
+    n = 65536
+    g = torch.arange(n, dtype=torch.int32).to(torch.int16).view(BF16)  # every bf16 bit pattern
+    gf = g.float()
+    M, K = 16, 128
+    a8 = torch.zeros((M, K), dtype=torch.float32)
+    a8[:, 0] = 1.0
+    a8 = a8.to(torch.float8_e4m3fn).to(DEV)
+    sa = torch.ones(M, device=DEV)
+    w8 = torch.zeros((2 * n, K), dtype=torch.float32)
+    w8[:, 0] = 1.0
+    w8 = w8.to(torch.float8_e4m3fn).to(DEV)
+    sw = torch.ones((n // 128, 2, 128), dtype=torch.float32)  # tile t: gate channels, then up
+    sw[:, 0, :] = gf.view(n // 128, 128)
+    sw = sw.reshape(-1).to(DEV)
+    out = torch.empty((M, n), device=DEV, dtype=BF16)
+    call("ffb_fp8_gemm", ptr(a8), ptr(sa), 1, ptr(w8), ptr(sw), 1, L.EPI_SWIGLU, ptr(out), None, 1, 0, M, 2 * n, K, _sp())
+    direct = ops.swiglu(g.view(1, n).to(DEV), torch.ones((1, n), device=DEV, dtype=BF16))
+    torch.cuda.synchronize()
+    fin = torch.isfinite(gf)
+    got = out[0].cpu().view(torch.int16)[fin]
+    assert torch.equal(got, out[M - 1].cpu().view(torch.int16)[fin])
+    assert torch.equal(got, direct[0].cpu().view(torch.int16)[fin]), "table != device formula"
+    ref = oracle.swiglu(g.view(1, n), torch.ones((1, n), dtype=BF16))[0].view(torch.int16)[fin]
+    print(f"\nlooked-up SiLU vs the oracle (CPU exp): {(got != ref).sum().item()} of {int(fin.sum())} bf16 gates differ")
+
+
 @pytest.mark.parametrize("T,HQ,HK,K", [(320, 32, 8, 2560), (77, 16, 8, 2048), (1, 8, 8, 512)])
 def test_fp8_gemm_qk_rope_fused(T, HQ, HK, K):
     """qkv projection with the per-head norm + RoPE in its epilogue, against the oracle's
