@@ -101,10 +101,16 @@ __device__ __forceinline__ float hi_bf(uint32_t w) { return __uint_as_float(w & 
 // token's cos (cs[0..2)) and sin (cs[2..4)) at elements [16*PART, 16*PART + 16).  The
 // tables' two halves are equal (rotate-half tables are cat(freqs, freqs)), so those values
 // also serve the partners.  Writes the 32 outputs to dst (the 128-wide head row).
-// Rounding as _legacy/lower_kernels.py:66-86.
+// Rounding as _legacy/lower_kernels.py:66-86: n = bf16(bf16(x * inv) * w), then
+// y[e] = bf16(bf16(n[e] c) - bf16(n[e+64] s)), y[e+64] = bf16(bf16(n[e+64] c) + bf16(n[e] s)).
+// Every product after the first is of two bf16 values, so the bf16x2 multiply (exact
+// product, one rounding) and add (exact sum, one rounding) give those roundings exactly;
+// the _rn forms keep the compiler from contracting a multiply and an add into one fma.
 template <int PART>
 __device__ __forceinline__ void qk_rope_part(const uint32_t (&xk)[16], float inv, const uint16_t* __restrict__ wn,
                                              const uint4 (&cs)[4], uint16_t* __restrict__ dst) {
+  auto b2 = [](uint32_t w) { return *reinterpret_cast<const __nv_bfloat162*>(&w); };
+  auto u32 = [](__nv_bfloat162 v) { return *reinterpret_cast<const uint32_t*>(&v); };
   // elements e and e+64 are rotate-half partners: handle 8 of each per step
 #pragma unroll
   for (int r0 = 0; r0 < 16; r0 += 8) {
@@ -118,21 +124,12 @@ __device__ __forceinline__ void qk_rope_part(const uint32_t (&xk)[16], float inv
     uint32_t ya[4], yb[4];
 #pragma unroll
     for (int p = 0; p < 4; ++p) {
-      const uint32_t xa = xk[(r0 >> 1) + p], xb = xk[8 + (r0 >> 1) + p];
-      float out_a[2], out_b[2];
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const float va = h ? hi_bf(xa) : lo_bf(xa);  // element e (< 64)
-        const float vb = h ? hi_bf(xb) : lo_bf(xb);  // element e + 64
-        const float na = round_bf(round_bf(va * inv) * (h ? hi_bf(wa[p]) : lo_bf(wa[p])));
-        const float nb = round_bf(round_bf(vb * inv) * (h ? hi_bf(wb[p]) : lo_bf(wb[p])));
-        const float ce = h ? hi_bf(ca[p]) : lo_bf(ca[p]);
-        const float se = h ? hi_bf(sa[p]) : lo_bf(sa[p]);
-        out_a[h] = round_bf(na * ce) + round_bf(-nb * se);  // y[e]    = xn[e]*c - xn[e+64]*s
-        out_b[h] = round_bf(nb * ce) + round_bf(na * se);   // y[e+64] = xn[e+64]*c + xn[e]*s
-      }
-      ya[p] = pack2(out_a[0], out_a[1]);
-      yb[p] = pack2(out_b[0], out_b[1]);
+      const uint32_t xa = xk[(r0 >> 1) + p], xb = xk[8 + (r0 >> 1) + p];  // elements e / e + 64
+      const __nv_bfloat162 na = __hmul2_rn(__floats2bfloat162_rn(lo_bf(xa) * inv, hi_bf(xa) * inv), b2(wa[p]));
+      const __nv_bfloat162 nb = __hmul2_rn(__floats2bfloat162_rn(lo_bf(xb) * inv, hi_bf(xb) * inv), b2(wb[p]));
+      const __nv_bfloat162 c = b2(ca[p]), sn = b2(sa[p]);
+      ya[p] = u32(__hadd2_rn(__hmul2_rn(na, c), __hmul2_rn(__hneg2(nb), sn)));  // y[e]    = n[e] c - n[e+64] s
+      yb[p] = u32(__hadd2_rn(__hmul2_rn(nb, c), __hmul2_rn(na, sn)));           // y[e+64] = n[e+64] c + n[e] s
     }
     *reinterpret_cast<uint4*>(dst + e0) = make_uint4(ya[0], ya[1], ya[2], ya[3]);
     *reinterpret_cast<uint4*>(dst + e0 + 64) = make_uint4(yb[0], yb[1], yb[2], yb[3]);
