@@ -14,6 +14,15 @@ LIB_PATH = Path(__file__).resolve().with_name("libffb200.so")
 OK, EINVAL, EUNSUPPORTED, ECUDA, ETIMEOUT = 0, -1, -2, -3, -4
 QUANT_NONE, QUANT_STATIC, QUANT_ROWWISE = 0, 1, 2
 EPI_BF16, EPI_F32_PARTIAL, EPI_SWIGLU = 0, 1, 2
+PRO_QUANT, PRO_ADD_RMSNORM = 1, 2
+
+
+class Prologue(ctypes.Structure):
+    """`ffb_gemm_prologue` (include/ffb200.h): the producer fused into the front of a GEMM."""
+    _fields_ = [("kind", c_int), ("x", c_void_p), ("b", c_void_p), ("b32", c_void_p), ("splits", c_int),
+                ("add", c_int), ("deep", c_void_p), ("start", c_int), ("nv", c_int), ("norm_w", c_void_p),
+                ("eps", c_float), ("residual", c_void_p), ("quant_mode", c_int), ("inv_scale", c_float),
+                ("sync", c_void_p)]
 
 P, I, F = c_void_p, c_int, c_float
 
@@ -34,6 +43,8 @@ SIGNATURES = {
     "ffb_quantize_weight_fp8_noalloc": [P, I, P, P, I, I, P],
     "ffb_fp8_gemm": [P, P, I, P, P, I, I, P, P, I, I, I, I, I, P],
     "ffb_fp8_gemm_qk_rope": [P, P, I, P, P, I, P, P, F, P, P, P, P, P, I, I, I, I, P],
+    "ffb_fp8_gemm_fused": [P, P, P, I, P, P, I, I, P, P, I, I, I, I, I, P],
+    "ffb_fp8_gemm_qk_rope_fused": [P, P, P, I, P, P, I, P, P, F, P, P, P, P, P, I, I, I, I, P],
     "ffb_pack_gateup": [P, P, I, I, I, P],
     "ffb_swiglu": [P, P, I, P, I, I, P],
     "ffb_readout": [P, P, P, I, P, F, P, I, I, P, P, I, P],

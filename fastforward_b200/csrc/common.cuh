@@ -31,6 +31,7 @@ enum : uint32_t {
   ERR_GEMM_TIMEOUT = 1u << 0,
   ERR_W4_TIMEOUT = 1u << 1,
   ERR_ATTN_TIMEOUT = 1u << 2,
+  ERR_GRID_SYNC_TIMEOUT = 1u << 3,
 };
 
 // Fills ffb_silu_table on this device once (stream-ordered, before the caller's next
@@ -66,6 +67,8 @@ __device__ __forceinline__ uint8_t f2e4m3(float f) {
   return (uint8_t)__nv_cvt_float_to_fp8(f, __NV_SATFINITE, __NV_E4M3);
 }
 __device__ __forceinline__ float clamp448(float v) { return fminf(448.f, fmaxf(-448.f, v)); }
+
+
 
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
@@ -140,6 +143,56 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
     }
   }
   return false;
+}
+
+// ------------------------------------------------------------------ grid-wide barrier
+__device__ __forceinline__ uint64_t ld_acquire_gpu_u64(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ uint64_t atom_add_acq_rel_gpu(uint64_t* p, uint64_t v) {
+  uint64_t old;
+  asm volatile("atom.acq_rel.gpu.global.add.u64 %0, [%1], %2;" : "=l"(old) : "l"(p), "l"(v) : "memory");
+  return old;
+}
+// Orders this thread's earlier generic-proxy accesses to global memory before its later
+// async-proxy (TMA) accesses.
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+// Barrier over every CTA of the grid, for kernels whose CTAs are all resident at once
+// (one per SM, grid <= SMs: the host checks the occupancy).  One 64-bit word: the high
+// half is the generation, the low half counts arrivals.  Each CTA's thread 0 arrives with
+// an acq_rel atomic add (releasing the CTA's writes, ordered before it by __syncthreads);
+// the last arrival adds 2^32 - G, which clears the count and advances the generation in
+// one atomic, so the word needs no reset between launches (launches that use the same
+// word must not overlap: one word per stream).  The others poll the word with acquire
+// loads.  Thread 0 gives up after `limit_ns`; the result (the same in every thread) is
+// false then.
+__device__ __forceinline__ bool grid_barrier(uint64_t* bar, int* flag_smem, uint64_t limit_ns = 2000000000ull) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int ok = 1;
+    const uint64_t old = atom_add_acq_rel_gpu(bar, 1ull);
+    const uint32_t gen = (uint32_t)(old >> 32);
+    if ((uint32_t)old + 1u == gridDim.x) {
+      atom_add_acq_rel_gpu(bar, (1ull << 32) - (uint64_t)gridDim.x);
+    } else {
+      const uint64_t t0 = global_timer_ns();
+      uint32_t polls = 0;
+      while ((uint32_t)(ld_acquire_gpu_u64(bar) >> 32) == gen) {
+        if ((++polls & 63u) == 0 && global_timer_ns() - t0 > limit_ns) {
+          ok = 0;
+          break;
+        }
+      }
+    }
+    *flag_smem = ok;
+  }
+  __syncthreads();
+  return *flag_smem != 0;
 }
 
 // ------------------------------------------------------------------ PTX: TMA

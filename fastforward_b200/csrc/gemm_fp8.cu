@@ -68,6 +68,24 @@ struct RopeSide {
   int HQ, HK;
 };
 
+// The fused prologue (FFB_PRO_*): bf16 rows -> the GEMM's FP8 operand and row scales.
+struct ProArgs {
+  const uint16_t* x;    // QUANT: source rows; ADD_RMSNORM: residual input a
+  const uint16_t* b;    // bf16 addend or NULL
+  const float* b32;     // fp32 split partials [splits][M][K] when b is NULL
+  int splits, add;
+  const uint16_t* deep;
+  int start, nv;
+  const uint16_t* w;    // RMSNorm weight
+  float eps;
+  uint16_t* residual;
+  int quant_mode;
+  float inv;
+  uint8_t* q8;          // = the GEMM's A operand
+  float* qscale;        // ROWWISE: = the GEMM's per-row A scale
+  uint64_t* sync;       // grid barrier word
+};
+
 struct GemmArgs {
   const float* a_scale;
   const float* w_scale;
@@ -76,7 +94,301 @@ struct GemmArgs {
   int a_per_row, w_per_col, epilogue;
   int M, N, K, n_ttiles, splits, n_tiles;
   RopeSide rope;
+  ProArgs pro;
 };
+
+constexpr int PRO_NONE = 0;
+constexpr int PRO_ROWS = 4;        // rows per prologue batch (at most)
+constexpr int PRO_ITEMS_Q = 8;     // 8-element vectors per thread and batch: QUANT
+constexpr int PRO_ITEMS_N = 2;     //                                         ADD_RMSNORM
+constexpr int PRO_MAX_SPLITS = 8;
+__host__ __device__ constexpr int pro_items(int pro) { return pro == FFB_PRO_QUANT ? PRO_ITEMS_Q : PRO_ITEMS_N; }
+
+// Slot-indexed register arrays: the row slot of an item is a run-time value, so select
+// it with unrolled compares instead of dynamic indexing (which would go to local memory).
+template <typename T, int N>
+__device__ __forceinline__ void slot_add(T (&a)[N], int k, T v) {
+#pragma unroll
+  for (int i = 0; i < N; ++i)
+    if (i == k) a[i] += v;
+}
+template <int N>
+__device__ __forceinline__ void slot_max(float (&a)[N], int k, float v) {
+#pragma unroll
+  for (int i = 0; i < N; ++i)
+    if (i == k) a[i] = fmaxf(a[i], v);
+}
+template <typename T, int N>
+__device__ __forceinline__ T slot_get(const T (&a)[N], int k) {
+  T r = a[0];
+#pragma unroll
+  for (int i = 1; i < N; ++i)
+    if (i == k) r = a[i];
+  return r;
+}
+__device__ __forceinline__ void unpack8(const uint4& u, float (&f)[8]) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    f[2 * i] = __uint_as_float(w[i] << 16);
+    f[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+  }
+}
+__device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
+  uint32_t w[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) w[i] = (uint32_t)f2bf(f[2 * i]) | ((uint32_t)f2bf(f[2 * i + 1]) << 16);
+  return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+// Per-row statistics of a prologue batch: every thread adds its items' contributions into
+// PRO_ROWS register slots; the block reduces them (warp shuffles, then one thread per row
+// over the warps' partials, fixed order) and that thread derives the row's values into
+// shared memory, where every thread reads them by row index.
+//   sum:  v = exact float64 sum of squares  -> out[r] = 1/rms (inv_rms_from_ss)
+//   max:  v = max |y|                        -> out[r] = scale = max(v, 1e-12)/448
+// red: NW * PRO_ROWS doubles; out: PRO_ROWS floats (shared memory).
+__device__ __forceinline__ void row_inv_rms(const double (&v)[PRO_ROWS], int n, int K, float eps, double* red,
+                                            float* out) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+#pragma unroll
+  for (int r = 0; r < PRO_ROWS; ++r) {
+    if (r < n) {
+      const double t = warp_sum_d(v[r]);
+      if (lane == 0) red[warp * PRO_ROWS + r] = t;
+    }
+  }
+  __syncthreads();
+  if ((int)threadIdx.x < n) {
+    double t = 0.0;
+    for (int w = 0; w < nw; ++w) t += red[w * PRO_ROWS + threadIdx.x];
+    out[threadIdx.x] = inv_rms_from_ss(t, K, eps);
+  }
+  __syncthreads();
+}
+__device__ __forceinline__ void row_scales(const float (&v)[PRO_ROWS], int n, float* red, float* out) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+#pragma unroll
+  for (int r = 0; r < PRO_ROWS; ++r) {
+    if (r < n) {
+      const float t = warp_max(v[r]);
+      if (lane == 0) red[warp * PRO_ROWS + r] = t;
+    }
+  }
+  __syncthreads();
+  if ((int)threadIdx.x < n) {
+    float t = 0.f;
+    for (int w = 0; w < nw; ++w) t = fmaxf(t, red[w * PRO_ROWS + threadIdx.x]);
+    out[threadIdx.x] = fmaxf(t, 1e-12f) / 448.f;
+  }
+  __syncthreads();
+}
+
+// The fused prologue: CTA c owns rows [c*M/G, (c+1)*M/G) and processes them in batches of
+// up to PRO_ROWS rows, the batch's 8-element vectors spread over all threads (at most
+// pro_items(PRO) per thread).  Each batch first issues every load it needs (so their
+// latencies overlap), then computes.  The arithmetic is that of add_rmsnorm_kernel
+// (norm.cu) and quant_rows_vec_kernel (quant.cu), element for element, so the bytes are
+// the same:
+//   ADD_RMSNORM: x = bf16(a + bf16(sum of partials in split order) | b) (+ deep:
+//                bf16(x + d)), inv = 1/sqrt(sum(x^2)/K + eps) (exact float64 sum),
+//                y = bf16(bf16(x inv) w);
+//   QUANT:       y = the bf16 input row;
+//   then STATIC q = e4m3(clamp(y * inv_scale)), ROWWISE s = max(max|y|, 1e-12)/448,
+//   q = e4m3(y / s) with an IEEE divide.
+// `issue_prefetch()` is called once by every thread right after the first batch's loads
+// are in flight (the caller's weight prefetch then queues behind them).
+// scratch: NW * PRO_ROWS doubles + PRO_ROWS floats of shared memory.
+template <int PRO, typename F>
+__device__ void prologue_rows(const GemmArgs& g, uint8_t* scratch, F&& issue_prefetch) {
+  constexpr int ITEMS = pro_items(PRO);
+  const ProArgs& p = g.pro;
+  const int M = g.M, K = g.K, nvec = K >> 3, NT = blockDim.x, G = gridDim.x, c = blockIdx.x;
+  const int r_begin = (int)((long long)c * M / G), r_end = (int)((long long)(c + 1) * M / G);
+  int rb_max = ITEMS * NT / nvec;
+  rb_max = rb_max > PRO_ROWS ? PRO_ROWS : rb_max;  // >= 1 (host check)
+  double* red_d = reinterpret_cast<double*>(scratch);
+  float* red_f = reinterpret_cast<float*>(scratch);
+  float* stat = reinterpret_cast<float*>(scratch + (NT >> 5) * PRO_ROWS * sizeof(double));
+  const bool rowwise = p.quant_mode == FFB_QUANT_ROWWISE;
+  bool prefetched = false;
+  if (r_begin >= r_end) {
+    issue_prefetch();
+    prefetched = true;
+  }
+  for (int r0 = r_begin; r0 < r_end; r0 += rb_max) {
+    const int rb = r_end - r0 < rb_max ? r_end - r0 : rb_max;
+    const int items = rb * nvec;
+    uint4 xv[ITEMS];  // the bf16 rows to quantise (after the norm, for ADD_RMSNORM)
+    float amax[PRO_ROWS];
+#pragma unroll
+    for (int r = 0; r < PRO_ROWS; ++r) amax[r] = 0.f;
+    if constexpr (PRO == FFB_PRO_ADD_RMSNORM) {
+      // ---- loads: residual row, norm weight, bf16 addend
+      uint4 wv[ITEMS];
+      float bs[ITEMS][8];
+#pragma unroll
+      for (int j = 0; j < ITEMS; ++j) {
+        const int i = threadIdx.x + j * NT;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) bs[j][e] = 0.f;
+        if (i < items) {
+          const int rr = i / nvec, v = i - rr * nvec;
+          const size_t off = (size_t)(r0 + rr) * K + (size_t)v * 8;
+          xv[j] = *reinterpret_cast<const uint4*>(p.x + off);
+          wv[j] = __ldg(reinterpret_cast<const uint4*>(p.w + (size_t)v * 8));
+          if (p.add && p.b) unpack8(*reinterpret_cast<const uint4*>(p.b + off), bs[j]);
+        }
+      }
+      if (!prefetched) {
+        issue_prefetch();
+        prefetched = true;
+      }
+      // ---- split-K partials, summed in split order; two splits of every item per round trip
+      if (p.add && !p.b) {
+#pragma unroll 1
+        for (int s0 = 0; s0 < p.splits; s0 += 2) {
+          float4 lo[ITEMS][2], hi[ITEMS][2];
+#pragma unroll
+          for (int j = 0; j < ITEMS; ++j) {
+            const int i = threadIdx.x + j * NT;
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+              if (i < items && s0 + u < p.splits) {
+                const int rr = i / nvec, v = i - rr * nvec;
+                const float4* src =
+                    reinterpret_cast<const float4*>(p.b32 + ((size_t)(s0 + u) * M + r0 + rr) * K + (size_t)v * 8);
+                lo[j][u] = __ldcg(src);
+                hi[j][u] = __ldcg(src + 1);
+              }
+            }
+          }
+#pragma unroll
+          for (int j = 0; j < ITEMS; ++j) {
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+              if (s0 + u < p.splits) {
+                bs[j][0] += lo[j][u].x; bs[j][1] += lo[j][u].y; bs[j][2] += lo[j][u].z; bs[j][3] += lo[j][u].w;
+                bs[j][4] += hi[j][u].x; bs[j][5] += hi[j][u].y; bs[j][6] += hi[j][u].z; bs[j][7] += hi[j][u].w;
+              }
+            }
+          }
+        }
+      }
+      // ---- residual x, its sum of squares
+      double ss[PRO_ROWS];
+#pragma unroll
+      for (int r = 0; r < PRO_ROWS; ++r) ss[r] = 0.0;
+#pragma unroll
+      for (int j = 0; j < ITEMS; ++j) {
+        const int i = threadIdx.x + j * NT;
+        if (i < items) {
+          const int rr = i / nvec, v = i - rr * nvec, row = r0 + rr;
+          float x[8];
+          unpack8(xv[j], x);
+          if (p.add) {
+#pragma unroll
+            for (int e = 0; e < 8; ++e) x[e] = round_bf(x[e] + round_bf(bs[j][e]));  // the linear's bf16 output
+            if (p.deep && row >= p.start && row < p.start + p.nv) {  // deepstack rows (first layers only)
+              float d[8];
+              unpack8(*reinterpret_cast<const uint4*>(p.deep + (size_t)(row - p.start) * K + (size_t)v * 8), d);
+#pragma unroll
+              for (int e = 0; e < 8; ++e) x[e] = round_bf(x[e] + d[e]);
+            }
+            xv[j] = pack8(x);
+            if (p.residual) *reinterpret_cast<uint4*>(p.residual + (size_t)row * K + (size_t)v * 8) = xv[j];
+          }
+          double sq = 0.0;
+#pragma unroll
+          for (int e = 0; e < 8; ++e) sq += (double)(x[e] * x[e]);  // x*x exact in fp32
+          slot_add(ss, rr, sq);
+        }
+      }
+      row_inv_rms(ss, rb, K, p.eps, red_d, stat);
+      // ---- y = bf16(bf16(x inv) w)
+#pragma unroll
+      for (int j = 0; j < ITEMS; ++j) {
+        const int i = threadIdx.x + j * NT;
+        if (i < items) {
+          const int rr = i / nvec;
+          const float iv = stat[rr];
+          float x[8], w[8];
+          unpack8(xv[j], x);
+          unpack8(wv[j], w);
+          float m = 0.f;
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            x[e] = round_bf(round_bf(x[e] * iv) * w[e]);
+            m = fmaxf(m, fabsf(x[e]));
+          }
+          xv[j] = pack8(x);
+          slot_max(amax, rr, m);
+        }
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < ITEMS; ++j) {
+        const int i = threadIdx.x + j * NT;
+        if (i < items) {
+          const int rr = i / nvec, v = i - rr * nvec;
+          xv[j] = __ldcg(reinterpret_cast<const uint4*>(p.x + (size_t)(r0 + rr) * K + (size_t)v * 8));
+        }
+      }
+      if (!prefetched) {
+        issue_prefetch();
+        prefetched = true;
+      }
+      if (rowwise) {
+#pragma unroll
+        for (int j = 0; j < ITEMS; ++j) {
+          const int i = threadIdx.x + j * NT;
+          if (i < items) {
+            float x[8];
+            unpack8(xv[j], x);
+            float m = 0.f;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) m = fmaxf(m, fabsf(x[e]));
+            slot_max(amax, i / nvec, m);
+          }
+        }
+      }
+    }
+    // ---- scales and the e4m3 cast
+    if (rowwise) {
+      row_scales(amax, rb, red_f, stat);
+      if ((int)threadIdx.x < rb) p.qscale[r0 + threadIdx.x] = stat[threadIdx.x];
+    }
+#pragma unroll
+    for (int j = 0; j < ITEMS; ++j) {
+      const int i = threadIdx.x + j * NT;
+      if (i < items) {
+        const int rr = i / nvec, v = i - rr * nvec;
+        float x[8];
+        unpack8(xv[j], x);
+        uint32_t lo = 0, hi = 0;
+        if (rowwise) {
+          const float sc = stat[rr];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const uint32_t bq = f2e4m3(clamp448(__fdiv_rn(x[e], sc)));
+            if (e < 4) lo |= bq << (8 * e);
+            else hi |= bq << (8 * (e - 4));
+          }
+        } else {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const uint32_t bq = f2e4m3(clamp448(x[e] * p.inv));
+            if (e < 4) lo |= bq << (8 * e);
+            else hi |= bq << (8 * (e - 4));
+          }
+        }
+        *reinterpret_cast<uint2*>(p.q8 + (size_t)(r0 + rr) * K + (size_t)v * 8) = make_uint2(lo, hi);
+      }
+    }
+    __syncthreads();  // the next batch reuses the statistics in shared memory
+  }
+  if (!prefetched) issue_prefetch();
+}
 
 __device__ __forceinline__ void tile_coords(const GemmArgs& a, int t, int& tt, int& ks, int& ft) {
   tt = t % a.n_ttiles;
@@ -136,7 +448,7 @@ __device__ __forceinline__ void qk_rope_part(const uint32_t (&xk)[16], float inv
   }
 }
 
-template <int BN, int EPI>
+template <int BN, int EPI, int PRO>
 __global__ void __launch_bounds__(threads_of(EPI), 1)
     fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_w,
                     const __grid_constant__ CUtensorMap tmap_o, const GemmArgs args) {
@@ -155,6 +467,7 @@ __global__ void __launch_bounds__(threads_of(EPI), 1)
   uint64_t* xbar = tempty + 2;          // [4]: qkv epilogue, per lane quarter, 4 arrivals
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(xbar + 4);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int* sync_flag = reinterpret_cast<int*>(tmem_slot + 2);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int nkb = (args.K + BK - 1) / BK;
@@ -186,22 +499,45 @@ __global__ void __launch_bounds__(threads_of(EPI), 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
+  // The weight half of the first ring pass does not depend on the previous kernel:
+  // request it before the programmatic-launch wait -- or, with a fused prologue, right
+  // after the prologue's own first loads (which would otherwise queue behind it).
+  int pre = 0;
+  auto prefetch_weights = [&]() {
+    if (warp == 0 && lane == 0 && (int)blockIdx.x < args.n_tiles) {
+      int tt, ks, ft, kb0, kb1;
+      tile_coords(args, blockIdx.x, tt, ks, ft);
+      k_range(args, ks, nkb, kb0, kb1);
+      pre = kb1 - kb0 < C::STAGES ? kb1 - kb0 : C::STAGES;
+      const uint64_t pol_w = policy_evict_first();
+      for (int i = 0; i < pre; ++i) {
+        mbar_arrive_expect_tx(&full[i], C::STAGE_BYTES);
+        tma_load_2d(smem + i * C::STAGE_BYTES + A_TILE_BYTES, &tmap_w, &full[i], (kb0 + i) * BK, ft * BN, pol_w);
+      }
+    }
+  };
+  if constexpr (PRO == PRO_NONE) prefetch_weights();
+  if constexpr (PRO != PRO_NONE) {
+    // Fused prologue: every CTA writes its slice of the A rows (and scales), then the grid
+    // meets; the TMA loads of A below read rows other CTAs wrote.
+    pdl_wait();
+    prologue_rows<PRO>(args, stg_all, prefetch_weights);
+    fence_proxy_async_global();  // this thread's rows, before the TMA loads of any CTA
+    if (!grid_barrier(args.pro.sync, sync_flag)) {
+      if (tid == 0) {
+        *abort_flag = 1;
+        atomicOr(&ffb_device_error_word, ffb::ERR_GRID_SYNC_TIMEOUT);
+      }
+      __syncthreads();
+    }
+  }
+
   if (warp == 0) {
     // ------------------------------------------------------------------ TMA producer
     if (lane == 0) {
       const uint64_t pol_w = policy_evict_first(), pol_a = policy_evict_last();
-      int pre = 0;
-      if ((int)blockIdx.x < args.n_tiles) {
-        int tt, ks, ft, kb0, kb1;
-        tile_coords(args, blockIdx.x, tt, ks, ft);
-        k_range(args, ks, nkb, kb0, kb1);
-        pre = kb1 - kb0 < C::STAGES ? kb1 - kb0 : C::STAGES;
-        for (int i = 0; i < pre; ++i) {
-          mbar_arrive_expect_tx(&full[i], C::STAGE_BYTES);
-          tma_load_2d(smem + i * C::STAGE_BYTES + A_TILE_BYTES, &tmap_w, &full[i], (kb0 + i) * BK, ft * BN, pol_w);
-        }
-      }
       pdl_wait();
+      if (PRO != PRO_NONE) fence_proxy_async_global();  // the A rows other CTAs wrote, before the TMA reads them
       int it = 0;
       for (int t = blockIdx.x; t < args.n_tiles && !*abort_flag; t += gridDim.x) {
         int tt, ks, ft, kb0, kb1;
@@ -225,6 +561,13 @@ __global__ void __launch_bounds__(threads_of(EPI), 1)
       }
       if (*abort_flag) {  // every slot whose copy was issued must land before the CTA exits
         volatile int never = 0;
+        if (it < pre) {  // weight half requested, activation half not: request it so the slot completes
+          int tt, ks, ft, kb0, kb1;
+          tile_coords(args, blockIdx.x, tt, ks, ft);
+          k_range(args, ks, nkb, kb0, kb1);
+          for (int i = it; i < pre; ++i)
+            tma_load_2d(smem + i * C::STAGE_BYTES, &tmap_a, &full[i], (kb0 + i) * BK, tt * BM, pol_a);
+        }
         const int issued = it > pre ? it : pre;
         for (int i = (issued > C::STAGES ? issued - C::STAGES : 0); i < issued; ++i)
           mbar_wait_bounded(&full[i % C::STAGES], (uint32_t)(i / C::STAGES) & 1u, &never, 200000000ull);
@@ -290,7 +633,7 @@ __global__ void __launch_bounds__(threads_of(EPI), 1)
       // the tile's scales (and the RoPE tables of this thread's token) come from HBM / L2:
       // request them while the tile's MMAs run
       if (args.w_per_col && lane < BN / 32) prefetch_l1(args.w_scale + n0 + lane * 32);
-      if (args.a_per_row && row_ok) prefetch_l1(args.a_scale + m);
+      if (PRO == PRO_NONE && args.a_per_row && row_ok) prefetch_l1(args.a_scale + m);
       uint4 cs[4];  // qkv: this token's cos (loaded now) / sin (after the wait) at its 16 head elements
       if constexpr (EPI == EPI_QKROPE) {
         const RopeSide& r = args.rope;
@@ -309,7 +652,9 @@ __global__ void __launch_bounds__(threads_of(EPI), 1)
         break;
       }
       tc_fence_after();
-      const float sa = args.a_per_row ? (row_ok ? args.a_scale[m] : 0.f) : args.a_scale[0];
+      // (a fused prologue wrote the per-row scales in this kernel: read them from L2)
+      const float sa = args.a_per_row ? (row_ok ? (PRO == PRO_NONE ? args.a_scale[m] : __ldcg(args.a_scale + m)) : 0.f)
+                                      : args.a_scale[0];
       const uint32_t acc = tmem + (uint32_t)(buf * BN) + ((uint32_t)(q * 32) << 16);
       // per-feature scales of tile columns [c, c + 8)
       auto scales8 = [&](int c, float (&w)[8]) {
@@ -536,21 +881,50 @@ int num_sms() {
   return sms;
 }
 
-template <int BN, int EPI>
+template <int BN, int EPI, int PRO>
 cudaError_t launch_instance(const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap& to, const GemmArgs& ga,
                             int grid, cudaStream_t stream) {
   using C = Cfg<BN>;
   static bool attr_set = false;  // the attribute is per function (one device per process here)
   if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(fp8_gemm_kernel<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+    cudaError_t e =
+        cudaFuncSetAttribute(fp8_gemm_kernel<BN, EPI, PRO>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
     if (e != cudaSuccess) return e;
     attr_set = true;
   }
-  return ffb::launch(fp8_gemm_kernel<BN, EPI>, dim3(grid), dim3(threads_of(EPI)), C::SMEM, stream, ta, tw, to, ga);
+  if constexpr (PRO != PRO_NONE) {
+    // the fused prologue's grid barrier needs every CTA resident at once
+    static int per_sm = -1;
+    if (per_sm < 0) {
+      cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fp8_gemm_kernel<BN, EPI, PRO>,
+                                                                    threads_of(EPI), C::SMEM);
+      if (e != cudaSuccess) return e;
+    }
+    if (grid > per_sm * num_sms()) return cudaErrorCooperativeLaunchTooLarge;
+  }
+  return ffb::launch(fp8_gemm_kernel<BN, EPI, PRO>, dim3(grid), dim3(threads_of(EPI)), C::SMEM, stream, ta, tw, to,
+                     ga);
+}
+
+template <int BN, int PRO>
+cudaError_t launch_epi(const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap& to, const GemmArgs& ga,
+                       int grid, cudaStream_t stream) {
+  if constexpr (BN == 128) {
+    if (ga.epilogue == EPI_QKROPE) return launch_instance<128, EPI_QKROPE, PRO>(ta, tw, to, ga, grid, stream);
+    if (ga.epilogue == FFB_EPI_BF16) return launch_instance<128, FFB_EPI_BF16, PRO>(ta, tw, to, ga, grid, stream);
+    if (ga.epilogue == FFB_EPI_F32_PARTIAL)
+      return launch_instance<128, FFB_EPI_F32_PARTIAL, PRO>(ta, tw, to, ga, grid, stream);
+  } else {
+    if (ga.epilogue == FFB_EPI_SWIGLU) return launch_instance<256, FFB_EPI_SWIGLU, PRO>(ta, tw, to, ga, grid, stream);
+    if (ga.epilogue == FFB_EPI_BF16) return launch_instance<256, FFB_EPI_BF16, PRO>(ta, tw, to, ga, grid, stream);
+    if (ga.epilogue == FFB_EPI_F32_PARTIAL)
+      return launch_instance<256, FFB_EPI_F32_PARTIAL, PRO>(ta, tw, to, ga, grid, stream);
+  }
+  return cudaErrorInvalidValue;
 }
 
 template <int BN>
-int launch_bn(const uint8_t* a8, const uint8_t* w8, GemmArgs& ga, cudaStream_t stream) {
+int launch_bn(const uint8_t* a8, const uint8_t* w8, GemmArgs& ga, int pro, cudaStream_t stream) {
   CUtensorMap ta, tw, to;
   memset(&to, 0, sizeof(to));
   int rc = ffb::make_tmap_2d(&ta, a8, (uint64_t)ga.M, (uint64_t)ga.K, (uint64_t)ga.K, BM, BK, 1);
@@ -571,15 +945,9 @@ int launch_bn(const uint8_t* a8, const uint8_t* w8, GemmArgs& ga, cudaStream_t s
     if (rc) return rc;
   }
   cudaError_t e = cudaErrorInvalidValue;
-  if constexpr (BN == 128) {
-    if (ga.epilogue == EPI_QKROPE) e = launch_instance<128, EPI_QKROPE>(ta, tw, to, ga, grid, stream);
-    else if (ga.epilogue == FFB_EPI_BF16) e = launch_instance<128, FFB_EPI_BF16>(ta, tw, to, ga, grid, stream);
-    else if (ga.epilogue == FFB_EPI_F32_PARTIAL) e = launch_instance<128, FFB_EPI_F32_PARTIAL>(ta, tw, to, ga, grid, stream);
-  } else {
-    if (ga.epilogue == FFB_EPI_SWIGLU) e = launch_instance<256, FFB_EPI_SWIGLU>(ta, tw, to, ga, grid, stream);
-    else if (ga.epilogue == FFB_EPI_BF16) e = launch_instance<256, FFB_EPI_BF16>(ta, tw, to, ga, grid, stream);
-    else if (ga.epilogue == FFB_EPI_F32_PARTIAL) e = launch_instance<256, FFB_EPI_F32_PARTIAL>(ta, tw, to, ga, grid, stream);
-  }
+  if (pro == FFB_PRO_QUANT) e = launch_epi<BN, FFB_PRO_QUANT>(ta, tw, to, ga, grid, stream);
+  else if (pro == FFB_PRO_ADD_RMSNORM) e = launch_epi<BN, FFB_PRO_ADD_RMSNORM>(ta, tw, to, ga, grid, stream);
+  else e = launch_epi<BN, PRO_NONE>(ta, tw, to, ga, grid, stream);
   if (e != cudaSuccess) return ffb::fail(FFB_ECUDA, "ffb_fp8_gemm: launch: %s", cudaGetErrorString(e));
   return FFB_OK;
 }
@@ -595,11 +963,10 @@ int check_common(const uint8_t* a8, const float* a_scale, const uint8_t* w8, con
   return FFB_OK;
 }
 
-}  // namespace
-
-extern "C" int ffb_fp8_gemm(const uint8_t* a8, const float* a_scale, int a_per_row, const uint8_t* w8,
-                            const float* w_scale, int w_per_col, int epilogue, uint16_t* out, float* ws, int splits,
-                            int feature_tile, int M, int N, int K, void* stream) {
+// Validates the arguments of an FP8 GEMM and fills `ga`; returns the feature tile in bn.
+int prep_gemm(GemmArgs& ga, int& bn, const uint8_t* a8, const float* a_scale, int a_per_row, const uint8_t* w8,
+              const float* w_scale, int w_per_col, int epilogue, uint16_t* out, float* ws, int splits,
+              int feature_tile, int M, int N, int K) {
   int rc = check_common(a8, a_scale, w8, w_scale, M, N, K);
   if (rc) return rc;
   FFB_REQUIRE(epilogue == FFB_EPI_BF16 || epilogue == FFB_EPI_F32_PARTIAL || epilogue == FFB_EPI_SWIGLU,
@@ -612,11 +979,11 @@ extern "C" int ffb_fp8_gemm(const uint8_t* a8, const float* a_scale, int a_per_r
     FFB_REQUIRE(out != nullptr && ffb::aligned(out, 16), "ffb_fp8_gemm: out must be non-NULL, 16-byte aligned");
     FFB_REQUIRE(splits == 1, "ffb_fp8_gemm: splits must be 1 unless the epilogue is F32_PARTIAL");
   }
-  int bn = feature_tile > 0 ? feature_tile : (N % 256 == 0 ? 256 : 128);
+  bn = feature_tile > 0 ? feature_tile : (N % 256 == 0 ? 256 : 128);
   if (epilogue == FFB_EPI_SWIGLU) bn = 256;  // the gate/up interleave is per 128 channels
   FFB_REQUIRE(bn == 128 || bn == 256, "ffb_fp8_gemm: feature tile %d (128 or 256)", bn);
   FFB_REQUIRE(N % bn == 0, "ffb_fp8_gemm: N=%d must be a multiple of the feature tile %d", N, bn);
-  GemmArgs ga = {};
+  ga = GemmArgs{};
   ga.a_scale = a_scale;
   ga.w_scale = w_scale;
   ga.out = out;
@@ -628,24 +995,22 @@ extern "C" int ffb_fp8_gemm(const uint8_t* a8, const float* a_scale, int a_per_r
   ga.N = N;
   ga.K = K;
   ga.splits = splits;
-  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  return bn == 256 ? launch_bn<256>(a8, w8, ga, s) : launch_bn<128>(a8, w8, ga, s);
+  return FFB_OK;
 }
 
-extern "C" int ffb_fp8_gemm_qk_rope(const uint8_t* a8, const float* a_scale, int a_per_row, const uint8_t* w8,
-                                    const float* w_scale, int w_per_col, const uint16_t* q_norm,
-                                    const uint16_t* k_norm, float eps, const uint16_t* cos, const uint16_t* sin,
-                                    uint16_t* yq, uint16_t* yk, uint16_t* yv, int T, int HQ, int HK, int K,
-                                    void* stream) {
+int prep_rope(GemmArgs& ga, const uint8_t* a8, const float* a_scale, int a_per_row, const uint8_t* w8,
+              const float* w_scale, int w_per_col, const uint16_t* q_norm, const uint16_t* k_norm, float eps,
+              const uint16_t* cos, const uint16_t* sin, uint16_t* yq, uint16_t* yk, uint16_t* yv, int T, int HQ,
+              int HK, int K) {
+  FFB_REQUIRE(HQ > 0 && HK > 0 && HQ % HK == 0, "ffb_fp8_gemm_qk_rope: bad heads HQ=%d HK=%d", HQ, HK);
   const int N = (HQ + 2 * HK) * 128;
   int rc = check_common(a8, a_scale, w8, w_scale, T, N, K);
   if (rc) return rc;
   FFB_REQUIRE(q_norm && k_norm && cos && sin && yq && yk && yv, "ffb_fp8_gemm_qk_rope: NULL pointer");
-  FFB_REQUIRE(HQ > 0 && HK > 0 && HQ % HK == 0, "ffb_fp8_gemm_qk_rope: bad heads HQ=%d HK=%d", HQ, HK);
   FFB_REQUIRE(ffb::aligned(q_norm, 16) && ffb::aligned(k_norm, 16) && ffb::aligned(cos, 16) && ffb::aligned(sin, 16) &&
                   ffb::aligned(yq, 16) && ffb::aligned(yk, 16) && ffb::aligned(yv, 16),
               "ffb_fp8_gemm_qk_rope: 16-byte alignment");
-  GemmArgs ga = {};
+  ga = GemmArgs{};
   ga.a_scale = a_scale;
   ga.w_scale = w_scale;
   ga.a_per_row = a_per_row;
@@ -656,5 +1021,114 @@ extern "C" int ffb_fp8_gemm_qk_rope(const uint8_t* a8, const float* a_scale, int
   ga.K = K;
   ga.splits = 1;
   ga.rope = RopeSide{q_norm, k_norm, cos, sin, yq, yk, yv, eps, HQ, HK};
-  return launch_bn<128>(a8, w8, ga, reinterpret_cast<cudaStream_t>(stream));
+  return FFB_OK;
+}
+
+// Validates a fused prologue and fills ga.pro (ga.M / ga.K already set).
+int prep_prologue(GemmArgs& ga, const ffb_gemm_prologue* pro, uint8_t* a8, float* a_scale, int a_per_row) {
+  FFB_REQUIRE(pro != nullptr, "ffb_fp8_gemm_fused: NULL prologue");
+  FFB_REQUIRE(pro->kind == FFB_PRO_QUANT || pro->kind == FFB_PRO_ADD_RMSNORM, "ffb_fp8_gemm_fused: unknown kind %d",
+              pro->kind);
+  FFB_REQUIRE(pro->quant_mode == FFB_QUANT_STATIC || pro->quant_mode == FFB_QUANT_ROWWISE,
+              "ffb_fp8_gemm_fused: quant_mode must be STATIC or ROWWISE");
+  FFB_REQUIRE(a_per_row == (pro->quant_mode == FFB_QUANT_ROWWISE),
+              "ffb_fp8_gemm_fused: a_per_row must be 1 exactly when quant_mode is ROWWISE");
+  FFB_REQUIRE(pro->sync && ffb::aligned(pro->sync, 8), "ffb_fp8_gemm_fused: sync must be 8-byte aligned device words");
+  FFB_REQUIRE(pro->x && ffb::aligned(pro->x, 16), "ffb_fp8_gemm_fused: x must be non-NULL, 16-byte aligned");
+  const int K = ga.K, M = ga.M, NT = threads_of(0);
+  FFB_REQUIRE(K % 8 == 0, "ffb_fp8_gemm_fused: K=%d must be a multiple of 8", K);
+  FFB_REQUIRE(K / 8 <= pro_items(pro->kind) * NT, "ffb_fp8_gemm_fused: K=%d exceeds the prologue's %d", K,
+              pro_items(pro->kind) * NT * 8);
+  ProArgs& p = ga.pro;
+  p = ProArgs{};
+  p.x = pro->x;
+  p.quant_mode = pro->quant_mode;
+  p.inv = pro->inv_scale;
+  p.q8 = a8;
+  p.qscale = a_scale;
+  p.sync = pro->sync;
+  if (pro->kind == FFB_PRO_ADD_RMSNORM) {
+    FFB_REQUIRE(pro->norm_w && ffb::aligned(pro->norm_w, 16), "ffb_fp8_gemm_fused: norm_w must be 16-byte aligned");
+    p.w = pro->norm_w;
+    p.eps = pro->eps;
+    p.add = pro->add ? 1 : 0;
+    if (p.add) {
+      if (pro->b) {
+        FFB_REQUIRE(ffb::aligned(pro->b, 16), "ffb_fp8_gemm_fused: b must be 16-byte aligned");
+        p.b = pro->b;
+      } else if (pro->b32) {
+        FFB_REQUIRE(ffb::aligned(pro->b32, 16), "ffb_fp8_gemm_fused: b32 must be 16-byte aligned");
+        FFB_REQUIRE(pro->splits >= 1 && pro->splits <= PRO_MAX_SPLITS, "ffb_fp8_gemm_fused: splits=%d outside [1, %d]",
+                    pro->splits, PRO_MAX_SPLITS);
+        p.b32 = pro->b32;
+        p.splits = pro->splits;
+      }
+      FFB_REQUIRE(p.b || p.b32, "ffb_fp8_gemm_fused: add needs b or b32");
+      if (pro->deep) {
+        FFB_REQUIRE(ffb::aligned(pro->deep, 16), "ffb_fp8_gemm_fused: deep must be 16-byte aligned");
+        FFB_REQUIRE(pro->start >= 0 && pro->nv >= 0 && pro->start + pro->nv <= M,
+                    "ffb_fp8_gemm_fused: deep rows [%d, %d) outside [0, %d)", pro->start, pro->start + pro->nv, M);
+        p.deep = pro->deep;
+        p.start = pro->start;
+        p.nv = pro->nv;
+      }
+      if (pro->residual) {
+        FFB_REQUIRE(ffb::aligned(pro->residual, 16), "ffb_fp8_gemm_fused: residual must be 16-byte aligned");
+        p.residual = pro->residual;
+      }
+    }
+  }
+  return FFB_OK;
+}
+
+}  // namespace
+
+extern "C" int ffb_fp8_gemm(const uint8_t* a8, const float* a_scale, int a_per_row, const uint8_t* w8,
+                            const float* w_scale, int w_per_col, int epilogue, uint16_t* out, float* ws, int splits,
+                            int feature_tile, int M, int N, int K, void* stream) {
+  GemmArgs ga;
+  int bn = 0;
+  int rc = prep_gemm(ga, bn, a8, a_scale, a_per_row, w8, w_scale, w_per_col, epilogue, out, ws, splits, feature_tile,
+                     M, N, K);
+  if (rc) return rc;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  return bn == 256 ? launch_bn<256>(a8, w8, ga, PRO_NONE, s) : launch_bn<128>(a8, w8, ga, PRO_NONE, s);
+}
+
+extern "C" int ffb_fp8_gemm_fused(const ffb_gemm_prologue* pro, uint8_t* a8, float* a_scale, int a_per_row,
+                                  const uint8_t* w8, const float* w_scale, int w_per_col, int epilogue, uint16_t* out,
+                                  float* ws, int splits, int feature_tile, int M, int N, int K, void* stream) {
+  GemmArgs ga;
+  int bn = 0;
+  int rc = prep_gemm(ga, bn, a8, a_scale, a_per_row, w8, w_scale, w_per_col, epilogue, out, ws, splits, feature_tile,
+                     M, N, K);
+  if (!rc) rc = prep_prologue(ga, pro, a8, a_scale, a_per_row);
+  if (rc) return rc;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  return bn == 256 ? launch_bn<256>(a8, w8, ga, pro->kind, s) : launch_bn<128>(a8, w8, ga, pro->kind, s);
+}
+
+extern "C" int ffb_fp8_gemm_qk_rope(const uint8_t* a8, const float* a_scale, int a_per_row, const uint8_t* w8,
+                                    const float* w_scale, int w_per_col, const uint16_t* q_norm,
+                                    const uint16_t* k_norm, float eps, const uint16_t* cos, const uint16_t* sin,
+                                    uint16_t* yq, uint16_t* yk, uint16_t* yv, int T, int HQ, int HK, int K,
+                                    void* stream) {
+  GemmArgs ga;
+  int rc = prep_rope(ga, a8, a_scale, a_per_row, w8, w_scale, w_per_col, q_norm, k_norm, eps, cos, sin, yq, yk, yv, T,
+                     HQ, HK, K);
+  if (rc) return rc;
+  return launch_bn<128>(a8, w8, ga, PRO_NONE, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int ffb_fp8_gemm_qk_rope_fused(const ffb_gemm_prologue* pro, uint8_t* a8, float* a_scale, int a_per_row,
+                                          const uint8_t* w8, const float* w_scale, int w_per_col,
+                                          const uint16_t* q_norm, const uint16_t* k_norm, float eps,
+                                          const uint16_t* cos, const uint16_t* sin, uint16_t* yq, uint16_t* yk,
+                                          uint16_t* yv, int T, int HQ, int HK, int K, void* stream) {
+  GemmArgs ga;
+  int rc = prep_rope(ga, a8, a_scale, a_per_row, w8, w_scale, w_per_col, q_norm, k_norm, eps, cos, sin, yq, yk, yv, T,
+                     HQ, HK, K);
+  if (!rc) rc = prep_prologue(ga, pro, a8, a_scale, a_per_row);
+  if (rc) return rc;
+  return launch_bn<128>(a8, w8, ga, pro->kind, reinterpret_cast<cudaStream_t>(stream));
 }

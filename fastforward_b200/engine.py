@@ -16,6 +16,7 @@ and takes the log-softmax over the k choices.  `Engine.capture` records the whol
 sequence into one CUDA graph per request geometry (bucket, image window, k), replayed
 with the request's ids / visual rows / deepstack rows / pick copied into static buffers.
 """
+import ctypes
 import math
 from dataclasses import dataclass, field
 
@@ -184,6 +185,11 @@ def pick_feature_tile(n):
     return 256 if n % 256 == 0 else 128
 
 
+# Largest K-split of a plan: the consumers of the fp32 partials (add+RMSNorm, standalone or
+# as a fused GEMM prologue) sum at most this many.
+MAX_PLAN_SPLITS = 8
+
+
 def plan_splits(m, n, k, bn=None, allow_split=True, sms=SMS):
     """K-split count that minimises (waves x k-blocks per CTA) plus a small per-split cost
     for the fp32 partial tiles the consumer has to read back."""
@@ -193,7 +199,7 @@ def plan_splits(m, n, k, bn=None, allow_split=True, sms=SMS):
     if not allow_split:
         return 1
     best, best_cost = 1, None
-    for s in range(1, min(nkb, 16) + 1):
+    for s in range(1, min(nkb, MAX_PLAN_SPLITS) + 1):
         waves = math.ceil(base * s / sms)
         cost = waves * (math.ceil(nkb / s) + 1.5) + (0.0 if s == 1 else 0.4 * s * m * n / (2048 * 320))
         if best_cost is None or cost < best_cost - 1e-9:
@@ -239,6 +245,7 @@ class Buffers:
         self.hp = z(1, h)
         self.res1 = z(1, h)
         self.mlp1 = z(1, h)
+        self.sync = z(2, dt=torch.int32)  # grid-barrier words of the fused GEMM prologues
         self.logits = z(8, dt=torch.float32)
         self.logprobs = z(8, dt=torch.float32)
         if mode == "int4":
@@ -249,9 +256,17 @@ class Buffers:
 class Engine:
     """Runs prefill + choice scoring for one packed model on one device."""
 
-    def __init__(self, model: PackedModel, pdl=True, autotune=True, tp_group=None):
+    def __init__(self, model: PackedModel, pdl=True, autotune=True, tp_group=None, fuse="tail"):
         """tp_group: the torch.distributed (NCCL) group of a tensor-parallel model
-        (`PackedModel(tp=...)`); o_proj and down_proj partial sums are all-reduced in it."""
+        (`PackedModel(tp=...)`); o_proj and down_proj partial sums are all-reduced in it.
+        fuse (FP8 modes): where an activation quantiser or an add+RMSNorm runs as the fused
+        prologue of the GEMM that consumes it (`ffb_fp8_gemm_fused`) instead of a launch of
+        its own -- "tail": in the one-row tail only (where the row work is a few hundred
+        elements and the launch is the whole cost); "all" (or True): everywhere, five
+        launches per layer instead of nine; "none" (or False): nowhere.  Every choice
+        computes the same bytes.  At T = 320 the separate row kernels are faster than the
+        prologues (which run the same row work on fewer warps per row, then meet at a grid
+        barrier), hence the default."""
         L.require_cuda()
         self.m = model
         self.d = model.dims
@@ -266,6 +281,10 @@ class Engine:
         self.plans = {}
         self.autotune_enabled = autotune and model.mode != "int4"
         self.tuned = {}
+        mode_ = {True: "all", False: "none"}.get(fuse, fuse)
+        if mode_ not in ("none", "tail", "all"):
+            raise ValueError(f"fuse must be 'none', 'tail' or 'all', not {fuse!r}")
+        self.fuse = "none" if model.mode == "int4" else mode_
         L.set_pdl(pdl)
 
     # ------------------------------------------------------------------ plans / buffers
@@ -299,7 +318,7 @@ class Engine:
                 self._autotune(T)
         return self.buffers[T]
 
-    MAX_SPLITS = 8
+    MAX_SPLITS = MAX_PLAN_SPLITS
 
     def _autotune(self, T, reps=5):
         """Times candidate (token tile, K-split) choices of every GEMM of the forward on this
@@ -358,6 +377,38 @@ class Engine:
              ptr(ws) if plan.epilogue == L.EPI_F32_PARTIAL else None, plan.splits, plan.bn, plan.m, plan.n, plan.k,
              self._s)
 
+    def _pro_quant(self, x, qmode, inv, b):
+        """Prologue quantising bf16 rows x (the former ffb_quantize_fp8 launch)."""
+        return L.Prologue(kind=L.PRO_QUANT, x=ptr(x), quant_mode=qmode, inv_scale=float(inv), sync=ptr(b.sync))
+
+    def _pro_norm(self, a, bsum, deep, start, nv, w, qmode, inv, residual, b):
+        """Prologue add(+partials, +deepstack) + RMSNorm + quantisation (the former
+        ffb_add_rmsnorm / ffb_rmsnorm launch); bsum = (b, b32, splits) or None (no add)."""
+        p = L.Prologue(kind=L.PRO_ADD_RMSNORM, x=ptr(a), norm_w=ptr(w), eps=float(self.d.eps), quant_mode=qmode,
+                       inv_scale=float(inv), sync=ptr(b.sync))
+        if bsum is not None:
+            p.add = 1
+            p.b, p.b32, p.splits = bsum
+            p.residual = ptr(residual)
+            if deep is not None:
+                p.deep, p.start, p.nv = ptr(deep), int(start), int(nv)
+        return p
+
+    def _gemm_fused(self, pro, plan, a8, ascale, lin, out, ws, per_row):
+        call("ffb_fp8_gemm_fused", ctypes.addressof(pro), ptr(a8), ptr(ascale), int(per_row), ptr(lin["w8"]),
+             ptr(lin["scale"]), int(lin["scale"].numel() > 1), plan.epilogue,
+             ptr(out) if plan.epilogue != L.EPI_F32_PARTIAL else None,
+             ptr(ws) if plan.epilogue == L.EPI_F32_PARTIAL else None, plan.splits, plan.bn, plan.m, plan.n, plan.k,
+             self._s)
+
+    def _qkv_fused(self, pro, b, lay, cos, sin, T, rowwise):
+        d = self.d
+        lin = lay.lin["qkv"]
+        call("ffb_fp8_gemm_qk_rope_fused", ctypes.addressof(pro), ptr(b.x8), ptr(b.xs if rowwise else lay.ascale["qkv"]),
+             int(rowwise), ptr(lin["w8"]), ptr(lin["scale"]), int(lin["scale"].numel() > 1), ptr(lay.q_norm),
+             ptr(lay.k_norm), float(d.eps), ptr(cos), ptr(sin), ptr(b.yq), ptr(b.yk), ptr(b.yv), T, d.hq, d.hk,
+             d.hidden, self._s)
+
     def _w4(self, plan, x, lin, out, ws):
         call("ffb_w4a16_gemm", ptr(x), ptr(lin["packed"]), ptr(lin["scales"]), plan.epilogue,
              ptr(out) if plan.epilogue != L.EPI_F32_PARTIAL else None,
@@ -402,6 +453,8 @@ class Engine:
         (ROLES order), the largest per-token activation scale max|x|/448 entering that
         linear (calibration).
         Results land in b.logits [8] / b.logprobs [:k]."""
+        if self.fuse == "all":
+            return self._enqueue_fused(T, image_start, nv, grid_h, grid_w, k, visual, deep, b, on_layer, observe)
         d, m = self.d, self.m
         b = b or self.buffers_for(T)
         pl = self._plans(T)
@@ -492,6 +545,8 @@ class Engine:
             on_layer(depth - 1, h_cur)
         lay = m.layers[depth - 1]
         self._qkv(pl[("full", "qkv")], b, lay, cos, sin, T, int4, rowwise)
+        if self.fuse == "tail":
+            return self._tail_fused(b, h_cur, k, obs, sa, qmode)
         call("ffb_attention", ptr(b.yq), ptr(b.yk), ptr(b.yv), ptr(b.pick), 1, ptr(b.attn), 1, T, HQ, HK, scale,
              self._s)
         p = pl[("tail", "o")]
@@ -529,11 +584,114 @@ class Engine:
              ptr(b.logits), ptr(b.logprobs), H, self._s)
         return b
 
+    def _enqueue_fused(self, T, image_start, nv, grid_h, grid_w, k, visual, deep, b, on_layer, observe):
+        """`enqueue` with every row kernel of a decoder layer fused into the GEMM after it:
+        per layer qkv(+add/RMSNorm prologue, QK-norm/RoPE epilogue), attention,
+        o(+quant prologue), gate/up(+add/RMSNorm prologue, SwiGLU epilogue),
+        down(+quant prologue); the add+RMSNorm of the down output is the next layer's qkv
+        prologue (the first layer's is the plain RMSNorm of the embeddings)."""
+        d, m = self.d, self.m
+        b = b or self.buffers_for(T)
+        pl = self._plans(T)
+        self._s = torch.cuda.current_stream(self.device).cuda_stream
+        cos, sin = self.rope_tables(T, image_start, grid_h, grid_w)
+        H, D, HQ, HK, I = d.hidden, d.d, d.hq, d.hk, d.inter
+        eps = float(d.eps)
+        rowwise = m.mode == "rowwise"
+        qmode = L.QUANT_ROWWISE if rowwise else L.QUANT_STATIC
+        scale = D ** -0.5
+        if observe is not None and not rowwise:
+            raise ValueError("activation observation needs the rowwise (per-token scale) forward")
+
+        def sa(lay_, role, rowbuf):
+            return rowbuf if rowwise else lay_.ascale[role]
+
+        def obs(j, role, scales, rows):
+            if observe is not None:
+                r = ROLES.index(role)
+                observe[j, r] = torch.maximum(observe[j, r], scales[:rows].amax())
+
+        call("ffb_embed_gather", ptr(b.ids), ptr(m.embed), d.vocab, ptr(visual), image_start,
+             nv if visual is not None else 0, ptr(b.hA), T, H, self._s)
+        h_cur, h_mid = b.hA, b.hB
+        depth = m.depth
+        # the qkv prologue of layer 0: RMSNorm of the embeddings
+        pro = self._pro_norm(h_cur, None, None, 0, 0, m.layers[0].in_norm, qmode, m.layers[0].inv["qkv"], None, b)
+        for j in range(depth):
+            lay = m.layers[j]
+            self._qkv_fused(pro, b, lay, cos, sin, T, rowwise)
+            obs(j, "qkv", b.xs, T)
+            if on_layer is not None:  # the residual entering layer j (written by the prologue above)
+                on_layer(j, h_cur)
+            if j == depth - 1:
+                break
+            nxt = m.layers[j + 1]
+            call("ffb_attention", ptr(b.yq), ptr(b.yk), ptr(b.yv), None, 0, ptr(b.attn), T, T, HQ, HK, scale,
+                 self._s)
+            p = pl[("full", "o")]
+            self._gemm_fused(self._pro_quant(b.attn, qmode, lay.inv["o"], b), p, b.o8, sa(lay, "o", b.os),
+                             lay.lin["o"], b.lin_out, b.ws, rowwise)
+            obs(j, "o", b.os, T)
+            self._tp_reduce(p, b.ws)
+            pro = self._pro_norm(h_cur, self._split_args(p, b.lin_out, b.ws), None, 0, 0, lay.post_norm, qmode,
+                                 lay.inv["gateup"], h_mid, b)
+            self._gemm_fused(pro, pl[("full", "gateup")], b.post8, sa(lay, "gateup", b.posts), lay.lin["gateup"],
+                             b.act, b.ws, rowwise)
+            obs(j, "gateup", b.posts, T)
+            p = pl[("full", "down")]
+            self._gemm_fused(self._pro_quant(b.act, qmode, lay.inv["down"], b), p, b.act8, sa(lay, "down", b.acts),
+                             lay.lin["down"], b.lin_out, b.ws, rowwise)
+            obs(j, "down", b.acts, T)
+            self._tp_reduce(p, b.ws)
+            dp = deep[j] if (deep is not None and j < len(deep)) else None
+            pro = self._pro_norm(h_mid, self._split_args(p, b.lin_out, b.ws), dp, image_start,
+                                 nv if dp is not None else 0, nxt.in_norm, qmode, nxt.inv["qkv"], h_cur, b)
+        # ---- tail: last layer on the pick row (night_runtime.py:92-105); its qkv ran above
+        return self._tail_fused(b, h_cur, k, obs, sa, qmode)
+
+    def _tail_fused(self, b, h_cur, k, obs, sa, qmode):
+        """The last layer after its full-T qkv (`_family/night_runtime.py:92-105`): attention,
+        o_proj, MLP and readout on the pick row, with the one-row quantisers and the
+        add+RMSNorm as fused GEMM prologues."""
+        d, m = self.d, self.m
+        T = b.ids.shape[0]
+        pl = self._plans(T)
+        H, D, HQ, HK = d.hidden, d.d, d.hq, d.hk
+        rowwise = m.mode == "rowwise"
+        depth = m.depth
+        lay = m.layers[depth - 1]
+        call("ffb_attention", ptr(b.yq), ptr(b.yk), ptr(b.yv), ptr(b.pick), 1, ptr(b.attn), 1, T, HQ, HK, D ** -0.5,
+             self._s)
+        p = pl[("tail", "o")]
+        self._gemm_fused(self._pro_quant(b.attn, qmode, lay.inv["o"], b), p, b.o8, sa(lay, "o", b.os), lay.lin["o"],
+                         b.lin_out, b.ws, rowwise)
+        obs(depth - 1, "o", b.os, 1)
+        self._tp_reduce(p, b.ws)
+        ob, o32, os_ = self._split_args(p, b.lin_out, b.ws)
+        call("ffb_gather_rows", ptr(h_cur), ptr(b.pick), ptr(b.hp), 1, H * 2, self._s)
+        pro = self._pro_norm(b.hp, (ob, o32, os_), None, 0, 0, lay.post_norm, qmode, lay.inv["gateup"], b.res1, b)
+        self._gemm_fused(pro, pl[("tail", "gateup")], b.post8, sa(lay, "gateup", b.posts), lay.lin["gateup"], b.act,
+                         b.ws, rowwise)
+        obs(depth - 1, "gateup", b.posts, 1)
+        p = pl[("tail", "down")]
+        self._gemm_fused(self._pro_quant(b.act, qmode, lay.inv["down"], b), p, b.act8, sa(lay, "down", b.acts),
+                         lay.lin["down"], b.mlp1, b.ws, rowwise)
+        obs(depth - 1, "down", b.acts, 1)
+        self._tp_reduce(p, b.ws)
+        mb, m32, ms = self._split_args(p, b.mlp1, b.ws)
+        call("ffb_readout", ptr(b.res1), mb, m32, ms, ptr(m.final_norm), float(d.eps), ptr(m.head), m.head.shape[0],
+             int(k), ptr(b.logits), ptr(b.logprobs), H, self._s)
+        return b
+
     def launches_per_forward(self):
         """Kernel launches `enqueue` issues (for the bench's gpu_launches count)."""
+        tail = 6 if self.fuse != "none" else 9  # attention, (quant,) o, gather, (add+norm,) gate/up, (quant,) down, readout
+        if self.fuse == "all":  # embed, 5 per layer, the last layer's qkv, tail
+            return 1 + 5 * (self.m.depth - 1) + 1 + tail
         per_layer = 9 if self.m.mode != "int4" else 8
-        tail = 10 if self.m.mode != "int4" else 9
-        return 2 + per_layer * (self.m.depth - 1) + tail
+        if self.m.mode == "int4":
+            tail = 8
+        return 2 + per_layer * (self.m.depth - 1) + 1 + tail
 
     # ------------------------------------------------------------------ request I/O
     def stage(self, T, ids, visual, pick):

@@ -172,6 +172,56 @@ int ffb_fp8_gemm_qk_rope(const uint8_t* a8, const float* a_scale, int a_per_row,
                          uint16_t* yq, uint16_t* yk, uint16_t* yv,
                          int T, int HQ, int HK, int K, void* stream);
 
+/* Producers fused into the front of an FP8 GEMM (ffb_fp8_gemm_fused,
+ * ffb_fp8_gemm_qk_rope_fused).  The GEMM's CTAs first compute its FP8 activation operand
+ * a8 (and the per-row scales) from bf16 rows, each CTA a slice of the M rows, then meet
+ * at a bounded grid-wide barrier and run the GEMM on the rows just written: the pair
+ * costs one launch instead of two, with results bit-identical to the separate calls. */
+#define FFB_PRO_QUANT 1        /* a8 = ffb_quantize_fp8(x)                                         */
+#define FFB_PRO_ADD_RMSNORM 2  /* a8 = the q8 output of ffb_add_rmsnorm(x, b | b32, deep, norm_w)  */
+
+typedef struct ffb_gemm_prologue {
+  int kind;                /* FFB_PRO_QUANT or FFB_PRO_ADD_RMSNORM                          */
+  const uint16_t* x;       /* QUANT: bf16 [M,K] to quantise; ADD_RMSNORM: residual input a  */
+  const uint16_t* b;       /* ADD_RMSNORM: bf16 addend [M,K], or NULL (then b32 / no add)   */
+  const float* b32;        /* ADD_RMSNORM: fp32 split-K partials [splits][M][K] if b is NULL */
+  int splits;              /* 1..8 partial tiles in b32                                     */
+  int add;                 /* ADD_RMSNORM: 0 = plain RMSNorm of x (ffb_rmsnorm)             */
+  const uint16_t* deep;    /* ADD_RMSNORM: deepstack rows [nv,K] added to [start, start+nv) */
+  int start, nv;
+  const uint16_t* norm_w;  /* ADD_RMSNORM: RMSNorm weight [K]                               */
+  float eps;
+  uint16_t* residual;      /* ADD_RMSNORM: bf16 residual rows out (may be NULL)             */
+  int quant_mode;          /* FFB_QUANT_STATIC or FFB_QUANT_ROWWISE                         */
+  float inv_scale;         /* STATIC: multiplier applied before the e4m3 cast               */
+  uint64_t* sync;          /* one 8-byte device word, zero before the first call; one word
+                              per stream (calls on different streams must not share it);
+                              zero it again after a FFB_ETIMEOUT device error              */
+} ffb_gemm_prologue;
+
+/* ffb_fp8_gemm whose activation operand is produced by the fused prologue `pro`:
+ * replaces ffb_quantize_fp8 (or ffb_add_rmsnorm / ffb_rmsnorm with FP8 output) followed by
+ * ffb_fp8_gemm - in the reference, `quantize_rows` / `_runtime_scale`
+ * (_legacy/fp8_private.py:11-18, _family/depth_fp8.py:8-12) or `add_rms`
+ * (_legacy/lower_kernels.py:24-32) followed by the linear (_family/depth_fp8.py:22-26).
+ * a8 [M,K] and a_scale ([M] when ROWWISE, written here; the per-tensor device scale when
+ * STATIC, read) are the prologue's outputs and the GEMM's inputs; a_per_row must equal
+ * (pro->quant_mode == FFB_QUANT_ROWWISE).  K must be a multiple of 8 and at most 36864
+ * (QUANT) or 9216 (ADD_RMSNORM).  Other arguments as ffb_fp8_gemm. */
+int ffb_fp8_gemm_fused(const ffb_gemm_prologue* pro, uint8_t* a8, float* a_scale, int a_per_row,
+                       const uint8_t* w8, const float* w_scale, int w_per_col,
+                       int epilogue, uint16_t* out, float* ws, int splits, int feature_tile,
+                       int M, int N, int K, void* stream);
+
+/* ffb_fp8_gemm_qk_rope with the fused prologue `pro` (as ffb_fp8_gemm_fused): replaces the
+ * add_rms / rms_one of the layer input, its quantisation, and the qkv linear + qk_pair. */
+int ffb_fp8_gemm_qk_rope_fused(const ffb_gemm_prologue* pro, uint8_t* a8, float* a_scale, int a_per_row,
+                               const uint8_t* w8, const float* w_scale, int w_per_col,
+                               const uint16_t* q_norm, const uint16_t* k_norm, float eps,
+                               const uint16_t* cos, const uint16_t* sin,
+                               uint16_t* yq, uint16_t* yk, uint16_t* yv,
+                               int T, int HQ, int HK, int K, void* stream);
+
 /* Reorders the rows of a [2I,K] gate/up weight (gate rows 0..I-1, up rows I..2I-1) into
  * the FFB_EPI_SWIGLU tile order: tile t = gate rows 128t..128t+127 then up rows
  * 128t..128t+127 (I must be a multiple of 128).  Works on rows of `elem_bytes`*K bytes:

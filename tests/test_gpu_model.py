@@ -116,7 +116,9 @@ def test_layer_ops_teacher_forced(name, mode):
     from tests._util import assert_bf16_near, assert_bytes_equal
     dims, src, req, layout = small_case(MODELS[name], 2, vocab=4096)
     prof = _profile(dims, src, req, layout) if mode == "static" else None
-    eng = Engine(PackedModel(dims, src, mode=mode, device=DEV, profile=prof), autotune=False)
+    # unfused launches, so every intermediate buffer still holds layer 0's values when the
+    # hook for layer 1 runs (the fused forward is bit-identical: tests/test_gpu_fused.py)
+    eng = Engine(PackedModel(dims, src, mode=mode, device=DEV, profile=prof), autotune=False, fuse=False)
     T = layout.bucket
     eng.buffers_for(T)
     for key, p in eng.plans[T].items():          # keep every GEMM output in its bf16 buffer
