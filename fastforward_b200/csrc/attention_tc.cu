@@ -5,21 +5,25 @@
 // in fp32 scaled by 1/sqrt(128); online softmax over 64-key blocks (running max m,
 // denominator l = l * alpha + sum(p), accumulator acc = acc * alpha + P.V with
 // alpha = exp(m_old - m_new)); P cast to bf16 before its product with V; output
-// bf16(acc / l).  Keys past the query's position (and past T) are masked.
+// bf16(acc / l).  Keys past the query's position (and past T) are masked.  Exponentials
+// are 2^(x * log2 e - m) on the special-function unit, as the reference's tl.exp; the final
+// quotient is correctly rounded before the bf16 cast.
 //
-// One CTA = 128 query rows of one head (the M of the MMA); 320 threads:
+// One CTA = 128 query rows of one head (the M of the MMA); 576 threads:
 //   warp 0     TMA producer: the Q tile once ([128 x 128] as two 64-column swizzled
 //              halves), K and V blocks of 64 keys into a ring of KV_STAGES slots;
 //   warp 1     TMEM allocator + single-thread MMA issuer:
 //                S_j = Q . K_j^T  (M 128, N 64, 8 x K16, both operands K-major) -> TMEM;
 //                O_j = P_j . V_j  (M 128, N 128, 4 x K16; V read MN-major straight from
 //                                  its row-major [key][d] tile) -> TMEM;
-//   warps 2..9 softmax, two threads per query row (TMEM lane quarter = warp % 4; warps w
-//              and w + 4 share a quarter): each reads 32 of the block's 64 scores, the two
-//              exchange their row maxima through shared memory, each writes its half of
-//              the bf16 P row into a swizzled [128 x 64] tile, keeps its own part of the
-//              denominator (same alpha) and folds its 64 columns of the previous block's O
-//              into an fp32 accumulator in registers (o = o * alpha + O, one block late).
+//   warps 2..17 softmax, four threads per query row (TMEM lane quarter = warp % 4; the four
+//              warps of a quarter are its parts 0..3): part p reads keys [16p, 16p + 16) of
+//              the block's 64 scores, the four exchange their row maxima through shared
+//              memory, each writes its 16 bf16 P values into the swizzled [128 x 64] P tile,
+//              keeps its own part of the denominator (same alpha) and folds output
+//              columns [32p, 32p + 32) of the previous block's O into fp32 registers
+//              (o = o * alpha + O, one block late).  At the end the rows' quotients are
+//              staged in shared memory (the P tiles, by then free) and leave by TMA store.
 // S, P and O are double-buffered: the MMA warp issues S_{j+2} as soon as the softmax has
 // read S_j and P_j . V_j as soon as P_j is written, so the tensor core works on the next
 // blocks while the softmax runs.  Barriers: q_full, kv_full/kv_empty[stage],
@@ -38,10 +42,31 @@ constexpr int Q_HALF = BM * 128;    // one 64-column half of the Q tile: 16 KB
 constexpr int KV_HALF = BN * 128;   // one 64-column half of a K or V block: 8 KB
 constexpr int STAGE = 4 * KV_HALF;  // K (2 halves) + V (2 halves)
 constexpr int P_BYTES = BM * 128;   // [128 x 64] bf16
-constexpr int THREADS = 320;
-constexpr int XCH_BYTES = 2 * 2 * BM * 4;  // row-max exchange [2 buffers][2 halves][128 rows]
+constexpr int SOFTMAX_WARPS = 16;
+constexpr int THREADS = 64 + SOFTMAX_WARPS * 32;
+constexpr int XCH_BYTES = 2 * 4 * BM * 4;  // row exchange [2 buffers][4 parts][128 rows]
 constexpr int SMEM = 2 * Q_HALF + KV_STAGES * STAGE + 2 * P_BYTES + XCH_BYTES + 256 + 1024;
 constexpr int TMEM_COLS = 512;      // S[b] at column 64b (64 wide), O[b] at 128 + 128b (128 wide)
+
+// 2^x on the special-function unit (ex2.approx: relative error ~2^-22, well inside the
+// bf16 rounding of P).  The reference's `tl.exp` lowers to the same instruction.
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// bf16(o / l) with the quotient correctly rounded to fp32 first.  y = o * (1/l) (the
+// reciprocal correctly rounded) is within 3 fp32 ulps of the rounded quotient q, so bf16(y)
+// and bf16(q) agree unless y lies within 3 ulps of a bf16 rounding midpoint (the fp32
+// values whose 16 low bits are 0x8000); those, and quotients near the fp32 subnormal
+// range, take the IEEE divide.
+__device__ __forceinline__ uint16_t bf16_quotient(float o, float l, float rl) {
+  float y = o * rl;
+  const int d = (int)(__float_as_uint(y) & 0xFFFFu) - 0x8000;
+  if ((d > -4 && d < 4) || fabsf(y) < 1e-30f) y = __fdiv_rn(o, l);
+  return f2bf(y);
+}
 
 struct TcArgs {
   uint16_t* out;
@@ -51,7 +76,8 @@ struct TcArgs {
 
 __global__ void __launch_bounds__(THREADS, 1)
     attention_tc_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_k,
-                        const __grid_constant__ CUtensorMap tmap_v, const TcArgs args) {
+                        const __grid_constant__ CUtensorMap tmap_v, const __grid_constant__ CUtensorMap tmap_o,
+                        const TcArgs args) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sq = smem;                          // [2][128 x 128 B]
@@ -65,7 +91,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint64_t* s_free = s_full + 2;            // [2]
   uint64_t* p_full = s_free + 2;            // [2]
   uint64_t* o_full = p_full + 2;            // [2]
-  uint64_t* x_bar = o_full + 2;             // [4]: one per lane quarter, two arrivals
+  uint64_t* x_bar = o_full + 2;             // [4]: one per lane quarter, four arrivals
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(x_bar + 4);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -84,11 +110,11 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&s_full[b], 1);
-      mbar_init(&s_free[b], 8);
-      mbar_init(&p_full[b], 8);
+      mbar_init(&s_free[b], SOFTMAX_WARPS);
+      mbar_init(&p_full[b], SOFTMAX_WARPS);
       mbar_init(&o_full[b], 1);
     }
-    for (int q = 0; q < 4; ++q) mbar_init(&x_bar[q], 2);
+    for (int q = 0; q < 4; ++q) mbar_init(&x_bar[q], 4);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -96,6 +122,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     tma_prefetch_desc(&tmap_q);
     tma_prefetch_desc(&tmap_k);
     tma_prefetch_desc(&tmap_v);
+    tma_prefetch_desc(&tmap_o);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, TMEM_COLS);
@@ -180,39 +207,42 @@ __global__ void __launch_bounds__(THREADS, 1)
   } else {
     // ------------------------------------------------------------------ softmax
     const int quarter = warp & 3;
-    const int hc = (warp - 2) >> 2;     // which half: keys [32hc, 32hc+32), columns [64hc, 64hc+64)
+    const int part = (warp - 2) >> 2;   // keys [16 part, 16 part + 16), output columns [32 part, 32 part + 32)
     const int r = quarter * 32 + lane;  // this thread's query row in the tile
     const int qpos = q0 + r;
     const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
-    float o[D / 2];
+    float o[D / 4];
 #pragma unroll
-    for (int i = 0; i < D / 2; ++i) o[i] = 0.f;
+    for (int i = 0; i < D / 4; ++i) o[i] = 0.f;
     float m = -INFINITY, l = 0.f, alpha_prev = 0.f;
     int xph = 0;  // phases of this quarter's exchange barrier used so far
-    // The partner thread's value of the row (written to xch[buffer][half][row] by both).
-    auto exchange = [&](float mine) -> float {
-      float* slot = xch + (xph & 1) * 2 * BM;
-      slot[hc * BM + r] = mine;
+    // The four parts' values of the row (written to xch[buffer][part][row] by each), in part order.
+    auto exchange = [&](float mine, float (&all)[4]) -> bool {
+      float* slot = xch + (xph & 1) * 4 * BM;
+      slot[part * BM + r] = mine;
       __syncwarp();
       if (lane == 0) mbar_arrive(&x_bar[quarter]);
-      float other = 0.f;
-      if (mbar_wait_bounded(&x_bar[quarter], (uint32_t)xph & 1u, abort_flag)) other = slot[(hc ^ 1) * BM + r];
-      else *abort_flag = 1;
+      const bool got = mbar_wait_bounded(&x_bar[quarter], (uint32_t)xph & 1u, abort_flag);
       ++xph;
-      return other;
+#pragma unroll
+      for (int p2 = 0; p2 < 4; ++p2) all[p2] = got ? slot[p2 * BM + r] : 0.f;
+      return got;
     };
-    // o = o * alpha + O_j for this thread's 64 columns (the fold of block j's P.V)
+    // o = o * alpha + O_j for this thread's 32 output columns (the fold of block j's P.V)
     auto fold = [&](int j, float alpha) -> bool {
       if (!(mbar_wait_bounded(&o_full[j & 1], (uint32_t)(j >> 1) & 1u, abort_flag) && !*abort_flag)) return false;
       tc_fence_after();
+      uint32_t t0[16], t1[16];
+      const uint32_t oa = tmem + lane_addr + 128 + 128 * (j & 1) + 32 * part;
+      tmem_ld16_async(oa, t0);
+      tmem_ld16_async(oa + 16, t1);
+      tmem_wait_ld();
+      reg_fence(t0);
+      reg_fence(t1);
 #pragma unroll
-      for (int c = 0; c < D / 2; c += 16) {
-        uint32_t t16[16];
-        tmem_ld16_async(tmem + lane_addr + 128 + 128 * (j & 1) + 64 * hc + (uint32_t)c, t16);
-        tmem_wait_ld();
-        reg_fence(t16);
-#pragma unroll
-        for (int i = 0; i < 16; ++i) o[c + i] = o[c + i] * alpha + __uint_as_float(t16[i]);
+      for (int i = 0; i < 16; ++i) {
+        o[i] = o[i] * alpha + __uint_as_float(t0[i]);
+        o[16 + i] = o[16 + i] * alpha + __uint_as_float(t1[i]);
       }
       tc_fence_before();
       return true;
@@ -225,51 +255,61 @@ __global__ void __launch_bounds__(THREADS, 1)
         break;
       }
       tc_fence_after();
-      uint32_t sr[32];
-      asm volatile("tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-                   : "=r"(sr[0]), "=r"(sr[1]), "=r"(sr[2]), "=r"(sr[3]), "=r"(sr[4]), "=r"(sr[5]), "=r"(sr[6]), "=r"(sr[7]), "=r"(sr[8]), "=r"(sr[9]), "=r"(sr[10]), "=r"(sr[11]), "=r"(sr[12]), "=r"(sr[13]), "=r"(sr[14]), "=r"(sr[15]), "=r"(sr[16]), "=r"(sr[17]), "=r"(sr[18]), "=r"(sr[19]), "=r"(sr[20]), "=r"(sr[21]), "=r"(sr[22]), "=r"(sr[23]), "=r"(sr[24]), "=r"(sr[25]), "=r"(sr[26]), "=r"(sr[27]), "=r"(sr[28]), "=r"(sr[29]), "=r"(sr[30]), "=r"(sr[31])
-                   : "r"(tmem + lane_addr + 64 * b + 32 * hc));
+      uint32_t sr[16];
+      tmem_ld16_async(tmem + lane_addr + 64 * b + 16 * part, sr);
       tmem_wait_ld();
       reg_fence(sr);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&s_free[b]);  // the MMA warp may overwrite S[b]
-      // mask + online softmax in base 2 (score * scale * log2 e), in place
+      // mask (blocks reaching past the tile's first row or past T) + scale into base 2, in place
       float bmax = -INFINITY;
+      const int key0 = j * BN + 16 * part;
+      if (j * BN + BN - 1 > q0 || j * BN + BN > args.T) {
 #pragma unroll
-      for (int c = 0; c < 32; ++c) {
-        const int key = j * BN + 32 * hc + c;
-        const float x = (key > qpos || key >= args.T) ? -INFINITY : __uint_as_float(sr[c]) * args.scale_log2;
-        sr[c] = __float_as_uint(x);
-        bmax = fmaxf(bmax, x);
+        for (int c = 0; c < 16; ++c) {
+          const int key = key0 + c;
+          const float x = (key > qpos || key >= args.T) ? -INFINITY : __uint_as_float(sr[c]) * args.scale_log2;
+          sr[c] = __float_as_uint(x);
+          bmax = fmaxf(bmax, x);
+        }
+      } else {
+#pragma unroll
+        for (int c = 0; c < 16; ++c) {
+          const float x = __uint_as_float(sr[c]) * args.scale_log2;
+          sr[c] = __float_as_uint(x);
+          bmax = fmaxf(bmax, x);
+        }
       }
-      bmax = fmaxf(bmax, exchange(bmax));  // the row's maximum over all 64 keys
-      if (*abort_flag) {
+      float parts[4];
+      if (!exchange(bmax, parts)) {
+        *abort_flag = 1;
         ok = false;
         break;
       }
+      bmax = fmaxf(fmaxf(parts[0], parts[1]), fmaxf(parts[2], parts[3]));  // the row's maximum over 64 keys
       const float nm = fmaxf(m, bmax);
       const float base = nm == -INFINITY ? 0.f : nm;
-      const float alpha = exp2f(m - base);
+      const float alpha = ex2_approx(m - base);
       m = nm;
       float psum = 0.f;
-      // this half of P_j row r into P[b]: 4 chunks of 16 bytes, 128-byte swizzle.  P[b] was
+      // this part of P_j row r into P[b]: 2 chunks of 16 bytes, 128-byte swizzle.  P[b] was
       // last read by P_{j-2} . V_{j-2}, whose completion the fold of block j-2 waited for.
       uint8_t* prow = sp + b * P_BYTES + r * 128;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 0; c < 2; ++c) {
         uint32_t w[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          const float p0 = exp2f(__uint_as_float(sr[8 * c + 2 * e]) - base);
-          const float p1 = exp2f(__uint_as_float(sr[8 * c + 2 * e + 1]) - base);
+          const float p0 = ex2_approx(__uint_as_float(sr[8 * c + 2 * e]) - base);
+          const float p1 = ex2_approx(__uint_as_float(sr[8 * c + 2 * e + 1]) - base);
           psum += p0 + p1;
           w[e] = (uint32_t)f2bf(p0) | ((uint32_t)f2bf(p1) << 16);
         }
-        const int chunk = 4 * hc + c;
+        const int chunk = 2 * part + c;
         *reinterpret_cast<uint4*>(prow + ((chunk ^ (r & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
       }
-      l = l * alpha + psum;  // this half's part of the denominator
+      l = l * alpha + psum;  // this part's share of the denominator
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[b]);
@@ -278,21 +318,35 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     if (ok && nb > 0) ok = fold(nb - 1, alpha_prev);
     if (ok) {
-      l += exchange(l);  // both halves' parts of the denominator
-      ok = !*abort_flag;
+      float parts[4];
+      ok = exchange(l, parts) && !*abort_flag;
+      l = ((parts[0] + parts[1]) + parts[2]) + parts[3];  // the four parts of the denominator
     }
-    if (!ok) {
-      *abort_flag = 1;
-    } else if (qpos < args.T) {
-      uint16_t* dst = args.out + ((size_t)qpos * args.HQ + h) * D + 64 * hc;
+    if (!ok) *abort_flag = 1;
+    // Output tile [128 rows x 128 columns] bf16 staged as two 128-byte-swizzled [128 x 64]
+    // boxes in the P tiles (every P.V has completed: the last fold waited for it), then TMA
+    // stores; rows past T are clipped by the store.
+    const bool stage = ok && !*abort_flag;
+    if (stage) {
+      const float rl = __frcp_rn(l);
+      uint8_t* orow = sp + (part >> 1) * P_BYTES + r * 128;
 #pragma unroll
-      for (int i = 0; i < D / 2; i += 8) {
+      for (int c = 0; c < 4; ++c) {
         uint32_t w[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e)
-          w[e] = (uint32_t)f2bf(__fdiv_rn(o[i + 2 * e], l)) | ((uint32_t)f2bf(__fdiv_rn(o[i + 2 * e + 1], l)) << 16);
-        *reinterpret_cast<uint4*>(dst + i) = make_uint4(w[0], w[1], w[2], w[3]);
+          w[e] = (uint32_t)bf16_quotient(o[8 * c + 2 * e], l, rl) | ((uint32_t)bf16_quotient(o[8 * c + 2 * e + 1], l, rl) << 16);
+        const int chunk = 4 * (part & 1) + c;
+        *reinterpret_cast<uint4*>(orow + ((chunk ^ (r & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
       }
+      fence_proxy_async_smem();
+    }
+    named_barrier(1, SOFTMAX_WARPS * 32);
+    if (warp == 2 && lane == 0 && !*abort_flag) {
+      tma_store_2d(&tmap_o, sp, h * D, q0);
+      tma_store_2d(&tmap_o, sp + P_BYTES, h * D + 64, q0);
+      bulk_commit();
+      bulk_wait_read<0>();  // the staging tile has been read; the writes complete with the grid
     }
   }
 
@@ -318,10 +372,12 @@ __global__ void __launch_bounds__(THREADS, 1)
 // [T, HQ*128]); called by ffb_attention for positions == NULL.
 int ffb_attention_tc(const uint16_t* q, const uint16_t* k, const uint16_t* v, uint16_t* out, int T, int HQ, int HK,
                      float scale, cudaStream_t stream) {
-  CUtensorMap tq, tk, tv;
+  CUtensorMap tq, tk, tv, to;
   int rc = ffb::make_tmap_3d_bf16(&tq, q, D, (uint64_t)T, (uint64_t)HQ, 64, BM);
   if (!rc) rc = ffb::make_tmap_3d_bf16(&tk, k, D, (uint64_t)T, (uint64_t)HK, 64, BN);
   if (!rc) rc = ffb::make_tmap_3d_bf16(&tv, v, D, (uint64_t)T, (uint64_t)HK, 64, BN);
+  // out [T, HQ*128] bf16, stored in [128 rows x 64 columns] boxes
+  if (!rc) rc = ffb::make_tmap_2d(&to, out, (uint64_t)T, (uint64_t)HQ * D, (uint64_t)HQ * D * 2, BM, 64, 2);
   if (rc) return rc;
   static bool attr = false;
   if (!attr) {
@@ -331,7 +387,7 @@ int ffb_attention_tc(const uint16_t* q, const uint16_t* k, const uint16_t* v, ui
   }
   TcArgs a = {out, T, HQ, HK, scale * 1.4426950408889634f};
   cudaError_t e = ffb::launch(attention_tc_kernel, dim3((T + BM - 1) / BM, HQ), dim3(THREADS), SMEM, stream, tq, tk, tv,
-                              a);
+                              to, a);
   if (e != cudaSuccess) return ffb::fail(FFB_ECUDA, "ffb_attention: %s", cudaGetErrorString(e));
   return FFB_OK;
 }
