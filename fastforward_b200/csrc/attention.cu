@@ -75,6 +75,7 @@ struct AttnArgs {
   const uint16_t* k;
   const uint16_t* v;
   const int64_t* positions;
+  const int* key_lo;  // per query row: its lowest visible key, or NULL = 0
   int q_gather;
   uint16_t* out;
   int S, T, HQ, HK;
@@ -101,6 +102,22 @@ __global__ void __launch_bounds__(128) attention_kernel(const AttnArgs p) {
     return p.positions ? (int)p.positions[r] : r;
   };
   const int pa = pos_of(ra), pb = pos_of(rb);
+  const int loa = p.key_lo && ra < p.S ? p.key_lo[ra] : 0, lob = p.key_lo && rb < p.S ? p.key_lo[rb] : 0;
+  // first key block: the lowest key any row of the block can see
+  int kstart = 0;
+  if (p.key_lo) {
+    int mn = 1 << 30;
+    for (int r = q0 + threadIdx.x; r < min(q0 + BMQ, p.S); r += 128) mn = min(mn, p.key_lo[r]);
+    __shared__ int red_lo[4];
+    mn = min(mn, __shfl_xor_sync(0xffffffffu, mn, 16));
+    mn = min(mn, __shfl_xor_sync(0xffffffffu, mn, 8));
+    mn = min(mn, __shfl_xor_sync(0xffffffffu, mn, 4));
+    mn = min(mn, __shfl_xor_sync(0xffffffffu, mn, 2));
+    mn = min(mn, __shfl_xor_sync(0xffffffffu, mn, 1));
+    if (lane == 0) red_lo[warp] = mn;
+    __syncthreads();
+    kstart = max(0, min(min(red_lo[0], red_lo[1]), min(red_lo[2], red_lo[3])));
+  }
   int kend;
   if (p.positions) {
     int mx = -1;
@@ -117,7 +134,8 @@ __global__ void __launch_bounds__(128) attention_kernel(const AttnArgs p) {
   } else {
     kend = min(p.T, min(q0 + BMQ, p.S));
   }
-  const int nblk = (kend + BNK - 1) / BNK;
+  const int blk0 = min(kstart / BNK, (kend + BNK - 1) / BNK);
+  const int nblk = (kend + BNK - 1) / BNK - blk0;  // key blocks visited, from key blk0 * BNK
 
   const uint16_t* kh = p.k + (size_t)kvh * p.T * D;
   const uint16_t* vh = p.v + (size_t)kvh * p.T * D;
@@ -138,8 +156,8 @@ __global__ void __launch_bounds__(128) attention_kernel(const AttnArgs p) {
     load_tile(sQ, p.q + (size_t)h * p.S * D, q0, p.S);
   }
   if (nblk > 0) {
-    load_tile(sK0, kh, 0, p.T);
-    load_tile(sV0, vh, 0, p.T);
+    load_tile(sK0, kh, blk0 * BNK, p.T);
+    load_tile(sV0, vh, blk0 * BNK, p.T);
   }
   cp_commit();
 
@@ -152,8 +170,8 @@ __global__ void __launch_bounds__(128) attention_kernel(const AttnArgs p) {
   for (int blk = 0; blk < nblk; ++blk) {
     const uint32_t sK = (blk & 1) ? sK1 : sK0, sV = (blk & 1) ? sV1 : sV0;
     if (blk + 1 < nblk) {
-      load_tile((blk & 1) ? sK0 : sK1, kh, (blk + 1) * BNK, p.T);
-      load_tile((blk & 1) ? sV0 : sV1, vh, (blk + 1) * BNK, p.T);
+      load_tile((blk & 1) ? sK0 : sK1, kh, (blk0 + blk + 1) * BNK, p.T);
+      load_tile((blk & 1) ? sV0 : sV1, vh, (blk0 + blk + 1) * BNK, p.T);
     }
     cp_commit();
     cp_wait<1>();
@@ -187,10 +205,10 @@ __global__ void __launch_bounds__(128) attention_kernel(const AttnArgs p) {
     for (int j = 0; j < 8; ++j) {
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
-        const int key = blk * BNK + j * 8 + 2 * t4 + e;
+        const int key = (blk0 + blk) * BNK + j * 8 + 2 * t4 + e;
         float va = s[j][e] * p.scale_log2, vb = s[j][2 + e] * p.scale_log2;
-        if (key > pa || key >= p.T) va = -INFINITY;
-        if (key > pb || key >= p.T) vb = -INFINITY;
+        if (key > pa || key >= p.T || key < loa) va = -INFINITY;
+        if (key > pb || key >= p.T || key < lob) vb = -INFINITY;
         s[j][e] = va;
         s[j][2 + e] = vb;
         bmax_a = fmaxf(bmax_a, va);
@@ -264,11 +282,12 @@ __global__ void __launch_bounds__(128) attention_kernel(const AttnArgs p) {
 
 }  // namespace
 
-int ffb_attention_tc(const uint16_t* q, const uint16_t* k, const uint16_t* v, uint16_t* out, int T, int HQ, int HK,
-                     float scale, cudaStream_t stream);
+int ffb_attention_tc(const uint16_t* q, const uint16_t* k, const uint16_t* v, const int* key_lo, uint16_t* out, int T,
+                     int HQ, int HK, float scale, cudaStream_t stream);
 
-extern "C" int ffb_attention(const uint16_t* q, const uint16_t* k, const uint16_t* v, const int64_t* positions,
-                             int q_gather, uint16_t* out, int S, int T, int HQ, int HK, float scale, void* stream) {
+extern "C" int ffb_attention_segmented(const uint16_t* q, const uint16_t* k, const uint16_t* v,
+                                       const int64_t* positions, int q_gather, const int* key_lo, uint16_t* out, int S,
+                                       int T, int HQ, int HK, float scale, void* stream) {
   FFB_REQUIRE(q && k && v && out, "ffb_attention: NULL pointer");
   FFB_REQUIRE(S > 0 && T > 0 && HQ > 0 && HK > 0 && HQ % HK == 0, "ffb_attention: bad shape S=%d T=%d HQ=%d HK=%d", S,
               T, HQ, HK);
@@ -276,17 +295,23 @@ extern "C" int ffb_attention(const uint16_t* q, const uint16_t* k, const uint16_
   FFB_REQUIRE(!q_gather || positions, "ffb_attention: q_gather needs positions");
   FFB_REQUIRE(ffb::aligned(q, 16) && ffb::aligned(k, 16) && ffb::aligned(v, 16) && ffb::aligned(out, 4),
               "ffb_attention: alignment");
+  FFB_REQUIRE(!key_lo || ffb::aligned(key_lo, 4), "ffb_attention: key_lo alignment");
   if (!positions && S == T && ffb::aligned(out, 16))  // causal prefill: the tcgen05 kernel
-    return ffb_attention_tc(q, k, v, out, T, HQ, HK, scale, (cudaStream_t)stream);
+    return ffb_attention_tc(q, k, v, key_lo, out, T, HQ, HK, scale, (cudaStream_t)stream);
   static bool attr = false;
   if (!attr) {
     cudaError_t e = cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
     if (e != cudaSuccess) return ffb::fail(FFB_ECUDA, "ffb_attention: %s", cudaGetErrorString(e));
     attr = true;
   }
-  AttnArgs a = {q, k, v, positions, q_gather, out, S, T, HQ, HK, scale * 1.4426950408889634f};
+  AttnArgs a = {q, k, v, positions, key_lo, q_gather, out, S, T, HQ, HK, scale * 1.4426950408889634f};
   cudaError_t e = ffb::launch(attention_kernel, dim3((S + BMQ - 1) / BMQ, HQ), dim3(128), SMEM,
                               (cudaStream_t)stream, a);
   if (e != cudaSuccess) return ffb::fail(FFB_ECUDA, "ffb_attention: %s", cudaGetErrorString(e));
   return FFB_OK;
+}
+
+extern "C" int ffb_attention(const uint16_t* q, const uint16_t* k, const uint16_t* v, const int64_t* positions,
+                             int q_gather, uint16_t* out, int S, int T, int HQ, int HK, float scale, void* stream) {
+  return ffb_attention_segmented(q, k, v, positions, q_gather, nullptr, out, S, T, HQ, HK, scale, stream);
 }

@@ -70,6 +70,7 @@ __device__ __forceinline__ uint16_t bf16_quotient(float o, float l, float rl) {
 
 struct TcArgs {
   uint16_t* out;
+  const int* key_lo;  // per row: its lowest visible key (several requests in one sequence), or NULL = 0
   int T, HQ, HK;
   float scale_log2;  // scale * log2(e)
 };
@@ -101,6 +102,9 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int q0 = qt * BM;
   const int kend = min(args.T, q0 + BM);      // keys any row of this tile can see
   const int nb = (kend + BN - 1) / BN;
+  // first key block: the tile's lowest visible key (rows' key_lo are non-decreasing)
+  const int jb0 = args.key_lo ? min(max(args.key_lo[min(q0, args.T - 1)], 0) / BN, nb) : 0;
+  const int nit = nb - jb0;                   // key blocks this tile visits
 
   if (tid == 0) {
     mbar_init(q_full, 1);
@@ -143,7 +147,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       tma_load_3d(sq, &tmap_q, q_full, 0, q0, h, pol);
       tma_load_3d(sq + Q_HALF, &tmap_q, q_full, 64, q0, h, pol);
       int issued = 0;
-      for (int j = 0; j < nb && !*abort_flag; ++j, ++issued) {
+      for (int j = 0; j < nit && !*abort_flag; ++j, ++issued) {
         const int s = j % KV_STAGES;
         if (j >= KV_STAGES &&
             !mbar_wait_bounded(&kv_empty[s], ((uint32_t)(j / KV_STAGES) & 1u) ^ 1u, abort_flag)) {
@@ -152,10 +156,11 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         uint8_t* st = skv + s * STAGE;
         mbar_arrive_expect_tx(&kv_full[s], STAGE);
-        tma_load_3d(st, &tmap_k, &kv_full[s], 0, j * BN, kvh, pol);
-        tma_load_3d(st + KV_HALF, &tmap_k, &kv_full[s], 64, j * BN, kvh, pol);
-        tma_load_3d(st + 2 * KV_HALF, &tmap_v, &kv_full[s], 0, j * BN, kvh, pol);
-        tma_load_3d(st + 3 * KV_HALF, &tmap_v, &kv_full[s], 64, j * BN, kvh, pol);
+        const int key = (jb0 + j) * BN;
+        tma_load_3d(st, &tmap_k, &kv_full[s], 0, key, kvh, pol);
+        tma_load_3d(st + KV_HALF, &tmap_k, &kv_full[s], 64, key, kvh, pol);
+        tma_load_3d(st + 2 * KV_HALF, &tmap_v, &kv_full[s], 0, key, kvh, pol);
+        tma_load_3d(st + 3 * KV_HALF, &tmap_v, &kv_full[s], 64, key, kvh, pol);
       }
       if (*abort_flag) {  // copies in flight must land before the CTA exits
         volatile int never = 0;
@@ -184,8 +189,8 @@ __global__ void __launch_bounds__(THREADS, 1)
         return true;
       };
       bool ok = mbar_wait_bounded(q_full, 0, abort_flag);
-      for (int j = 0; j < 2 && j < nb && ok; ++j) ok = issue_s(j);
-      for (int j = 0; j < nb && ok; ++j) {
+      for (int j = 0; j < 2 && j < nit && ok; ++j) ok = issue_s(j);
+      for (int j = 0; j < nit && ok; ++j) {
         const int b = j & 1, st = j % KV_STAGES;
         ok = mbar_wait_bounded(&p_full[b], (uint32_t)(j >> 1) & 1u, abort_flag);
         if (!ok) break;
@@ -197,7 +202,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                    idesc_o, kk > 0 ? 1u : 0u);
         umma_commit(&o_full[b]);
         umma_commit(&kv_empty[st]);
-        if (j + 2 < nb) {  // S[b] is free once the softmax has read S_j
+        if (j + 2 < nit) {  // S[b] is free once the softmax has read S_j
           ok = mbar_wait_bounded(&s_free[b], (uint32_t)(j >> 1) & 1u, abort_flag);
           if (ok) ok = issue_s(j + 2);
         }
@@ -216,6 +221,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     for (int i = 0; i < D / 4; ++i) o[i] = 0.f;
     float m = -INFINITY, l = 0.f, alpha_prev = 0.f;
     int xph = 0;  // phases of this quarter's exchange barrier used so far
+    const int lo = args.key_lo && qpos < args.T ? args.key_lo[qpos] : 0;  // this row's lowest visible key
     // The four parts' values of the row (written to xch[buffer][part][row] by each), in part order.
     auto exchange = [&](float mine, float (&all)[4]) -> bool {
       float* slot = xch + (xph & 1) * 4 * BM;
@@ -248,7 +254,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       return true;
     };
     bool ok = true;
-    for (int j = 0; j < nb && ok; ++j) {
+    for (int j = 0; j < nit && ok; ++j) {
       const int b = j & 1;
       if (!(mbar_wait_bounded(&s_full[b], (uint32_t)(j >> 1) & 1u, abort_flag) && !*abort_flag)) {
         ok = false;
@@ -262,14 +268,15 @@ __global__ void __launch_bounds__(THREADS, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&s_free[b]);  // the MMA warp may overwrite S[b]
-      // mask (blocks reaching past the tile's first row or past T) + scale into base 2, in place
+      // mask (blocks reaching past the tile's first row or past T, or below a row's first
+      // visible key) + scale into base 2, in place
       float bmax = -INFINITY;
-      const int key0 = j * BN + 16 * part;
-      if (j * BN + BN - 1 > q0 || j * BN + BN > args.T) {
+      const int kb = (jb0 + j) * BN, key0 = kb + 16 * part;
+      if (kb + BN - 1 > q0 || kb + BN > args.T || args.key_lo) {
 #pragma unroll
         for (int c = 0; c < 16; ++c) {
           const int key = key0 + c;
-          const float x = (key > qpos || key >= args.T) ? -INFINITY : __uint_as_float(sr[c]) * args.scale_log2;
+          const float x = (key > qpos || key >= args.T || key < lo) ? -INFINITY : __uint_as_float(sr[c]) * args.scale_log2;
           sr[c] = __float_as_uint(x);
           bmax = fmaxf(bmax, x);
         }
@@ -316,7 +323,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (j > 0) ok = fold(j - 1, alpha_prev);  // block j-1's P.V ran while this softmax did
       alpha_prev = alpha;
     }
-    if (ok && nb > 0) ok = fold(nb - 1, alpha_prev);
+    if (ok && nit > 0) ok = fold(nit - 1, alpha_prev);
     if (ok) {
       float parts[4];
       ok = exchange(l, parts) && !*abort_flag;
@@ -370,8 +377,8 @@ __global__ void __launch_bounds__(THREADS, 1)
 
 // Causal self-attention over all T rows (q, k, v head-major [H, T, 128] bf16, out
 // [T, HQ*128]); called by ffb_attention for positions == NULL.
-int ffb_attention_tc(const uint16_t* q, const uint16_t* k, const uint16_t* v, uint16_t* out, int T, int HQ, int HK,
-                     float scale, cudaStream_t stream) {
+int ffb_attention_tc(const uint16_t* q, const uint16_t* k, const uint16_t* v, const int* key_lo, uint16_t* out, int T,
+                     int HQ, int HK, float scale, cudaStream_t stream) {
   CUtensorMap tq, tk, tv, to;
   int rc = ffb::make_tmap_3d_bf16(&tq, q, D, (uint64_t)T, (uint64_t)HQ, 64, BM);
   if (!rc) rc = ffb::make_tmap_3d_bf16(&tk, k, D, (uint64_t)T, (uint64_t)HK, 64, BN);
@@ -385,7 +392,7 @@ int ffb_attention_tc(const uint16_t* q, const uint16_t* k, const uint16_t* v, ui
     if (e != cudaSuccess) return ffb::fail(FFB_ECUDA, "ffb_attention: %s", cudaGetErrorString(e));
     attr = true;
   }
-  TcArgs a = {out, T, HQ, HK, scale * 1.4426950408889634f};
+  TcArgs a = {out, key_lo, T, HQ, HK, scale * 1.4426950408889634f};
   cudaError_t e = ffb::launch(attention_tc_kernel, dim3((T + BM - 1) / BM, HQ), dim3(THREADS), SMEM, stream, tq, tk, tv,
                               to, a);
   if (e != cudaSuccess) return ffb::fail(FFB_ECUDA, "ffb_attention: %s", cudaGetErrorString(e));

@@ -253,6 +253,27 @@ class Buffers:
             self.postb = z(T, h)
 
 
+class BatchBuffers(Buffers):
+    """Buffers of a batched forward: T concatenated rows of R requests (`Engine.forward_batch`)."""
+
+    def __init__(self, dims, T, R, ws_elems, device, mode):
+        super().__init__(dims, T, ws_elems, device, mode)
+        h = dims.hidden
+        z = lambda *s, dt=BF16: torch.zeros(s, device=device, dtype=dt)
+        self.R = R
+        self.pick = z(R, dt=torch.long)           # the pick rows in the concatenated sequence
+        self.hp, self.res1, self.mlp1 = z(R, h), z(R, h), z(R, h)
+        self.logits = z(R, 8, dt=torch.float32)
+        self.logprobs = z(R, 8, dt=torch.float32)
+        self.key_lo = z(T, dt=torch.int32)        # first row of each row's request
+        self.tail_lo = z(R, dt=torch.int32)       # first row of each pick row's request
+        self.cos = z(T, dims.d)
+        self.sin = z(T, dims.d)
+        # deepstack rows of the batch: -0.0 outside the requests' visual rows (x + -0.0 == x
+        # for every x, so those rows are untouched, bit for bit)
+        self.deep = [torch.full((T, h), -0.0, device=device, dtype=BF16) for _ in range(dims.deepstack)]
+
+
 class Engine:
     """Runs prefill + choice scoring for one packed model on one device."""
 
@@ -289,11 +310,15 @@ class Engine:
 
     # ------------------------------------------------------------------ plans / buffers
     def _plans(self, T):
-        if T in self.plans:
-            return self.plans[T]
+        if T not in self.plans:
+            self.plans[T] = self._make_plans(T, 1)
+        return self.plans[T]
+
+    def _make_plans(self, T, tail_rows):
+        """GEMM plans of a forward over T rows whose tail scores `tail_rows` pick rows."""
         d = self.d
         pl = {}
-        for tag, m in (("full", T), ("tail", 1)):
+        for tag, m in (("full", T), ("tail", tail_rows)):
             for role, n, k in (("qkv", d.qkv_out, d.hidden), ("o", d.hidden, d.hq * d.d),
                                ("gateup", 2 * d.inter, d.hidden), ("down", d.hidden, d.inter)):
                 if tag == "tail" and role == "qkv":
@@ -305,7 +330,6 @@ class Engine:
                 if self.world > 1 and role in ("o", "down"):  # fp32 partial for the all-reduce
                     s, epi = 1, L.EPI_F32_PARTIAL
                 pl[(tag, role)] = GemmPlan(m, n, k, bn, s, epi)
-        self.plans[T] = pl
         return pl
 
     def buffers_for(self, T):
@@ -681,6 +705,145 @@ class Engine:
         call("ffb_readout", ptr(b.res1), mb, m32, ms, ptr(m.final_norm), float(d.eps), ptr(m.head), m.head.shape[0],
              int(k), ptr(b.logits), ptr(b.logprobs), H, self._s)
         return b
+
+    # ------------------------------------------------------------------ batched prefill
+    def forward_batch(self, requests):
+        """Prefill + choice scoring of several independent requests in ONE forward pass.
+
+        Their tokens are concatenated, each request padded with id 0 to a multiple of 64 rows
+        (request i at rows [off_i, off_i + n_i), off_i a multiple of 64, so its 64-key
+        softmax blocks are the ones of its own forward); every GEMM and
+        row kernel runs once over all rows -- the weights stream from HBM once per batch
+        instead of once per request -- attention keeps each request to its own keys
+        (`ffb_attention_segmented`) and the tail scores every request's pick row.  The
+        reference serialises requests (README.md:53); per request the arithmetic is the
+        single-request forward's, except that the K-split of o_proj / down_proj follows the
+        batch's row count (fp32 partials summed in another grouping) and the tail's down_proj
+        is unsplit.
+        requests: list of dicts with ids [n] int64, visual [nv, H] bf16 or None, deep (list
+        of [nv, H]), pick (row within the request; default n - 1), k, image_start, grid_h,
+        grid_w -- device or host tensors.  Launched eagerly on the current stream.  Returns
+        [(logits [k], logprobs [k])] as device tensors (views of the batch buffers, valid
+        until the next batch)."""
+        d, m = self.d, self.m
+        if m.mode == "int4":
+            raise NotImplementedError("batched prefill runs the FP8 modes")
+        if self.world > 1:
+            raise NotImplementedError("batched prefill runs on one GPU (replicas)")
+        R = len(requests)
+        if R == 0:
+            return []
+        ns = [int(r["ids"].shape[0]) for r in requests]
+        rows = [-(-n // 64) * 64 for n in ns]       # rows per request, padding included
+        offs = [sum(rows[:i]) for i in range(R)]
+        T = sum(rows)
+        picks, ks = [], []
+        for r, n, off in zip(requests, ns, offs):
+            pk = n - 1 if r.get("pick") is None else int(r["pick"])
+            if not 0 <= pk < n:
+                raise ValueError(f"pick {pk} outside the request's {n} rows")
+            k = int(r["k"])
+            if not 2 <= k <= 8:
+                raise ValueError("Provide two to eight choices")
+            picks.append(off + pk)
+            ks.append(k)
+        if (T, R) not in self.plans:
+            pl = self._make_plans(T, R)
+            tp = pl[("tail", "down")]
+            pl[("tail", "down")] = GemmPlan(tp.m, tp.n, tp.k, tp.bn, 1, L.EPI_BF16)  # one bf16 row per request
+            self.plans[(T, R)] = pl
+        pl = self.plans[(T, R)]
+        # buffers for up to T_alloc rows (a multiple of 256), used for the first T: head-major
+        # Q/K/V take the head stride T from the kernels' arguments, row-major ones the prefix
+        t_alloc = -(-T // 256) * 256
+        key = ("batch", t_alloc, R)
+        if key not in self.buffers:
+            ws = self.MAX_SPLITS * t_alloc * max(d.hidden, d.qkv_out)
+            for b_old in [k_ for k_ in self.buffers if isinstance(k_, tuple) and k_[0] == "batch"]:
+                del self.buffers[b_old]  # one batch geometry resident at a time
+            self.buffers[key] = BatchBuffers(d, t_alloc, R, ws, self.device, m.mode)
+        b = self.buffers[key]
+        self._s = torch.cuda.current_stream(self.device).cuda_stream
+        dev = self.device
+        H, D, HQ, HK, I = d.hidden, d.d, d.hq, d.hk, d.inter
+        eps = float(d.eps)
+        rowwise = m.mode == "rowwise"
+        qmode = L.QUANT_ROWWISE if rowwise else L.QUANT_STATIC
+        scale = D ** -0.5
+        lo = torch.repeat_interleave(torch.tensor(offs, dtype=torch.int32), torch.tensor(rows))
+        b.key_lo[:T].copy_(lo, non_blocking=True)
+        b.tail_lo.copy_(torch.tensor(offs, dtype=torch.int32), non_blocking=True)
+        b.pick.copy_(torch.tensor(picks, dtype=torch.long), non_blocking=True)
+        for x in b.deep:
+            x.fill_(-0.0)
+        b.ids[:T].zero_()
+        for r, n, nr, off in zip(requests, ns, rows, offs):
+            b.ids[off:off + n].copy_(r["ids"], non_blocking=True)
+            c, s_ = self.rope_tables(nr, int(r["image_start"]), int(r["grid_h"]), int(r["grid_w"]))
+            b.cos[off:off + nr].copy_(c)
+            b.sin[off:off + nr].copy_(s_)
+            vis = r.get("visual")
+            nv = int(vis.shape[0]) if vis is not None else 0
+            if nv:
+                st = off + int(r["image_start"])
+                for x, src in zip(b.deep, r.get("deep") or []):
+                    x[st:st + nv].copy_(src, non_blocking=True)
+                vis = vis.to(dev, non_blocking=True)
+            call("ffb_embed_gather", ptr(b.ids) + 8 * off, ptr(m.embed), d.vocab, ptr(vis) if nv else None,
+                 int(r["image_start"]), nv, ptr(b.hA) + 2 * H * off, nr, H, self._s)
+        cos, sin = b.cos, b.sin
+        lay0 = m.layers[0]
+        call("ffb_rmsnorm", ptr(b.hA), ptr(lay0.in_norm), eps, None, qmode, lay0.inv["qkv"], ptr(b.x8), ptr(b.xs), T,
+             H, self._s)
+        sa = lambda lay_, role, rowbuf: rowbuf if rowwise else lay_.ascale[role]
+        h_cur, h_mid = b.hA, b.hB
+        depth = m.depth
+        for j in range(depth - 1):
+            lay, nxt = m.layers[j], m.layers[j + 1]
+            self._qkv(pl[("full", "qkv")], b, lay, cos, sin, T, False, rowwise)
+            call("ffb_attention_segmented", ptr(b.yq), ptr(b.yk), ptr(b.yv), None, 0, ptr(b.key_lo), ptr(b.attn), T,
+                 T, HQ, HK, scale, self._s)
+            p = pl[("full", "o")]
+            call("ffb_quantize_fp8", ptr(b.attn), qmode, lay.inv["o"], ptr(b.o8), ptr(b.os), T, HQ * D, self._s)
+            self._gemm(p, b.o8, sa(lay, "o", b.os), lay.lin["o"], b.lin_out, b.ws, rowwise)
+            ob, o32, os_ = self._split_args(p, b.lin_out, b.ws)
+            call("ffb_add_rmsnorm", ptr(h_cur), ob, o32, os_, None, 0, 0, ptr(lay.post_norm), eps, ptr(h_mid), None,
+                 qmode, lay.inv["gateup"], ptr(b.post8), ptr(b.posts), T, H, self._s)
+            self._gemm(pl[("full", "gateup")], b.post8, sa(lay, "gateup", b.posts), lay.lin["gateup"], b.act, b.ws,
+                       rowwise)
+            p = pl[("full", "down")]
+            call("ffb_quantize_fp8", ptr(b.act), qmode, lay.inv["down"], ptr(b.act8), ptr(b.acts), T, I, self._s)
+            self._gemm(p, b.act8, sa(lay, "down", b.acts), lay.lin["down"], b.lin_out, b.ws, rowwise)
+            db, d32, ds = self._split_args(p, b.lin_out, b.ws)
+            dp = b.deep[j] if j < len(b.deep) else None
+            call("ffb_add_rmsnorm", ptr(h_mid), db, d32, ds, ptr(dp), 0, T if dp is not None else 0,
+                 ptr(nxt.in_norm), eps, ptr(h_cur), None, qmode, nxt.inv["qkv"], ptr(b.x8), ptr(b.xs), T, H, self._s)
+        # ---- tail: the last layer's K/V over all rows, the rest on the R pick rows
+        lay = m.layers[depth - 1]
+        self._qkv(pl[("full", "qkv")], b, lay, cos, sin, T, False, rowwise)
+        call("ffb_attention_segmented", ptr(b.yq), ptr(b.yk), ptr(b.yv), ptr(b.pick), 1, ptr(b.tail_lo), ptr(b.attn),
+             R, T, HQ, HK, scale, self._s)
+        p = pl[("tail", "o")]
+        call("ffb_quantize_fp8", ptr(b.attn), qmode, lay.inv["o"], ptr(b.o8), ptr(b.os), R, HQ * D, self._s)
+        self._gemm(p, b.o8, sa(lay, "o", b.os), lay.lin["o"], b.lin_out, b.ws, rowwise)
+        ob, o32, os_ = self._split_args(p, b.lin_out, b.ws)
+        call("ffb_gather_rows", ptr(h_cur), ptr(b.pick), ptr(b.hp), R, H * 2, self._s)
+        call("ffb_add_rmsnorm", ptr(b.hp), ob, o32, os_, None, 0, 0, ptr(lay.post_norm), eps, ptr(b.res1), None, qmode,
+             lay.inv["gateup"], ptr(b.post8), ptr(b.posts), R, H, self._s)
+        self._gemm(pl[("tail", "gateup")], b.post8, sa(lay, "gateup", b.posts), lay.lin["gateup"], b.act, b.ws,
+                   rowwise)
+        p = pl[("tail", "down")]
+        call("ffb_quantize_fp8", ptr(b.act), qmode, lay.inv["down"], ptr(b.act8), ptr(b.acts), R, I, self._s)
+        self._gemm(p, b.act8, sa(lay, "down", b.acts), lay.lin["down"], b.mlp1, b.ws, rowwise)
+        for i, k in enumerate(ks):
+            call("ffb_readout", ptr(b.res1) + 2 * H * i, ptr(b.mlp1) + 2 * H * i, None, 0, ptr(m.final_norm), eps,
+                 ptr(m.head), m.head.shape[0], int(k), ptr(b.logits) + 32 * i, ptr(b.logprobs) + 32 * i, H, self._s)
+        return [(b.logits[i, :k], b.logprobs[i, :k]) for i, k in enumerate(ks)]
+
+    def launches_per_batch(self, R):
+        """Kernel launches of `forward_batch` for R requests (embed and readout per request)."""
+        per_layer = 9
+        return R + 1 + per_layer * (self.m.depth - 1) + 1 + 1 + 2 + 1 + 1 + 2 + R
 
     def launches_per_forward(self):
         """Kernel launches `enqueue` issues (for the bench's gpu_launches count)."""

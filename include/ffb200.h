@@ -105,6 +105,17 @@ int ffb_attention(const uint16_t* q, const uint16_t* k, const uint16_t* v,
                   const int64_t* positions, int q_gather, uint16_t* out,
                   int S, int T, int HQ, int HK, float scale, void* stream);
 
+/* ffb_attention over a sequence that holds several independent requests one after the
+ * other (batched prefill): query row s sees keys [key_lo[s], position of s], where key_lo
+ * (int32 [S], device) is the first row of the row's own request (NULL: 0, i.e. ffb_attention).
+ * For the causal prefill (positions == NULL) key_lo must be non-decreasing with
+ * key_lo[s] <= s.  No counterpart in the reference (it serialises requests,
+ * README.md:53); each request's rows get exactly the keys its own ffb_attention call
+ * would give them. */
+int ffb_attention_segmented(const uint16_t* q, const uint16_t* k, const uint16_t* v,
+                            const int64_t* positions, int q_gather, const int* key_lo, uint16_t* out,
+                            int S, int T, int HQ, int HK, float scale, void* stream);
+
 /* Copies rows index[i] of src [*, row_bytes] to dst [n, row_bytes] (index on device;
  * the tail's `h.index_select(1, pick)`, _family/night_runtime.py:103). */
 int ffb_gather_rows(const void* src, const int64_t* index, void* dst, int n, int row_bytes,
