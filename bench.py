@@ -52,6 +52,9 @@ def parse():
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--workload", default="4B-fp8-T320")
     p.add_argument("--cpu-layers", type=int, default=2, help="decoder layers in the CPU sample")
+    p.add_argument("--batch", type=int, default=1,
+                   help="request streams: requests concatenated into one forward (Engine.forward_batch); "
+                        "1 = one graph replay per request")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--layers", type=int, default=None,
                    help="build only this many decoder layers (same shapes; for small profiler captures)")
@@ -509,6 +512,8 @@ def run_stream(args):
             r = make_request(dims, lay, seed=100 + i)
             reqs.append(dict(lay=lay, ids=r["ids"][:lay.n_tokens].pin_memory(), visual=r["visual"].pin_memory(),
                              deep=[x.pin_memory() for x in r["deep"]], pick=r["pick"], k=r["k"]))
+        if args.batch > 1:
+            return run_stream_batched(args, eng, reqs, dims, name, mode, n_req, world, rank, local, dev)
         entries = {}
         for r in reqs:  # capture every geometry (and autotune every bucket) before timing
             lay = r["lay"]
@@ -616,6 +621,104 @@ def run_stream(args):
         dist.barrier()
         entries.clear()
         eng.graphs.clear()
+        dist.destroy_process_group()
+
+
+def run_stream_batched(args, eng, reqs, dims, name, mode, n_req, world, rank, local, dev):
+    """The request stream served in batches of `args.batch` consecutive requests, each batch
+    one eager forward over the requests' concatenated tokens (`Engine.forward_batch`).
+    value = requests/s with inputs in HBM (device-timed, max over ranks); latency = each
+    batch's device time (every request of a batch completes with it); e2e = the stream
+    through `Accelerator.prefill_score_batch` with pinned host inputs."""
+    import torch
+    import torch.distributed as dist
+    from fastforward_b200.api import Accelerator
+    from fastforward_b200.config import BUCKETS
+    B = args.batch
+
+    def as_req(r, d):
+        lay = r["lay"]
+        return dict(ids=d["ids"], visual=d["visual"], deep=d["deep"], pick=lay.n_tokens - 1, k=r["k"],
+                    image_start=lay.image_start, grid_h=lay.grid_h, grid_w=lay.grid_w)
+    dev_reqs = [as_req(r, dict(ids=r["ids"].to(dev), visual=r["visual"].to(dev), deep=[x.to(dev) for x in r["deep"]]))
+                for r in reqs]
+    batches = [dev_reqs[i:i + B] for i in range(0, n_req, B)]
+    for bt in batches[:max(3, args.warmup)]:
+        eng.forward_batch(bt)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    s = torch.cuda.current_stream()
+    ev = []
+    with Clocks(local) as clk:
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record(s)
+        for bt in batches:
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(s)
+            eng.forward_batch(bt)
+            e1.record(s)
+            ev.append((e0, e1))
+        t1.record(s)
+        torch.cuda.synchronize()
+    total_s = t0.elapsed_time(t1) * 1e-3
+    lat = sorted(a.elapsed_time(b_) for a, b_ in ev)
+    if world > 1:
+        t = torch.tensor([total_s], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_s = t.item()
+    value = world * n_req / total_s
+
+    class _Bound(Accelerator):
+        def __init__(self, engine, buckets):
+            import threading
+            self.engine = engine
+            self.dims = dims
+            self.device = dev
+            self.lock = threading.RLock()
+            self.buckets = buckets
+    acc = _Bound(eng, BUCKETS)
+    host_reqs = [as_req(r, r) for r in reqs]
+    hb = [host_reqs[i:i + B] for i in range(0, n_req, B)]
+    acc.prefill_score_batch(hb[0])
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    for bt in hb:
+        acc.prefill_score_batch(bt)
+    e1.record(s)
+    torch.cuda.synchronize()
+    e2e_s = e0.elapsed_time(e1) * 1e-3
+    if world > 1:
+        t = torch.tensor([e2e_s], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = t.item()
+    h2d = sum(r["ids"].numel() * 8 + r["visual"].numel() * 2 + sum(x.numel() * 2 for x in r["deep"]) for r in reqs) / n_req
+    d2h = sum(2 * r["k"] * 4 for r in reqs) / n_req
+    tokens = sum(r["lay"].n_tokens for r in reqs)
+    clk_sum = clk.summary()
+    if rank == 0:
+        pct = lambda xs, q: xs[min(len(xs) - 1, int(round(q * (len(xs) - 1))))]
+        line = dict(metric=f"requests/s (Qwen3-VL-{name} FP8, {n_req}-request stream: 64/144/256 visual tokens, "
+                           "32-128 text, 2-8 choices); p50 latency in ms_per_step",
+                    value=value, unit="req/s", n_gpus=world, steps=n_req, warmup=args.warmup,
+                    ms_per_step=pct(lat, 0.5), higher_is_better=True, scaling="weak", vs_baseline=None,
+                    dtype="fp8-e4m3", data="synthetic (seeded weights, request geometries and inputs)",
+                    config=dict(workload=args.workload, model=f"Qwen3-VL-{name}-shaped", global_batch=world * B,
+                                seq_len="96-384 per request, requests concatenated at 64-row offsets",
+                                parallelism=f"replicas{world}", quant=mode, requests_per_forward=B,
+                                prefill_tokens_per_replica=tokens, l2="weights (6.9 GB) exceed L2; no flush needed"),
+                    latency_ms=dict(p50=pct(lat, 0.5), p99=pct(lat, 0.99), mean=sum(lat) / len(lat),
+                                    note="per batch: every request of a batch completes with it"),
+                    prefill_tok_per_s=world * tokens / total_s,
+                    e2e=dict(value=world * n_req / e2e_s, unit="req/s", h2d_bytes_per_step=h2d,
+                             d2h_bytes_per_step=d2h, api="Accelerator.prefill_score_batch"),
+                    gpu_launches=sum(eng.launches_per_batch(len(bt)) for bt in batches), clocks=clk_sum,
+                    cpu_baseline=None)
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
         dist.destroy_process_group()
 
 

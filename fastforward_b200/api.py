@@ -212,6 +212,37 @@ class Accelerator:
             out = torch.stack([z, lp]).cpu()  # one device->host read, synchronises the stream
         return out[0].tolist(), out[1].tolist()
 
+    def prefill_score_batch(self, requests):
+        """Prefill + choice scoring of several requests in one forward pass over their
+        concatenated tokens (`Engine.forward_batch`; the reference serialises requests).
+        requests: list of dicts with ids [n] int64, visual [nv, H] bf16, deep (list of
+        [nv, H]), k, image_start, grid_h, grid_w, optional pick (default n - 1) -- host
+        (pinned or pageable) or device tensors.  Returns [(logits [k], logprobs [k])] lists,
+        one pair per request, in order."""
+        import torch
+        reqs = []
+        for r in requests:
+            k = int(r["k"])
+            if not 2 <= k <= 8:
+                raise ValueError("Provide two to eight choices")
+            vis = r.get("visual")
+            nv = int(vis.shape[0]) if vis is not None else 0
+            if nv != (int(r["grid_h"]) // 2) * (int(r["grid_w"]) // 2):
+                raise ValueError("visual rows must match the merged image grid")
+            reqs.append(r)
+        with self.lock, torch.no_grad(), torch.cuda.device(self.device):
+            dev = [dict(r, ids=r["ids"].to(self.device, non_blocking=True),
+                        visual=r["visual"].to(self.device, non_blocking=True) if r.get("visual") is not None else None,
+                        deep=[x.to(self.device, non_blocking=True) for x in (r.get("deep") or [])]) for r in reqs]
+            outs = self.engine.forward_batch(dev)
+            flat = torch.cat([torch.cat([z, lp]) for z, lp in outs]).cpu()  # one device->host read
+        res, i = [], 0
+        for r in reqs:
+            k = int(r["k"])
+            res.append((flat[i:i + k].tolist(), flat[i + k:i + 2 * k].tolist()))
+            i += 2 * k
+        return res
+
     def predict(self, image, question, candidates, item_id="request", *, backend=None):
         validate_request(image, question, candidates)
         mode = self.backend if backend is None else backend

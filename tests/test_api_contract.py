@@ -77,3 +77,19 @@ def test_static_profile_bundle_fields(tmp_path):
         Accelerator._read_profile(dict(c, variant="v2"))
     with pytest.raises(FileNotFoundError):
         Accelerator._read_profile(dict(c, profile_path=str(tmp_path / "missing.json")))
+
+
+def test_prefill_score_batch_validates_before_the_device():
+    """The batched entry rejects a bad request (choice count, visual rows vs grid) before
+    anything reaches the engine."""
+    import threading
+    import torch
+    acc = Accelerator.__new__(Accelerator)
+    acc.lock = threading.RLock()
+    acc.engine = None  # never reached
+    good = dict(ids=torch.zeros(8, dtype=torch.long), visual=torch.zeros((16, 8)), deep=[], k=4, image_start=0,
+                grid_h=8, grid_w=8)
+    with pytest.raises(ValueError, match="two to eight"):
+        acc.prefill_score_batch([good, dict(good, k=9)])
+    with pytest.raises(ValueError, match="merged image grid"):
+        acc.prefill_score_batch([dict(good, grid_h=6)])

@@ -119,3 +119,22 @@ def test_forward_batch_matches_oracle_per_request(mode):
         torch.testing.assert_close(lp, oracle.log_softmax(z), atol=1e-5, rtol=1e-5)
     oracle.set_attention_block(old)
     assert L.device_error() == 0
+
+
+def test_accelerator_prefill_score_batch_matches_forward_batch():
+    """The public batched entry (host inputs, one device->host read) returns the engine's
+    batched answers, request by request."""
+    import threading
+    from dataclasses import replace
+    from fastforward_b200.api import Accelerator
+    dims = replace(MODELS["2B"], vocab=4096)
+    src = make_model_bf16(dims, seed=0, device="cpu", layers=2)
+    eng = Engine(PackedModel(dims, src, device=DEV), autotune=False)
+    acc = Accelerator.__new__(Accelerator)
+    acc.engine, acc.dims, acc.device, acc.lock = eng, dims, DEV, threading.RLock()
+    reqs = _requests(dims)
+    got = acc.prefill_score_batch(reqs)
+    want = eng.forward_batch([dict(r, ids=r["ids"].to(DEV), visual=r["visual"].to(DEV),
+                                   deep=[x.to(DEV) for x in r["deep"]]) for r in reqs])
+    for (z, lp), (zw, lw), r in zip(got, want, reqs):
+        assert len(z) == r["k"] and z == zw.cpu().tolist() and lp == lw.cpu().tolist()
