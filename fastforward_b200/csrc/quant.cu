@@ -46,7 +46,7 @@ __device__ __forceinline__ float block_max_any(float v, float* red) {  // blockD
 
 // One CTA per row, the row held in registers as 8-element vectors (QV per thread):
 // absmax (ROWWISE only), then quantise with 8-byte stores.  K % 8 == 0.
-constexpr int QV = 4;
+constexpr int QV = 2;
 __global__ void __launch_bounds__(1024) quant_rows_vec_kernel(const uint16_t* __restrict__ x, int mode, float inv,
                                                              uint8_t* __restrict__ q8, float* __restrict__ qscale,
                                                              int K) {
