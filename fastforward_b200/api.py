@@ -212,6 +212,75 @@ class Accelerator:
             out = torch.stack([z, lp]).cpu()  # one device->host read, synchronises the stream
         return out[0].tolist(), out[1].tolist()
 
+    def prefill_score_stream(self, requests):
+        """Scores a sequence of requests, one forward (graph replay) each -- the same answers
+        as `prefill_score` on each, in order -- with the host<->device traffic overlapped:
+        request i+1's inputs are copied from host memory on a copy stream while request i's
+        forward runs, and request i's answer is copied back into pinned host memory without
+        waiting for it.  requests: dicts of `prefill_score`'s arguments (ids, visual, deep,
+        k, image_start, grid_h, grid_w, optional pick).  Returns [(logits [k], logprobs [k])]."""
+        import torch
+        plan = []
+        for r in requests:
+            ids, vis, deep = r["ids"], r.get("visual"), list(r.get("deep") or [])
+            n, k = int(ids.shape[0]), int(r["k"])
+            if not 2 <= k <= 8:
+                raise ValueError("Provide two to eight choices")
+            bucket = next((b for b in self.buckets if b >= n), None)
+            if bucket is None:
+                raise ValueError(f"{n} tokens exceed the largest bucket {self.buckets[-1]} (no truncation)")
+            nv = int(vis.shape[0]) if vis is not None else 0
+            gh, gw = int(r.get("grid_h", 32)), int(r.get("grid_w", 32))
+            if nv != (gh // 2) * (gw // 2):
+                raise ValueError("visual rows must match the merged image grid")
+            pick = n - 1 if r.get("pick") is None else int(r["pick"])
+            plan.append((r, n, nv, bucket, k, pick, int(r.get("image_start", 0)), gh, gw, deep))
+        if not plan:
+            return []
+        dev = self.device
+        with self.lock, torch.no_grad(), torch.cuda.device(dev):
+            main = torch.cuda.current_stream(dev)
+            copy = torch.cuda.Stream(dev)
+            n_max = max(p[1] for p in plan)
+            nv_max = max([p[2] for p in plan] + [1])
+            n_deep = max(len(p[9]) for p in plan)
+            H = self.dims.hidden
+            slots = [dict(ids=torch.empty(n_max, dtype=torch.long, device=dev),
+                          visual=torch.empty((nv_max, H), dtype=torch.bfloat16, device=dev),
+                          deep=[torch.empty((nv_max, H), dtype=torch.bfloat16, device=dev) for _ in range(n_deep)])
+                     for _ in range(2)]
+            ready = [torch.cuda.Event() for _ in range(2)]
+            free = [torch.cuda.Event() for _ in range(2)]
+            out = torch.zeros((len(plan), 2, 8), dtype=torch.float32, pin_memory=True)
+            for i, (r, n, nv, bucket, k, pick, start, gh, gw, deep) in enumerate(plan):
+                entry = self.engine.capture(bucket, start, nv, gh, gw, k, len(deep))
+                sl = slots[i % 2]
+                with torch.cuda.stream(copy):  # this request's inputs, once its slot is free again
+                    if i >= 2:
+                        copy.wait_event(free[i % 2])
+                    sl["ids"][:n].copy_(r["ids"], non_blocking=True)
+                    if nv:
+                        sl["visual"][:nv].copy_(r["visual"], non_blocking=True)
+                    for dst, src in zip(sl["deep"], deep):
+                        dst[:nv].copy_(src, non_blocking=True)
+                    ready[i % 2].record(copy)
+                main.wait_event(ready[i % 2])
+                b = entry["buffers"]
+                if n < bucket:
+                    b.ids[n:].zero_()
+                b.ids[:n].copy_(sl["ids"][:n])
+                if nv:
+                    entry["visual"][:nv].copy_(sl["visual"][:nv])
+                for dst, src in zip(entry["deep"], sl["deep"][:len(deep)]):
+                    dst[:nv].copy_(src[:nv])
+                b.pick.fill_(pick)
+                free[i % 2].record(main)
+                entry["graph"].replay()
+                out[i, 0, :k].copy_(b.logits[:k], non_blocking=True)
+                out[i, 1, :k].copy_(b.logprobs[:k], non_blocking=True)
+            main.synchronize()
+        return [(out[i, 0, :p[4]].tolist(), out[i, 1, :p[4]].tolist()) for i, p in enumerate(plan)]
+
     def prefill_score_batch(self, requests):
         """Prefill + choice scoring of several requests in one forward pass over their
         concatenated tokens (`Engine.forward_batch`; the reference serialises requests).

@@ -138,3 +138,24 @@ def test_accelerator_prefill_score_batch_matches_forward_batch():
                                    deep=[x.to(DEV) for x in r["deep"]]) for r in reqs])
     for (z, lp), (zw, lw), r in zip(got, want, reqs):
         assert len(z) == r["k"] and z == zw.cpu().tolist() and lp == lw.cpu().tolist()
+
+
+def test_accelerator_prefill_score_stream_matches_single_calls():
+    """The streamed entry (copies overlapped with the forwards) answers each request exactly
+    as a `prefill_score` call does."""
+    import threading
+    from dataclasses import replace
+    from fastforward_b200.api import Accelerator
+    from fastforward_b200.config import BUCKETS
+    dims = replace(MODELS["2B"], vocab=4096)
+    src = make_model_bf16(dims, seed=0, device="cpu", layers=2)
+    eng = Engine(PackedModel(dims, src, device=DEV), autotune=False)
+    acc = Accelerator.__new__(Accelerator)
+    acc.engine, acc.dims, acc.device, acc.lock, acc.buckets = eng, dims, DEV, threading.RLock(), BUCKETS
+    reqs = _requests(dims) * 2  # six requests, three geometries, slots reused
+    got = acc.prefill_score_stream([dict(r, ids=r["ids"].pin_memory(), visual=r["visual"].pin_memory(),
+                                         deep=[x.pin_memory() for x in r["deep"]]) for r in reqs])
+    for (z, lp), r in zip(got, reqs):
+        zw, lw = acc.prefill_score(r["ids"], r["visual"], r["deep"], r["k"], r["image_start"], r["grid_h"],
+                                   r["grid_w"], r["pick"])
+        assert z == zw and lp == lw
