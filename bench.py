@@ -732,9 +732,145 @@ def run_stream_batched(args, eng, reqs, dims, name, mode, n_req, world, rank, lo
         dist.destroy_process_group()
 
 
+# ---------------------------------------------------------------------------- input packing
+
+PACK_WORKLOADS = {"pack-rgb-256": (256, 256), "pack-rgb-320": (320, 320), "pack-rect-192x320": (192, 320)}
+PACK_UNIT = "canvases/s"
+
+
+def _pack_common(args):
+    H, W = PACK_WORKLOADS[args.workload]
+    n = args.batch if args.batch > 1 else 256  # canvases per step
+    patch_rows = (H // 16) * (W // 16)
+    bytes_per_canvas = H * W * 3 + patch_rows * 1536 * 2  # u8 canvas read + bf16 rows written
+    metric = (f"input packing canvases/s ({H}x{W} RGB u8 -> {patch_rows}x1536 bf16 patch rows, "
+              f"{n} canvases per step)")
+    return H, W, n, patch_rows, bytes_per_canvas, metric
+
+
+def run_pack_reference(args):
+    """The reference's packing arithmetic on the host (the oracle restatement: the reference
+    packs on the GPU only), a bounded sample of canvases per step."""
+    import numpy as np
+    import oracle
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    H, W, n, _, _, metric = _pack_common(args)
+    g = np.random.default_rng(0)
+    canvases = g.integers(0, 256, (4, H, W, 3), dtype=np.uint8)
+    times = []
+    for i in range(args.warmup + args.steps):
+        t0 = time.perf_counter()
+        oracle.pack_rgb(canvases[i % 4])
+        if i >= args.warmup:
+            times.append(time.perf_counter() - t0)
+    value = 1.0 / statistics.median(times)
+    print(json.dumps(dict(metric=metric, value=value, unit=PACK_UNIT, n_gpus=args.gpus, steps=args.steps,
+                          warmup=args.warmup, ms_per_step=statistics.median(times) * 1e3 * n,
+                          higher_is_better=True, scaling="weak", vs_baseline=None, dtype="u8->bf16",
+                          data="synthetic (uniform random bytes)", impl="reference",
+                          config=dict(workload=args.workload, canvases_per_step=n, parallelism="cpu"),
+                          cpu_baseline=dict(value=value, unit=PACK_UNIT, cores=1, kind="port",
+                                            sample="one canvas per timed step (numpy restatement), rate per canvas"),
+                          e2e=dict(value=value, unit=PACK_UNIT, h2d_bytes_per_step=0, d2h_bytes_per_step=0))),
+          flush=True)
+
+
+def run_pack(args):
+    """Input packing (`ffb_pack_rgb_batch`): one step = a batch of canvases packed into patch
+    rows.  value = canvases/s with the canvases in HBM (CUDA events, max over ranks; the
+    step's footprint exceeds L2 because 4 rotating input/output sets are used); e2e = the same
+    through the public staging path: `staging.Packet.stage` (host copy into the pinned packet
+    + ONE host->device copy) + `ops.pack_rgb`, reading back the last patch row."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    from fastforward_b200 import ops, staging
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+    H, W, n, patch_rows, bpc, metric = _pack_common(args)
+    peaks = read_peaks()
+    g = np.random.default_rng(rank)
+    host = [g.integers(0, 256, (n, H, W, 3), dtype=np.uint8) for _ in range(2)]
+    sets = 4
+    rgb = [torch.from_numpy(host[i % 2]).to(dev) for i in range(sets)]
+    pix = [torch.empty((n * patch_rows, 1536), dtype=torch.bfloat16, device=dev) for _ in range(sets)]
+    s = torch.cuda.current_stream()
+    for i in range(args.warmup):
+        ops.pack_rgb(rgb[i % sets], pixels=pix[i % sets])
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(local) as clk:
+        e0.record(s)
+        for i in range(args.steps):
+            ops.pack_rgb(rgb[i % sets], pixels=pix[i % sets])
+        e1.record(s)
+        torch.cuda.synchronize()
+        dev_s = e0.elapsed_time(e1) / 1e3
+        # e2e through the staging packet: host canvases -> pinned packet -> one H2D -> pack
+        pk = staging.Packet([(n, H, W, 3)], [torch.uint8], device=dev)
+        out = torch.empty((2, 1536), dtype=torch.bfloat16, pin_memory=True)
+        for i in range(args.warmup):
+            pk.stage(host[i % 2])
+            ops.pack_rgb(pk.device_views[0], pixels=pix[0])
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for i in range(args.steps):
+            pk.stage(host[i % 2])
+            ops.pack_rgb(pk.device_views[0], pixels=pix[0])
+            out[i % 2].copy_(pix[0][-1], non_blocking=True)
+        torch.cuda.synchronize()
+        e2e_s = time.perf_counter() - t0
+    if world > 1:
+        t = torch.tensor([dev_s, e2e_s], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dev_s, e2e_s = t.tolist()
+    value = world * n * args.steps / dev_s
+    achieved = n * bpc / (dev_s / args.steps) / 1e9
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        import oracle
+        ts = []
+        for i in range(6):
+            t0 = time.perf_counter()
+            oracle.pack_rgb(host[0][i % n])
+            ts.append(time.perf_counter() - t0)
+        cpu = dict(value=1.0 / statistics.median(ts[1:]), unit=PACK_UNIT, cores=1, kind="port",
+                   sample="5 canvases through the numpy restatement, median per canvas")
+    if rank == 0:
+        print(json.dumps(dict(
+            metric=metric, value=value, unit=PACK_UNIT, n_gpus=world, steps=args.steps, warmup=args.warmup,
+            ms_per_step=dev_s / args.steps * 1e3, higher_is_better=True, scaling="weak", vs_baseline=None,
+            dtype="u8->bf16", data="synthetic (uniform random bytes)",
+            config=dict(workload=args.workload, canvases_per_step=n, parallelism=f"replicas{world}",
+                        l2=f"4 rotating input/output sets of {n * bpc / 1e6:.0f} MB each: footprint above L2"),
+            roofline=dict(bound="hbm", achieved=achieved, peak=peaks["hbm"], unit="GB/s", frac=achieved / peaks["hbm"],
+                          traffic=None, kernel="pack_rgb_kernel",
+                          traffic_note=f"algorithmic bytes per canvas {bpc} (u8 read + bf16 write)",
+                          peak_note=f"{peaks['src']} HBM copy bandwidth"),
+            e2e=dict(value=world * n * args.steps / e2e_s, unit=PACK_UNIT, h2d_bytes_per_step=n * H * W * 3,
+                     d2h_bytes_per_step=1536 * 2, api="staging.Packet.stage + ops.pack_rgb",
+                     note="includes the host copy of the canvases into the pinned packet"),
+            gpu_launches=args.steps, clocks=clk.summary(), cpu_baseline=cpu)), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main():
     args = parse()
     from fastforward_b200.config import STREAMS
+    if args.workload in PACK_WORKLOADS:
+        return run_pack_reference(args) if args.impl == "reference" else run_pack(args)
     if args.impl == "reference":
         if args.workload in STREAMS:
             print(json.dumps(dict(impl="reference", unavailable="the CPU reference arm times the fixed-geometry "

@@ -51,6 +51,8 @@ SIGNATURES = {
     "ffb_readout": [P, P, P, I, P, F, P, I, I, P, P, I, P],
     "ffb_pack_int4": [P, P, P, I, I, P],
     "ffb_w4a16_gemm": [P, P, P, I, P, P, I, I, I, I, I, P],
+    "ffb_pack_rgb": [P, P, I, I, P],
+    "ffb_pack_rgb_batch": [P, P, I, I, I, P],
 }
 
 

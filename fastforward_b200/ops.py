@@ -14,6 +14,8 @@ code written against the reference runs unchanged:
     RuntimeScaleLinear _family/depth_fp8.py:22-26
     FP8Linear          _legacy/fp8_private.py:21-38
     Int4               _family/night_runtime.py:15-42 (symmetric group-128 scheme)
+    pack_rgb           _legacy/sub10_runtime.py:21-29
+    pack_rectangle     _family/depth_runtime.py:18-25
 
 Outputs are allocated with torch on the input's device (stream-ordered, graph-safe
 through the caching allocator).  Argument errors raise ValueError (the reference uses
@@ -277,3 +279,38 @@ class Int4:
         call("ffb_w4a16_gemm", ptr(flat), ptr(self.packed), ptr(self.scales), L.EPI_BF16, ptr(out), None, 1, 0, m,
              n, k, stream_ptr(x.device))
         return out.reshape(*x.shape[:-1], n)
+
+
+# ---------------------------------------------------------------------------- input packing
+
+def _pack(rgb, pixels):
+    _need(rgb.is_cuda and rgb.dtype == torch.uint8, "rgb: CUDA uint8 canvas")
+    _need(rgb.dim() in (3, 4) and rgb.shape[-1] == 3 and rgb.is_contiguous(),
+          "rgb must be a contiguous [H, W, 3] or [n, H, W, 3] canvas")
+    n = rgb.shape[0] if rgb.dim() == 4 else 1
+    h, w = rgb.shape[-3], rgb.shape[-2]
+    _need(h % 32 == 0 and w % 32 == 0, f"canvas {h}x{w}: sides must be multiples of 32")
+    rows = n * (h // 16) * (w // 16)
+    if pixels is None:
+        pixels = torch.empty((rows, 1536), device=rgb.device, dtype=BF16)
+    _need(pixels.shape == (rows, 1536) and pixels.dtype == BF16 and pixels.is_contiguous() and pixels.is_cuda,
+          f"pixels must be a contiguous CUDA bf16 [{rows}, 1536] tensor")
+    call("ffb_pack_rgb_batch", ptr(rgb), ptr(pixels), n, h, w, stream_ptr(rgb.device))
+    return pixels
+
+
+def pack_rgb(rgb, side=None, pixels=None):
+    """Square canvas [S, S, 3] uint8 -> patch rows [(S/16)^2, 1536] bf16 (the reference's
+    `pack_rgb[grid](rgb, pixels, S, N, 1024)`, `_legacy/sub10_runtime.py:21-29`).  A
+    [n, S, S, 3] batch gives n canvases' rows one after the other."""
+    if side is not None:
+        _need(rgb.shape[-3] == rgb.shape[-2] == side, f"canvas is not {side}x{side}")
+    return _pack(rgb, pixels)
+
+
+def pack_rectangle(rgb, width=None, pixels=None):
+    """Canvas [H, W, 3] uint8 (H, W multiples of 32) -> [(H/16)(W/16), 1536] bf16
+    (`pack_rectangle`, `_family/depth_runtime.py:18-25`)."""
+    if width is not None:
+        _need(rgb.shape[-2] == width, f"canvas width is not {width}")
+    return _pack(rgb, pixels)

@@ -275,6 +275,22 @@ int ffb_w4a16_gemm(const uint16_t* x, const uint8_t* packed, const uint16_t* sca
                    int epilogue, uint16_t* out, float* ws, int splits, int feature_tile,
                    int M, int N, int K, void* stream);
 
+/* Input packing in front of the vision tower: RGB canvas -> patch rows.
+ * Replaces _legacy/sub10_runtime.py:21-29 (`pack_rgb`, height == width) and
+ * _family/depth_runtime.py:18-25 (`pack_rectangle`).  rgb [height, width, 3] u8 (HWC,
+ * row-major, any alignment); pixels [(height/16)*(width/16), 1536] bf16, 16-byte aligned:
+ * row p = patch p in 2x2 merge-group order, element c*512 + t*256 + y*16 + x =
+ * bf16((rgb[y', x', c] - 127.5) / 127.5) for both temporal copies t.  height and width
+ * must be positive multiples of 32 (at most 2^26 pixels). */
+int ffb_pack_rgb(const uint8_t* rgb, uint16_t* pixels, int height, int width, void* stream);
+
+/* ffb_pack_rgb over n canvases of one size in one launch (no reference counterpart: the
+ * reference packs one canvas per request; batched prefill packs a batch at once).
+ * rgb [n, height, width, 3] u8; pixels [n * (height/16)*(width/16), 1536] bf16, canvas i's
+ * patch rows at rows [i*P, (i+1)*P); n * height * width <= 2^30. */
+int ffb_pack_rgb_batch(const uint8_t* rgb, uint16_t* pixels, int n, int height, int width,
+                       void* stream);
+
 #ifdef __cplusplus
 }
 #endif

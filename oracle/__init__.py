@@ -14,3 +14,4 @@ fixtures; `tests/test_oracle_golden.py` checks every oracle function against
 those fixtures.
 """
 from .qwen_path import *  # noqa: F401,F403
+from .pack import *  # noqa: F401,F403,E402

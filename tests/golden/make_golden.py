@@ -10,7 +10,8 @@ box):
 What runs: the reference's Triton kernels (`_legacy/lower_kernels.add_rms`,
 `_legacy/sub10_runtime.fast_norm`, `_legacy/broad_kernels.qk_pair`,
 `_legacy/limit_kernels.attention_direct` / `lm_readout`, `_legacy/search_kernels.swiglu`,
-`_family/depth_fp8.quantize_runtime`, `_legacy/fp8_private.quantize_rows`) under Triton's
+`_family/depth_fp8.quantize_runtime`, `_legacy/fp8_private.quantize_rows`,
+`_legacy/sub10_runtime.pack_rgb`, `_family/depth_runtime.pack_rectangle`) under Triton's
 CPU interpreter (TRITON_INTERPRET=1), the reference's torch code (`StaticFP8Linear`,
 `FP8Linear`, `RuntimeScaleLinear` through CPU `torch._scaled_mm`, `Int4`), and
 transformers' Qwen3-VL `get_rope_index` / `Qwen3VLTextRotaryEmbedding`.
@@ -126,12 +127,12 @@ def _import_reference(root):
     sys.modules[stub.__name__] = stub
     from fastforward_accel._legacy import lower_kernels, limit_kernels, broad_kernels, search_kernels, fp8_private
     from fastforward_accel._legacy import sub10_runtime
-    from fastforward_accel._family import depth_fp8, night_runtime
+    from fastforward_accel._family import depth_fp8, night_runtime, depth_runtime
     search_kernels.libdevice = _Libdevice()
     limit_kernels.libdevice = _Libdevice()
     return types.SimpleNamespace(lower=lower_kernels, limit=limit_kernels, broad=broad_kernels,
                                  search=search_kernels, fp8p=fp8_private, sub10=sub10_runtime, depth=depth_fp8,
-                                 night=night_runtime)
+                                 night=night_runtime, depth_rt=depth_runtime)
 
 
 class _ClaimsCuda(torch.Tensor):
@@ -287,6 +288,24 @@ def main(root):
         cases.append(dict(n_tokens=n_tokens, image_start=start, grid_h=gh, grid_w=gw, position_ids=pos[:, 0],
                           cos=c[0], sin=s[0]))
     out["mrope"] = cases
+
+    # input packing: pack_rgb (sub10_runtime.py:21-29) and pack_rectangle
+    # (depth_runtime.py:18-25), launched as the reference launches them (1024 per program)
+    import triton
+    gp = torch.Generator().manual_seed(77)
+    packs = []
+    for kind, (H, W) in (("square", (64, 64)), ("square", (96, 96)), ("rectangle", (64, 160)),
+                         ("rectangle", (96, 32))):
+        rgb = torch.randint(0, 256, (H, W, 3), generator=gp, dtype=torch.uint8)
+        rgb.view(-1)[:256] = torch.arange(256, dtype=torch.uint8)  # every byte value
+        pixels = torch.empty(((H // 16) * (W // 16), 1536), dtype=BF16)
+        grid = (triton.cdiv(pixels.numel(), 1024),)
+        if kind == "square":
+            R.sub10.pack_rgb[grid](rgb, pixels, W, pixels.numel(), 1024, enable_fp_fusion=False)
+        else:
+            R.depth_rt.pack_rectangle[grid](rgb, pixels, W, pixels.numel(), 1024, enable_fp_fusion=False)
+        packs.append(dict(kind=kind, height=H, width=W, rgb=rgb, pixels=pixels))
+    out["pack_rgb"] = packs
 
     out["_note"] = "outputs of the reference's own code; see make_golden.py"
     torch.save(out, OUT)
