@@ -51,6 +51,25 @@ def test_pixel_values_do_not_depend_on_division_rounding():
         assert len(bf) == 1, (u, neigh)
 
 
+def test_kernel_value_arithmetic_matches_ieee_division():
+    """The kernel computes (u - 127.5) * fp32(2/255) (exact byte-to-float and subtraction,
+    one rounded product); for all 256 bytes its bf16 equals the bf16 of the IEEE quotient
+    (u - 127.5) / 127.5 that the reference and the oracle compute."""
+    src = (Path(__file__).resolve().parents[1] / "fastforward_b200" / "csrc" / "pack.cu").read_text()
+    assert "TWO_OVER_255 = 0x1.010102p-7f" in src
+    k = np.float32(float.fromhex("0x1.010102p-7"))
+    lo, hi = np.nextafter(k, np.float32(0)), np.nextafter(k, np.float32(1))
+    exact = Fraction(2, 255)
+    assert abs(Fraction(float(k)) - exact) <= min(abs(Fraction(float(lo)) - exact), abs(Fraction(float(hi)) - exact))
+    u = np.arange(256, dtype=np.uint32)
+    m = (u | np.uint32(0x4B000000)).view(np.float32)  # 2^23 + u, as the byte permute builds it
+    x = (m - np.float32(8388608.0)) - np.float32(127.5)
+    assert np.array_equal(x, u.astype(np.float32) - np.float32(127.5))
+    got = torch.from_numpy(x * k).to(torch.bfloat16)
+    want = torch.from_numpy(x / np.float32(127.5)).to(torch.bfloat16)
+    assert torch.equal(got.view(torch.int16), want.view(torch.int16))
+
+
 def test_pack_layout_is_the_patch_merge_order():
     """Hand-checked elements of the packing: patch rows in 2x2 merge-group order, channel
     planes of 512, both temporal copies equal."""
