@@ -9,9 +9,12 @@ serialises calls).  Behind them the B200 engine runs the prefill + scoring path.
 
 What lies before the path in the reference -- image decode, resize, vision tower,
 tokenizer (`_family/depth_runtime.py:54-82`) -- is outside this package: `predict` takes
-it from an `encoder(image, question, candidates) -> Request` callable.  Bundles with a
-`synthetic` block (seeded random weights, no checkpoint files) get a deterministic
-synthetic encoder so the whole surface runs without model assets.  `prefill_score` is the
+it from an `encoder(image, question, candidates) -> Request` callable.  Checkpoint bundles
+(the reference's `configs/*.json`: `model` = a Hugging Face Qwen3-VL directory, the recovery
+`checkpoint`, the calibration `profile_path`) load the language decoder's weights from the
+safetensors files (`fastforward_b200.checkpoint`); bundles with a `synthetic` block (seeded
+random weights, no checkpoint files) get a deterministic synthetic encoder so the whole
+surface runs without model assets.  `prefill_score` is the
 internal entry that `predict` calls after the encoder; benchmarks call it directly.
 """
 import hashlib
@@ -111,12 +114,7 @@ class Accelerator:
             raise ValueError("Unknown backend")
         synthetic = c.get("synthetic")
         if synthetic is None:
-            for key in ("model", "checkpoint"):
-                if not Path(c[key]).exists():
-                    raise FileNotFoundError(c[key])
-            if sha256(c["checkpoint"]) != c["checkpoint_sha256"]:
-                raise ValueError("Recovery checkpoint SHA256 mismatch")
-            raise ValueError("Checkpoint loading is not part of this package; use a synthetic bundle")
+            self._check_assets(c)
         import torch
         if not torch.cuda.is_available():
             raise RuntimeError("A CUDA GPU is required; CPU fallback is disabled")
@@ -132,25 +130,70 @@ class Accelerator:
         self.backend = backend
         self.lock = threading.RLock()
         self.device = dev
-        self.dims = MODELS[synthetic["model"]]
         self.buckets = tuple(c.get("buckets", BUCKETS))
-        mode = synthetic.get("mode", "rowwise")
-        layers = synthetic.get("layers")
-        lay = synthetic.get("layout", {})
-        self.layout = Layout(int(lay.get("image_start", 0)), int(lay.get("grid_h", 32)), int(lay.get("grid_w", 32)),
-                             int(lay.get("n_text", 64)))
+        if synthetic is not None:
+            self.dims = MODELS[synthetic["model"]]
+            mode = synthetic.get("mode", "rowwise")
+            lay = synthetic.get("layout", {})
+            self.layout = Layout(int(lay.get("image_start", 0)), int(lay.get("grid_h", 32)),
+                                 int(lay.get("grid_w", 32)), int(lay.get("n_text", 64)))
+        else:
+            mode = self._checkpoint_mode(c)
+            self.layout = None
         profile = self._read_profile(c) if mode == "static" else None
         with torch.cuda.device(dev), torch.no_grad():
-            src = make_model_bf16(self.dims, seed=int(synthetic.get("seed", 0)), device=dev, layers=layers)
-            if mode == "static" and profile is None and synthetic.get("calibrate"):
-                profile = self._calibrate(src, int(synthetic["calibrate"]), float(c.get("fp8_calibration_margin", 1.5)))
+            if synthetic is not None:
+                src = make_model_bf16(self.dims, seed=int(synthetic.get("seed", 0)), device=dev,
+                                      layers=synthetic.get("layers"))
+                if mode == "static" and profile is None and synthetic.get("calibrate"):
+                    profile = self._calibrate(src, int(synthetic["calibrate"]),
+                                              float(c.get("fp8_calibration_margin", 1.5)))
+            else:
+                from .checkpoint import load_language_model
+                self.dims, src = load_language_model(c["model"], device=dev, option_ids=c.get("option_ids"),
+                                                      expected_dimensions=c.get("expected_dimensions"))
+                if mode == "static" and profile is None:
+                    raise ValueError("execution_mode fp8 needs the bundle's calibration profile (profile_path)")
             self.profile = profile
             self.model = PackedModel(self.dims, src, mode=mode, device=dev, free_source=True, profile=profile)
             del src
             torch.cuda.empty_cache()
             self.engine = Engine(self.model)
-        self.encoder = encoder or SyntheticEncoder(self.dims, self.layout)
+        if encoder is None and synthetic is not None:
+            encoder = SyntheticEncoder(self.dims, self.layout)
+        self.encoder = encoder
         self._staging = {}
+
+    # ------------------------------------------------------------------ checkpoint bundles
+    @staticmethod
+    def _check_assets(c):
+        """The reference's checks of a checkpoint bundle (`api.py:56-66`,
+        `_family/family_api.py:19-23`): the model directory and the recovery checkpoint
+        exist, the checkpoint's SHA256 matches, and its repair adapter is zero (the serving
+        path applies it as the identity, `_family/night_runtime.py:88-94`)."""
+        for key in ("model", "checkpoint"):
+            if not Path(c[key]).exists():
+                raise FileNotFoundError(c[key])
+        if sha256(c["checkpoint"]) != c["checkpoint_sha256"]:
+            raise ValueError("Recovery checkpoint SHA256 mismatch")
+        import torch
+        state = torch.load(c["checkpoint"], map_location="cpu", weights_only=True)
+        state = state.get("state_dict", state)
+        for key in ("up", "bias"):
+            if key not in state or torch.count_nonzero(state[key]) != 0:
+                raise ValueError(f"The recovery adapter's {key!r} is not zero; only the identity adapter is served")
+
+    @staticmethod
+    def _checkpoint_mode(c):
+        """Weight format of a checkpoint bundle: `execution_mode` "fp8" is the reference's
+        static-scale FP8 (`RuntimeScaleLinear` with the profile's bounds,
+        `_family/family_api.py:27-31`), "fp8_rowwise" the per-row scheme
+        (`_legacy/fp8_private.py`), "int4" the W4A16 path."""
+        em = c.get("execution_mode", "fp8")
+        modes = {"fp8": "static", "fp8_rowwise": "rowwise", "int4": "int4"}
+        if em not in modes:
+            raise ValueError(f"Unsupported execution_mode {em!r}")
+        return modes[em]
 
     # ------------------------------------------------------------------ static FP8 profile
     @staticmethod
@@ -317,6 +360,9 @@ class Accelerator:
         mode = self.backend if backend is None else backend
         if mode not in BACKENDS:
             raise ValueError("Unknown backend")
+        if self.encoder is None:
+            raise RuntimeError("No encoder: the vision tower and tokenizer are outside this package; construct the "
+                               "Accelerator with encoder=callable(image, question, candidates) -> Request")
         with self.lock:
             r = self.encoder(str(image), question, list(candidates))
             z, lp = self.prefill_score(r.ids, r.visual, r.deep, len(candidates), r.image_start, r.grid_h,
