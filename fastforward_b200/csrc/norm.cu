@@ -75,42 +75,77 @@ struct NormArgs {
   int add;  // 0: plain RMSNorm of a
 };
 
-template <int V>
+// S >= 1: b is the sum of S fp32 split-K partial planes (all loads issued before the first
+// add, summed in plane order); S == 0: b is bf16 (or there is no add); S == -1: any number
+// of planes, loaded plane by plane.
+template <int V, int S>
 __global__ void __launch_bounds__(MAXT) add_rmsnorm_kernel(const NormArgs p) {
   __shared__ float red[MAXT / 32];
   __shared__ double redd[MAXT / 32];
   const int NT = blockDim.x;
-  pdl_wait();
-  pdl_launch();
   const int row = blockIdx.x;
   const int nvec = p.H / 8;
   const size_t base = (size_t)row * p.H;
+  // the norm weight does not depend on the previous kernel: fetch it before waiting
+  float w[V][8];
+#pragma unroll
+  for (int i = 0; i < V; ++i) {
+    const int v = threadIdx.x + i * NT;
+    if (v < nvec) load8(p.w + v * 8, w[i]);
+  }
+  pdl_wait();
+  pdl_launch();
   const bool deep_row = p.deep && row >= p.start && row < p.start + p.nv;
-  float x[V][8];
-  double ss = 0.0;
+  float x[V][8], b[V][8];
+  constexpr int SP = S > 0 ? S : 1;
+  float4 part[V][SP][2];
+  // every load of the row in flight before the first use
 #pragma unroll
   for (int i = 0; i < V; ++i) {
     const int v = threadIdx.x + i * NT;
     if (v < nvec) {
       load8(p.a + base + v * 8, x[i]);
       if (p.add) {
-        float b[8];
-        if (p.b) {
-          load8(p.b + base + v * 8, b);
-        } else {
+        if constexpr (S == 0) {
+          load8(p.b + base + v * 8, b[i]);
+        } else if constexpr (S > 0) {
 #pragma unroll
-          for (int e = 0; e < 8; ++e) b[e] = 0.f;
-          for (int s = 0; s < p.splits; ++s) {
+          for (int s = 0; s < S; ++s) {
             const float4* src = reinterpret_cast<const float4*>(p.b32 + (size_t)s * p.T * p.H + base + v * 8);
-            const float4 lo = src[0], hi = src[1];
-            b[0] += lo.x; b[1] += lo.y; b[2] += lo.z; b[3] += lo.w;
-            b[4] += hi.x; b[5] += hi.y; b[6] += hi.z; b[7] += hi.w;
+            part[i][s][0] = src[0];
+            part[i][s][1] = src[1];
+          }
+        }
+      }
+    }
+  }
+  double ss = 0.0;
+#pragma unroll
+  for (int i = 0; i < V; ++i) {
+    const int v = threadIdx.x + i * NT;
+    if (v < nvec) {
+      if (p.add) {
+        if constexpr (S != 0) {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) b[i][e] = 0.f;
+          auto add_plane = [&](const float4 lo, const float4 hi) {
+            b[i][0] += lo.x; b[i][1] += lo.y; b[i][2] += lo.z; b[i][3] += lo.w;
+            b[i][4] += hi.x; b[i][5] += hi.y; b[i][6] += hi.z; b[i][7] += hi.w;
+          };
+          if constexpr (S > 0) {
+#pragma unroll
+            for (int s = 0; s < S; ++s) add_plane(part[i][s][0], part[i][s][1]);
+          } else {
+            for (int s = 0; s < p.splits; ++s) {
+              const float4* src = reinterpret_cast<const float4*>(p.b32 + (size_t)s * p.T * p.H + base + v * 8);
+              add_plane(src[0], src[1]);
+            }
           }
 #pragma unroll
-          for (int e = 0; e < 8; ++e) b[e] = round_bf(b[e]);  // the linear's bf16 output
+          for (int e = 0; e < 8; ++e) b[i][e] = round_bf(b[i][e]);  // the linear's bf16 output
         }
 #pragma unroll
-        for (int e = 0; e < 8; ++e) x[i][e] = round_bf(x[i][e] + b[e]);
+        for (int e = 0; e < 8; ++e) x[i][e] = round_bf(x[i][e] + b[i][e]);
         if (deep_row) {
           float d[8];
           load8(p.deep + (size_t)(row - p.start) * p.H + v * 8, d);
@@ -129,11 +164,9 @@ __global__ void __launch_bounds__(MAXT) add_rmsnorm_kernel(const NormArgs p) {
   for (int i = 0; i < V; ++i) {
     const int v = threadIdx.x + i * NT;
     if (v < nvec) {
-      float w[8];
-      load8(p.w + v * 8, w);
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
-        x[i][e] = round_bf(round_bf(x[i][e] * inv) * w[e]);
+        x[i][e] = round_bf(round_bf(x[i][e] * inv) * w[i][e]);
         amax = fmaxf(amax, fabsf(x[i][e]));
       }
       if (p.out) store8(p.out + base + v * 8, x[i]);
@@ -177,7 +210,18 @@ int run(const NormArgs& p, const char* who, void* stream) {
   const int nvec = p.H / 8;
   int nt = (nvec + 1) / 2;     // two vectors per thread
   nt = (nt + 31) / 32 * 32;    // whole warps
-  cudaError_t e = ffb::launch(add_rmsnorm_kernel<MAXV>, dim3(p.T), dim3(nt), 0, (cudaStream_t)stream, p);
+  const bool planes = p.add && !p.b;
+  const int sp = planes ? p.splits : 0;
+  auto kernel = add_rmsnorm_kernel<MAXV, -1>;
+  switch (sp) {
+    case 0: kernel = add_rmsnorm_kernel<MAXV, 0>; break;
+    case 1: kernel = add_rmsnorm_kernel<MAXV, 1>; break;
+    case 2: kernel = add_rmsnorm_kernel<MAXV, 2>; break;
+    case 3: kernel = add_rmsnorm_kernel<MAXV, 3>; break;
+    case 4: kernel = add_rmsnorm_kernel<MAXV, 4>; break;
+    default: break;
+  }
+  cudaError_t e = ffb::launch(kernel, dim3(p.T), dim3(nt), 0, (cudaStream_t)stream, p);
   if (e != cudaSuccess) return ffb::fail(FFB_ECUDA, "%s: launch: %s", who, cudaGetErrorString(e));
   return FFB_OK;
 }

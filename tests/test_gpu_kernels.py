@@ -81,6 +81,29 @@ def test_add_rmsnorm_deep(T, H, start, nv):
     assert_bytes_equal(y, yy, "normed")
 
 
+@pytest.mark.parametrize("S", [1, 2, 4, 5, 8])
+def test_add_rmsnorm_partial_planes_in_plane_order(S):
+    """The split-K planes are summed in plane order from 0 (fp32), then rounded to bf16 --
+    bit-exact for every split count (the kernel loads up to 4 planes at once, more plane by
+    plane)."""
+    T, H = 24, 2560
+    a = _randn((T, H), 17)
+    parts = torch.randn((S, T, H), generator=_g(18)) * 0.5
+    w = (1 + 0.1 * torch.randn(H, generator=_g(19))).to(BF16)
+    res = torch.empty((T, H), device=DEV, dtype=BF16)
+    out = torch.empty((T, H), device=DEV, dtype=BF16)
+    a_d, p_d, w_d = a.to(DEV), parts.to(DEV), w.to(DEV)  # referenced until the kernel has run
+    call("ffb_add_rmsnorm", ptr(a_d), None, ptr(p_d), S, None, 0, 0, ptr(w_d), 1e-6, ptr(res), ptr(out),
+         L.QUANT_NONE, 0.0, None, None, T, H, _sp())
+    torch.cuda.synchronize()
+    acc = torch.zeros((T, H))
+    for s in range(S):
+        acc = acc + parts[s]
+    rr, yy = oracle.add_rms(a, acc.to(BF16), None, w, 1e-6)
+    assert_bytes_equal(res, rr, f"residual, {S} planes")
+    assert_bytes_equal(out, yy, f"normed, {S} planes")
+
+
 @pytest.mark.parametrize("mode", [L.QUANT_ROWWISE, L.QUANT_STATIC])
 def test_add_rmsnorm_partials_and_fused_quant(mode):
     T, H, S = 40, 2560, 3
