@@ -44,6 +44,7 @@ SIGNATURES = {
     "ffb_quantize_weight_fp8_noalloc": [P, I, P, P, I, I, P],
     "ffb_fp8_gemm": [P, P, I, P, P, I, I, P, P, I, I, I, I, I, P],
     "ffb_fp8_gemm_qk_rope": [P, P, I, P, P, I, P, P, F, P, P, P, P, P, I, I, I, I, P],
+    "ffb_fp8_gemm_swiglu_fp8": [P, P, I, P, P, I, F, P, I, I, I, P],
     "ffb_fp8_gemm_fused": [P, P, P, I, P, P, I, I, P, P, I, I, I, I, I, P],
     "ffb_fp8_gemm_qk_rope_fused": [P, P, P, I, P, P, I, P, P, F, P, P, P, P, P, I, I, I, I, P],
     "ffb_pack_gateup": [P, P, I, I, I, P],

@@ -135,14 +135,19 @@ int make_tmap_out(CUtensorMap* map, const void* base, int elem_bytes, uint64_t i
   if (row_bytes % 16 != 0 || depth_bytes % 16 != 0)
     return fail(FFB_EINVAL, "TMA strides (%llu, %llu bytes) must be multiples of 16", (unsigned long long)row_bytes,
                 (unsigned long long)depth_bytes);
-  if ((uint64_t)box_inner * elem_bytes != 64) return fail(FFB_EINVAL, "store box must be 64 bytes wide");
-  const CUtensorMapDataType dt = elem_bytes == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  // 16/32-bit elements: 64-byte boxes with the 64-byte swizzle; bytes: 32-byte unswizzled boxes
+  if ((uint64_t)box_inner * elem_bytes != (elem_bytes == 1 ? 32u : 64u))
+    return fail(FFB_EINVAL, "store box must be %d bytes wide", elem_bytes == 1 ? 32 : 64);
+  const CUtensorMapDataType dt = elem_bytes == 4   ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                 : elem_bytes == 1 ? CU_TENSOR_MAP_DATA_TYPE_UINT8
+                                                   : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   cuuint64_t dims[3] = {inner, rows, depth};
   cuuint64_t strides[2] = {row_bytes, depth_bytes};
   cuuint32_t box[3] = {box_inner, box_rows, 1};
   cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = fn(map, dt, 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                  CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                  elem_bytes == 1 ? CU_TENSOR_MAP_SWIZZLE_NONE : CU_TENSOR_MAP_SWIZZLE_64B,
+                  CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(FFB_ECUDA, "cuTensorMapEncodeTiled (store) failed (%d)", (int)r);
   return FFB_OK;
 }

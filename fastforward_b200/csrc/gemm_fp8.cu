@@ -39,6 +39,7 @@ constexpr int UMMA_K = 32;   // K per tcgen05.mma for 8-bit operands
 constexpr int A_TILE_BYTES = BM * BK;
 constexpr int SMEM_LIMIT = 232448;
 constexpr int EPI_QKROPE = 100;  // internal epilogue code of ffb_fp8_gemm_qk_rope
+constexpr int EPI_SWIGLU_Q8 = 101;  // internal epilogue code of ffb_fp8_gemm_swiglu_fp8
 // Epilogue warps per instance: four per TMEM lane quarter.
 __host__ __device__ constexpr int epi_warps(int) { return 16; }
 __host__ __device__ constexpr int threads_of(int epi) { return 64 + epi_warps(epi) * 32; }
@@ -93,6 +94,7 @@ struct GemmArgs {
   float* ws;
   int a_per_row, w_per_col, epilogue;
   int M, N, K, n_ttiles, splits, n_tiles;
+  float out_inv;  // EPI_SWIGLU_Q8: static inverse scale of the next linear's input
   RopeSide rope;
   ProArgs pro;
 };
@@ -453,7 +455,7 @@ __global__ void __launch_bounds__(threads_of(EPI), 1)
     fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_w,
                     const __grid_constant__ CUtensorMap tmap_o, const GemmArgs args) {
   static_assert(EPI != EPI_QKROPE || BN == 128, "one head per tile");
-  static_assert(EPI != FFB_EPI_SWIGLU || BN == 256, "gate/up pairs of 128 channels per tile");
+  static_assert((EPI != FFB_EPI_SWIGLU && EPI != EPI_SWIGLU_Q8) || BN == 256, "gate/up pairs of 128 channels per tile");
   constexpr int EPI_WARPS = epi_warps(EPI);
   constexpr int BUFS = 16 / EPI_WARPS;  // staging buffers per epilogue warp
   using C = Cfg<BN>;
@@ -755,15 +757,36 @@ __global__ void __launch_bounds__(threads_of(EPI), 1)
           }
           ++sc;
         };
-        if constexpr (EPI == FFB_EPI_SWIGLU) {
+        // The same for a [32 tokens x 32 B] chunk of e4m3 bytes (unswizzled 32-byte rows).
+        auto staged_store8 = [&](const uint32_t (&w8)[8], int x) {
+          uint8_t* sb = stg_all + ((warp - 2) * BUFS + (int)(sc % BUFS)) * 2048;
+          if (lane == 0) {
+            if constexpr (BUFS == 2) bulk_wait_read<1>();
+            else bulk_wait_read<0>();
+          }
+          __syncwarp();
+          *reinterpret_cast<uint4*>(sb + lane * 32) = make_uint4(w8[0], w8[1], w8[2], w8[3]);
+          *reinterpret_cast<uint4*>(sb + lane * 32 + 16) = make_uint4(w8[4], w8[5], w8[6], w8[7]);
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_3d(&tmap_o, sb, x, tt * BM + q * 32, 0);
+            bulk_commit();
+          }
+          ++sc;
+        };
+        if constexpr (EPI == FFB_EPI_SWIGLU || EPI == EPI_SWIGLU_Q8) {
           // columns [0, BN/2) are gate channels ft*BN/2 + j, [BN/2, BN) the matching up rows;
-          // 8 channels at a time, the next group's TMEM loads in flight during the math
+          // 8 channels at a time, the next group's TMEM loads in flight during the math.
+          // EPI_SWIGLU_Q8 stores e4m3(clamp(bf16 output * out_inv, +-448)) instead: the static
+          // FP8 quantisation of the down projection's input, done here instead of its own launch
           constexpr int HALFC = BN / 2;
           constexpr int PER_WARP = HALFC / (EPI_WARPS / 4);  // gate channels per warp
           const int cb = half * PER_WARP;
 #pragma unroll 1
           for (int c0 = cb; c0 < cb + PER_WARP; c0 += 32) {
             uint32_t o[16];
+            uint32_t o8[8];  // EPI_SWIGLU_Q8: 32 e4m3 bytes
             uint32_t g[2][8], u[2][8];
             tmem_ld8_async(acc + (uint32_t)c0, g[0]);
             tmem_ld8_async(acc + (uint32_t)(HALFC + c0), u[0]);
@@ -791,7 +814,16 @@ __global__ void __launch_bounds__(threads_of(EPI), 1)
                   const float uv = round_bf(__uint_as_float(u[cur][j + h]) * sa * wu[j + h]);  // bf16 up
                   y2[h] = act[j + h] * uv;
                 }
-                o[grp * 4 + (j >> 1)] = pack2(y2[0], y2[1]);
+                if constexpr (EPI == EPI_SWIGLU_Q8) {
+                  uint32_t qb = 0;
+#pragma unroll
+                  for (int h = 0; h < 2; ++h)
+                    qb |= (uint32_t)f2e4m3(clamp448(round_bf(y2[h]) * args.out_inv)) << (8 * ((j + h) & 3));
+                  if ((j & 3) == 0) o8[grp * 2 + (j >> 2)] = qb;
+                  else o8[grp * 2 + (j >> 2)] |= qb;
+                } else {
+                  o[grp * 4 + (j >> 1)] = pack2(y2[0], y2[1]);
+                }
               }
               if (grp < 3) {
                 tmem_wait_ld();
@@ -799,7 +831,8 @@ __global__ void __launch_bounds__(threads_of(EPI), 1)
                 reg_fence(u[cur ^ 1]);
               }
             }
-            staged_store(o, ft * HALFC + c0, 0);
+            if constexpr (EPI == EPI_SWIGLU_Q8) staged_store8(o8, ft * HALFC + c0);
+            else staged_store(o, ft * HALFC + c0, 0);
           }
         } else if constexpr (EPI == FFB_EPI_F32_PARTIAL) {
           constexpr int SHARE = BN / (EPI_WARPS / 4);  // columns per warp
@@ -916,6 +949,8 @@ cudaError_t launch_epi(const CUtensorMap& ta, const CUtensorMap& tw, const CUten
       return launch_instance<128, FFB_EPI_F32_PARTIAL, PRO>(ta, tw, to, ga, grid, stream);
   } else {
     if (ga.epilogue == FFB_EPI_SWIGLU) return launch_instance<256, FFB_EPI_SWIGLU, PRO>(ta, tw, to, ga, grid, stream);
+    if constexpr (PRO == PRO_NONE)
+      if (ga.epilogue == EPI_SWIGLU_Q8) return launch_instance<256, EPI_SWIGLU_Q8, PRO>(ta, tw, to, ga, grid, stream);
     if (ga.epilogue == FFB_EPI_BF16) return launch_instance<256, FFB_EPI_BF16, PRO>(ta, tw, to, ga, grid, stream);
     if (ga.epilogue == FFB_EPI_F32_PARTIAL)
       return launch_instance<256, FFB_EPI_F32_PARTIAL, PRO>(ta, tw, to, ga, grid, stream);
@@ -933,6 +968,8 @@ int launch_bn(const uint8_t* a8, const uint8_t* w8, GemmArgs& ga, int pro, cudaS
     rc = ffb::make_tmap_out(&to, ga.out, 2, ga.N, ga.M, 1, (uint64_t)ga.N * 2, (uint64_t)ga.N * ga.M * 2, 32, 32);
   if (!rc && ga.epilogue == FFB_EPI_SWIGLU)
     rc = ffb::make_tmap_out(&to, ga.out, 2, ga.N / 2, ga.M, 1, (uint64_t)ga.N, (uint64_t)ga.N * ga.M, 32, 32);
+  if (!rc && ga.epilogue == EPI_SWIGLU_Q8)
+    rc = ffb::make_tmap_out(&to, ga.out, 1, ga.N / 2, ga.M, 1, (uint64_t)ga.N / 2, (uint64_t)ga.N / 2 * ga.M, 32, 32);
   if (!rc && ga.epilogue == FFB_EPI_F32_PARTIAL)
     rc = ffb::make_tmap_out(&to, ga.ws, 4, ga.N, ga.M, ga.splits, (uint64_t)ga.N * 4, (uint64_t)ga.N * ga.M * 4, 16,
                             32);
@@ -940,7 +977,7 @@ int launch_bn(const uint8_t* a8, const uint8_t* w8, GemmArgs& ga, int pro, cudaS
   ga.n_ttiles = (ga.M + BM - 1) / BM;
   ga.n_tiles = (ga.N / BN) * ga.splits * ga.n_ttiles;
   const int grid = ga.n_tiles < num_sms() ? ga.n_tiles : num_sms();
-  if (ga.epilogue == FFB_EPI_SWIGLU) {
+  if (ga.epilogue == FFB_EPI_SWIGLU || ga.epilogue == EPI_SWIGLU_Q8) {
     rc = ffb::ensure_silu_table(stream);
     if (rc) return rc;
   }
@@ -1093,6 +1130,21 @@ extern "C" int ffb_fp8_gemm(const uint8_t* a8, const float* a_scale, int a_per_r
   if (rc) return rc;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   return bn == 256 ? launch_bn<256>(a8, w8, ga, PRO_NONE, s) : launch_bn<128>(a8, w8, ga, PRO_NONE, s);
+}
+
+extern "C" int ffb_fp8_gemm_swiglu_fp8(const uint8_t* a8, const float* a_scale, int a_per_row, const uint8_t* w8,
+                                       const float* w_scale, int w_per_col, float out_inv, uint8_t* out8, int M,
+                                       int N, int K, void* stream) {
+  GemmArgs ga;
+  int bn = 0;
+  FFB_REQUIRE(out8 != nullptr && ffb::aligned(out8, 16), "ffb_fp8_gemm_swiglu_fp8: out8 must be 16-byte aligned");
+  FFB_REQUIRE(out_inv > 0.f, "ffb_fp8_gemm_swiglu_fp8: out_inv must be positive");
+  int rc = prep_gemm(ga, bn, a8, a_scale, a_per_row, w8, w_scale, w_per_col, FFB_EPI_SWIGLU,
+                     reinterpret_cast<uint16_t*>(out8), nullptr, 1, 256, M, N, K);
+  if (rc) return rc;
+  ga.epilogue = EPI_SWIGLU_Q8;
+  ga.out_inv = out_inv;
+  return launch_bn<256>(a8, w8, ga, PRO_NONE, reinterpret_cast<cudaStream_t>(stream));
 }
 
 extern "C" int ffb_fp8_gemm_fused(const ffb_gemm_prologue* pro, uint8_t* a8, float* a_scale, int a_per_row,

@@ -306,6 +306,9 @@ class Engine:
         if mode_ not in ("none", "tail", "all"):
             raise ValueError(f"fuse must be 'none', 'tail' or 'all', not {fuse!r}")
         self.fuse = "none" if model.mode == "int4" else mode_
+        # static scales: the gate/up launch also writes the down projection's FP8 input
+        # (`ffb_fp8_gemm_swiglu_fp8`), so the activation quantiser has no launch of its own
+        self.static_q8 = model.mode == "static" and self.fuse != "none"
         L.set_pdl(pdl)
 
     # ------------------------------------------------------------------ plans / buffers
@@ -399,6 +402,12 @@ class Engine:
              int(lin["scale"].numel() > 1), plan.epilogue, ptr(out) if plan.epilogue != L.EPI_F32_PARTIAL else None,
              ptr(ws) if plan.epilogue == L.EPI_F32_PARTIAL else None, plan.splits, plan.bn, plan.m, plan.n, plan.k,
              self._s)
+
+    def _gemm_swiglu_q8(self, plan, a8, ascale, lin, out_inv, out8):
+        """gate/up GEMM + SwiGLU + the down projection's static FP8 quantisation in one launch;
+        byte-identical to the SwiGLU epilogue followed by `ffb_quantize_fp8` (STATIC)."""
+        call("ffb_fp8_gemm_swiglu_fp8", ptr(a8), ptr(ascale), 0, ptr(lin["w8"]), ptr(lin["scale"]),
+             int(lin["scale"].numel() > 1), float(out_inv), ptr(out8), plan.m, plan.n, plan.k, self._s)
 
     def _pro_quant(self, x, qmode, inv, b):
         """Prologue quantising bf16 rows x (the former ffb_quantize_fp8 launch)."""
@@ -542,15 +551,19 @@ class Engine:
             p = pl[("full", "gateup")]
             if int4:
                 self._w4(p, b.postb, lay.lin["gateup"], b.act, b.ws)
+            elif self.static_q8:
+                self._gemm_swiglu_q8(p, b.post8, sa(lay, "gateup", b.posts), lay.lin["gateup"], lay.inv["down"],
+                                     b.act8)
             else:
                 self._gemm(p, b.post8, sa(lay, "gateup", b.posts), lay.lin["gateup"], b.act, b.ws, rowwise)
             p = pl[("full", "down")]
             if int4:
                 self._w4(p, b.act, lay.lin["down"], b.lin_out, b.ws)
             else:
-                call("ffb_quantize_fp8", ptr(b.act), qmode, lay.inv["down"], ptr(b.act8), ptr(b.acts), T, I,
-                     self._s)
-                obs(j, "down", b.acts, T)
+                if not self.static_q8:
+                    call("ffb_quantize_fp8", ptr(b.act), qmode, lay.inv["down"], ptr(b.act8), ptr(b.acts), T, I,
+                         self._s)
+                    obs(j, "down", b.acts, T)
                 self._gemm(p, b.act8, sa(lay, "down", b.acts), lay.lin["down"], b.lin_out, b.ws, rowwise)
             self._tp_reduce(p, b.ws)
             db, d32, ds = self._split_args(p, b.lin_out, b.ws)
@@ -809,10 +822,14 @@ class Engine:
             ob, o32, os_ = self._split_args(p, b.lin_out, b.ws)
             call("ffb_add_rmsnorm", ptr(h_cur), ob, o32, os_, None, 0, 0, ptr(lay.post_norm), eps, ptr(h_mid), None,
                  qmode, lay.inv["gateup"], ptr(b.post8), ptr(b.posts), T, H, self._s)
-            self._gemm(pl[("full", "gateup")], b.post8, sa(lay, "gateup", b.posts), lay.lin["gateup"], b.act, b.ws,
-                       rowwise)
+            if self.static_q8:
+                self._gemm_swiglu_q8(pl[("full", "gateup")], b.post8, sa(lay, "gateup", b.posts), lay.lin["gateup"],
+                                     lay.inv["down"], b.act8)
+            else:
+                self._gemm(pl[("full", "gateup")], b.post8, sa(lay, "gateup", b.posts), lay.lin["gateup"], b.act,
+                           b.ws, rowwise)
+                call("ffb_quantize_fp8", ptr(b.act), qmode, lay.inv["down"], ptr(b.act8), ptr(b.acts), T, I, self._s)
             p = pl[("full", "down")]
-            call("ffb_quantize_fp8", ptr(b.act), qmode, lay.inv["down"], ptr(b.act8), ptr(b.acts), T, I, self._s)
             self._gemm(p, b.act8, sa(lay, "down", b.acts), lay.lin["down"], b.lin_out, b.ws, rowwise)
             db, d32, ds = self._split_args(p, b.lin_out, b.ws)
             dp = b.deep[j] if j < len(b.deep) else None
@@ -842,7 +859,7 @@ class Engine:
 
     def launches_per_batch(self, R):
         """Kernel launches of `forward_batch` for R requests (embed and readout per request)."""
-        per_layer = 9
+        per_layer = 8 if self.static_q8 else 9
         return R + 1 + per_layer * (self.m.depth - 1) + 1 + 1 + 2 + 1 + 1 + 2 + R
 
     def launches_per_forward(self):
@@ -850,7 +867,7 @@ class Engine:
         tail = 6 if self.fuse != "none" else 9  # attention, (quant,) o, gather, (add+norm,) gate/up, (quant,) down, readout
         if self.fuse == "all":  # embed, 5 per layer, the last layer's qkv, tail
             return 1 + 5 * (self.m.depth - 1) + 1 + tail
-        per_layer = 9 if self.m.mode != "int4" else 8
+        per_layer = 9 if self.m.mode != "int4" and not self.static_q8 else 8
         if self.m.mode == "int4":
             tail = 8
         return 2 + per_layer * (self.m.depth - 1) + 1 + tail

@@ -233,6 +233,17 @@ int ffb_fp8_gemm_qk_rope_fused(const ffb_gemm_prologue* pro, uint8_t* a8, float*
                                uint16_t* yq, uint16_t* yk, uint16_t* yv,
                                int T, int HQ, int HK, int K, void* stream);
 
+/* Gate/up GEMM with the SwiGLU epilogue followed by the STATIC FP8 quantisation of the down
+ * projection's input, in one launch: out8[m,c] = e4m3(clamp(bf16(bf16(silu(g)) * u) * out_inv,
+ * +-448)) (u8 [M, N/2]), byte-identical to FFB_EPI_SWIGLU followed by ffb_quantize_fp8
+ * (FFB_QUANT_STATIC, out_inv).  Replaces `swiglu` (_legacy/search_kernels.py:18-23) plus the
+ * down projection's `_runtime_scale` (_family/depth_fp8.py:8-12) on the static-scale path.
+ * Operands and scales as ffb_fp8_gemm with the gate/up interleave of ffb_pack_gateup;
+ * feature tile 256; out_inv > 0. */
+int ffb_fp8_gemm_swiglu_fp8(const uint8_t* a8, const float* a_scale, int a_per_row,
+                            const uint8_t* w8, const float* w_scale, int w_per_col, float out_inv,
+                            uint8_t* out8, int M, int N, int K, void* stream);
+
 /* Reorders the rows of a [2I,K] gate/up weight (gate rows 0..I-1, up rows I..2I-1) into
  * the FFB_EPI_SWIGLU tile order: tile t = gate rows 128t..128t+127 then up rows
  * 128t..128t+127 (I must be a multiple of 128).  Works on rows of `elem_bytes`*K bytes:

@@ -234,6 +234,42 @@ def test_fp8_gemm_swiglu_epilogue(M, I):
     assert_bytes_equal(out, want, "swiglu epilogue")
 
 
+@pytest.mark.parametrize("M,I,a_per_row", [(320, 9728, 0), (57, 512, 0), (1, 768, 0), (200, 1024, 1)])
+def test_fp8_gemm_swiglu_fp8_is_swiglu_then_static_quant(M, I, a_per_row):
+    """The fused SwiGLU + static FP8 output (`ffb_fp8_gemm_swiglu_fp8`) writes exactly the
+    bytes of the SwiGLU epilogue followed by `ffb_quantize_fp8` (STATIC), with rows of the
+    last token tile clipped; the oracle's static quantiser of the same SwiGLU output agrees."""
+    K = 2560
+    x = _randn((M, K), 25)
+    w = _randn((2 * I, K), 26, std=0.02)
+    if a_per_row:
+        q, sa = oracle.quantize_rows(x)
+    else:
+        inv_in = 448.0 / 6.0
+        q, sa = oracle.quantize_static(x, inv_in), torch.tensor([1.0 / inv_in])
+    w_d = w.to(DEV)
+    packed = torch.empty_like(w_d)
+    call("ffb_pack_gateup", ptr(w_d), ptr(packed), I, K, 2, _sp())
+    w8p, swp = ops.quantize_weight(packed, per_channel=True)
+    q_d, sa_d = _keep(q.to(DEV)), _keep(sa.to(DEV))
+    act = torch.empty((M, I), device=DEV, dtype=BF16)
+    call("ffb_fp8_gemm", ptr(q_d), ptr(sa_d), a_per_row, ptr(w8p), ptr(swp), 1, L.EPI_SWIGLU, ptr(act), None, 1, 0, M,
+         2 * I, K, _sp())
+    inv = 448.0 / 0.35
+    want8 = torch.empty((M, I), device=DEV, dtype=E4M3)
+    call("ffb_quantize_fp8", ptr(act), L.QUANT_STATIC, inv, ptr(want8), None, M, I, _sp())
+    got8 = torch.full((M + 1, I), 0x7F, device=DEV, dtype=torch.uint8)  # a guard row after the output
+    call("ffb_fp8_gemm_swiglu_fp8", ptr(q_d), ptr(sa_d), a_per_row, ptr(w8p), ptr(swp), 1, inv, ptr(got8), M, 2 * I,
+         K, _sp())
+    torch.cuda.synchronize()
+    assert_bytes_equal(got8[:M], want8, "fused swiglu + static quant")
+    assert bool((got8[M] == 0x7F).all()), "wrote past the last row"
+    assert_bytes_equal(got8[:M], oracle.quantize_static(act.cpu(), inv)[:M], "oracle static quantiser")
+    with pytest.raises(ValueError):
+        call("ffb_fp8_gemm_swiglu_fp8", ptr(q_d), ptr(sa_d), a_per_row, ptr(w8p), ptr(swp), 1, 0.0, ptr(got8), M,
+             2 * I, K, _sp())
+
+
 def test_swiglu_epilogue_every_bf16_gate():
     """The SwiGLU epilogues look the activation bf16(g / (1 + exp(-g))) up by the bf16 gate's
     bits; the table must equal the formula evaluated on the device (the standalone swiglu
