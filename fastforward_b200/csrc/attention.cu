@@ -282,8 +282,8 @@ __global__ void __launch_bounds__(128) attention_kernel(const AttnArgs p) {
 
 }  // namespace
 
-int ffb_attention_tc(const uint16_t* q, const uint16_t* k, const uint16_t* v, const int* key_lo, uint16_t* out, int T,
-                     int HQ, int HK, float scale, cudaStream_t stream);
+int ffb_attention_tc(const uint16_t* q, const uint16_t* k, const uint16_t* v, const int* key_lo, void* out, int T,
+                     int HQ, int HK, float scale, float out_inv, cudaStream_t stream);
 
 extern "C" int ffb_attention_segmented(const uint16_t* q, const uint16_t* k, const uint16_t* v,
                                        const int64_t* positions, int q_gather, const int* key_lo, uint16_t* out, int S,
@@ -297,7 +297,7 @@ extern "C" int ffb_attention_segmented(const uint16_t* q, const uint16_t* k, con
               "ffb_attention: alignment");
   FFB_REQUIRE(!key_lo || ffb::aligned(key_lo, 4), "ffb_attention: key_lo alignment");
   if (!positions && S == T && ffb::aligned(out, 16))  // causal prefill: the tcgen05 kernel
-    return ffb_attention_tc(q, k, v, key_lo, out, T, HQ, HK, scale, (cudaStream_t)stream);
+    return ffb_attention_tc(q, k, v, key_lo, out, T, HQ, HK, scale, 0.f, (cudaStream_t)stream);
   static bool attr = false;
   if (!attr) {
     cudaError_t e = cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
@@ -309,6 +309,17 @@ extern "C" int ffb_attention_segmented(const uint16_t* q, const uint16_t* k, con
                               (cudaStream_t)stream, a);
   if (e != cudaSuccess) return ffb::fail(FFB_ECUDA, "ffb_attention: %s", cudaGetErrorString(e));
   return FFB_OK;
+}
+
+extern "C" int ffb_attention_fp8(const uint16_t* q, const uint16_t* k, const uint16_t* v, const int* key_lo,
+                                 float out_inv, uint8_t* out8, int T, int HQ, int HK, float scale, void* stream) {
+  FFB_REQUIRE(q && k && v && out8, "ffb_attention_fp8: NULL pointer");
+  FFB_REQUIRE(T > 0 && HQ > 0 && HK > 0 && HQ % HK == 0, "ffb_attention_fp8: bad shape T=%d HQ=%d HK=%d", T, HQ, HK);
+  FFB_REQUIRE(out_inv > 0.f, "ffb_attention_fp8: out_inv must be positive");
+  FFB_REQUIRE(ffb::aligned(q, 16) && ffb::aligned(k, 16) && ffb::aligned(v, 16) && ffb::aligned(out8, 16),
+              "ffb_attention_fp8: alignment");
+  FFB_REQUIRE(!key_lo || ffb::aligned(key_lo, 4), "ffb_attention_fp8: key_lo alignment");
+  return ffb_attention_tc(q, k, v, key_lo, out8, T, HQ, HK, scale, out_inv, (cudaStream_t)stream);
 }
 
 extern "C" int ffb_attention(const uint16_t* q, const uint16_t* k, const uint16_t* v, const int64_t* positions,

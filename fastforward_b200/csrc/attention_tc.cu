@@ -73,6 +73,7 @@ struct TcArgs {
   const int* key_lo;  // per row: its lowest visible key (several requests in one sequence), or NULL = 0
   int T, HQ, HK;
   float scale_log2;  // scale * log2(e)
+  float out_inv;     // > 0: e4m3 output, e4m3(clamp(bf16 output * out_inv, +-448)); 0: bf16 output
 };
 
 __global__ void __launch_bounds__(THREADS, 1)
@@ -334,7 +335,31 @@ __global__ void __launch_bounds__(THREADS, 1)
     // boxes in the P tiles (every P.V has completed: the last fold waited for it), then TMA
     // stores; rows past T are clipped by the store.
     const bool stage = ok && !*abort_flag;
-    if (stage) {
+    const bool fp8_out = args.out_inv > 0.f;
+    if (stage && fp8_out) {
+      // the static FP8 quantisation of the o projection's input, applied to the bf16 output:
+      // one 128-byte-swizzled [128 rows x 128 B] box in P tile 0, this part's 32 columns
+      // as two 16-byte chunks
+      const float rl = __frcp_rn(l);
+      uint8_t* orow = sp + r * 128;
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        uint32_t w[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          uint32_t word = 0;
+#pragma unroll
+          for (int b = 0; b < 4; ++b) {
+            const float y = bf2f(bf16_quotient(o[16 * c + 4 * e + b], l, rl));
+            word |= (uint32_t)f2e4m3(clamp448(y * args.out_inv)) << (8 * b);
+          }
+          w[e] = word;
+        }
+        const int chunk = 2 * part + c;
+        *reinterpret_cast<uint4*>(orow + ((chunk ^ (r & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+      fence_proxy_async_smem();
+    } else if (stage) {
       const float rl = __frcp_rn(l);
       uint8_t* orow = sp + (part >> 1) * P_BYTES + r * 128;
 #pragma unroll
@@ -350,8 +375,12 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     named_barrier(1, SOFTMAX_WARPS * 32);
     if (warp == 2 && lane == 0 && !*abort_flag) {
-      tma_store_2d(&tmap_o, sp, h * D, q0);
-      tma_store_2d(&tmap_o, sp + P_BYTES, h * D + 64, q0);
+      if (fp8_out) {
+        tma_store_2d(&tmap_o, sp, h * D, q0);
+      } else {
+        tma_store_2d(&tmap_o, sp, h * D, q0);
+        tma_store_2d(&tmap_o, sp + P_BYTES, h * D + 64, q0);
+      }
       bulk_commit();
       bulk_wait_read<0>();  // the staging tile has been read; the writes complete with the grid
     }
@@ -377,14 +406,17 @@ __global__ void __launch_bounds__(THREADS, 1)
 
 // Causal self-attention over all T rows (q, k, v head-major [H, T, 128] bf16, out
 // [T, HQ*128]); called by ffb_attention for positions == NULL.
-int ffb_attention_tc(const uint16_t* q, const uint16_t* k, const uint16_t* v, const int* key_lo, uint16_t* out, int T,
-                     int HQ, int HK, float scale, cudaStream_t stream) {
+int ffb_attention_tc(const uint16_t* q, const uint16_t* k, const uint16_t* v, const int* key_lo, void* out, int T,
+                     int HQ, int HK, float scale, float out_inv, cudaStream_t stream) {
   CUtensorMap tq, tk, tv, to;
   int rc = ffb::make_tmap_3d_bf16(&tq, q, D, (uint64_t)T, (uint64_t)HQ, 64, BM);
   if (!rc) rc = ffb::make_tmap_3d_bf16(&tk, k, D, (uint64_t)T, (uint64_t)HK, 64, BN);
   if (!rc) rc = ffb::make_tmap_3d_bf16(&tv, v, D, (uint64_t)T, (uint64_t)HK, 64, BN);
-  // out [T, HQ*128] bf16, stored in [128 rows x 64 columns] boxes
-  if (!rc) rc = ffb::make_tmap_2d(&to, out, (uint64_t)T, (uint64_t)HQ * D, (uint64_t)HQ * D * 2, BM, 64, 2);
+  // out [T, HQ*128]: bf16 in [128 rows x 64 columns] boxes, or e4m3 in [128 x 128] boxes
+  if (!rc && out_inv > 0.f)
+    rc = ffb::make_tmap_2d(&to, out, (uint64_t)T, (uint64_t)HQ * D, (uint64_t)HQ * D, BM, 128, 1);
+  else if (!rc)
+    rc = ffb::make_tmap_2d(&to, out, (uint64_t)T, (uint64_t)HQ * D, (uint64_t)HQ * D * 2, BM, 64, 2);
   if (rc) return rc;
   static bool attr = false;
   if (!attr) {
@@ -392,7 +424,7 @@ int ffb_attention_tc(const uint16_t* q, const uint16_t* k, const uint16_t* v, co
     if (e != cudaSuccess) return ffb::fail(FFB_ECUDA, "ffb_attention: %s", cudaGetErrorString(e));
     attr = true;
   }
-  TcArgs a = {out, key_lo, T, HQ, HK, scale * 1.4426950408889634f};
+  TcArgs a = {static_cast<uint16_t*>(out), key_lo, T, HQ, HK, scale * 1.4426950408889634f, out_inv};
   cudaError_t e = ffb::launch(attention_tc_kernel, dim3((T + BM - 1) / BM, HQ), dim3(THREADS), SMEM, stream, tq, tk, tv,
                               to, a);
   if (e != cudaSuccess) return ffb::fail(FFB_ECUDA, "ffb_attention: %s", cudaGetErrorString(e));

@@ -306,8 +306,9 @@ class Engine:
         if mode_ not in ("none", "tail", "all"):
             raise ValueError(f"fuse must be 'none', 'tail' or 'all', not {fuse!r}")
         self.fuse = "none" if model.mode == "int4" else mode_
-        # static scales: the gate/up launch also writes the down projection's FP8 input
-        # (`ffb_fp8_gemm_swiglu_fp8`), so the activation quantiser has no launch of its own
+        # static scales: attention and the gate/up launch also write the FP8 input of the
+        # linear after them (`ffb_attention_fp8`, `ffb_fp8_gemm_swiglu_fp8`), so neither
+        # activation quantiser has a launch of its own
         self.static_q8 = model.mode == "static" and self.fuse != "none"
         L.set_pdl(pdl)
 
@@ -528,15 +529,20 @@ class Engine:
             nxt = m.layers[j + 1]
             # ---- attention block
             self._qkv(pl[("full", "qkv")], b, lay, cos, sin, T, int4, rowwise)
-            call("ffb_attention", ptr(b.yq), ptr(b.yk), ptr(b.yv), None, 0, ptr(b.attn), T, T, HQ, HK, scale,
-                 self._s)
+            if self.static_q8:  # attention writes the o projection's FP8 input itself
+                call("ffb_attention_fp8", ptr(b.yq), ptr(b.yk), ptr(b.yv), None, float(lay.inv["o"]), ptr(b.o8),
+                     T, HQ, HK, scale, self._s)
+            else:
+                call("ffb_attention", ptr(b.yq), ptr(b.yk), ptr(b.yv), None, 0, ptr(b.attn), T, T, HQ, HK, scale,
+                     self._s)
             p = pl[("full", "o")]
             if int4:
                 self._w4(p, b.attn, lay.lin["o"], b.lin_out, b.ws)
             else:
-                call("ffb_quantize_fp8", ptr(b.attn), qmode, lay.inv["o"], ptr(b.o8), ptr(b.os), T, HQ * D,
-                     self._s)
-                obs(j, "o", b.os, T)
+                if not self.static_q8:
+                    call("ffb_quantize_fp8", ptr(b.attn), qmode, lay.inv["o"], ptr(b.o8), ptr(b.os), T, HQ * D,
+                         self._s)
+                    obs(j, "o", b.os, T)
                 self._gemm(p, b.o8, sa(lay, "o", b.os), lay.lin["o"], b.lin_out, b.ws, rowwise)
             self._tp_reduce(p, b.ws)
             ob, o32, os_ = self._split_args(p, b.lin_out, b.ws)
@@ -814,10 +820,14 @@ class Engine:
         for j in range(depth - 1):
             lay, nxt = m.layers[j], m.layers[j + 1]
             self._qkv(pl[("full", "qkv")], b, lay, cos, sin, T, False, rowwise)
-            call("ffb_attention_segmented", ptr(b.yq), ptr(b.yk), ptr(b.yv), None, 0, ptr(b.key_lo), ptr(b.attn), T,
-                 T, HQ, HK, scale, self._s)
+            if self.static_q8:
+                call("ffb_attention_fp8", ptr(b.yq), ptr(b.yk), ptr(b.yv), ptr(b.key_lo), float(lay.inv["o"]),
+                     ptr(b.o8), T, HQ, HK, scale, self._s)
+            else:
+                call("ffb_attention_segmented", ptr(b.yq), ptr(b.yk), ptr(b.yv), None, 0, ptr(b.key_lo), ptr(b.attn),
+                     T, T, HQ, HK, scale, self._s)
+                call("ffb_quantize_fp8", ptr(b.attn), qmode, lay.inv["o"], ptr(b.o8), ptr(b.os), T, HQ * D, self._s)
             p = pl[("full", "o")]
-            call("ffb_quantize_fp8", ptr(b.attn), qmode, lay.inv["o"], ptr(b.o8), ptr(b.os), T, HQ * D, self._s)
             self._gemm(p, b.o8, sa(lay, "o", b.os), lay.lin["o"], b.lin_out, b.ws, rowwise)
             ob, o32, os_ = self._split_args(p, b.lin_out, b.ws)
             call("ffb_add_rmsnorm", ptr(h_cur), ob, o32, os_, None, 0, 0, ptr(lay.post_norm), eps, ptr(h_mid), None,
@@ -859,7 +869,7 @@ class Engine:
 
     def launches_per_batch(self, R):
         """Kernel launches of `forward_batch` for R requests (embed and readout per request)."""
-        per_layer = 8 if self.static_q8 else 9
+        per_layer = 7 if self.static_q8 else 9
         return R + 1 + per_layer * (self.m.depth - 1) + 1 + 1 + 2 + 1 + 1 + 2 + R
 
     def launches_per_forward(self):
@@ -867,7 +877,7 @@ class Engine:
         tail = 6 if self.fuse != "none" else 9  # attention, (quant,) o, gather, (add+norm,) gate/up, (quant,) down, readout
         if self.fuse == "all":  # embed, 5 per layer, the last layer's qkv, tail
             return 1 + 5 * (self.m.depth - 1) + 1 + tail
-        per_layer = 9 if self.m.mode != "int4" and not self.static_q8 else 8
+        per_layer = 7 if self.static_q8 else (9 if self.m.mode != "int4" else 8)
         if self.m.mode == "int4":
             tail = 8
         return 2 + per_layer * (self.m.depth - 1) + 1 + tail

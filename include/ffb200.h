@@ -116,6 +116,16 @@ int ffb_attention_segmented(const uint16_t* q, const uint16_t* k, const uint16_t
                             const int64_t* positions, int q_gather, const int* key_lo, uint16_t* out,
                             int S, int T, int HQ, int HK, float scale, void* stream);
 
+/* Causal prefill attention (as ffb_attention_segmented with positions == NULL, S == T)
+ * whose output is the STATIC FP8 input of the o projection: out8[t, h*128 + d] =
+ * e4m3(clamp(bf16(attention output) * out_inv, +-448)) (u8 [T, HQ*128]), byte-identical to
+ * ffb_attention followed by ffb_quantize_fp8 (FFB_QUANT_STATIC, out_inv).  Replaces
+ * `attention_direct` (_legacy/limit_kernels.py:36-45) plus the o projection's
+ * `_runtime_scale` (_family/depth_fp8.py:8-12) on the static-scale path.  key_lo as in
+ * ffb_attention_segmented (NULL: one request); out_inv > 0; out8 16-byte aligned. */
+int ffb_attention_fp8(const uint16_t* q, const uint16_t* k, const uint16_t* v, const int* key_lo,
+                      float out_inv, uint8_t* out8, int T, int HQ, int HK, float scale, void* stream);
+
 /* Copies rows index[i] of src [*, row_bytes] to dst [n, row_bytes] (index on device;
  * the tail's `h.index_select(1, pick)`, _family/night_runtime.py:103). */
 int ffb_gather_rows(const void* src, const int64_t* index, void* dst, int n, int row_bytes,

@@ -270,6 +270,36 @@ def test_fp8_gemm_swiglu_fp8_is_swiglu_then_static_quant(M, I, a_per_row):
              2 * I, K, _sp())
 
 
+@pytest.mark.parametrize("T,HQ,HK,segments", [(320, 32, 8, None), (100, 16, 8, None), (512, 8, 2, (200, 130, 64))])
+def test_attention_fp8_is_attention_then_static_quant(T, HQ, HK, segments):
+    """`ffb_attention_fp8` writes exactly the bytes of the causal attention (segmented when
+    several requests share the sequence) followed by `ffb_quantize_fp8` (STATIC)."""
+    g = _g(41)
+    q = torch.randn((HQ, T, 128), generator=g).to(BF16).to(DEV)
+    k = torch.randn((HK, T, 128), generator=g).to(BF16).to(DEV)
+    v = torch.randn((HK, T, 128), generator=g).to(BF16).to(DEV)
+    lo = None
+    if segments:
+        rows = [-(-n // 64) * 64 for n in segments]
+        assert sum(rows) == T
+        offs = [sum(rows[:i]) for i in range(len(rows))]
+        lo = torch.repeat_interleave(torch.tensor(offs, dtype=torch.int32), torch.tensor(rows)).to(DEV)
+    out = torch.empty((T, HQ * 128), device=DEV, dtype=BF16)
+    call("ffb_attention_segmented", ptr(q), ptr(k), ptr(v), None, 0, ptr(lo), ptr(out), T, T, HQ, HK, 128 ** -0.5,
+         _sp())
+    inv = 448.0 / 3.0
+    want8 = torch.empty((T, HQ * 128), device=DEV, dtype=E4M3)
+    call("ffb_quantize_fp8", ptr(out), L.QUANT_STATIC, inv, ptr(want8), None, T, HQ * 128, _sp())
+    got8 = torch.full((T + 1, HQ * 128), 0x7F, device=DEV, dtype=torch.uint8)
+    call("ffb_attention_fp8", ptr(q), ptr(k), ptr(v), ptr(lo), inv, ptr(got8), T, HQ, HK, 128 ** -0.5, _sp())
+    torch.cuda.synchronize()
+    assert_bytes_equal(got8[:T], want8, "fused attention + static quant")
+    assert bool((got8[T] == 0x7F).all()), "wrote past the last row"
+    assert L.device_error() == 0
+    with pytest.raises(ValueError):
+        call("ffb_attention_fp8", ptr(q), ptr(k), ptr(v), None, 0.0, ptr(got8), T, HQ, HK, 128 ** -0.5, _sp())
+
+
 def test_swiglu_epilogue_every_bf16_gate():
     """The SwiGLU epilogues look the activation bf16(g / (1 + exp(-g))) up by the bf16 gate's
     bits; the table must equal the formula evaluated on the device (the standalone swiglu
