@@ -8,13 +8,16 @@
 //
 // Tile = 128 tokens x BN output features, 64 K elements (one 128-byte bf16 swizzle row)
 // per stage.  Persistent kernel, one CTA per SM, tiles round-robin (token tile fastest).
-// Roles (448 threads):
+// Roles (576 threads):
 //   warp 0       TMA producer: bf16 activation tile [128 x 64] (128-byte swizzle) and the
 //                packed weight tile [BN rows x 32 bytes] into a ring of STAGES slots;
 //   warp 1       TMEM allocator + single-thread MMA issuer (4 x K=16 MMAs per stage);
-//   warps 2..5   converters: packed nibbles of slot s -> bf16 weight tile in one of two
+//   warps 2..9   converters: packed nibbles of slot s -> bf16 weight tile in one of two
 //                swizzled buffers (the layout TMA would write), fence to the async proxy;
-//   warps 6..13  epilogue, as in the FP8 GEMM (no scales: they are inside the weights).
+//                each thread owns a fixed row (half a row for BN = 128) and holds its group
+//                scale and, fetched one group ahead, the next one, so the scale loads never
+//                stall the conversion;
+//   warps 10..17 epilogue, as in the FP8 GEMM (no scales: they are inside the weights).
 // Barriers: full[s] (TMA), empty[s] (MMA done with the slot), wfull[j] (converters done),
 // wempty[j] (MMA done with the bf16 tile), tfull/tempty (two TMEM accumulators).  Every
 // wait is bounded; a timeout sets the abort flag and the device error word.
@@ -29,7 +32,8 @@ constexpr int BM = 128;                 // tokens per tile (UMMA M)
 constexpr int BKE = 64;                 // K elements per stage
 constexpr int UMMA_K = 16;              // K per tcgen05.mma for 16-bit operands
 constexpr int A_BYTES = BM * BKE * 2;   // 16 KB
-constexpr int CONV_WARPS = 4;
+constexpr int CONV_WARPS = 8;
+constexpr int NWB = 2;  // bf16 weight buffers (three measured no faster and cost a TMA stage)
 constexpr int EPI_WARPS = 8;
 constexpr int EPI_WARP0 = 2 + CONV_WARPS;
 constexpr int THREADS = 64 + (CONV_WARPS + EPI_WARPS) * 32;
@@ -41,7 +45,7 @@ struct W4Cfg {
   static constexpr int STAGE_BYTES = A_BYTES + WP_BYTES;
   static constexpr int WB_BYTES = BN * BKE * 2;      // bf16 weight tile, 128-byte rows
   static constexpr int STG_BYTES = EPI_WARPS * 2 * 2048;
-  static constexpr int FIXED = 2 * WB_BYTES + STG_BYTES + 512 + 1024;
+  static constexpr int FIXED = NWB * WB_BYTES + STG_BYTES + 512 + 1024;
   static constexpr int FIT = (SMEM_LIMIT - FIXED) / STAGE_BYTES;
   static constexpr int STAGES = FIT > 8 ? 8 : FIT;
   static constexpr int SMEM = STAGES * STAGE_BYTES + FIXED;
@@ -96,13 +100,13 @@ __global__ void __launch_bounds__(THREADS, 1)
   static_assert(EPI != FFB_EPI_SWIGLU || BN == 256, "gate/up pairs of 128 channels per tile");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* wb_all = smem + C::STAGES * C::STAGE_BYTES;  // [2][WB_BYTES], 1024-aligned
-  uint8_t* stg_all = wb_all + 2 * C::WB_BYTES;
+  uint8_t* wb_all = smem + C::STAGES * C::STAGE_BYTES;  // [NWB][WB_BYTES], 1024-aligned
+  uint8_t* stg_all = wb_all + NWB * C::WB_BYTES;
   uint64_t* full = reinterpret_cast<uint64_t*>(stg_all + C::STG_BYTES);
   uint64_t* empty = full + C::STAGES;
-  uint64_t* wfull = empty + C::STAGES;  // [2]
-  uint64_t* wempty = wfull + 2;         // [2]
-  uint64_t* tfull = wempty + 2;         // [2]
+  uint64_t* wfull = empty + C::STAGES;  // [NWB]
+  uint64_t* wempty = wfull + NWB;       // [NWB]
+  uint64_t* tfull = wempty + NWB;       // [2]
   uint64_t* tempty = tfull + 2;         // [2]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -115,9 +119,11 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < NWB; ++b) {
       mbar_init(&wfull[b], CONV_WARPS);
       mbar_init(&wempty[b], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
       mbar_init(&tempty[b], EPI_WARPS);
     }
@@ -203,9 +209,9 @@ __global__ void __launch_bounds__(THREADS, 1)
         const uint32_t acc = tmem + (uint32_t)(buf * BN);
         bool ok = true;
         for (int kb = kb0; kb < kb1; ++kb, ++it) {
-          const int s = it % C::STAGES, j = it & 1;
+          const int s = it % C::STAGES, j = it % NWB;
           if (!mbar_wait_bounded(&full[s], (uint32_t)(it / C::STAGES) & 1u, abort_flag) ||
-              !mbar_wait_bounded(&wfull[j], (uint32_t)(it >> 1) & 1u, abort_flag)) {
+              !mbar_wait_bounded(&wfull[j], (uint32_t)(it / NWB) & 1u, abort_flag)) {
             ok = false;
             break;
           }
@@ -228,40 +234,55 @@ __global__ void __launch_bounds__(THREADS, 1)
   } else if (warp < EPI_WARP0) {
     // ------------------------------------------------------------------ converters
     pdl_wait();
-    const int ct = tid - 64;  // 0 .. 127
+    constexpr int CT = CONV_WARPS * 32;
+    constexpr int CPT = BN * 8 / CT;  // 16-byte output chunks per thread and stage (8 or 4)
+    static_assert(CPT == 8 || CPT == 4, "a whole or half 64-element row per converter thread");
+    const int ct = tid - 64;
+    const int row = ct * CPT / 8, c0 = ct * CPT % 8;
     const int groups = args.K / 128;
     int it = 0;
     for (int t = blockIdx.x; t < args.n_tiles && !*abort_flag; t += gridDim.x) {
       int tt, ks, ft, kb0, kb1;
       tile_coords(args, t, tt, ks, ft);
       k_range(args, ks, nkb, kb0, kb1);
+      // this row's scale of the current 128-element group and of the next one (the load is
+      // issued a whole group, two stages, before its first use)
+      const uint16_t* srow = args.scales + (size_t)(ft * BN + row) * groups;
+      int g = kb0 >> 1;
+      uint16_t s_cur = srow[g];
+      uint16_t s_nxt = g + 1 < groups ? srow[g + 1] : (uint16_t)0;
       bool ok = true;
       for (int kb = kb0; kb < kb1; ++kb, ++it) {
-        const int s = it % C::STAGES, j = it & 1;
-        // this thread's rows' group scales (issued before the waits to hide their latency)
-        uint16_t sraw[BN / 128];
-#pragma unroll
-        for (int r = 0; r < BN / 128; ++r)
-          sraw[r] = args.scales[(size_t)(ft * BN + ct + 128 * r) * groups + (kb >> 1)];
+        const int s = it % C::STAGES, j = it % NWB;
+        if ((kb >> 1) != g) {
+          g = kb >> 1;
+          s_cur = s_nxt;
+          s_nxt = g + 1 < groups ? srow[g + 1] : (uint16_t)0;
+        }
         if (!mbar_wait_bounded(&full[s], (uint32_t)(it / C::STAGES) & 1u, abort_flag) ||
-            !mbar_wait_bounded(&wempty[j], ((uint32_t)(it >> 1) & 1u) ^ 1u, abort_flag)) {
+            !mbar_wait_bounded(&wempty[j], ((uint32_t)(it / NWB) & 1u) ^ 1u, abort_flag)) {
           ok = false;
           break;
         }
-        const uint8_t* wp = smem + s * C::STAGE_BYTES + A_BYTES;
-        uint8_t* wb = wb_all + j * C::WB_BYTES;
-#pragma unroll
-        for (int r = 0; r < BN / 128; ++r) {
-          const int row = ct + 128 * r;
-          const uint4 p0 = *reinterpret_cast<const uint4*>(wp + row * 32);
-          const uint4 p1 = *reinterpret_cast<const uint4*>(wp + row * 32 + 16);
-          const uint32_t nib[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
-          const __nv_bfloat162 s2 = __halves2bfloat162(__ushort_as_bfloat16(sraw[r]), __ushort_as_bfloat16(sraw[r]));
-          uint8_t* dst = wb + row * 128;
-#pragma unroll
-          for (int c = 0; c < 8; ++c)  // 16-byte chunk c of the row, 128-byte swizzle
-            *reinterpret_cast<uint4*>(dst + ((c ^ (row & 7)) << 4)) = dequant8(nib[c], s2);
+        const uint8_t* wp = smem + s * C::STAGE_BYTES + A_BYTES + row * 32 + c0 * 4;
+        uint32_t nib[CPT];
+        const uint4 p0 = *reinterpret_cast<const uint4*>(wp);
+        nib[0] = p0.x;
+        nib[1] = p0.y;
+        nib[2] = p0.z;
+        nib[3] = p0.w;
+        if constexpr (CPT == 8) {
+          const uint4 p1 = *reinterpret_cast<const uint4*>(wp + 16);
+          nib[4] = p1.x;
+          nib[5] = p1.y;
+          nib[6] = p1.z;
+          nib[7] = p1.w;
         }
+        const __nv_bfloat162 s2 = __halves2bfloat162(__ushort_as_bfloat16(s_cur), __ushort_as_bfloat16(s_cur));
+        uint8_t* dst = wb_all + j * C::WB_BYTES + row * 128;
+#pragma unroll
+        for (int c = 0; c < CPT; ++c)  // 16-byte chunk c0 + c of the row, 128-byte swizzle
+          *reinterpret_cast<uint4*>(dst + (((c0 + c) ^ (row & 7)) << 4)) = dequant8(nib[c], s2);
         fence_proxy_async_smem();  // the bf16 tile is read by the tensor core (async proxy)
         __syncwarp();
         if (lane == 0) mbar_arrive(&wfull[j]);
