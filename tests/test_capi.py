@@ -55,3 +55,19 @@ def test_host_side_argument_errors():
 def test_pdl_toggle_roundtrip():
     old = L.set_pdl(0)
     assert L.set_pdl(old) == 0
+
+
+def test_fused_static_quant_entries_reject_bad_arguments():
+    """The epilogue-quantising entries check their arguments on the host before any launch."""
+    with pytest.raises(ValueError, match="out_inv"):
+        L.call("ffb_fp8_gemm_swiglu_fp8", 16, 16, 0, 16, 16, 1, 0.0, 16, 320, 512, 2560, None)
+    with pytest.raises(ValueError, match="aligned"):
+        L.call("ffb_fp8_gemm_swiglu_fp8", 16, 16, 0, 16, 16, 1, 10.0, 17, 320, 512, 2560, None)
+    with pytest.raises(ValueError, match="multiple of 128"):
+        L.call("ffb_fp8_gemm_swiglu_fp8", 16, 16, 0, 16, 16, 1, 10.0, 16, 320, 500, 2560, None)
+    with pytest.raises(ValueError, match="out_inv"):
+        L.call("ffb_attention_fp8", 16, 16, 16, None, -1.0, 16, 320, 32, 8, 0.1, None)
+    with pytest.raises(ValueError, match="NULL"):
+        L.call("ffb_attention_fp8", None, 16, 16, None, 1.0, 16, 320, 32, 8, 0.1, None)
+    with pytest.raises(ValueError, match="bad shape"):
+        L.call("ffb_attention_fp8", 16, 16, 16, None, 1.0, 16, 320, 30, 8, 0.1, None)
