@@ -15,3 +15,4 @@ those fixtures.
 """
 from .qwen_path import *  # noqa: F401,F403
 from .pack import *  # noqa: F401,F403,E402
+from .vision import *  # noqa: F401,F403,E402

@@ -11,7 +11,8 @@ What runs: the reference's Triton kernels (`_legacy/lower_kernels.add_rms`,
 `_legacy/sub10_runtime.fast_norm`, `_legacy/broad_kernels.qk_pair`,
 `_legacy/limit_kernels.attention_direct` / `lm_readout`, `_legacy/search_kernels.swiglu`,
 `_family/depth_fp8.quantize_runtime`, `_legacy/fp8_private.quantize_rows`,
-`_legacy/sub10_runtime.pack_rgb`, `_family/depth_runtime.pack_rectangle`) under Triton's
+`_legacy/sub10_runtime.pack_rgb`, `_family/depth_runtime.pack_rectangle`,
+`_legacy/search_kernels.vision_rope`) under Triton's
 CPU interpreter (TRITON_INTERPRET=1), the reference's torch code (`StaticFP8Linear`,
 `FP8Linear`, `RuntimeScaleLinear` through CPU `torch._scaled_mm`, `Int4`), and
 transformers' Qwen3-VL `get_rope_index` / `Qwen3VLTextRotaryEmbedding`.
@@ -306,6 +307,18 @@ def main(root):
             R.depth_rt.pack_rectangle[grid](rgb, pixels, W, pixels.numel(), 1024, enable_fp_fusion=False)
         packs.append(dict(kind=kind, height=H, width=W, rgb=rgb, pixels=pixels))
     out["pack_rgb"] = packs
+
+    # vision_rope (search_kernels.py:111-134): q/k strided views of the packed qkv rows, as
+    # NativeNormVision.core passes them (scaled_qwen_runtime.py:47-48)
+    gv = torch.Generator().manual_seed(91)
+    n, hv, dv = 24, 2, 64
+    qkv_v = _randn(gv, n, 3, hv, dv)
+    qv, kv = qkv_v[:, 0], qkv_v[:, 1]
+    ang = torch.rand((n, dv // 2), generator=gv) * 20.0
+    emb = torch.cat([ang, ang], dim=-1)
+    cv, sv = emb.cos(), emb.sin()
+    yq, yk = R.search.vision_rope(qv, kv, cv, sv)
+    out["vision_rope"] = dict(q=qv.contiguous(), k=kv.contiguous(), cos=cv, sin=sv, yq=yq, yk=yk)
 
     out["_note"] = "outputs of the reference's own code; see make_golden.py"
     torch.save(out, OUT)
