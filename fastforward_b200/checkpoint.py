@@ -171,6 +171,67 @@ def load_language_model(model_dir, *, device="cpu", layers=None, option_ids=None
     return dims, model
 
 
+VISUAL = "model.visual."
+
+
+def vision_dims_from_config(config):
+    """`VisionDims` of the vision tower described by a Qwen3-VL config.json (dict or path)."""
+    from .config import VisionDims
+    if not isinstance(config, dict):
+        config = json.loads(Path(config).read_text())
+    vc = config.get("vision_config")
+    if not vc:
+        raise CheckpointError("config has no vision_config")
+    tc = config.get("text_config", {})
+    try:
+        return VisionDims(int(vc["hidden_size"]), int(vc["num_heads"]), int(vc["intermediate_size"]),
+                          int(vc.get("out_hidden_size", tc.get("hidden_size", 0))), int(vc["depth"]),
+                          tuple(int(i) for i in vc.get("deepstack_visual_indexes", ())),
+                          int(vc.get("num_position_embeddings", 2304)), int(vc.get("patch_size", 16)),
+                          int(vc.get("temporal_patch_size", 2)), int(vc.get("spatial_merge_size", 2)),
+                          act=str(vc.get("hidden_act", "gelu_pytorch_tanh")))
+    except KeyError as e:
+        raise CheckpointError(f"vision config lacks {e}") from None
+
+
+def vision_param_shapes(v):
+    """Checkpoint name (without `model.visual.`) -> shape of every vision-tower tensor."""
+    C, I, O, m2 = v.hidden, v.inter, v.out_hidden, v.merge * v.merge
+    shapes = {"patch_embed.proj.weight": (C, 3, v.temporal, v.patch, v.patch), "patch_embed.proj.bias": (C,),
+              "pos_embed.weight": (v.num_pos, C)}
+    for j in range(v.depth):
+        b = f"blocks.{j}."
+        shapes.update({b + "norm1.weight": (C,), b + "norm1.bias": (C,), b + "norm2.weight": (C,),
+                       b + "norm2.bias": (C,), b + "attn.qkv.weight": (3 * C, C), b + "attn.qkv.bias": (3 * C,),
+                       b + "attn.proj.weight": (C, C), b + "attn.proj.bias": (C,),
+                       b + "mlp.linear_fc1.weight": (I, C), b + "mlp.linear_fc1.bias": (I,),
+                       b + "mlp.linear_fc2.weight": (C, I), b + "mlp.linear_fc2.bias": (C,)})
+    mergers = [("merger.", C)] + [(f"deepstack_merger_list.{i}.", C * m2) for i in range(len(v.deepstack))]
+    for prefix, norm in mergers:
+        shapes.update({prefix + "norm.weight": (norm,), prefix + "norm.bias": (norm,),
+                       prefix + "linear_fc1.weight": (C * m2, C * m2), prefix + "linear_fc1.bias": (C * m2,),
+                       prefix + "linear_fc2.weight": (O, C * m2), prefix + "linear_fc2.bias": (O,)})
+    return shapes
+
+
+def load_vision_tower(model_dir, *, device="cpu", dtype=BF16):
+    """(VisionDims, {name: tensor}) of the vision tower in `model_dir`: every tensor under
+    `model.visual.` read lazily and checked against the config's shapes (the names are
+    the checkpoint's without the prefix)."""
+    d = Path(model_dir)
+    if not (d / "config.json").exists():
+        raise CheckpointError(f"{d} has no config.json")
+    v = vision_dims_from_config(d / "config.json")
+    t = _Tensors(d)
+    params = {}
+    for name, shape in vision_param_shapes(v).items():
+        x = t.get(VISUAL + name)
+        if tuple(x.shape) != tuple(shape):
+            raise CheckpointError(f"{VISUAL + name}: shape {tuple(x.shape)}, expected {tuple(shape)}")
+        params[name] = x.to(device, dtype).contiguous()
+    return v, params
+
+
 def save_language_model(model_dir, dims, model, *, option_ids=OPTION_IDS, shards=1):
     """Writes `model` (the layout `load_language_model` returns, with every decoder layer)
     as a Hugging Face Qwen3-VL language-model checkpoint: config.json and `shards`

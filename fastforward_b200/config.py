@@ -50,6 +50,39 @@ MODELS = {
 }
 
 
+@dataclass(frozen=True)
+class VisionDims:
+    """Shape of a Qwen3-VL vision tower (patch embedding, blocks, deepstack and final
+    mergers).  `out_hidden` is the language model's hidden size."""
+    hidden: int
+    heads: int
+    inter: int
+    out_hidden: int
+    depth: int
+    deepstack: tuple
+    num_pos: int = 2304           # 48 x 48 learned position table, sampled bilinearly
+    patch: int = 16
+    temporal: int = 2
+    merge: int = 2
+    eps: float = 1e-6
+    theta: float = 10000.0
+    act: str = "gelu_pytorch_tanh"
+
+    @property
+    def head_dim(self):
+        return self.hidden // self.heads
+
+
+# The published Qwen3-VL vision configs; the depths agree with the bundles'
+# `expected_dimensions` (24 for 2B/4B, 27 for 8B/32B).
+VISION_MODELS = {
+    "2B": VisionDims(1024, 16, 4096, 2048, 24, (5, 11, 17)),
+    "4B": VisionDims(1024, 16, 4096, 2560, 24, (5, 11, 17)),
+    "8B": VisionDims(1152, 16, 4304, 4096, 27, (8, 16, 24)),
+    "32B": VisionDims(1152, 16, 4304, 5120, 27, (8, 16, 24)),
+}
+
+
 @dataclass
 class Layout:
     """Token layout of one request: [prefix text][image grid][suffix text] + bucket padding.

@@ -140,3 +140,44 @@ def test_bundle_asset_checks(tmp_path):
     assert Accelerator._checkpoint_mode({"execution_mode": "fp8_rowwise"}) == "rowwise"
     with pytest.raises(ValueError):
         Accelerator._checkpoint_mode({"execution_mode": "bf16"})
+
+
+def test_reads_the_vision_tower_written_by_transformers(tmp_path):
+    """The vision tower's tensors come back under their checkpoint names with the config's
+    shapes, and the vision oracle run on them reproduces transformers' own vision forward."""
+    transformers = pytest.importorskip("transformers")
+    import numpy as np
+    import oracle
+    cfg = transformers.Qwen3VLConfig(
+        text_config=dict(TINY), vision_config=dict(depth=2, hidden_size=64, intermediate_size=128, num_heads=2,
+                                                   out_hidden_size=256, deepstack_visual_indexes=[1]))
+    torch.manual_seed(3)
+    m = transformers.Qwen3VLForConditionalGeneration(cfg).to(BF16)
+    m.save_pretrained(str(tmp_path), safe_serialization=True)
+    vd, params = C.load_vision_tower(tmp_path)
+    assert (vd.hidden, vd.heads, vd.inter, vd.out_hidden, vd.depth, vd.deepstack) == (64, 2, 128, 256, 2, (1,))
+    sd = m.state_dict()
+    assert set(params) == {k[len(C.VISUAL):] for k in sd if k.startswith(C.VISUAL)}
+    for name, x in params.items():
+        assert torch.equal(x, sd[C.VISUAL + name]), name
+    rgb = np.random.default_rng(0).integers(0, 256, (64, 64, 3), dtype=np.uint8)
+    pixels = oracle.pack_rgb(rgb).float()
+    visual = m.model.visual.float()
+    with torch.no_grad():
+        want = visual(pixels, grid_thw=torch.tensor([[1, 4, 4]]))
+        got, deep = oracle.vision_tower({k: v.float() for k, v in params.items()},
+                                        oracle.VisionDims.from_config(cfg.vision_config), pixels, 4, 4)
+    torch.testing.assert_close(got, want.pooler_output, atol=2e-5, rtol=2e-5)
+    torch.testing.assert_close(deep[0], want.deepstack_features[0], atol=2e-5, rtol=2e-5)
+    (tmp_path / "model.safetensors").unlink()
+    with pytest.raises(C.CheckpointError):
+        C.load_vision_tower(tmp_path)
+
+
+def test_vision_shapes_of_the_shipped_families():
+    from fastforward_b200.config import VISION_MODELS
+    for name, v in VISION_MODELS.items():
+        assert v.out_hidden == MODELS[name].hidden and v.head_dim in (64, 72) and v.depth in (24, 27)
+        shapes = C.vision_param_shapes(v)
+        assert shapes["deepstack_merger_list.2.linear_fc2.weight"] == (v.out_hidden, 4 * v.hidden)
+        assert len([k for k in shapes if k.startswith("blocks.")]) == 12 * v.depth
