@@ -14,6 +14,7 @@ LIB_PATH = Path(__file__).resolve().with_name("libffb200.so")
 OK, EINVAL, EUNSUPPORTED, ECUDA, ETIMEOUT = 0, -1, -2, -3, -4
 QUANT_NONE, QUANT_STATIC, QUANT_ROWWISE = 0, 1, 2
 EPI_BF16, EPI_F32_PARTIAL, EPI_SWIGLU = 0, 1, 2
+TILE_STREAM = 1  # ffb_fp8_gemm feature_tile: the weight-stationary schedule
 PRO_QUANT, PRO_ADD_RMSNORM = 1, 2
 
 
@@ -44,6 +45,7 @@ SIGNATURES = {
     "ffb_quantize_weight_fp8": [P, I, P, P, P, I, I, P],
     "ffb_quantize_weight_fp8_noalloc": [P, I, P, P, I, I, P],
     "ffb_fp8_gemm": [P, P, I, P, P, I, I, P, P, I, I, I, I, I, P],
+    "ffb_fp8_gemm_stream_ctas": [I, I, I, I, I],
     "ffb_fp8_gemm_qk_rope": [P, P, I, P, P, I, P, P, F, P, P, P, P, P, I, I, I, I, P],
     "ffb_fp8_gemm_swiglu_fp8": [P, P, I, P, P, I, F, P, I, I, I, P],
     "ffb_fp8_gemm_fused": [P, P, P, I, P, P, I, I, P, P, I, I, I, I, I, P],
@@ -123,6 +125,12 @@ def device_error(clear=False):
     w = c_uint32(0)
     call("ffb_device_error", ctypes.addressof(w), int(clear))
     return w.value
+
+
+def stream_ctas(m, n, k, epilogue, splits=1):
+    """CTAs of ffb_fp8_gemm's weight-stationary schedule for this GEMM, 0 if it does not
+    apply (host query)."""
+    return int(lib().ffb_fp8_gemm_stream_ctas(int(m), int(n), int(k), int(epilogue), int(splits)))
 
 
 def set_pdl(enable):

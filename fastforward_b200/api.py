@@ -295,6 +295,10 @@ class Accelerator:
             ready = [torch.cuda.Event() for _ in range(2)]
             free = [torch.cuda.Event() for _ in range(2)]
             out = torch.zeros((len(plan), 2, 8), dtype=torch.float32, pin_memory=True)
+            # The copy stream starts after everything already queued on the caller's stream:
+            # device inputs the caller produced there are complete, and the slot buffers
+            # (just allocated on that stream) are no longer in use by earlier work.
+            copy.wait_stream(main)
             for i, (r, n, nv, bucket, k, pick, start, gh, gw, deep) in enumerate(plan):
                 entry = self.engine.capture(bucket, start, nv, gh, gw, k, len(deep))
                 sl = slots[i % 2]

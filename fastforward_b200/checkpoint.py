@@ -129,6 +129,14 @@ def load_language_model(model_dir, *, device="cpu", layers=None, option_ids=None
     if expected_dimensions is not None and tuple(expected_dimensions[:2]) != (dims.layers, dims.hidden):
         raise CheckpointError(f"expected (layers, hidden) {tuple(expected_dimensions[:2])}, "
                               f"checkpoint has {(dims.layers, dims.hidden)}")
+    if expected_dimensions is not None and len(expected_dimensions) > 2:
+        # the third entry is the vision tower's depth, as the reference asserts
+        # (`scaled_qwen_runtime.py:69`); checked whenever the config states one (a
+        # language-only checkpoint written by `save_language_model` does not)
+        vc = json.loads((d / "config.json").read_text()).get("vision_config") or {}
+        if "depth" in vc and int(expected_dimensions[2]) != int(vc["depth"]):
+            raise CheckpointError(f"expected {int(expected_dimensions[2])} vision blocks, "
+                                  f"checkpoint has {int(vc['depth'])}")
     t = _Tensors(d)
     dev = torch.device(device)
 

@@ -5,9 +5,16 @@
 // in fp32 scaled by 1/sqrt(128); online softmax over 64-key blocks (running max m,
 // denominator l = l * alpha + sum(p), accumulator acc = acc * alpha + P.V with
 // alpha = exp(m_old - m_new)); P cast to bf16 before its product with V; output
-// bf16(acc / l).  Keys past the query's position (and past T) are masked.  Exponentials
-// are 2^(x * log2 e - m) on the special-function unit, as the reference's tl.exp; the final
-// quotient is correctly rounded before the bf16 cast.
+// bf16(acc / l).  Keys past the query's position (and past T) are masked.  The reference
+// leaves the exponential (tl.exp) and the reduction orders to its compiler; this kernel
+// fixes every one of them so that its output is a function of its inputs alone, restated
+// operation for operation by the oracle (oracle/attn.c):
+//   x = fp32(s * scale * log2 e); m_new = max(m, block max); base = m_new;
+//   alpha = exp2_poly(m - base), p = exp2_poly(x - base) (this file's polynomial
+//   exponential, on the FMA pipe); each of a row's four parts keeps its denominator share
+//   l = fma(l, alpha, psum) with psum its 16 keys summed pairwise in key order;
+//   o = fma(o, alpha, O_j); l = ((l0 + l1) + l2) + l3; the final quotient is correctly
+//   rounded before the bf16 cast.
 //
 // One CTA = 128 query rows of one head (the M of the MMA); 576 threads:
 //   warp 0     TMA producer: the Q tile once ([128 x 128] as two 64-column swizzled
@@ -32,6 +39,8 @@
 #include "common.cuh"
 #include "pdl.cuh"
 
+#include <string.h>
+
 namespace {
 
 constexpr int D = 128;
@@ -48,12 +57,24 @@ constexpr int XCH_BYTES = 2 * 4 * BM * 4;  // row exchange [2 buffers][4 parts][
 constexpr int SMEM = 2 * Q_HALF + KV_STAGES * STAGE + 2 * P_BYTES + XCH_BYTES + 256 + 1024;
 constexpr int TMEM_COLS = 512;      // S[b] at column 64b (64 wide), O[b] at 128 + 128b (128 wide)
 
-// 2^x on the special-function unit (ex2.approx: relative error ~2^-22, well inside the
-// bf16 rounding of P).  The reference's `tl.exp` lowers to the same instruction.
-__device__ __forceinline__ float ex2_approx(float x) {
-  float y;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
+// exp2_poly: 2^x = 2^n * 2^f with n = rint(x) and f = x - n in [-1/2, 1/2] (exact); 2^f
+// is the degree-7 Taylor polynomial of e^(f ln 2) (coefficients (ln 2)^k / k! rounded to
+// fp32) in Horner form with fused multiply-adds, and 2^n is added to the exponent field.
+// Results below 2^-125 (and x = -inf) are 0.  Within 1 ulp of 2^x for the x <= 0 it is
+// used on; every operation is an IEEE-rounded one, so a CPU with fmaf reproduces it.
+__device__ __forceinline__ float exp2_poly(float x) {
+  if (!(x >= -125.f)) return 0.f;
+  const float n = rintf(x);
+  const float f = __fsub_rn(x, n);
+  float p = 1.52527338040598403e-05f;
+  p = __fmaf_rn(p, f, 0.000154035303933816099f);
+  p = __fmaf_rn(p, f, 0.00133335581464284434f);
+  p = __fmaf_rn(p, f, 0.00961812910762847717f);
+  p = __fmaf_rn(p, f, 0.0555041086648215800f);
+  p = __fmaf_rn(p, f, 0.240226506959100712f);
+  p = __fmaf_rn(p, f, 0.693147180559945309f);
+  p = __fmaf_rn(p, f, 1.f);
+  return __int_as_float(__float_as_int(p) + ((int)n << 23));
 }
 
 // bf16(o / l) with the quotient correctly rounded to fp32 first.  y = o * (1/l) (the
@@ -70,7 +91,13 @@ __device__ __forceinline__ uint16_t bf16_quotient(float o, float l, float rl) {
 
 struct TcArgs {
   uint16_t* out;
-  const int* key_lo;  // per row: its lowest visible key (several requests in one sequence), or NULL = 0
+  const int* key_lo;  // per output row: its lowest visible key (several requests in one sequence), or NULL = 0
+  // Selected rows (NULL: causal prefill over all T rows).  CTA x computes output row x, the
+  // query at position sel[x]: its Q row is row sel[x] of q (q_gather) or row x; the CTA's
+  // 128-row Q box starts there and only its first row is kept (a row's arithmetic does not
+  // depend on the other rows of its tile, so the bytes equal the causal prefill's row).
+  const int64_t* sel;
+  int q_gather;
   int T, HQ, HK;
   float scale_log2;  // scale * log2(e)
   float out_inv;     // > 0: e4m3 output, e4m3(clamp(bf16 output * out_inv, +-448)); 0: bf16 output
@@ -98,13 +125,17 @@ __global__ void __launch_bounds__(THREADS, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int qt = gridDim.x - 1 - blockIdx.x;  // heaviest (latest) query tiles first
   const int h = blockIdx.y, kvh = h / (args.HQ / args.HK);
-  const int q0 = qt * BM;
-  const int kend = min(args.T, q0 + BM);      // keys any row of this tile can see
+  const bool rows_mode = args.sel != nullptr;
+  // causal prefill: the tile's first query row; selected rows: this row's position
+  const int spos = rows_mode ? (int)min(max(args.sel[blockIdx.x], (int64_t)0), (int64_t)(args.T - 1)) : 0;
+  const int q0 = rows_mode ? spos : (int)(gridDim.x - 1 - blockIdx.x) * BM;  // heaviest (latest) tiles first
+  const int qrow0 = rows_mode ? (args.q_gather ? spos : (int)blockIdx.x) : q0;  // the Q box's first row
+  const int kend = min(args.T, rows_mode ? spos + 1 : q0 + BM);  // keys any row of this tile can see
   const int nb = (kend + BN - 1) / BN;
   // first key block: the tile's lowest visible key (rows' key_lo are non-decreasing)
-  const int jb0 = args.key_lo ? min(max(args.key_lo[min(q0, args.T - 1)], 0) / BN, nb) : 0;
+  const int lo0 = args.key_lo ? max(args.key_lo[rows_mode ? (int)blockIdx.x : min(q0, args.T - 1)], 0) : 0;
+  const int jb0 = min(lo0 / BN, nb);
   const int nit = nb - jb0;                   // key blocks this tile visits
 
   if (tid == 0) {
@@ -127,7 +158,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     tma_prefetch_desc(&tmap_q);
     tma_prefetch_desc(&tmap_k);
     tma_prefetch_desc(&tmap_v);
-    tma_prefetch_desc(&tmap_o);
+    if (!rows_mode) tma_prefetch_desc(&tmap_o);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, TMEM_COLS);
@@ -145,8 +176,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (lane == 0) {
       const uint64_t pol = policy_evict_last();
       mbar_arrive_expect_tx(q_full, 2 * Q_HALF);
-      tma_load_3d(sq, &tmap_q, q_full, 0, q0, h, pol);
-      tma_load_3d(sq + Q_HALF, &tmap_q, q_full, 64, q0, h, pol);
+      tma_load_3d(sq, &tmap_q, q_full, 0, qrow0, h, pol);
+      tma_load_3d(sq + Q_HALF, &tmap_q, q_full, 64, qrow0, h, pol);
       int issued = 0;
       for (int j = 0; j < nit && !*abort_flag; ++j, ++issued) {
         const int s = j % KV_STAGES;
@@ -215,14 +246,15 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int quarter = warp & 3;
     const int part = (warp - 2) >> 2;   // keys [16 part, 16 part + 16), output columns [32 part, 32 part + 32)
     const int r = quarter * 32 + lane;  // this thread's query row in the tile
-    const int qpos = q0 + r;
+    const int qpos = rows_mode ? spos : q0 + r;  // selected rows: every row of the tile masks as row 0
     const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
     float o[D / 4];
 #pragma unroll
     for (int i = 0; i < D / 4; ++i) o[i] = 0.f;
     float m = -INFINITY, l = 0.f, alpha_prev = 0.f;
     int xph = 0;  // phases of this quarter's exchange barrier used so far
-    const int lo = args.key_lo && qpos < args.T ? args.key_lo[qpos] : 0;  // this row's lowest visible key
+    // this row's lowest visible key
+    const int lo = rows_mode ? lo0 : (args.key_lo && qpos < args.T ? args.key_lo[qpos] : 0);
     // The four parts' values of the row (written to xch[buffer][part][row] by each), in part order.
     auto exchange = [&](float mine, float (&all)[4]) -> bool {
       float* slot = xch + (xph & 1) * 4 * BM;
@@ -248,8 +280,8 @@ __global__ void __launch_bounds__(THREADS, 1)
       reg_fence(t1);
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
-        o[i] = o[i] * alpha + __uint_as_float(t0[i]);
-        o[16 + i] = o[16 + i] * alpha + __uint_as_float(t1[i]);
+        o[i] = __fmaf_rn(o[i], alpha, __uint_as_float(t0[i]));
+        o[16 + i] = __fmaf_rn(o[16 + i], alpha, __uint_as_float(t1[i]));
       }
       tc_fence_before();
       return true;
@@ -277,14 +309,15 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
         for (int c = 0; c < 16; ++c) {
           const int key = key0 + c;
-          const float x = (key > qpos || key >= args.T || key < lo) ? -INFINITY : __uint_as_float(sr[c]) * args.scale_log2;
+          const float x =
+              (key > qpos || key >= args.T || key < lo) ? -INFINITY : __fmul_rn(__uint_as_float(sr[c]), args.scale_log2);
           sr[c] = __float_as_uint(x);
           bmax = fmaxf(bmax, x);
         }
       } else {
 #pragma unroll
         for (int c = 0; c < 16; ++c) {
-          const float x = __uint_as_float(sr[c]) * args.scale_log2;
+          const float x = __fmul_rn(__uint_as_float(sr[c]), args.scale_log2);
           sr[c] = __float_as_uint(x);
           bmax = fmaxf(bmax, x);
         }
@@ -298,7 +331,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       bmax = fmaxf(fmaxf(parts[0], parts[1]), fmaxf(parts[2], parts[3]));  // the row's maximum over 64 keys
       const float nm = fmaxf(m, bmax);
       const float base = nm == -INFINITY ? 0.f : nm;
-      const float alpha = ex2_approx(m - base);
+      const float alpha = exp2_poly(__fsub_rn(m, base));
       m = nm;
       float psum = 0.f;
       // this part of P_j row r into P[b]: 2 chunks of 16 bytes, 128-byte swizzle.  P[b] was
@@ -309,15 +342,15 @@ __global__ void __launch_bounds__(THREADS, 1)
         uint32_t w[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          const float p0 = ex2_approx(__uint_as_float(sr[8 * c + 2 * e]) - base);
-          const float p1 = ex2_approx(__uint_as_float(sr[8 * c + 2 * e + 1]) - base);
-          psum += p0 + p1;
+          const float p0 = exp2_poly(__fsub_rn(__uint_as_float(sr[8 * c + 2 * e]), base));
+          const float p1 = exp2_poly(__fsub_rn(__uint_as_float(sr[8 * c + 2 * e + 1]), base));
+          psum = __fadd_rn(psum, __fadd_rn(p0, p1));
           w[e] = (uint32_t)f2bf(p0) | ((uint32_t)f2bf(p1) << 16);
         }
         const int chunk = 2 * part + c;
         *reinterpret_cast<uint4*>(prow + ((chunk ^ (r & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
       }
-      l = l * alpha + psum;  // this part's share of the denominator
+      l = __fmaf_rn(l, alpha, psum);  // this part's share of the denominator
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[b]);
@@ -328,7 +361,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (ok) {
       float parts[4];
       ok = exchange(l, parts) && !*abort_flag;
-      l = ((parts[0] + parts[1]) + parts[2]) + parts[3];  // the four parts of the denominator
+      l = __fadd_rn(__fadd_rn(__fadd_rn(parts[0], parts[1]), parts[2]), parts[3]);  // the four parts, in order
     }
     if (!ok) *abort_flag = 1;
     // Output tile [128 rows x 128 columns] bf16 staged as two 128-byte-swizzled [128 x 64]
@@ -336,7 +369,23 @@ __global__ void __launch_bounds__(THREADS, 1)
     // stores; rows past T are clipped by the store.
     const bool stage = ok && !*abort_flag;
     const bool fp8_out = args.out_inv > 0.f;
-    if (stage && fp8_out) {
+    if (rows_mode) {
+      // only the tile's first row is the selected query: its four threads (row 0 of lane
+      // quarter 0) store their 32 output columns of output row x with plain stores
+      if (stage && r == 0) {
+        const float rl = __frcp_rn(l);
+        uint16_t* dst = args.out + (size_t)blockIdx.x * args.HQ * D + (size_t)h * D + 32 * part;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t w[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            w[e] = (uint32_t)bf16_quotient(o[8 * c + 2 * e], l, rl) |
+                   ((uint32_t)bf16_quotient(o[8 * c + 2 * e + 1], l, rl) << 16);
+          *reinterpret_cast<uint4*>(dst + 8 * c) = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+      }
+    } else if (stage && fp8_out) {
       // the static FP8 quantisation of the o projection's input, applied to the bf16 output:
       // one 128-byte-swizzled [128 rows x 128 B] box in P tile 0, this part's 32 columns
       // as two 16-byte chunks
@@ -374,7 +423,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       fence_proxy_async_smem();
     }
     named_barrier(1, SOFTMAX_WARPS * 32);
-    if (warp == 2 && lane == 0 && !*abort_flag) {
+    if (!rows_mode && warp == 2 && lane == 0 && !*abort_flag) {
       if (fp8_out) {
         tma_store_2d(&tmap_o, sp, h * D, q0);
       } else {
@@ -404,29 +453,33 @@ __global__ void __launch_bounds__(THREADS, 1)
 
 }  // namespace
 
-// Causal self-attention over all T rows (q, k, v head-major [H, T, 128] bf16, out
-// [T, HQ*128]); called by ffb_attention for positions == NULL.
-int ffb_attention_tc(const uint16_t* q, const uint16_t* k, const uint16_t* v, const int* key_lo, void* out, int T,
-                     int HQ, int HK, float scale, float out_inv, cudaStream_t stream) {
+// Causal self-attention (q, k, v head-major [H, rows, 128] bf16).  sel == NULL: every one
+// of the T rows, out [T, HQ*128] (bf16, or e4m3 when out_inv > 0); otherwise the S
+// selected rows at positions sel[0..S) (q rows sel[x] of a [HQ, T, 128] q when q_gather,
+// else rows x of a [HQ, S, 128] q), out [S, HQ*128] bf16.  key_lo: per output row.
+// Called by the host entries of attention.cu after their argument checks.
+int ffb_attention_tc(const uint16_t* q, const uint16_t* k, const uint16_t* v, const int64_t* sel, int q_gather,
+                     int S, const int* key_lo, void* out, int T, int HQ, int HK, float scale, float out_inv,
+                     cudaStream_t stream) {
   CUtensorMap tq, tk, tv, to;
-  int rc = ffb::make_tmap_3d_bf16(&tq, q, D, (uint64_t)T, (uint64_t)HQ, 64, BM);
+  const uint64_t q_rows = (sel && !q_gather) ? (uint64_t)S : (uint64_t)T;
+  int rc = ffb::make_tmap_3d_bf16(&tq, q, D, q_rows, (uint64_t)HQ, 64, BM);
   if (!rc) rc = ffb::make_tmap_3d_bf16(&tk, k, D, (uint64_t)T, (uint64_t)HK, 64, BN);
   if (!rc) rc = ffb::make_tmap_3d_bf16(&tv, v, D, (uint64_t)T, (uint64_t)HK, 64, BN);
   // out [T, HQ*128]: bf16 in [128 rows x 64 columns] boxes, or e4m3 in [128 x 128] boxes
-  if (!rc && out_inv > 0.f)
+  // (selected rows: plain stores, the map is not used)
+  if (sel)
+    memset(&to, 0, sizeof(to));
+  else if (!rc && out_inv > 0.f)
     rc = ffb::make_tmap_2d(&to, out, (uint64_t)T, (uint64_t)HQ * D, (uint64_t)HQ * D, BM, 128, 1);
   else if (!rc)
     rc = ffb::make_tmap_2d(&to, out, (uint64_t)T, (uint64_t)HQ * D, (uint64_t)HQ * D * 2, BM, 64, 2);
   if (rc) return rc;
-  static bool attr = false;
-  if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(attention_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
-    if (e != cudaSuccess) return ffb::fail(FFB_ECUDA, "ffb_attention: %s", cudaGetErrorString(e));
-    attr = true;
-  }
-  TcArgs a = {static_cast<uint16_t*>(out), key_lo, T, HQ, HK, scale * 1.4426950408889634f, out_inv};
-  cudaError_t e = ffb::launch(attention_tc_kernel, dim3((T + BM - 1) / BM, HQ), dim3(THREADS), SMEM, stream, tq, tk, tv,
-                              to, a);
+  cudaError_t e = ffb::set_smem_attr(reinterpret_cast<const void*>(attention_tc_kernel), SMEM);
+  if (e != cudaSuccess) return ffb::fail(FFB_ECUDA, "ffb_attention: %s", cudaGetErrorString(e));
+  TcArgs a = {static_cast<uint16_t*>(out), key_lo, sel, q_gather, T, HQ, HK, scale * 1.4426950408889634f, out_inv};
+  const dim3 grid(sel ? S : (T + BM - 1) / BM, HQ);
+  e = ffb::launch(attention_tc_kernel, grid, dim3(THREADS), SMEM, stream, tq, tk, tv, to, a);
   if (e != cudaSuccess) return ffb::fail(FFB_ECUDA, "ffb_attention: %s", cudaGetErrorString(e));
   return FFB_OK;
 }

@@ -45,6 +45,42 @@ int fail(int code, const char* fmt, ...) {
   return code;
 }
 
+// (function, device) pairs whose dynamic shared-memory limit is already raised.  The
+// attribute is per function and per device, so a process that drives several devices
+// sets it once on each; the table is guarded by a mutex (host threads may launch
+// concurrently).
+namespace {
+constexpr int kAttrSlots = 256;
+struct AttrSlot {
+  const void* fn;
+  int dev;
+  int bytes;
+};
+AttrSlot g_attr[kAttrSlots];
+int g_attr_n = 0;
+std::mutex g_attr_mu;
+}  // namespace
+
+cudaError_t set_smem_attr(const void* fn, int bytes) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  std::lock_guard<std::mutex> lock(g_attr_mu);
+  for (int i = 0; i < g_attr_n; ++i)
+    if (g_attr[i].fn == fn && g_attr[i].dev == dev && g_attr[i].bytes >= bytes) return cudaSuccess;
+  e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e != cudaSuccess) return e;
+  if (g_attr_n < kAttrSlots) g_attr[g_attr_n++] = AttrSlot{fn, dev, bytes};
+  return cudaSuccess;
+}
+
+int sm_count() {
+  int dev = 0, sms = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) return 148;
+  return sms;
+}
+
 int check_launch(const char* what) {
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return fail(FFB_ECUDA, "%s: launch failed: %s", what, cudaGetErrorString(e));
@@ -124,6 +160,27 @@ int make_tmap_2d_bytes(CUtensorMap* map, const void* base, uint64_t rows, uint64
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(FFB_ECUDA, "cuTensorMapEncodeTiled (bytes) failed (%d)", (int)r);
+  return FFB_OK;
+}
+
+int make_tmap_3d_bytes(CUtensorMap* map, const void* base, uint64_t inner, uint64_t rows, uint64_t depth,
+                       uint64_t row_bytes, uint64_t depth_bytes, uint32_t box_inner, uint32_t box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(FFB_ECUDA, "cuTensorMapEncodeTiled is unavailable from the driver");
+  if (!aligned(base, 16)) return fail(FFB_EINVAL, "TMA base address must be 16-byte aligned");
+  if (row_bytes % 16 != 0 || depth_bytes % 16 != 0)
+    return fail(FFB_EINVAL, "TMA strides (%llu, %llu bytes) must be multiples of 16", (unsigned long long)row_bytes,
+                (unsigned long long)depth_bytes);
+  if (box_inner % 16 != 0 || box_inner > 256 || box_rows > 256)
+    return fail(FFB_EINVAL, "TMA byte box %u x %u: inner extent a multiple of 16, both <= 256", box_inner, box_rows);
+  cuuint64_t dims[3] = {inner, rows, depth};
+  cuuint64_t strides[2] = {row_bytes, depth_bytes};
+  cuuint32_t box[3] = {box_inner, box_rows, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(FFB_ECUDA, "cuTensorMapEncodeTiled (3-D bytes) failed (%d)", (int)r);
   return FFB_OK;
 }
 

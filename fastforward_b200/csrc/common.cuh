@@ -18,6 +18,23 @@ namespace ffb {
 void set_error(const char* fmt, ...);
 int fail(int code, const char* fmt, ...);
 int check_launch(const char* what);
+// Raises `fn`'s dynamic shared-memory limit to `bytes` on the current device, once per
+// (function, device); thread-safe.
+cudaError_t set_smem_attr(const void* fn, int bytes);
+// Streaming multiprocessors of the current device.
+int sm_count();
+
+// The weight-stationary FP8 GEMM (gemm_fp8_stream.cu): weights on the MMA's M side, tokens
+// on N, one (weight tile, token range, K range) item per CTA.  `ctas` is its CTA count for
+// this M x N x K, epilogue (FFB_EPI_BF16, FFB_EPI_F32_PARTIAL, FFB_EPI_SWIGLU, 100 = qkv +
+// QK-norm + RoPE, 101 = SwiGLU + static FP8 output) and K split, or 0 when it does not
+// apply; `stream_gemm` runs it (the caller has checked the arguments; rope_side points to
+// the qkv epilogue's argument block).
+int stream_gemm_ctas(int M, int N, int K, int epilogue, int splits);
+bool stream_gemm_preferred(int M, int N, int K, int epilogue);
+int stream_gemm(const uint8_t* a8, const float* a_scale, int a_per_row, const uint8_t* w8, const float* w_scale,
+                int w_per_col, int epilogue, void* out, int splits, float out_inv, const void* rope_side, int M, int N,
+                int K, cudaStream_t stream);
 
 #define FFB_REQUIRE(cond, ...)                                   \
   do {                                                           \
@@ -409,6 +426,11 @@ int make_tmap_3d_bf16(CUtensorMap* map, const void* base, uint64_t inner, uint64
 // multiple of 16), zero fill out of bounds; the tile lands row after row in shared memory.
 int make_tmap_2d_bytes(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t row_bytes,
                        uint32_t box_rows, uint32_t box_cols);
+// 3-D byte map without swizzle: [depth][rows][inner bytes] (row and plane pitches in
+// bytes), box {box_inner bytes (a multiple of 16), box_rows, 1}; out-of-range rows of a
+// plane are clipped (stores) or zero filled (loads).
+int make_tmap_3d_bytes(CUtensorMap* map, const void* base, uint64_t inner, uint64_t rows, uint64_t depth,
+                       uint64_t row_bytes, uint64_t depth_bytes, uint32_t box_inner, uint32_t box_rows);
 // 3-D store map [depth][rows][inner] (bf16 or fp32), box {64 bytes, box_rows, 1}, 64-byte
 // swizzle: the staging tile in shared memory holds row r's 16-byte chunk c at
 // r*64 + ((c ^ ((r >> 1) & 3)) << 4), in a buffer aligned to 512 bytes.

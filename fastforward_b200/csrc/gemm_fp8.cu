@@ -904,35 +904,20 @@ __global__ void __launch_bounds__(threads_of(EPI), 1)
   }
 }
 
-int num_sms() {
-  static int sms = 0;
-  if (!sms) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) sms = 148;
-  }
-  return sms;
-}
+int num_sms() { return ffb::sm_count(); }
 
 template <int BN, int EPI, int PRO>
 cudaError_t launch_instance(const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap& to, const GemmArgs& ga,
                             int grid, cudaStream_t stream) {
   using C = Cfg<BN>;
-  static bool attr_set = false;  // the attribute is per function (one device per process here)
-  if (!attr_set) {
-    cudaError_t e =
-        cudaFuncSetAttribute(fp8_gemm_kernel<BN, EPI, PRO>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
-    if (e != cudaSuccess) return e;
-    attr_set = true;
-  }
+  cudaError_t ea = ffb::set_smem_attr(reinterpret_cast<const void*>(fp8_gemm_kernel<BN, EPI, PRO>), C::SMEM);
+  if (ea != cudaSuccess) return ea;
   if constexpr (PRO != PRO_NONE) {
     // the fused prologue's grid barrier needs every CTA resident at once
-    static int per_sm = -1;
-    if (per_sm < 0) {
-      cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fp8_gemm_kernel<BN, EPI, PRO>,
-                                                                    threads_of(EPI), C::SMEM);
-      if (e != cudaSuccess) return e;
-    }
+    int per_sm = 0;
+    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fp8_gemm_kernel<BN, EPI, PRO>,
+                                                                  threads_of(EPI), C::SMEM);
+    if (e != cudaSuccess) return e;
     if (grid > per_sm * num_sms()) return cudaErrorCooperativeLaunchTooLarge;
   }
   return ffb::launch(fp8_gemm_kernel<BN, EPI, PRO>, dim3(grid), dim3(threads_of(EPI)), C::SMEM, stream, ta, tw, to,
@@ -1125,10 +1110,18 @@ extern "C" int ffb_fp8_gemm(const uint8_t* a8, const float* a_scale, int a_per_r
                             int feature_tile, int M, int N, int K, void* stream) {
   GemmArgs ga;
   int bn = 0;
-  int rc = prep_gemm(ga, bn, a8, a_scale, a_per_row, w8, w_scale, w_per_col, epilogue, out, ws, splits, feature_tile,
-                     M, N, K);
+  const bool stream_tile = feature_tile == FFB_TILE_STREAM;
+  int rc = prep_gemm(ga, bn, a8, a_scale, a_per_row, w8, w_scale, w_per_col, epilogue, out, ws, splits,
+                     stream_tile ? 0 : feature_tile, M, N, K);
   if (rc) return rc;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  FFB_REQUIRE(!stream_tile || ffb::stream_gemm_ctas(M, N, K, epilogue, splits) > 0,
+              "ffb_fp8_gemm: the weight-stationary schedule does not apply (M=%d N=%d K=%d splits=%d: at most "
+              "256 tokens per CTA and tiles x splits <= SMs)", M, N, K, splits);
+  if (stream_tile || (feature_tile == 0 && splits == 1 && ffb::stream_gemm_preferred(M, N, K, epilogue)))
+    return ffb::stream_gemm(a8, a_scale, a_per_row, w8, w_scale, w_per_col, epilogue,
+                            epilogue == FFB_EPI_F32_PARTIAL ? static_cast<void*>(ws) : static_cast<void*>(out), splits,
+                            0.f, nullptr, M, N, K, s);
   return bn == 256 ? launch_bn<256>(a8, w8, ga, PRO_NONE, s) : launch_bn<128>(a8, w8, ga, PRO_NONE, s);
 }
 
@@ -1144,6 +1137,9 @@ extern "C" int ffb_fp8_gemm_swiglu_fp8(const uint8_t* a8, const float* a_scale, 
   if (rc) return rc;
   ga.epilogue = EPI_SWIGLU_Q8;
   ga.out_inv = out_inv;
+  if (ffb::stream_gemm_preferred(M, N, K, EPI_SWIGLU_Q8))
+    return ffb::stream_gemm(a8, a_scale, a_per_row, w8, w_scale, w_per_col, EPI_SWIGLU_Q8, out8, 1, out_inv, nullptr,
+                            M, N, K, reinterpret_cast<cudaStream_t>(stream));
   return launch_bn<256>(a8, w8, ga, PRO_NONE, reinterpret_cast<cudaStream_t>(stream));
 }
 
@@ -1169,6 +1165,9 @@ extern "C" int ffb_fp8_gemm_qk_rope(const uint8_t* a8, const float* a_scale, int
   int rc = prep_rope(ga, a8, a_scale, a_per_row, w8, w_scale, w_per_col, q_norm, k_norm, eps, cos, sin, yq, yk, yv, T,
                      HQ, HK, K);
   if (rc) return rc;
+  if (ffb::stream_gemm_preferred(T, ga.N, K, EPI_QKROPE))  // same field order as the stream kernel's block
+    return ffb::stream_gemm(a8, a_scale, a_per_row, w8, w_scale, w_per_col, EPI_QKROPE, nullptr, 1, 0.f, &ga.rope, T,
+                            ga.N, K, reinterpret_cast<cudaStream_t>(stream));
   return launch_bn<128>(a8, w8, ga, PRO_NONE, reinterpret_cast<cudaStream_t>(stream));
 }
 
@@ -1183,4 +1182,9 @@ extern "C" int ffb_fp8_gemm_qk_rope_fused(const ffb_gemm_prologue* pro, uint8_t*
   if (!rc) rc = prep_prologue(ga, pro, a8, a_scale, a_per_row);
   if (rc) return rc;
   return launch_bn<128>(a8, w8, ga, pro->kind, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int ffb_fp8_gemm_stream_ctas(int M, int N, int K, int epilogue, int splits) {
+  if (epilogue != FFB_EPI_BF16 && epilogue != FFB_EPI_F32_PARTIAL && epilogue != FFB_EPI_SWIGLU) return 0;
+  return ffb::stream_gemm_ctas(M, N, K, epilogue, splits);
 }

@@ -416,27 +416,14 @@ __global__ void __launch_bounds__(THREADS, 1)
   }
 }
 
-int num_sms() {
-  static int sms = 0;
-  if (!sms) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) sms = 148;
-  }
-  return sms;
-}
+int num_sms() { return ffb::sm_count(); }
 
 template <int BN, int EPI>
 cudaError_t launch_instance(const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap& to, const W4Args& wa,
                             int grid, cudaStream_t stream) {
   using C = W4Cfg<BN>;
-  static bool attr_set = false;  // the attribute is per function (one device per process here)
-  if (!attr_set) {
-    cudaError_t e =
-        cudaFuncSetAttribute(w4a16_gemm_kernel<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
-    if (e != cudaSuccess) return e;
-    attr_set = true;
-  }
+  cudaError_t e = ffb::set_smem_attr(reinterpret_cast<const void*>(w4a16_gemm_kernel<BN, EPI>), C::SMEM);
+  if (e != cudaSuccess) return e;
   return ffb::launch(w4a16_gemm_kernel<BN, EPI>, dim3(grid), dim3(THREADS), C::SMEM, stream, ta, tw, to, wa);
 }
 

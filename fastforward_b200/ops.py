@@ -114,7 +114,7 @@ def attention_direct(q, k, v, scale, bm=16, bn=64, warps=4, positions=None, tria
         _need(tuple(positions.shape) == (s,) and positions.is_contiguous(), "positions must be [S] contiguous")
         pos = positions.to(torch.int64)
     else:
-        _need(s <= t, "causal attention needs S <= T")
+        _need(s == t, "causal attention over all rows needs S == T (pass positions for selected rows)")
     y = torch.empty((1, s, hq, d), device=q.device, dtype=BF16)
     call("ffb_attention", ptr(q), ptr(k), ptr(vv), ptr(pos), 0, ptr(y), s, t, hq, hk, float(scale),
          stream_ptr(q.device))

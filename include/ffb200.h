@@ -172,7 +172,20 @@ int ffb_quantize_weight_fp8_noalloc(const uint16_t* w, int per_channel, uint8_t*
  * epilogue FFB_EPI_BF16: out [M,N] bf16; FFB_EPI_F32_PARTIAL: ws [splits][M][N] fp32
  * (K split `splits` ways; the consumer sums the splits); FFB_EPI_SWIGLU: out [M,N/2] bf16
  * with w8 rows (and a per-channel w_scale) in ffb_pack_gateup order.
- * feature_tile: 128 or 256 output features per tile (0 = 256 when N allows). */
+ * feature_tile: 128 or 256 output features per token-major tile (128 tokens x 128/256
+ * features per MMA tile); FFB_TILE_STREAM: the weight-stationary schedule (weights on the
+ * MMA's M side, each CTA one 128-feature weight tile (two, gate and up, for SwiGLU), a
+ * range of at most 256 tokens and one of the `splits` K ranges; needs M <= 256 x CTAs per
+ * tile and tiles x splits <= SMs); 0 = the weight-stationary schedule when splits == 1,
+ * M <= 512 and it applies, else 256 when N allows, else 128.  Every choice gives the same
+ * bytes for the same `splits`. */
+#define FFB_TILE_STREAM 1
+/* The number of CTAs ffb_fp8_gemm's weight-stationary schedule (FFB_TILE_STREAM) launches
+ * for an M x N x K GEMM with this epilogue (FFB_EPI_BF16, FFB_EPI_F32_PARTIAL or
+ * FFB_EPI_SWIGLU) and K split on the current device, or 0 when it does not apply.  A
+ * host-side query (no device work) for planners; part of the same replacement as
+ * ffb_fp8_gemm. */
+int ffb_fp8_gemm_stream_ctas(int M, int N, int K, int epilogue, int splits);
 int ffb_fp8_gemm(const uint8_t* a8, const float* a_scale, int a_per_row,
                  const uint8_t* w8, const float* w_scale, int w_per_col,
                  int epilogue, uint16_t* out, float* ws, int splits, int feature_tile,

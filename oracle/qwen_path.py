@@ -27,7 +27,7 @@ E4M3 = torch.float8_e4m3fn
 FP8_MAX = 448.0
 
 __all__ = [
-    "rms_one", "add_rms", "qk_pair", "attention_direct", "set_attention_block", "quantize_static",
+    "rms_one", "add_rms", "qk_pair", "attention_direct", "attention_tc", "set_attention_block", "quantize_static",
     "quantize_rows", "quantize_weight_tensor", "quantize_weight_channel",
     "fp8_linear_static", "fp8_linear_rowwise", "swiglu", "lm_readout",
     "log_softmax", "int4_sym_quantize", "int4_sym_dequantize", "int4_sym_pack",
@@ -58,8 +58,13 @@ def _inv_rms(x, eps):
     reference.  Returns [..., 1] fp32."""
     n = x.shape[-1]
     ss = (x.double() * x.double()).sum(-1, keepdim=True).float()
-    var = ss / _f32(n)
-    return _f32(1.0) / torch.sqrt(var + _f32(eps))
+    # Each fp32 operation is evaluated in float64 and rounded once to fp32, which is the
+    # correctly rounded fp32 result (float64 has more than 2 x 24 + 2 bits).  torch's own
+    # fp32 sqrt on the CPU is not always correctly rounded (1 ulp off on some inputs).
+    var = (ss.double() / n).float()
+    v = (var.double() + float(_f32(eps))).float()
+    r = torch.sqrt(v.double()).float()
+    return (1.0 / r.double()).float()
 
 
 # ----------------------------------------------------------------------------- norms
@@ -168,6 +173,30 @@ def attention_direct(q, k, v, scale, positions=None, block_n=64):
         mx = new
     out = (acc / den[..., None]).to(BF16)
     return out.transpose(0, 1).contiguous()
+
+
+def attention_tc(q, k, v, scale, positions=None, key_lo=None):
+    """Causal GQA attention with the arithmetic of the CUDA kernel fixed operation by
+    operation (oracle/attn.c): the same blocked online softmax as `attention_direct`
+    (`_legacy/limit_kernels.py:8-33`, 64-key blocks, bf16 P), with Q.K^T and P.V
+    accumulated as the tensor core accumulates (`_tc.acc_bf16`), the exponential
+    exp2_poly(x * scale * log2 e - m) and the kernel's summation order.  Agrees with
+    `attention_direct` to rounding and with the GPU bit for bit.
+    q: [HQ, S, D], k, v: [HK, T, D] bf16; positions: [S] or None (= arange(S));
+    key_lo: [S] lowest visible key of each row or None (= 0).  Returns [S, HQ, D] bf16."""
+    from . import _tc
+    hq, s_len, d = q.shape
+    hk, t_len, _ = k.shape
+    assert d == 128
+    group = hq // hk
+    qpos = torch.arange(s_len) if positions is None else positions.long()
+    lo = torch.zeros(s_len, dtype=torch.long) if key_lo is None else key_lo.long()
+    scale_log2 = float(torch.tensor(float(scale), dtype=torch.float32) * torch.tensor(1.4426950408889634, dtype=torch.float32))
+    out = torch.empty(s_len, hq, d, dtype=BF16)
+    for h in range(hq):
+        out[:, h] = _tc.attention_head(q[h].to(BF16), k[h // group].to(BF16), v[h // group].to(BF16), qpos, lo,
+                                       scale_log2)
+    return out
 
 
 # ----------------------------------------------------------------------------- FP8
@@ -558,11 +587,17 @@ def _attention_block(layer, x, cos, sin, dims, mode, pick=None):
     v = qkv[:, (hq + hk) * d:].reshape(t, hk, d).transpose(0, 1).contiguous()
     yq, yk = qk_pair(q, k, layer["q_norm"], layer["k_norm"], cos, sin, dims["eps"], dims["eps"])
     scale = d ** -0.5
+    # Under the tensor-core accumulation model the layers use the attention kernel's own
+    # arithmetic (`attention_tc`, bit-identical to the GPU); otherwise the reference
+    # restatement with its exact products (`attention_direct`).
+    kernel_model = ACCUMULATION == "tcgen05" and ATTENTION_BLOCK_N == 64
     if pick is None:
-        out = attention_direct(yq, yk, v, scale, block_n=ATTENTION_BLOCK_N)
+        out = attention_tc(yq, yk, v, scale) if kernel_model else \
+            attention_direct(yq, yk, v, scale, block_n=ATTENTION_BLOCK_N)
     else:
         sel = torch.tensor([pick])
-        out = attention_direct(yq[:, sel], yk, v, scale, positions=sel, block_n=ATTENTION_BLOCK_N)
+        out = attention_tc(yq[:, sel], yk, v, scale, positions=sel) if kernel_model else \
+            attention_direct(yq[:, sel], yk, v, scale, positions=sel, block_n=ATTENTION_BLOCK_N)
     return _linear(out.reshape(out.shape[0], hq * d), layer["o"], mode, tail=pick is not None)
 
 

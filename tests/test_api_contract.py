@@ -9,6 +9,15 @@ import pytest
 from fastforward_b200.api import Accelerator, response, validate_request
 
 
+def test_reference_import_name_resolves_to_this_surface():
+    """`fastforward_accel.Accelerator(config, backend="fast")` -- the reference's import
+    name -- is this package's surface, so the reference's callers run unchanged."""
+    import fastforward_accel
+    assert fastforward_accel.Accelerator is Accelerator
+    assert fastforward_accel.validate_request is validate_request
+    assert fastforward_accel.response is response
+
+
 def test_request_validation(tmp_path):
     image = tmp_path / "input.png"
     image.touch()

@@ -34,6 +34,15 @@ def _hf_checkpoint(path, tied):
     return {k: v.detach().clone() for k, v in m.state_dict().items()}
 
 
+def test_expected_vision_depth_is_checked(tmp_path):
+    """A bundle's expected_dimensions (layers, hidden, vision blocks) must match the
+    checkpoint's vision depth too (`scaled_qwen_runtime.py:69`)."""
+    _hf_checkpoint(tmp_path, True)
+    C.load_language_model(tmp_path, option_ids=OPT, expected_dimensions=[2, 256, 2])
+    with pytest.raises(C.CheckpointError, match="vision blocks"):
+        C.load_language_model(tmp_path, option_ids=OPT, expected_dimensions=[2, 256, 24])
+
+
 @pytest.mark.parametrize("tied", [True, False])
 def test_reads_checkpoints_written_by_transformers(tmp_path, tied):
     sd = _hf_checkpoint(tmp_path, tied)

@@ -53,3 +53,64 @@ def test_bf16_model_reproduces_gpu_accumulators():
     for name in ("normal", "wide"):
         got = _tc.acc_bf16(d[name]["x"], d[name]["w"], 0, d[name]["x"].shape[1])
         assert torch.equal(got, d[name]["acc"]), f"{name}: {(got != d[name]['acc']).sum().item()} differ"
+
+
+def test_vector_path_equals_scalar_model():
+    """The vectorised accumulation model (AVX-512, used when the CPU has it) computes the
+    scalar model's accumulators bit for bit: e4m3 and bf16 operands with zeros, subnormals,
+    wide exponent spreads and K ranges that are not whole chunks."""
+    g = torch.Generator().manual_seed(5)
+    for scale in (30.0, 1.0, 300.0):
+        a = torch.randn(37, 1000, generator=g) * scale
+        a[torch.rand(37, 1000, generator=g) < 0.1] = 0
+        a = a.clamp(-448, 448).to(torch.float8_e4m3fn)
+        w = (torch.randn(53, 1000, generator=g) * scale * torch.exp(2 * torch.randn(53, 1000, generator=g)))
+        w = w.clamp(-448, 448).to(torch.float8_e4m3fn)
+        for k0, k1 in ((0, 1000), (128, 640), (0, 984)):
+            assert torch.equal(_tc.acc(a, w, k0, k1).view(torch.int32),
+                               _tc.acc_scalar(0, a, w, k0, k1).view(torch.int32)), (scale, k0, k1)
+    for scale in (1.0, 1e-3):
+        a = (torch.randn(41, 300, generator=g) * torch.exp(3 * torch.randn(41, 300, generator=g))).to(torch.bfloat16)
+        a[torch.rand(41, 300, generator=g) < 0.2] = 0
+        w = (torch.randn(29, 300, generator=g) * scale * torch.exp(4 * torch.randn(29, 300, generator=g)))
+        w = w.to(torch.bfloat16)
+        for k0, k1 in ((0, 300), (16, 300)):
+            assert torch.equal(_tc.acc_bf16(a, w, k0, k1).view(torch.int32),
+                               _tc.acc_scalar(1, a, w, k0, k1).view(torch.int32)), (scale, k0, k1)
+    print(f"\nvector path in use: {bool(_tc.lib().tc_vector_path())}")
+
+
+def test_exp2_poly_accuracy_and_edges():
+    """The attention kernel's exponential (oracle/attn.c, the same operations as the CUDA
+    kernel's exp2_poly): within 1 ulp of 2^x on [-30, 0], exact at 0, 0 below 2^-125."""
+    import numpy as np
+    x = torch.linspace(-30.0, 0.0, 200001, dtype=torch.float32)
+    y = _tc.exp2(x).double().numpy()
+    ref = np.exp2(x.double().numpy())
+    ulp = np.spacing(ref.astype(np.float32)).astype(np.float64)
+    assert (np.abs(y - ref) / ulp).max() <= 1.0
+    e = _tc.exp2(torch.tensor([0.0, -0.0, float("-inf"), -125.5, -126.0, -1.0, -0.5]))
+    assert e.tolist()[:5] == [1.0, 1.0, 0.0, 0.0, 0.0] and e[5].item() == 0.5
+
+
+def test_attention_tc_is_the_reference_softmax_to_rounding():
+    """`oracle.attention_tc` (the kernel's arithmetic) against `attention_direct` (the
+    reference's algorithm with exact products): within bf16 rounding, selected rows equal
+    the causal rows, and a request starting at a 64-row boundary of a segmented sequence
+    gets exactly its own attention."""
+    g = torch.Generator().manual_seed(9)
+    hq, hk, t = 4, 2, 200
+    q = torch.randn(hq, t, 128, generator=g).to(torch.bfloat16)
+    k = torch.randn(hk, t, 128, generator=g).to(torch.bfloat16)
+    v = torch.randn(hk, t, 128, generator=g).to(torch.bfloat16)
+    a = oracle.attention_tc(q, k, v, 128 ** -0.5)
+    b = oracle.attention_direct(q, k, v, 128 ** -0.5)
+    torch.testing.assert_close(a.float(), b.float(), atol=2e-2, rtol=2e-2)
+    assert (a.view(torch.int16) == b.view(torch.int16)).float().mean() > 0.99
+    sel = torch.tensor([199, 63, 64, 0])
+    c = oracle.attention_tc(q[:, sel], k, v, 128 ** -0.5, positions=sel)
+    assert torch.equal(c.view(torch.int16), a[sel].view(torch.int16))
+    lo = torch.where(torch.arange(t) >= 128, 128, 0)
+    e = oracle.attention_tc(q, k, v, 128 ** -0.5, key_lo=lo)
+    f = oracle.attention_tc(q[:, 128:], k[:, 128:], v[:, 128:], 128 ** -0.5)
+    assert torch.equal(e[128:].view(torch.int16), f.view(torch.int16))
