@@ -58,6 +58,15 @@ def parse():
                    help="request streams: requests concatenated into one forward (Engine.forward_batch); "
                         "1 = one graph replay per request")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-extra", action="store_true",
+                   help="N > 1: skip the 8B stream (C4) and 32B tensor-parallel (C5) blocks of the headline line")
+    p.add_argument("--extra-requests", type=int, default=128,
+                   help="N > 1: requests of the 8B stream block (C4)")
+    p.add_argument("--cpu-threads", type=int, default=0,
+                   help="--impl reference: host threads (0 = all; the reference runtime sets 1, api.py:60)")
+    p.add_argument("--cpu-layer", action="store_true",
+                   help="--impl reference: time one decoder layer of the workload's model per step (C1: "
+                        "--workload 2B-layer-T512) instead of whole requests")
     p.add_argument("--layers", type=int, default=None,
                    help="build only this many decoder layers (same shapes; for small profiler captures)")
     p.add_argument("--ncu-range", action="store_true",
@@ -76,28 +85,41 @@ def read_peaks():
 
 
 class Clocks:
-    """nvidia-smi sampling during the timed region."""
+    """nvidia-smi sampling (every 20 ms) of one GPU during the timed region.  The sampler is
+    started and its first sample awaited before the region begins (nvidia-smi takes ~0.1 s
+    to start, longer than a short timed region); the summary keeps the samples taken
+    inside the region (timestamps), or the first one after it starts if it was too short
+    for any."""
 
     def __init__(self, index):
         self.index = index
         self.proc = None
         self.path = None
+        self.t0 = self.t1 = None
 
     def __enter__(self):
+        import datetime
         fd, self.path = tempfile.mkstemp(suffix=".csv")
         os.close(fd)
-        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+        q = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={q}",
-                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                          "--format=csv,noheader,nounits", "-lms", "20"],
                                          stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+            deadline = time.time() + 5.0
+            while time.time() < deadline and not Path(self.path).read_text().strip():
+                time.sleep(0.01)
         except Exception:
             self.proc = None
+        self.t0 = datetime.datetime.now()
         return self
 
     def __exit__(self, *a):
+        import datetime
+        self.t1 = datetime.datetime.now()
+        time.sleep(0.05)  # the sample that covers the region's end
         if self.proc is not None:
             self.proc.terminate()
             try:
@@ -106,32 +128,47 @@ class Clocks:
                 self.proc.kill()
 
     def summary(self):
+        import datetime
         rows = []
         try:
             for line in Path(self.path).read_text().splitlines():
                 f = [x.strip() for x in line.split(",")]
-                if len(f) >= 9:
+                if len(f) >= 10:
                     rows.append(f)
         except Exception:
             pass
         if not rows:
             return dict(sm_mhz=None, sm_max_mhz=None, reasons=["unsampled"], samples=0)
-        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+
+        def ts(r):
+            try:
+                return datetime.datetime.strptime(r[0], "%Y/%m/%d %H:%M:%S.%f")
+            except ValueError:
+                return None
+        inside = [r for r in rows if ts(r) and self.t0 and self.t0 <= ts(r) <= self.t1 + datetime.timedelta(seconds=0.03)]
+        if not inside:
+            after = [r for r in rows if ts(r) and self.t0 and ts(r) >= self.t0]
+            inside = after[:1] or rows[-1:]
+        sm = [float(r[2]) for r in inside if r[2].replace(".", "").isdigit()]
         reasons = set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for r in rows:
-            for n, v in zip(names, r[5:9]):
+        for r in inside:
+            for n, v in zip(names, r[6:10]):
                 if v.lower().startswith("active"):
                     reasons.add(n)
-        return dict(sm_mhz=statistics.median(sm) if sm else None, sm_max_mhz=float(rows[0][2]),
-                    reasons=sorted(reasons), samples=len(rows))
+        return dict(sm_mhz=statistics.median(sm) if sm else None, sm_max_mhz=float(inside[0][3]),
+                    reasons=sorted(reasons), samples=len(inside))
 
-
-# ---------------------------------------------------------------------------- CPU side
 
 class CpuSample:
     """The oracle (the reference path's arithmetic restated on the CPU) on the workload's
-    model: built once, then timed one decoder layer (or the tail) at a time."""
+    model: built once (n_layers decoder layers + the tail layer), then timed one decoder
+    layer, the tail, or a whole request at a time.
+
+    Its linears multiply the e4m3 values in fp32 (products exact, fp32 sums, then the
+    reference's scales and bf16 rounding).  CPU `torch._scaled_mm` would be the same
+    arithmetic but is no usable CPU implementation: it accepts only per-tensor scales and
+    took 240 s for one 320 x 19456 x 2560 GEMM on this image (0.1 s as an fp32 matmul)."""
 
     def __init__(self, dims, layout, threads, n_layers=1, mode="rowwise"):
         import torch
@@ -139,18 +176,19 @@ class CpuSample:
         from fastforward_b200.synthetic import make_model_bf16, make_request
         from fastforward_b200.mrope import position_ids
         torch.set_num_threads(threads)
-        # a CPU implementation times ordinary fp32 GEMMs of the e4m3 values (as CPU
-        # torch._scaled_mm computes them), not the oracle's bit-level tensor-core model
+        # a CPU implementation times ordinary fp32 GEMMs of the e4m3 values, not the
+        # oracle's bit-level tensor-core accumulation model
         oracle.set_accumulation("fp32")
         self.o = oracle
         self.dims, self.layout = dims, layout
         src = make_model_bf16(dims, seed=0, device="cpu", layers=n_layers + 1)
         self.mode = mode
         self.om = oracle.quantized_model(dims, src, mode)
+        del src
         self.req = make_request(dims, layout, seed=1)
         T = layout.bucket
-        pos = position_ids(T, layout.image_start, layout.grid_h, layout.grid_w)
-        self.cos, self.sin = oracle.mrope_cos_sin(pos, dims.d, dims.theta)
+        self.pos = position_ids(T, layout.image_start, layout.grid_h, layout.grid_w)
+        self.cos, self.sin = oracle.mrope_cos_sin(self.pos, dims.d, dims.theta)
         self.h = oracle.embed_rows(self.om["embed"], self.req["ids"][:T], self.req["visual"], layout.image_start)
         self.n_layers = n_layers
 
@@ -167,37 +205,73 @@ class CpuSample:
                     self.req["pick"], om["final_norm"], om["head"], self.req["k"])
         return time.perf_counter() - t0
 
+    def request(self):
+        """One whole request: embedding, every decoder layer, the pick-row tail and the
+        option scoring (`oracle.prefill_score`).  Returns seconds."""
+        T = self.layout.bucket
+        t0 = time.perf_counter()
+        self.o.prefill_score(self.om, self.req["ids"][:T], self.req["visual"], self.req["deep"], self.pos,
+                             self.req["pick"], self.req["k"], mode=self.mode, image_start=self.layout.image_start)
+        return time.perf_counter() - t0
+
     def full_request_seconds(self, t_layer, t_tail):
         return t_layer * (self.dims.layers - 1) + t_tail
 
 
+def bench_config(workload, name, mode, T, world, weight_bytes):
+    """The `config` object of a bench line (the same for both arms)."""
+    tp_mode = name == "32B" and world > 1
+    return dict(workload=workload, model=f"Qwen3-VL-{name}-shaped", global_batch=1 if tp_mode else world,
+                seq_len=T, parallelism=f"tp{world}" if tp_mode else f"replicas{world}", quant=mode,
+                l2=f"weights ({weight_bytes / 1e9:.1f} GB) exceed L2; no flush needed", tokens_per_step=T)
+
+
 def run_reference(args):
+    """The reference's arithmetic for this path on the host CPU, whole requests: every step
+    is one full prefill + scoring of the workload's model (all layers), all host threads.
+    The reference itself has no CPU path (`api.py:56-57` refuses one) and its kernels are
+    Triton/CUDA, so its CPU implementation here is the oracle's restatement."""
     import torch
     from fastforward_b200.config import MODELS, WORKLOADS
     name, layout, mode = WORKLOADS[args.workload]
     dims = MODELS[name]
     rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", str(args.gpus)))
     if rank != 0:
         return
-    threads = os.cpu_count() or 1
-    cs = CpuSample(dims, layout, threads, mode=mode)
-    t_tail = cs.tail()
+    threads = args.cpu_threads or os.cpu_count() or 1
+    t_build = time.perf_counter()
+    cs = CpuSample(dims, layout, threads, n_layers=1 if args.cpu_layer else dims.layers - 1, mode=mode)
+    t_build = time.perf_counter() - t_build
     times = []
     for i in range(args.warmup + args.steps):
-        t = cs.layer()
+        t = cs.layer() if args.cpu_layer else cs.request()
         if i >= args.warmup:
-            times.append(cs.full_request_seconds(t, t_tail))
+            times.append(t)
     T = layout.bucket
     per_req = statistics.median(times)
     value = T / per_req
-    line = dict(metric=metric_for(args.workload), value=value, unit=UNIT, n_gpus=args.gpus, steps=args.steps, warmup=args.warmup,
-                ms_per_step=per_req * 1e3, higher_is_better=True, scaling="weak", vs_baseline=None, dtype="int4-bf16" if mode == "int4" else "fp8-e4m3",
-                data="synthetic", impl="reference",
-                config=dict(workload=args.workload, model=f"Qwen3-VL-{name}-shaped", global_batch=1, seq_len=T,
-                            parallelism="cpu"),
+    wfac = 0.5 + 2 / 128 if mode == "int4" else 1.0
+    weight_bytes = dims.params_per_layer() * dims.layers * wfac
+    cpu_model = ""
+    try:
+        cpu_model = next(l.split(":", 1)[1].strip() for l in open("/proc/cpuinfo") if l.startswith("model name"))
+    except (OSError, StopIteration):
+        pass
+    line = dict(metric=metric_for(args.workload), value=value, unit=UNIT, n_gpus=world, steps=args.steps,
+                warmup=args.warmup, ms_per_step=per_req * 1e3, higher_is_better=True,
+                scaling="strong" if (name == "32B" and world > 1) else "weak", vs_baseline=None,
+                dtype="int4-bf16" if mode == "int4" else "fp8-e4m3",
+                data="synthetic (seeded N(0,0.02) weights, N(0,1) visual/deepstack rows, uniform text ids)",
+                impl="reference", config=bench_config(args.workload, name, mode, T, world, weight_bytes),
+                latency_ms=dict(p50=per_req * 1e3, min=min(times) * 1e3, max=max(times) * 1e3),
                 cpu_baseline=dict(value=value, unit=UNIT, cores=threads, kind="port",
-                                  sample=f"1 decoder layer per step (tail timed once, {t_tail:.2f}s), scaled to "
-                                         f"{dims.layers - 1} layers + tail; fp32 GEMMs of the quantised weights"),
+                                  sample=(f"one decoder layer per step ({args.steps} timed, +{args.warmup} warm-up)"
+                                          if args.cpu_layer else
+                                          f"whole requests: {args.steps} timed (+{args.warmup} warm-up) full "
+                                          f"{dims.layers}-layer prefills + scoring") + f" at T={T} on {threads} threads "
+                                         f"({cpu_model}); fp32 GEMMs of the e4m3 values; model built in "
+                                         f"{t_build:.0f} s (untimed)"),
                 e2e=dict(value=value, unit=UNIT, h2d_bytes_per_step=0, d2h_bytes_per_step=0))
     print(json.dumps(line), flush=True)
 
@@ -456,15 +530,25 @@ def run_ours(args):
                               f"{dims.layers - 1} layers + tail; fp32 GEMMs of the quantised weights")
 
     clk_sum = clk.summary()
+    launches = eng.launches_per_forward() * args.steps
+    extra = {}
+    if world > 1 and args.workload == "4B-fp8-T320" and not args.no_extra:
+        # the multi-GPU configurations besides the headline's replicas, in the same line:
+        # the 8B request stream served by N replicas (C4) and the 32B model tensor-parallel
+        # over the N ranks (C5)
+        del entry
+        eng.graphs.clear()
+        del eng, pm
+        torch.cuda.empty_cache()
+        extra["stream_8b"] = _summarise_stream(stream_measure(args, "8B-fp8-stream", world, rank, local, dev,
+                                                              n_req=args.extra_requests))
+        extra["tp_32b"] = tp32b_measure(args, world, rank, local, dev)
     if rank == 0:
         line = dict(metric=metric_for(args.workload), value=value, unit=UNIT, n_gpus=world, steps=args.steps, warmup=args.warmup,
                     ms_per_step=p50, higher_is_better=True, scaling="strong" if tp_mode else "weak",
                     vs_baseline=None,
                     dtype="int4-bf16" if int4 else "fp8-e4m3", data="synthetic (seeded N(0,0.02) weights, N(0,1) visual/deepstack rows, uniform text ids)",
-                    config=dict(workload=args.workload, model=f"Qwen3-VL-{name}-shaped", global_batch=streams,
-                                seq_len=T, parallelism=f"tp{world}" if tp_mode else f"replicas{world}", quant=mode,
-                                l2=f"weights ({weight_bytes / 1e9:.1f} GB) exceed L2; no flush needed",
-                                tokens_per_step=T),
+                    config=bench_config(args.workload, name, mode, T, world, weight_bytes),
                     latency_ms=dict(p50=p50, p99=p99, mean=total_s / args.steps * 1e3),
                     requests_per_s=streams * args.steps / total_s,
                     roofline=roofline,
@@ -476,14 +560,106 @@ def run_ours(args):
                              wall_s=wall, api="Accelerator.prefill_score_stream",
                              one_call_per_request=dict(value=single_value, unit=UNIT, api="Accelerator.prefill_score",
                                                        requests=n_single)),
-                    gpu_launches=eng.launches_per_forward() * args.steps,
-                    clocks=clk_sum, cpu_baseline=cpu)
+                    gpu_launches=launches,
+                    clocks=clk_sum, cpu_baseline=cpu, **extra)
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
+        if not extra:
+            del entry
+            eng.graphs.clear()
+        dist.destroy_process_group()
+
+
+def _summarise_stream(line):
+    """The C4 block of a multi-GPU headline line (rank 0; None elsewhere)."""
+    if line is None:
+        return None
+    return dict(workload=line["config"]["workload"], requests=line["steps"], value=line["value"], unit=line["unit"],
+                latency_ms=line["latency_ms"], prefill_tok_per_s=line["prefill_tok_per_s"],
+                e2e=dict(value=line["e2e"]["value"], unit=line["e2e"]["unit"], api=line["e2e"]["api"]),
+                graphs=line["config"]["graphs"], parallelism=line["config"]["parallelism"], clocks=line["clocks"])
+
+
+def tp32b_measure(args, world, rank, local, dev):
+    """C5: the 32B FP8 model at T = 1024 tensor-parallel over the `world` ranks (each rank
+    one shard; the process group is the caller's).  Graph replays device-timed, max over
+    ranks; the two all-reduces of every decoder layer (fp32 [T, H] partials of o_proj and
+    down_proj) and the per-token scale MAX all-reduces are timed alone with CUDA events.
+    Returns rank 0's block (None elsewhere)."""
+    import torch
+    import torch.distributed as dist
+    from fastforward_b200.config import MODELS, WORKLOADS
+    from fastforward_b200.engine import Engine, PackedModel
+    from fastforward_b200.synthetic import make_model_bf16, make_request
+    wl = "32B-fp8-T1024"
+    name, layout, mode = WORKLOADS[wl]
+    dims = MODELS[name]
+    T = layout.bucket
+    s = torch.cuda.current_stream()
+    with torch.no_grad():
+        src = make_model_bf16(dims, seed=0, device=dev)
+        pm = PackedModel(dims, src, mode=mode, device=dev, free_source=True, tp=(rank, world))
+        del src
+        torch.cuda.empty_cache()
+        eng = Engine(pm, tp_group=dist.group.WORLD)
+        req = make_request(dims, layout, seed=1, device=dev)
+        entry = eng.capture(T, layout.image_start, layout.nv, layout.grid_h, layout.grid_w, layout.k, len(req["deep"]))
+        ids = req["ids"][:layout.n_tokens]
+        for _ in range(3):
+            eng.replay(entry, ids, req["visual"], req["deep"], req["pick"])
+        torch.cuda.synchronize()
+        dist.barrier()
+        steps = max(5, min(args.steps, 20))
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+        with Clocks(local) as clk:
+            t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            t0.record(s)
+            for a, b in evs:
+                a.record(s)
+                entry["graph"].replay()
+                b.record(s)
+            t1.record(s)
+            torch.cuda.synchronize()
+        total = torch.tensor([t0.elapsed_time(t1) * 1e-3], device=dev)
+        dist.all_reduce(total, op=dist.ReduceOp.MAX)
+        lat = sorted(a.elapsed_time(b) for a, b in evs)
+        p50 = lat[len(lat) // 2]
+        z = entry["buffers"].logits[:layout.k].float().cpu().tolist()
+
+        def coll_us(numel, op):  # one collective alone, device-timed, median of 20, max over ranks
+            buf = torch.zeros(numel, device=dev)
+            for _ in range(3):
+                dist.all_reduce(buf, op=op)
+            ts = []
+            for _ in range(20):
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record(s)
+                dist.all_reduce(buf, op=op)
+                b.record(s)
+                b.synchronize()
+                ts.append(a.elapsed_time(b) * 1e3)
+            t = torch.tensor([statistics.median(ts)], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            return t.item()
+        ar_us = coll_us(T * dims.hidden, dist.ReduceOp.SUM)
+        scale_us = coll_us(T, dist.ReduceOp.MAX)
         del entry
         eng.graphs.clear()
-        dist.destroy_process_group()
+        del eng, pm
+        torch.cuda.empty_cache()
+        dist.barrier()
+    if rank != 0:
+        return None
+    per_req = total.item() / steps
+    n_ar = 2 * (dims.layers - 1) + 2
+    return dict(workload=wl, parallelism=f"tp{world}", ms_per_request=per_req * 1e3,
+                latency_ms=dict(p50=p50, p99=lat[-1]), tok_per_s=T / per_req, requests_per_s=1.0 / per_req,
+                allreduce=dict(per_call_us=ar_us, bytes_per_call=T * dims.hidden * 4, calls_per_request=n_ar,
+                               busbw_gbs=2 * (world - 1) / world * T * dims.hidden * 4 / (ar_us * 1e-6) / 1e9,
+                               share_of_request=n_ar * ar_us * 1e-3 / (per_req * 1e3),
+                               scale_max_us=scale_us, scale_calls_per_request=n_ar),
+                logits=z, clocks=clk.summary())
 
 
 def run_stream(args):
@@ -508,7 +684,26 @@ def run_stream(args):
     if world > 1:
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=dev)
-    name, mode, n_req = STREAMS[args.workload]
+    line = stream_measure(args, args.workload, world, rank, local, dev)
+    if rank == 0 and line is not None:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def stream_measure(args, workload, world, rank, local, dev, n_req=None):
+    """The request-stream measurement of `run_stream` (the process group, if any, is the
+    caller's).  Returns rank 0's bench line (None elsewhere); n_req overrides the stream's
+    length."""
+    import torch
+    import torch.distributed as dist
+    from fastforward_b200.config import MODELS, STREAMS, BUCKETS, stream_layouts
+    from fastforward_b200.engine import Engine, PackedModel
+    from fastforward_b200.synthetic import make_model_bf16, make_request
+    from fastforward_b200.api import Accelerator
+    name, mode, n_stream = STREAMS[workload]
+    n_req = n_req or n_stream
     dims = MODELS[name]
     layouts = stream_layouts(n_req, seed=1)
     with torch.no_grad():
@@ -609,6 +804,7 @@ def run_stream(args):
         tokens = sum(r["lay"].n_tokens for r in reqs)
     clk_sum = clk.summary()
     host_lat.sort()
+    line = None
     if rank == 0:
         pct = lambda xs, q: xs[min(len(xs) - 1, int(round(q * (len(xs) - 1))))]
         line = dict(metric=f"requests/s (Qwen3-VL-{name} FP8, {n_req}-request stream: 64/144/256 visual tokens, "
@@ -616,7 +812,7 @@ def run_stream(args):
                     value=value, unit="req/s", n_gpus=world, steps=n_req, warmup=args.warmup,
                     ms_per_step=pct(lat, 0.5), higher_is_better=True, scaling="weak", vs_baseline=None,
                     dtype="fp8-e4m3", data="synthetic (seeded weights, request geometries and inputs)",
-                    config=dict(workload=args.workload, model=f"Qwen3-VL-{name}-shaped", global_batch=world,
+                    config=dict(workload=workload, model=f"Qwen3-VL-{name}-shaped", global_batch=world,
                                 seq_len="96-384 (bucketed)", parallelism=f"replicas{world}", quant=mode,
                                 graphs=len(entries), prefill_tokens_per_replica=tokens,
                                 l2="weights (6.9 GB) exceed L2; no flush needed"),
@@ -626,12 +822,13 @@ def run_stream(args):
                              d2h_bytes_per_step=d2h, api="Accelerator.prefill_score",
                              host_latency_ms=dict(p50=pct(host_lat, 0.5), p99=pct(host_lat, 0.99))),
                     gpu_launches=sum(eng.launches_per_forward() for _ in reqs), clocks=clk_sum, cpu_baseline=None)
-        print(json.dumps(line), flush=True)
+    entries.clear()
+    eng.graphs.clear()
+    del eng, pm, reqs, dev_reqs
+    torch.cuda.empty_cache()
     if world > 1:
         dist.barrier()
-        entries.clear()
-        eng.graphs.clear()
-        dist.destroy_process_group()
+    return line
 
 
 def run_stream_batched(args, eng, reqs, dims, name, mode, n_req, world, rank, local, dev):
@@ -726,10 +923,8 @@ def run_stream_batched(args, eng, reqs, dims, name, mode, n_req, world, rank, lo
                              d2h_bytes_per_step=d2h, api="Accelerator.prefill_score_batch"),
                     gpu_launches=sum(eng.launches_per_batch(len(bt)) for bt in batches), clocks=clk_sum,
                     cpu_baseline=None)
-        print(json.dumps(line), flush=True)
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
+        return line
+    return None
 
 
 # ---------------------------------------------------------------------------- input packing

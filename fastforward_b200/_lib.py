@@ -12,7 +12,7 @@ import torch
 LIB_PATH = Path(__file__).resolve().with_name("libffb200.so")
 
 OK, EINVAL, EUNSUPPORTED, ECUDA, ETIMEOUT = 0, -1, -2, -3, -4
-QUANT_NONE, QUANT_STATIC, QUANT_ROWWISE = 0, 1, 2
+QUANT_NONE, QUANT_STATIC, QUANT_ROWWISE, QUANT_ROWSCALE = 0, 1, 2, 3
 EPI_BF16, EPI_F32_PARTIAL, EPI_SWIGLU = 0, 1, 2
 TILE_STREAM = 1  # ffb_fp8_gemm feature_tile: the weight-stationary schedule
 PRO_QUANT, PRO_ADD_RMSNORM = 1, 2

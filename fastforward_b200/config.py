@@ -119,6 +119,9 @@ class Layout:
 WORKLOADS = {
     # 2B-shaped, 256 visual tokens on a 16x16 LLM grid + 64 text, 4 choices
     "2B-fp8-T320": ("2B", Layout(0, 32, 32, 64, k=4), "rowwise"),
+    # C1: the reference's CPU case, one 2B decoder layer at T = 512 (256 visual rows on a
+    # 16x16 merged grid + 256 text positions); timed on the host only (bench --cpu-layer)
+    "2B-layer-T512": ("2B", Layout(0, 32, 32, 256, k=4), "rowwise"),
     # north-star: 4B-shaped FP8 prefill of 320 tokens + choice scoring
     "4B-fp8-T320": ("4B", Layout(0, 32, 32, 64, k=4), "rowwise"),
     # the same with the reference's shipped FP8 scheme (per-tensor weight scales, static

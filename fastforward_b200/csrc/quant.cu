@@ -78,7 +78,10 @@ __global__ void __launch_bounds__(1024) quant_rows_vec_kernel(const uint16_t* __
     amax = block_max_any(amax, red);
     scale = fmaxf(amax, 1e-12f) / 448.f;
     if (threadIdx.x == 0) qscale[row] = scale;
+  } else if (mode == FFB_QUANT_ROWSCALE) {
+    scale = qscale[row];
   }
+  const bool divide = mode != FFB_QUANT_STATIC;
 #pragma unroll
   for (int i = 0; i < QV; ++i) {
     const int vi = threadIdx.x + i * blockDim.x;
@@ -86,7 +89,7 @@ __global__ void __launch_bounds__(1024) quant_rows_vec_kernel(const uint16_t* __
       uint32_t lo = 0, hi = 0;
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
-        const float qv = mode == FFB_QUANT_ROWWISE ? __fdiv_rn(v[i][e], scale) : v[i][e] * inv;
+        const float qv = divide ? __fdiv_rn(v[i][e], scale) : v[i][e] * inv;
         const uint32_t b = f2e4m3(clamp448(qv));
         if (e < 4) lo |= b << (8 * e);
         else hi |= b << (8 * (e - 4));
@@ -113,10 +116,12 @@ __global__ void __launch_bounds__(NT) quant_rows_kernel(const uint16_t* __restri
     amax = block_max(amax, red);
     scale = fmaxf(amax, 1e-12f) / 448.f;
     if (threadIdx.x == 0) qscale[row] = scale;
+  } else if (mode == FFB_QUANT_ROWSCALE) {
+    scale = qscale[row];
   }
   for (int k = threadIdx.x; k < K; k += NT) {
     const float v = bf2f(xr[k]);
-    const float qv = mode == FFB_QUANT_ROWWISE ? __fdiv_rn(v, scale) : v * inv;
+    const float qv = mode != FFB_QUANT_STATIC ? __fdiv_rn(v, scale) : v * inv;
     qr[k] = f2e4m3(clamp448(qv));
   }
 }
@@ -191,9 +196,9 @@ extern "C" int ffb_quantize_fp8(const uint16_t* x, int quant_mode, float inv_sca
                                 int M, int K, void* stream) {
   FFB_REQUIRE(x && q8, "ffb_quantize_fp8: NULL pointer");
   FFB_REQUIRE(M > 0 && K > 0, "ffb_quantize_fp8: bad shape M=%d K=%d", M, K);
-  FFB_REQUIRE(quant_mode == FFB_QUANT_STATIC || quant_mode == FFB_QUANT_ROWWISE, "ffb_quantize_fp8: bad mode %d",
-              quant_mode);
-  FFB_REQUIRE(quant_mode != FFB_QUANT_ROWWISE || qscale, "ffb_quantize_fp8: ROWWISE needs qscale");
+  FFB_REQUIRE(quant_mode == FFB_QUANT_STATIC || quant_mode == FFB_QUANT_ROWWISE || quant_mode == FFB_QUANT_ROWSCALE,
+              "ffb_quantize_fp8: bad mode %d", quant_mode);
+  FFB_REQUIRE(quant_mode == FFB_QUANT_STATIC || qscale, "ffb_quantize_fp8: ROWWISE / ROWSCALE need qscale");
   cudaError_t e;
   const int nvec = K / 8;
   if (K % 8 == 0 && ffb::aligned(x, 16) && ffb::aligned(q8, 8) && nvec <= 1024 * QV) {

@@ -329,7 +329,9 @@ class Engine:
         mode_ = {True: "all", False: "none"}.get(fuse, fuse)
         if mode_ not in ("none", "tail", "all"):
             raise ValueError(f"fuse must be 'none', 'tail' or 'all', not {fuse!r}")
-        self.fuse = "none" if model.mode == "int4" else mode_
+        # int4 has no FP8 prologue; tensor-parallel rowwise quantisers need a collective
+        # between the slice scales and the cast, so no quantiser runs as a GEMM prologue
+        self.fuse = "none" if (model.mode == "int4" or self.world > 1) else mode_
         # static scales: attention and the gate/up launch also write the FP8 input of the
         # linear after them (`ffb_attention_fp8`, `ffb_fp8_gemm_swiglu_fp8`), so neither
         # activation quantiser has a launch of its own
@@ -365,9 +367,9 @@ class Engine:
                 epi = L.EPI_SWIGLU if swiglu else (L.EPI_F32_PARTIAL if s > 1 else L.EPI_BF16)
                 if self.world > 1 and role in ("o", "down"):  # fp32 partial for the all-reduce
                     s, epi = 1, L.EPI_F32_PARTIAL
-                elif (tag == "full" and self.fuse != "all" and m <= self.STREAM_MAX_ROWS
+                elif (tag == "full" and self.fuse != "all" and m <= self.STREAM_MAX_ROWS and self.m.mode != "int4"
                       and (swiglu or (role in ("o", "down") and self.stream_od))):
-                    # (the fused-prologue GEMMs of the tail and of fuse="all" are token-major)
+                    # (FP8 only; the fused-prologue GEMMs of the tail and of fuse="all" are token-major)
                     ws_plan = weight_stationary_plan(m, n, k, swiglu)
                     if ws_plan is not None:
                         s, epi = ws_plan
@@ -504,6 +506,26 @@ class Engine:
              int(lin["scale"].numel() > 1), ptr(lay.q_norm), ptr(lay.k_norm), float(d.eps), ptr(cos), ptr(sin),
              ptr(b.yq), ptr(b.yk), ptr(b.yv), T, d.hq, d.hk, d.hidden, self._s)
 
+    def _quant_rows_tp(self, x, q8, qs, rows, K):
+        """Rowwise quantisation of a row-parallel linear's input x [rows, K] (this rank's
+        slice of each row): the slice's scales, all-reduced (MAX) over the tensor-parallel
+        group -- the whole row's scale, max(max|x_row|, 1e-12) / 448 being monotonic in the
+        maximum -- then the slice quantised with them (FFB_QUANT_ROWSCALE), so every rank
+        holds exactly the unsharded activation bytes.  One [rows] fp32 all-reduce on the
+        compute stream (captured in the graph with the kernels)."""
+        call("ffb_quantize_fp8", ptr(x), L.QUANT_ROWWISE, 0.0, ptr(q8), ptr(qs), rows, K, self._s)
+        import torch.distributed as dist
+        dist.all_reduce(qs[:rows], op=dist.ReduceOp.MAX, group=self.group)
+        call("ffb_quantize_fp8", ptr(x), L.QUANT_ROWSCALE, 0.0, ptr(q8), ptr(qs), rows, K, self._s)
+
+    def _quant_in(self, x, qmode, inv, q8, qs, rows, K):
+        """The activation quantiser in front of o_proj / down_proj (rank-complete rows under
+        tensor parallelism)."""
+        if self.world > 1 and qmode == L.QUANT_ROWWISE:
+            self._quant_rows_tp(x, q8, qs, rows, K)
+        else:
+            call("ffb_quantize_fp8", ptr(x), qmode, inv, ptr(q8), ptr(qs), rows, K, self._s)
+
     def _tp_reduce(self, plan, ws):
         """Sums this rank's fp32 partial [m, n] (in ws) over the tensor-parallel group, in
         place, on the current stream (captured into the graph with the kernels)."""
@@ -582,8 +604,7 @@ class Engine:
                 self._w4(p, b.attn, lay.lin["o"], b.lin_out, b.ws)
             else:
                 if not self.static_q8:
-                    call("ffb_quantize_fp8", ptr(b.attn), qmode, lay.inv["o"], ptr(b.o8), ptr(b.os), T, HQ * D,
-                         self._s)
+                    self._quant_in(b.attn, qmode, lay.inv["o"], b.o8, b.os, T, HQ * D)
                     obs(j, "o", b.os, T)
                 self._gemm(p, b.o8, sa(lay, "o", b.os), lay.lin["o"], b.lin_out, b.ws, rowwise)
             self._tp_reduce(p, b.ws)
@@ -609,8 +630,7 @@ class Engine:
                 self._w4(p, b.act, lay.lin["down"], b.lin_out, b.ws)
             else:
                 if not self.static_q8:
-                    call("ffb_quantize_fp8", ptr(b.act), qmode, lay.inv["down"], ptr(b.act8), ptr(b.acts), T, I,
-                         self._s)
+                    self._quant_in(b.act, qmode, lay.inv["down"], b.act8, b.acts, T, I)
                     obs(j, "down", b.acts, T)
                 self._gemm(p, b.act8, sa(lay, "down", b.acts), lay.lin["down"], b.lin_out, b.ws, rowwise)
             self._tp_reduce(p, b.ws)
@@ -637,7 +657,7 @@ class Engine:
         if int4:
             self._w4(p, b.attn, lay.lin["o"], b.lin_out, b.ws)
         else:
-            call("ffb_quantize_fp8", ptr(b.attn), qmode, lay.inv["o"], ptr(b.o8), ptr(b.os), 1, HQ * D, self._s)
+            self._quant_in(b.attn, qmode, lay.inv["o"], b.o8, b.os, 1, HQ * D)
             obs(depth - 1, "o", b.os, 1)
             self._gemm(p, b.o8, sa(lay, "o", b.os), lay.lin["o"], b.lin_out, b.ws, rowwise)
         self._tp_reduce(p, b.ws)
@@ -659,7 +679,7 @@ class Engine:
         if int4:
             self._w4(p, b.act, lay.lin["down"], b.mlp1, b.ws)
         else:
-            call("ffb_quantize_fp8", ptr(b.act), qmode, lay.inv["down"], ptr(b.act8), ptr(b.acts), 1, I, self._s)
+            self._quant_in(b.act, qmode, lay.inv["down"], b.act8, b.acts, 1, I)
             obs(depth - 1, "down", b.acts, 1)
             self._gemm(p, b.act8, sa(lay, "down", b.acts), lay.lin["down"], b.mlp1, b.ws, rowwise)
         self._tp_reduce(p, b.ws)

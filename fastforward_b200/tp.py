@@ -11,8 +11,10 @@ of the 32B shape divide by N = 2, 4, 8):
   down     row-split over the same channels -> fp32 partial, all-reduced.
 Embedding, deepstack, the norms and the readout are replicated.  Weights are quantised
 whole and then sliced, so every rank's FP8 (or int4) bytes and per-channel scales equal
-the unsharded model's; per-token activation scales are taken over the rank's slice of the
-o_proj / down_proj input (no extra collective).
+the unsharded model's.  Per-token activation scales of the o_proj / down_proj inputs are
+the whole row's: each rank quantises its slice with the MAX over the ranks' slice scales (a
+[T] fp32 all-reduce before the cast, `Engine._quant_rows_tp`), so the activation bytes are
+the unsharded ones too and each rank's partial is one K split of the unsharded linear.
 
 The packed weight layouts sliced here are those of `engine.PackedModel`: qkv rows
 [q heads; k heads; v heads]; gate/up rows interleaved per 128 channels (so a rank's

@@ -35,6 +35,9 @@ extern "C" {
 #define FFB_QUANT_NONE 0       /* no FP8 output                                           */
 #define FFB_QUANT_STATIC 1     /* q = e4m3(clamp(x * inv, +-448)); depth_fp8.py:8-12       */
 #define FFB_QUANT_ROWWISE 2    /* s = max|x_row|/448, q = e4m3(x / s); fp8_private.py:11-18 */
+#define FFB_QUANT_ROWSCALE 3   /* ffb_quantize_fp8 only: q = e4m3(clamp(x / s)) with s = qscale[row]
+                                  given (a row split over tensor-parallel ranks: the whole row's
+                                  ROWWISE scale, the MAX over the ranks' slice scales)          */
 
 /* GEMM epilogues. */
 #define FFB_EPI_BF16 0         /* out[m,n] = bf16(acc * sa * sw)                           */
@@ -133,7 +136,8 @@ int ffb_gather_rows(const void* src, const int64_t* index, void* dst, int n, int
 
 /* Activation FP8 quantisation of a bf16 [M,K] matrix.
  * STATIC replaces _family/depth_fp8.py:8-19 (`_runtime_scale`); ROWWISE replaces
- * _legacy/fp8_private.py:11-18 (`quantize_rows`).  q8 [M,K]; qscale [M] (ROWWISE). */
+ * _legacy/fp8_private.py:11-18 (`quantize_rows`).  q8 [M,K]; qscale [M] (ROWWISE: written;
+ * ROWSCALE: read, the quotient x / qscale[row] as ROWWISE forms it). */
 int ffb_quantize_fp8(const uint16_t* x, int quant_mode, float inv_scale,
                      uint8_t* q8, float* qscale, int M, int K, void* stream);
 

@@ -229,8 +229,10 @@ def quantize_rows(x):
     pad = (m + 15) // 16 * 16
     xp = torch.zeros(pad, k)
     xp[:m] = x
-    scale = torch.clamp(xp.abs().amax(-1), min=1e-12) / _f32(FP8_MAX)
-    q = (xp / scale[:, None]).clamp(-FP8_MAX, FP8_MAX).to(E4M3)
+    # fp32 quotients, each evaluated in float64 and rounded once (the correctly rounded fp32
+    # result; float64 has more than 2 x 24 + 2 bits)
+    scale = (torch.clamp(xp.abs().amax(-1), min=1e-12).double() / FP8_MAX).float()
+    q = (xp.double() / scale.double()[:, None]).float().clamp(-FP8_MAX, FP8_MAX).to(E4M3)
     return q, scale
 
 
@@ -515,18 +517,21 @@ def embed_rows(embed, ids, visual, image_start):
 
 def _tp_linear(x, lin, mode, world):
     """A K-split (row-parallel) linear over `world` tensor-parallel ranks: rank r holds
-    input columns [r*K/world, (r+1)*K/world) of x and of the weight, quantises its slice
-    of each row on its own (per-token scales over the slice) and produces an fp32 partial;
-    the partials are summed in rank order (the all-reduce) and rounded once to bf16."""
+    input columns [r*K/world, (r+1)*K/world) of x and of the weight and produces an fp32
+    partial; the partials are summed in rank order (the all-reduce) and rounded once to
+    bf16.  Rowwise: every rank quantises its slice with the whole row's per-token scale
+    (the ranks' slice maxima are combined first), so the FP8 bytes are the unsharded
+    ones and the result is the unsharded linear with a `world`-way K split."""
     x = x.reshape(-1, x.shape[-1])
     m, k = x.shape
     w = k // world
     total = None
+    q_full, sa_full = quantize_rows(x) if mode == "rowwise" else (None, None)
     for r in range(world):
         xs = x[:, r * w:(r + 1) * w]
         if mode == "rowwise":
-            q, sa = quantize_rows(xs)
-            part = _fp8_linear(q, sa, lin["w8"][:, r * w:(r + 1) * w].contiguous(), lin["w_scale"], 1)[:m]
+            q = q_full[:, r * w:(r + 1) * w].contiguous()
+            part = _fp8_linear(q, sa_full, lin["w8"][:, r * w:(r + 1) * w].contiguous(), lin["w_scale"], 1)[:m]
         elif mode == "static":
             q = quantize_static(xs, lin["inv"])
             sa = lin.get("a_scale")

@@ -146,6 +146,28 @@ def test_quantize_activation_bit_exact(M, K):
     assert_bytes_equal(q, oracle.quantize_static(x, inv), "static q8")
 
 
+def test_rowwise_quant_every_bf16_value():
+    """The rowwise quantiser's IEEE quotients: every finite bf16 value, quantised under row
+    maxima of several magnitudes, gives the bytes of the oracle's correctly rounded divide."""
+    allv = torch.arange(-32768, 32768, dtype=torch.int32).to(torch.int16).view(BF16).float()
+    allv = allv[torch.isfinite(allv)]
+    rows = []
+    for mx in (1.0, 3.71875, 448.0, 1e-3, 12345.0, 0.0302734375):
+        v = allv[allv.abs() <= mx]
+        idx = torch.linspace(0, v.numel() - 1, 16384).round().long()  # spread over the whole range
+        row = v[idx].clone()
+        row[-1] = mx  # the row maximum
+        rows.append(row)
+    x = torch.stack(rows).to(BF16)
+    M, K = x.shape
+    q8 = torch.empty((M, K), device=DEV, dtype=E4M3)
+    sc = torch.empty(M, device=DEV)
+    call("ffb_quantize_fp8", ptr(_keep(x.to(DEV))), L.QUANT_ROWWISE, 0.0, ptr(q8), ptr(sc), M, K, _sp())
+    want, want_s = oracle.quantize_rows(x)
+    assert torch.equal(sc.cpu(), want_s[:M])
+    assert_bytes_equal(q8, want[:M], "rowwise quant over every bf16 value")
+
+
 @pytest.mark.parametrize("N,K", [(256, 2048), (6144, 2560), (128, 9728)])
 def test_quantize_weight_bit_exact(N, K):
     w = _randn((N, K), 10, std=0.02)

@@ -1,9 +1,9 @@
 """Tensor-parallel engine on 2 GPUs (NCCL): a 32B-shaped model of two layers (one full
-layer and the pick-row tail) sharded over two ranks.  The logits must match the oracle's
-tensor-parallel path (per-rank activation scales, fp32 partials summed across ranks)
-within the attention-rounding noise floor, and the CUDA-graph replay -- which holds the
-NCCL all-reduces -- must equal the eager forward bit for bit.  Skipped with fewer than two
-GPUs."""
+layer and the pick-row tail) sharded over two ranks.  The logits must equal, bit for bit,
+the oracle's tensor-parallel path (whole-row activation scales, fp32 partials summed across
+ranks -- for two ranks the unsharded linear with a two-way K split), and the CUDA-graph
+replay -- which holds the NCCL all-reduces -- must equal the eager forward bit for bit.
+Skipped with fewer than two GPUs."""
 import os
 import socket
 
@@ -83,6 +83,7 @@ def test_tp2_engine_matches_oracle(tmp_path):
     zr = score(64)
     floor = (score(32) - zr).abs().max().item()
     err = (r["z"] - zr).abs().max().item()
-    print(f"\n32B TP=2 |dz| = {err:.3g} (oracle noise floor {floor:.3g})")
-    assert err <= max(2e-2, floor), (r["z"], zr, floor)
+    print(f"\n32B TP=2 |dz| = {err:.3g} (oracle's own blocking change {floor:.3g})")
+    assert err <= 2e-2, (r["z"], zr, floor)
     assert oracle.response_argmax(r["z"]) == oracle.response_argmax(zr)
+    assert torch.equal(r["z"].view(torch.int32), zr.view(torch.int32)), (r["z"], zr)
