@@ -83,7 +83,7 @@ class PackedModel:
     """A model's weights in the layouts the kernels read.
 
     mode "rowwise": FP8 e4m3 weights with per-output-channel scales, per-token activation
-    scales (the BASELINE scheme, `_legacy/fp8_private.py`); "static": per-tensor weight
+    scales (`_legacy/fp8_private.py`); "static": per-tensor weight
     scale + static per-tensor activation scale (`_family/depth_fp8.py`, the reference's
     shipped scheme); "int4": W4A16 symmetric group 128.
 

@@ -385,7 +385,7 @@ def lm_readout(x, norm_weight, head, eps):
 
 
 def log_softmax(logits):
-    """Log-softmax over the k option logits (fp32), the BASELINE scoring output."""
+    """Log-softmax over the k option logits (fp32): the scoring output next to the logits."""
     z = logits.float()
     m = z.max()
     return z - m - torch.log(torch.exp(z - m).sum())
@@ -400,7 +400,7 @@ def response_argmax(logits):
 # ----------------------------------------------------------------------------- int4
 
 def int4_sym_quantize(w, group=128):
-    """Symmetric int4, group 128, bf16 scales (the W4A16 scheme of the BASELINE config).
+    """Symmetric int4, group 128, bf16 scales (the W4A16 scheme the C3 workload runs).
 
     s = bf16(max|W_g| / 7) (floored at 1e-8 before rounding); q = clamp(rne(W / s), -8, 7).
     Returns (q [N, K] int8 in [-8, 7], scales [N, K/group] bf16).

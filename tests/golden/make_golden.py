@@ -25,7 +25,10 @@ reference):
     16-bit words) with a float64 accumulation rounded to fp32;
   * fp32 `tl.sum` is evaluated exactly (float64) and rounded once to fp32.  This is the
     one deliberate deviation from the GPU reference, shared by the oracle and the CUDA
-    kernels: the reference's fp32 reduction order is unspecified, an exact sum is not;
+    kernels: the reference's fp32 reduction order is unspecified, an exact sum is not.
+    The fixtures of add_rms / fast_norm / qk_pair / lm_readout are therefore the
+    reference's rounding points under an exact fp32 reduction, not the bytes of its GPU
+    tree sum;
   * `libdevice.exp` / `libdevice.div_rn` (CUDA-only) map to `tl.exp` / `tl.div_rn`.
 `sub10_runtime` and `night_runtime` import an un-vendored module
 (`_legacy/decision_pilot_contract.py:11-13`); it is replaced by an empty stand-in, which
