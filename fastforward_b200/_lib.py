@@ -14,6 +14,7 @@ LIB_PATH = Path(__file__).resolve().with_name("libffb200.so")
 OK, EINVAL, EUNSUPPORTED, ECUDA, ETIMEOUT = 0, -1, -2, -3, -4
 QUANT_NONE, QUANT_STATIC, QUANT_ROWWISE, QUANT_ROWSCALE = 0, 1, 2, 3
 EPI_BF16, EPI_F32_PARTIAL, EPI_SWIGLU = 0, 1, 2
+EPI_BIAS, EPI_BIAS_RES, EPI_BIAS_GELU_TANH, EPI_BIAS_GELU_ERF = 10, 11, 12, 13  # ffb_bf16_gemm
 TILE_STREAM = 1  # ffb_fp8_gemm feature_tile: the weight-stationary schedule
 PRO_QUANT, PRO_ADD_RMSNORM = 1, 2
 
@@ -57,6 +58,12 @@ SIGNATURES = {
     "ffb_w4a16_gemm": [P, P, P, I, P, P, I, I, I, I, I, P],
     "ffb_pack_rgb": [P, P, I, I, P],
     "ffb_pack_rgb_batch": [P, P, I, I, I, P],
+    "ffb_bf16_gemm": [P, P, P, P, I, P, I, I, I, I, P],
+    "ffb_bf16_gemm_feature_tile": [I, I],
+    "ffb_layernorm": [P, P, P, F, P, I, I, P],
+    "ffb_add_layernorm": [P, P, P, P, F, P, P, I, I, P],
+    "ffb_vision_rope": [P, P, P, I, I, I, I, P, P, P, P],
+    "ffb_attention_full": [P, P, P, P, I, I, I, F, P],
 }
 
 

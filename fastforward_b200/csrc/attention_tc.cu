@@ -57,26 +57,6 @@ constexpr int XCH_BYTES = 2 * 4 * BM * 4;  // row exchange [2 buffers][4 parts][
 constexpr int SMEM = 2 * Q_HALF + KV_STAGES * STAGE + 2 * P_BYTES + XCH_BYTES + 256 + 1024;
 constexpr int TMEM_COLS = 512;      // S[b] at column 64b (64 wide), O[b] at 128 + 128b (128 wide)
 
-// exp2_poly: 2^x = 2^n * 2^f with n = rint(x) and f = x - n in [-1/2, 1/2] (exact); 2^f
-// is the degree-7 Taylor polynomial of e^(f ln 2) (coefficients (ln 2)^k / k! rounded to
-// fp32) in Horner form with fused multiply-adds, and 2^n is added to the exponent field.
-// Results below 2^-125 (and x = -inf) are 0.  Within 1 ulp of 2^x for the x <= 0 it is
-// used on; every operation is an IEEE-rounded one, so a CPU with fmaf reproduces it.
-__device__ __forceinline__ float exp2_poly(float x) {
-  if (!(x >= -125.f)) return 0.f;
-  const float n = rintf(x);
-  const float f = __fsub_rn(x, n);
-  float p = 1.52527338040598403e-05f;
-  p = __fmaf_rn(p, f, 0.000154035303933816099f);
-  p = __fmaf_rn(p, f, 0.00133335581464284434f);
-  p = __fmaf_rn(p, f, 0.00961812910762847717f);
-  p = __fmaf_rn(p, f, 0.0555041086648215800f);
-  p = __fmaf_rn(p, f, 0.240226506959100712f);
-  p = __fmaf_rn(p, f, 0.693147180559945309f);
-  p = __fmaf_rn(p, f, 1.f);
-  return __int_as_float(__float_as_int(p) + ((int)n << 23));
-}
-
 // bf16(o / l) with the quotient correctly rounded to fp32 first.  y = o * (1/l) (the
 // reciprocal correctly rounded) is within 3 fp32 ulps of the rounded quotient q, so bf16(y)
 // and bf16(q) agree unless y lies within 3 ulps of a bf16 rounding midpoint (the fp32
@@ -101,6 +81,12 @@ struct TcArgs {
   int T, HQ, HK;
   float scale_log2;  // scale * log2(e)
   float out_inv;     // > 0: e4m3 output, e4m3(clamp(bf16 output * out_inv, +-448)); 0: bf16 output
+  // 0: every query row sees every key < T (the vision tower's attention over one image);
+  // the tile then visits all key blocks.  1: causal.
+  int causal;
+  // > 0: the first out_cols columns of each head's output (the rest is zero padding of the
+  // head dimension) go to out[row, h * out_cols + c] by plain stores; 0: TMA tile stores
+  int out_cols;
 };
 
 __global__ void __launch_bounds__(THREADS, 1)
@@ -131,7 +117,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int spos = rows_mode ? (int)min(max(args.sel[blockIdx.x], (int64_t)0), (int64_t)(args.T - 1)) : 0;
   const int q0 = rows_mode ? spos : (int)(gridDim.x - 1 - blockIdx.x) * BM;  // heaviest (latest) tiles first
   const int qrow0 = rows_mode ? (args.q_gather ? spos : (int)blockIdx.x) : q0;  // the Q box's first row
-  const int kend = min(args.T, rows_mode ? spos + 1 : q0 + BM);  // keys any row of this tile can see
+  const int kend = !args.causal ? args.T : min(args.T, rows_mode ? spos + 1 : q0 + BM);  // keys this tile sees
   const int nb = (kend + BN - 1) / BN;
   // first key block: the tile's lowest visible key (rows' key_lo are non-decreasing)
   const int lo0 = args.key_lo ? max(args.key_lo[rows_mode ? (int)blockIdx.x : min(q0, args.T - 1)], 0) : 0;
@@ -158,7 +144,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     tma_prefetch_desc(&tmap_q);
     tma_prefetch_desc(&tmap_k);
     tma_prefetch_desc(&tmap_v);
-    if (!rows_mode) tma_prefetch_desc(&tmap_o);
+    if (!rows_mode && args.out_cols == 0) tma_prefetch_desc(&tmap_o);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, TMEM_COLS);
@@ -246,7 +232,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int quarter = warp & 3;
     const int part = (warp - 2) >> 2;   // keys [16 part, 16 part + 16), output columns [32 part, 32 part + 32)
     const int r = quarter * 32 + lane;  // this thread's query row in the tile
-    const int qpos = rows_mode ? spos : q0 + r;  // selected rows: every row of the tile masks as row 0
+    // selected rows: every row of the tile masks as row 0; non-causal: as the last row
+    const int qpos = !args.causal ? args.T - 1 : rows_mode ? spos : q0 + r;
     const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
     float o[D / 4];
 #pragma unroll
@@ -305,7 +292,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       // visible key) + scale into base 2, in place
       float bmax = -INFINITY;
       const int kb = (jb0 + j) * BN, key0 = kb + 16 * part;
-      if (kb + BN - 1 > q0 || kb + BN > args.T || args.key_lo) {
+      if ((args.causal && kb + BN - 1 > q0) || kb + BN > args.T || args.key_lo) {
 #pragma unroll
         for (int c = 0; c < 16; ++c) {
           const int key = key0 + c;
@@ -385,6 +372,25 @@ __global__ void __launch_bounds__(THREADS, 1)
           *reinterpret_cast<uint4*>(dst + 8 * c) = make_uint4(w[0], w[1], w[2], w[3]);
         }
       }
+    } else if (args.out_cols > 0) {
+      // direct store: this thread's row, columns [32 part, 32 part + 32) below out_cols (a
+      // multiple of 8), 16 bytes at a time
+      const int row = q0 + r;
+      if (stage && row < args.T) {
+        const float rl = __frcp_rn(l);
+        uint16_t* dst = args.out + (size_t)row * args.HQ * args.out_cols + (size_t)h * args.out_cols;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const int col = 32 * part + 8 * c;
+          if (col + 8 > args.out_cols) break;
+          uint32_t w[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            w[e] = (uint32_t)bf16_quotient(o[8 * c + 2 * e], l, rl) |
+                   ((uint32_t)bf16_quotient(o[8 * c + 2 * e + 1], l, rl) << 16);
+          *reinterpret_cast<uint4*>(dst + col) = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+      }
     } else if (stage && fp8_out) {
       // the static FP8 quantisation of the o projection's input, applied to the bf16 output:
       // one 128-byte-swizzled [128 rows x 128 B] box in P tile 0, this part's 32 columns
@@ -423,7 +429,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       fence_proxy_async_smem();
     }
     named_barrier(1, SOFTMAX_WARPS * 32);
-    if (!rows_mode && warp == 2 && lane == 0 && !*abort_flag) {
+    if (!rows_mode && args.out_cols == 0 && warp == 2 && lane == 0 && !*abort_flag) {
       if (fp8_out) {
         tma_store_2d(&tmap_o, sp, h * D, q0);
       } else {
@@ -458,9 +464,11 @@ __global__ void __launch_bounds__(THREADS, 1)
 // selected rows at positions sel[0..S) (q rows sel[x] of a [HQ, T, 128] q when q_gather,
 // else rows x of a [HQ, S, 128] q), out [S, HQ*128] bf16.  key_lo: per output row.
 // Called by the host entries of attention.cu after their argument checks.
+// causal == 0: every row sees all T keys (sel must be NULL); out_cols > 0: out [T, HQ *
+// out_cols] bf16 holds the first out_cols columns of each head (plain stores).
 int ffb_attention_tc(const uint16_t* q, const uint16_t* k, const uint16_t* v, const int64_t* sel, int q_gather,
                      int S, const int* key_lo, void* out, int T, int HQ, int HK, float scale, float out_inv,
-                     cudaStream_t stream) {
+                     int causal, int out_cols, cudaStream_t stream) {
   CUtensorMap tq, tk, tv, to;
   const uint64_t q_rows = (sel && !q_gather) ? (uint64_t)S : (uint64_t)T;
   int rc = ffb::make_tmap_3d_bf16(&tq, q, D, q_rows, (uint64_t)HQ, 64, BM);
@@ -468,7 +476,7 @@ int ffb_attention_tc(const uint16_t* q, const uint16_t* k, const uint16_t* v, co
   if (!rc) rc = ffb::make_tmap_3d_bf16(&tv, v, D, (uint64_t)T, (uint64_t)HK, 64, BN);
   // out [T, HQ*128]: bf16 in [128 rows x 64 columns] boxes, or e4m3 in [128 x 128] boxes
   // (selected rows: plain stores, the map is not used)
-  if (sel)
+  if (sel || out_cols > 0)
     memset(&to, 0, sizeof(to));
   else if (!rc && out_inv > 0.f)
     rc = ffb::make_tmap_2d(&to, out, (uint64_t)T, (uint64_t)HQ * D, (uint64_t)HQ * D, BM, 128, 1);
@@ -477,7 +485,8 @@ int ffb_attention_tc(const uint16_t* q, const uint16_t* k, const uint16_t* v, co
   if (rc) return rc;
   cudaError_t e = ffb::set_smem_attr(reinterpret_cast<const void*>(attention_tc_kernel), SMEM);
   if (e != cudaSuccess) return ffb::fail(FFB_ECUDA, "ffb_attention: %s", cudaGetErrorString(e));
-  TcArgs a = {static_cast<uint16_t*>(out), key_lo, sel, q_gather, T, HQ, HK, scale * 1.4426950408889634f, out_inv};
+  TcArgs a = {static_cast<uint16_t*>(out), key_lo, sel, q_gather, T, HQ, HK, scale * 1.4426950408889634f, out_inv,
+              causal, out_cols};
   const dim3 grid(sel ? S : (T + BM - 1) / BM, HQ);
   e = ffb::launch(attention_tc_kernel, grid, dim3(THREADS), SMEM, stream, tq, tk, tv, to, a);
   if (e != cudaSuccess) return ffb::fail(FFB_ECUDA, "ffb_attention: %s", cudaGetErrorString(e));

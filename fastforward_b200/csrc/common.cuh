@@ -85,6 +85,26 @@ __device__ __forceinline__ uint8_t f2e4m3(float f) {
 }
 __device__ __forceinline__ float clamp448(float v) { return fminf(448.f, fmaxf(-448.f, v)); }
 
+// exp2_poly: 2^x = 2^n * 2^f with n = rint(x) and f = x - n in [-1/2, 1/2] (exact); 2^f
+// is the degree-7 Taylor polynomial of e^(f ln 2) (coefficients (ln 2)^k / k! rounded to
+// fp32) in Horner form with fused multiply-adds, and 2^n is added to the exponent field.
+// Results below 2^-125 (and x = -inf) are 0; x must stay below 128.  Within a few ulps of
+// 2^x; every operation is an IEEE-rounded one, so a CPU with fmaf reproduces it.
+__device__ __forceinline__ float exp2_poly(float x) {
+  if (!(x >= -125.f)) return 0.f;
+  const float n = rintf(x);
+  const float f = __fsub_rn(x, n);
+  float p = 1.52527338040598403e-05f;
+  p = __fmaf_rn(p, f, 0.000154035303933816099f);
+  p = __fmaf_rn(p, f, 0.00133335581464284434f);
+  p = __fmaf_rn(p, f, 0.00961812910762847717f);
+  p = __fmaf_rn(p, f, 0.0555041086648215800f);
+  p = __fmaf_rn(p, f, 0.240226506959100712f);
+  p = __fmaf_rn(p, f, 0.693147180559945309f);
+  p = __fmaf_rn(p, f, 1.f);
+  return __int_as_float(__float_as_int(p) + ((int)n << 23));
+}
+
 
 
 __device__ __forceinline__ float warp_sum(float v) {

@@ -1,0 +1,415 @@
+// bf16 linear with bias on the sm_100a tensor cores (tcgen05.mma kind::f16, fp32
+// accumulators in tensor memory), for the vision tower in front of the language path:
+// patch embedding, qkv / proj / fc1 / fc2 of every block and the mergers' two linears.
+//
+// Replaces the nn.Linear / Conv3d calls of the reference's vision wrappers
+// (_legacy/vision_graph_runtime.py:16-27 runs the HF blocks; scaled_qwen_runtime.py:42-55,
+// `NativeNormVision.core`): y = bf16(x W^T + b) with the bias added to the fp32
+// accumulator, and the operations the blocks apply to that bf16 output folded into the
+// epilogue: the residual add (bf16(res + y)) and the activations (bf16(gelu(y)), tanh
+// form in the blocks' MLP, erf form in the mergers).
+//
+// Tile = 128 tokens (UMMA M) x BN output features (UMMA N = 64, 128 or 256), 64 K
+// elements (one 128-byte swizzle row of bf16) per stage.  Persistent kernel, one CTA per
+// SM, tiles round-robin with the token tile fastest (CTAs that run at the same time share
+// weight tiles in L2).  Roles (320 threads):
+//   warp 0      TMA producer: activation tile [128 x 64] and weight tile [BN x 64], both
+//               K-major with the 128-byte swizzle, into a ring of STAGES slots; the first
+//               ring pass of weight tiles is requested before the wait on the previous
+//               kernel (weights do not depend on it);
+//   warp 1      TMEM allocator + single-thread MMA issuer (4 x K16 per stage) into one of
+//               two accumulators, so the epilogue of tile i overlaps the mainloop of i+1;
+//   warps 2..9  epilogue: lane quarter (warp % 4) x half of the tile's columns; 32
+//               columns at a time: fp32 accumulator + bias, the epilogue's operation,
+//               bf16, staged in shared memory and written by TMA store (rows past M and
+//               columns past N are clipped by the store).
+// K past the end of the operands is zero-filled by TMA (adds nothing), so K need not be
+// a multiple of 64.  Every wait is bounded; a timeout sets the abort flag and the device
+// error word, and TMEM is released.
+#include "common.cuh"
+#include "pdl.cuh"
+
+namespace {
+
+constexpr int BM = 128;
+constexpr int BKE = 64;
+constexpr int UMMA_K = 16;
+constexpr int A_BYTES = BM * BKE * 2;  // 16 KB
+constexpr int EPI_WARPS = 8;
+constexpr int THREADS = 64 + EPI_WARPS * 32;
+constexpr int SMEM_LIMIT = 232448;
+
+template <int BN>
+struct BCfg {
+  static constexpr int W_BYTES = BN * BKE * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + W_BYTES;
+  static constexpr int STG_BYTES = EPI_WARPS * 2 * 2048;
+  static constexpr int FIXED = STG_BYTES + 512 + 1024;
+  static constexpr int FIT = (SMEM_LIMIT - FIXED) / STAGE_BYTES;
+  static constexpr int STAGES = FIT > 8 ? 8 : FIT;
+  static constexpr int SMEM = STAGES * STAGE_BYTES + FIXED;
+  static constexpr int TMEM_COLS = 2 * BN;
+  static_assert(BN == 64 || BN == 128 || BN == 256, "feature tile 64, 128 or 256");
+  static_assert(STAGE_BYTES % 1024 == 0, "swizzled tiles need 1024-byte alignment");
+};
+
+struct BArgs {
+  const uint16_t* bias;  // [N] bf16 or NULL (no bias)
+  const uint16_t* res;   // [M][N] bf16 (FFB_EPI_BIAS_RES)
+  int M, N, K, n_ttiles, n_tiles;
+};
+
+// Both GELU forms are (x / 2) s with s = 1 + tanh(u) or 1 + erf(z), and s is evaluated
+// without the cancellation of 1 + (a value near -1): for u, z < 0 it is the small
+// positive term itself.  IEEE-rounded fp32 operations only (restated in oracle/act.c).
+//
+// tanh form: u = 0.7978845608 (x + 0.044715 x^3); with r = 2 / (e^(2|u|) + 1) (e by
+// exp2_poly of fp32(|u| 2 log2 e); r = 0 from |u| >= 40 on), s = r for u < 0, 2 - r
+// otherwise.  Absolute error of s below 1e-6.
+__device__ __forceinline__ float gelu_tanh(float x) {
+  const float x3 = __fmul_rn(__fmul_rn(x, x), x);
+  const float u = __fmul_rn(0.797884560802865355f, __fadd_rn(x, __fmul_rn(0.044715f, x3)));
+  const float a = fabsf(u);
+  float r = 0.f;
+  if (!(a >= 40.f)) r = __fdiv_rn(2.f, __fadd_rn(exp2_poly(__fmul_rn(a, 2.88539008177792681f)), 1.f));
+  const float s = u < 0.f ? r : __fsub_rn(2.f, r);
+  return __fmul_rn(__fmul_rn(0.5f, x), s);
+}
+// erf form: z = x / sqrt 2; erfc(|z|) ~ q = t (a1 + t (a2 + t (a3 + t (a4 + t a5))))
+// e^(-z^2), t = 1 / (1 + p |z|) (Abramowitz & Stegun 7.1.26, |error| <= 1.5e-7; Horner with
+// fused multiply-adds; e^(-z^2) by exp2_poly of fp32(fp32(z^2) * -log2 e)); s = q for
+// z < 0, 2 - q otherwise.
+__device__ __forceinline__ float gelu_erf(float x) {
+  const float z = __fmul_rn(x, 0.707106781186547524f);
+  const float a = fabsf(z);
+  const float t = __fdiv_rn(1.f, __fadd_rn(1.f, __fmul_rn(0.3275911f, a)));
+  float p = 1.061405429f;
+  p = __fmaf_rn(p, t, -1.453152027f);
+  p = __fmaf_rn(p, t, 1.421413741f);
+  p = __fmaf_rn(p, t, -0.284496736f);
+  p = __fmaf_rn(p, t, 0.254829592f);
+  p = __fmul_rn(p, t);
+  const float q = __fmul_rn(p, exp2_poly(__fmul_rn(__fmul_rn(a, a), -1.44269504088896341f)));
+  const float s = z < 0.f ? q : __fsub_rn(2.f, q);
+  return __fmul_rn(__fmul_rn(x, 0.5f), s);
+}
+
+__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+  return (uint32_t)f2bf(lo) | ((uint32_t)f2bf(hi) << 16);
+}
+__device__ __forceinline__ void unpack8(uint4 v, float* f) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    f[2 * i] = __uint_as_float(w[i] << 16);
+    f[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+  }
+}
+
+template <int EPI>
+__device__ __forceinline__ float epilogue_op(float acc, float b, float r) {
+  const float v = __fadd_rn(acc, b);
+  if constexpr (EPI == FFB_EPI_BIAS) return v;
+  if constexpr (EPI == FFB_EPI_BIAS_RES) return __fadd_rn(r, round_bf(v));
+  if constexpr (EPI == FFB_EPI_BIAS_GELU_TANH) return gelu_tanh(round_bf(v));
+  return gelu_erf(round_bf(v));
+}
+
+template <int BN, int EPI>
+__global__ void __launch_bounds__(THREADS, 1)
+    bf16_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_w,
+                     const __grid_constant__ CUtensorMap tmap_o, const BArgs args) {
+  using C = BCfg<BN>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* stg_all = smem + C::STAGES * C::STAGE_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(stg_all + C::STG_BYTES);
+  uint64_t* empty = full + C::STAGES;
+  uint64_t* tfull = empty + C::STAGES;  // [2]
+  uint64_t* tempty = tfull + 2;         // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int nkb = (args.K + BKE - 1) / BKE;
+
+  if (tid == 0) {
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], EPI_WARPS);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmap_a);
+    tma_prefetch_desc(&tmap_w);
+    tma_prefetch_desc(&tmap_o);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      const uint64_t pol_w = policy_evict_first(), pol_a = policy_evict_last();
+      int pre = 0;
+      if ((int)blockIdx.x < args.n_tiles) {  // weights do not depend on the previous kernel
+        const int ft = (int)blockIdx.x / args.n_ttiles;
+        pre = nkb < C::STAGES ? nkb : C::STAGES;
+        for (int i = 0; i < pre; ++i) {
+          mbar_arrive_expect_tx(&full[i], C::STAGE_BYTES);
+          tma_load_2d(smem + i * C::STAGE_BYTES + A_BYTES, &tmap_w, &full[i], i * BKE, ft * BN, pol_w);
+        }
+      }
+      pdl_wait();
+      int it = 0, s = 0;
+      uint32_t ph = 0;
+      for (int t = blockIdx.x; t < args.n_tiles && !*abort_flag; t += gridDim.x) {
+        const int tt = t % args.n_ttiles, ft = t / args.n_ttiles;
+        for (int kb = 0; kb < nkb; ++kb, ++it) {
+          uint8_t* st = smem + s * C::STAGE_BYTES;
+          if (it >= pre) {
+            if (!mbar_wait_bounded(&empty[s], ph ^ 1u, abort_flag)) {
+              *abort_flag = 1;
+              break;
+            }
+            mbar_arrive_expect_tx(&full[s], C::STAGE_BYTES);
+            tma_load_2d(st + A_BYTES, &tmap_w, &full[s], kb * BKE, ft * BN, pol_w);
+          }
+          tma_load_2d(st, &tmap_a, &full[s], kb * BKE, tt * BM, pol_a);
+          if (++s == C::STAGES) {
+            s = 0;
+            ph ^= 1u;
+          }
+        }
+      }
+      if (*abort_flag) {  // every slot whose copy was issued must land before the CTA exits
+        volatile int never = 0;
+        for (int j = it; j < pre; ++j)  // requested before the wait, never given their activations
+          tma_load_2d(smem + j * C::STAGE_BYTES, &tmap_a, &full[j], j * BKE,
+                      ((int)blockIdx.x % args.n_ttiles) * BM, pol_a);
+        const int issued = it > pre ? it : pre;
+        for (int j = (issued > C::STAGES ? issued - C::STAGES : 0); j < issued; ++j)
+          mbar_wait_bounded(&full[j % C::STAGES], (uint32_t)(j / C::STAGES) & 1u, &never, 200000000ull);
+      }
+    } else {
+      pdl_wait();
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    pdl_wait();
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16(BM, BN);
+      const uint32_t smem_base = smem_u32(smem);
+      int s = 0, lt = 0;
+      uint32_t ph = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < args.n_tiles && ok; t += gridDim.x, ++lt) {
+        const int buf = lt & 1;
+        if (!mbar_wait_bounded(&tempty[buf], ((uint32_t)(lt >> 1) & 1u) ^ 1u, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t acc = tmem + (uint32_t)(buf * BN);
+        for (int kb = 0; kb < nkb; ++kb) {
+          if (!mbar_wait_bounded(&full[s], ph, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t base = smem_base + (uint32_t)(s * C::STAGE_BYTES);
+          const uint64_t da = umma_desc_sw128(base);
+          const uint64_t dw = umma_desc_sw128(base + A_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < BKE / UMMA_K; ++kk)  // +32 bytes per K step = +2 encoded
+            umma_f16(acc, da + 2 * kk, dw + 2 * kk, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+          umma_commit(&empty[s]);
+          if (++s == C::STAGES) {
+            s = 0;
+            ph ^= 1u;
+          }
+        }
+        umma_commit(&tfull[buf]);  // fires when this tile's MMAs (or all issued) complete
+      }
+      if (!ok) *abort_flag = 1;
+    }
+  } else {
+    // ------------------------------------------------------------------ epilogue
+    pdl_wait();
+    if (warp == 2 && lane == 0) pdl_launch();
+    const int q = warp & 3;             // TMEM lane quarter = this warp's 32 tokens
+    const int half = (warp - 2) >> 2;  // which half of the tile's columns
+    int lt = 0;
+    uint32_t sc = 0;
+    for (int t = blockIdx.x; t < args.n_tiles; t += gridDim.x, ++lt) {
+      const int tt = t % args.n_ttiles, ft = t / args.n_ttiles;
+      const int buf = lt & 1;
+      if (!(mbar_wait_bounded(&tfull[buf], (uint32_t)(lt >> 1) & 1u, abort_flag) && !*abort_flag)) {
+        *abort_flag = 1;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t acc = tmem + (uint32_t)(buf * BN) + ((uint32_t)(q * 32) << 16);
+      const int row = tt * BM + q * 32 + lane;  // this thread's token
+#pragma unroll 1
+      for (int c = half * (BN / 2); c < (half + 1) * (BN / 2); c += 32) {
+        const int n = ft * BN + c;  // first output feature of the chunk
+        uint32_t r0[16], r1[16];
+        tmem_ld16_async(acc + (uint32_t)c, r0);
+        tmem_ld16_async(acc + (uint32_t)(c + 16), r1);
+        float bv[32], rv[32];
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {  // N is a multiple of 8: a group is all in or all out
+          const bool in = n + 8 * g < args.N;
+          const uint4 z = make_uint4(0, 0, 0, 0);
+          unpack8(args.bias && in ? __ldg(reinterpret_cast<const uint4*>(args.bias + n + 8 * g)) : z, bv + 8 * g);
+          if constexpr (EPI == FFB_EPI_BIAS_RES)
+            unpack8(in && row < args.M ? *reinterpret_cast<const uint4*>(args.res + (size_t)row * args.N + n + 8 * g)
+                                       : z,
+                    rv + 8 * g);
+        }
+        tmem_wait_ld();
+        reg_fence(r0);
+        reg_fence(r1);
+        uint32_t o[16];
+#pragma unroll
+        for (int j = 0; j < 16; j += 2) {
+          o[j >> 1] = pack2(epilogue_op<EPI>(__uint_as_float(r0[j]), bv[j], rv[j]),
+                            epilogue_op<EPI>(__uint_as_float(r0[j + 1]), bv[j + 1], rv[j + 1]));
+          o[8 + (j >> 1)] = pack2(epilogue_op<EPI>(__uint_as_float(r1[j]), bv[16 + j], rv[16 + j]),
+                                  epilogue_op<EPI>(__uint_as_float(r1[j + 1]), bv[17 + j], rv[17 + j]));
+        }
+        // 32 rows x 64 bytes, 64-byte swizzle (make_tmap_out), double-buffered per warp
+        uint8_t* sb = stg_all + ((warp - 2) * 2 + (int)(sc & 1)) * 2048;
+        if (lane == 0) bulk_wait_read<1>();
+        __syncwarp();
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          *reinterpret_cast<uint4*>(sb + lane * 64 + ((k ^ ((lane >> 1) & 3)) << 4)) =
+              make_uint4(o[4 * k], o[4 * k + 1], o[4 * k + 2], o[4 * k + 3]);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_3d(&tmap_o, sb, n, tt * BM + q * 32, 0);
+          bulk_commit();
+        }
+        ++sc;
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[buf]);
+    }
+    if (lane == 0) bulk_wait_all();
+    __syncwarp();
+  }
+
+  if (warp == 1 && lane == 0 && *abort_flag) {
+    // MMAs already issued must finish before their TMEM and shared memory are released
+    volatile int never = 0;
+    mbar_wait_bounded(&tfull[0], 0, &never, 100000000ull);
+    mbar_wait_bounded(&tfull[1], 0, &never, 100000000ull);
+  }
+  if (tid == 0 && *abort_flag) atomicOr(&ffb_device_error_word, ffb::ERR_GEMM_TIMEOUT);
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
+template <int BN, int EPI>
+cudaError_t launch_instance(const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap& to, const BArgs& ba,
+                            int grid, cudaStream_t stream) {
+  using C = BCfg<BN>;
+  cudaError_t e = ffb::set_smem_attr(reinterpret_cast<const void*>(bf16_gemm_kernel<BN, EPI>), C::SMEM);
+  if (e != cudaSuccess) return e;
+  return ffb::launch(bf16_gemm_kernel<BN, EPI>, dim3(grid), dim3(THREADS), C::SMEM, stream, ta, tw, to, ba);
+}
+
+template <int BN>
+cudaError_t launch_epi(int epilogue, const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap& to,
+                       const BArgs& ba, int grid, cudaStream_t stream) {
+  switch (epilogue) {
+    case FFB_EPI_BIAS: return launch_instance<BN, FFB_EPI_BIAS>(ta, tw, to, ba, grid, stream);
+    case FFB_EPI_BIAS_RES: return launch_instance<BN, FFB_EPI_BIAS_RES>(ta, tw, to, ba, grid, stream);
+    case FFB_EPI_BIAS_GELU_TANH: return launch_instance<BN, FFB_EPI_BIAS_GELU_TANH>(ta, tw, to, ba, grid, stream);
+    default: return launch_instance<BN, FFB_EPI_BIAS_GELU_ERF>(ta, tw, to, ba, grid, stream);
+  }
+}
+
+// Feature tile of the smallest cost: waves of the persistent grid x bytes each CTA receives
+// per 64-element K block (16 KB of activations + 128 bytes per feature).
+int auto_feature_tile(int M, int N) {
+  const int sms = ffb::sm_count();
+  const int ttiles = (M + BM - 1) / BM;
+  int best = 256;
+  long long best_cost = -1;
+  for (int bn : {256, 128, 64}) {
+    const long long tiles = (long long)ttiles * ((N + bn - 1) / bn);
+    const long long waves = (tiles + sms - 1) / sms;
+    const long long cost = waves * (A_BYTES + 128LL * bn);
+    if (best_cost < 0 || cost < best_cost) {
+      best = bn;
+      best_cost = cost;
+    }
+  }
+  return best;
+}
+
+}  // namespace
+
+extern "C" int ffb_bf16_gemm_feature_tile(int M, int N) {
+  if (M <= 0 || N <= 0) return 0;
+  return auto_feature_tile(M, N);
+}
+
+extern "C" int ffb_bf16_gemm(const uint16_t* a, const uint16_t* w, const uint16_t* bias, const uint16_t* res,
+                             int epilogue, uint16_t* out, int feature_tile, int M, int N, int K, void* stream) {
+  FFB_REQUIRE(a && w && out, "ffb_bf16_gemm: NULL operand");
+  FFB_REQUIRE(M > 0 && N > 0 && K > 0, "ffb_bf16_gemm: bad shape M=%d N=%d K=%d", M, N, K);
+  FFB_REQUIRE(K % 8 == 0 && N % 8 == 0, "ffb_bf16_gemm: K=%d and N=%d must be multiples of 8", K, N);
+  FFB_REQUIRE(ffb::aligned(a, 16) && ffb::aligned(w, 16) && ffb::aligned(out, 16) &&
+                  (!bias || ffb::aligned(bias, 16)) && (!res || ffb::aligned(res, 16)),
+              "ffb_bf16_gemm: pointers must be 16-byte aligned");
+  FFB_REQUIRE(epilogue == FFB_EPI_BIAS || epilogue == FFB_EPI_BIAS_RES || epilogue == FFB_EPI_BIAS_GELU_TANH ||
+                  epilogue == FFB_EPI_BIAS_GELU_ERF,
+              "ffb_bf16_gemm: unknown epilogue %d", epilogue);
+  FFB_REQUIRE(epilogue != FFB_EPI_BIAS_RES || res != nullptr, "ffb_bf16_gemm: BIAS_RES needs res");
+  const int bn = feature_tile > 0 ? feature_tile : auto_feature_tile(M, N);
+  FFB_REQUIRE(bn == 64 || bn == 128 || bn == 256, "ffb_bf16_gemm: feature tile %d (64, 128 or 256)", bn);
+  CUtensorMap ta, tw, to;
+  int rc = ffb::make_tmap_2d(&ta, a, (uint64_t)M, (uint64_t)K, (uint64_t)K * 2, BM, BKE, 2);
+  if (!rc) rc = ffb::make_tmap_2d(&tw, w, (uint64_t)N, (uint64_t)K, (uint64_t)K * 2, (uint32_t)bn, BKE, 2);
+  if (!rc) rc = ffb::make_tmap_out(&to, out, 2, (uint64_t)N, (uint64_t)M, 1, (uint64_t)N * 2, (uint64_t)N * M * 2, 32, 32);
+  if (rc) return rc;
+  BArgs ba = {};
+  ba.bias = bias;
+  ba.res = res;
+  ba.M = M;
+  ba.N = N;
+  ba.K = K;
+  ba.n_ttiles = (M + BM - 1) / BM;
+  ba.n_tiles = ba.n_ttiles * ((N + bn - 1) / bn);
+  const int sms = ffb::sm_count();
+  const int grid = ba.n_tiles < sms ? ba.n_tiles : sms;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  cudaError_t e = bn == 256 ? launch_epi<256>(epilogue, ta, tw, to, ba, grid, s)
+                  : bn == 128 ? launch_epi<128>(epilogue, ta, tw, to, ba, grid, s)
+                              : launch_epi<64>(epilogue, ta, tw, to, ba, grid, s);
+  if (e != cudaSuccess) return ffb::fail(FFB_ECUDA, "ffb_bf16_gemm: launch: %s", cudaGetErrorString(e));
+  return FFB_OK;
+}

@@ -16,6 +16,10 @@ code written against the reference runs unchanged:
     Int4               _family/night_runtime.py:15-42 (symmetric group-128 scheme)
     pack_rgb           _legacy/sub10_runtime.py:21-29
     pack_rectangle     _family/depth_runtime.py:18-25
+    add_layernorm      _legacy/lower_kernels.py:130-136
+    vision_rope        _legacy/search_kernels.py:127-134
+    vision_linear / vision_attention: the HF vision blocks' nn.Linear (+ residual / GELU)
+                       and SDPA (_legacy/vision_graph_runtime.py:16-27)
 
 Outputs are allocated with torch on the input's device (stream-ordered, graph-safe
 through the caching allocator).  Argument errors raise ValueError (the reference uses
@@ -314,3 +318,73 @@ def pack_rectangle(rgb, width=None, pixels=None):
     if width is not None:
         _need(rgb.shape[-2] == width, f"canvas width is not {width}")
     return _pack(rgb, pixels)
+
+
+# ---------------------------------------------------------------------------- vision tower
+
+_VISION_EPI = {"bias": L.EPI_BIAS, "res": L.EPI_BIAS_RES, "gelu_tanh": L.EPI_BIAS_GELU_TANH,
+               "gelu_erf": L.EPI_BIAS_GELU_ERF}
+
+
+def vision_linear(x, weight, bias=None, epilogue="bias", res=None, out=None, feature_tile=0):
+    """bf16 linear of the vision tower on tcgen05: epilogue "bias" = bf16(x W^T + b), "res" =
+    bf16(res + that), "gelu_tanh" / "gelu_erf" = bf16(gelu(that)) (nn.Linear + the residual
+    add or activation that follows it in the HF vision blocks and mergers)."""
+    _need(epilogue in _VISION_EPI, f"unknown epilogue {epilogue!r}")
+    _bf16_cuda(x, weight)
+    _need(x.dim() == 2 and weight.dim() == 2 and x.shape[1] == weight.shape[1], "x [M, K], weight [N, K]")
+    _need(x.is_contiguous() and weight.is_contiguous(), "contiguous operands")
+    m, k = x.shape
+    n = weight.shape[0]
+    if bias is not None:
+        _bf16_cuda(bias)
+        _need(bias.shape == (n,) and bias.is_contiguous(), "bias [N]")
+    if epilogue == "res":
+        _need(res is not None and res.shape == (m, n) and res.is_contiguous(), "res [M, N] contiguous")
+        _bf16_cuda(res)
+    out = torch.empty(m, n, dtype=BF16, device=x.device) if out is None else out
+    call("ffb_bf16_gemm", ptr(x), ptr(weight), ptr(bias), ptr(res), _VISION_EPI[epilogue], ptr(out),
+         int(feature_tile), m, n, k, stream_ptr(x.device))
+    return out
+
+
+def add_layernorm(a, b, module):
+    """residual = bf16(a + b), out = LayerNorm(residual) (`_legacy/lower_kernels.py:130-136`);
+    with b None only the LayerNorm (residual is a).  `module` has .weight, .bias, .eps."""
+    _need(a.is_contiguous() and (b is None or (b.shape == a.shape and b.is_contiguous())), "a, b contiguous")
+    _bf16_cuda(a, module.weight, module.bias)
+    d = a.shape[-1]
+    out = torch.empty_like(a)
+    residual = torch.empty_like(a) if b is not None else a
+    call("ffb_add_layernorm", ptr(a), ptr(b), ptr(module.weight), ptr(module.bias), float(module.eps),
+         ptr(residual) if b is not None else None, ptr(out), a.numel() // d, d, stream_ptr(a.device))
+    return residual, out
+
+
+def vision_rope(q, k, cos, sin, block=512):
+    """The reference's `vision_rope` (`_legacy/search_kernels.py:127-134`): q, k [n, h, d]
+    (any row stride), cos, sin [n, d] fp32; returns yq, yk [n, h, d] in q's dtype."""
+    _need(q.shape == k.shape and q.dim() == 3, "q, k [n, h, d]")
+    _bf16_cuda(q, k)
+    n, h, d = q.shape
+    qkv = torch.zeros(n, 3, h, d, dtype=BF16, device=q.device)
+    qkv[:, 0] = q
+    qkv[:, 1] = k
+    yq = torch.empty(h, n, d, dtype=BF16, device=q.device)
+    yk = torch.empty_like(yq)
+    yv = torch.empty_like(yq)
+    call("ffb_vision_rope", ptr(qkv), ptr(cos.float().contiguous()), ptr(sin.float().contiguous()), n, h, d, d,
+         ptr(yq), ptr(yk), ptr(yv), stream_ptr(q.device))
+    return yq.transpose(0, 1).contiguous(), yk.transpose(0, 1).contiguous()
+
+
+def vision_attention(q, k, v, d, scale):
+    """Non-causal attention over one image's patches: q, k, v [H, T, 128] bf16 (head dim d
+    zero-padded to 128); returns [T, H * d] bf16 (the vision blocks' SDPA)."""
+    _bf16_cuda(q, k, v)
+    _need(q.shape == k.shape == v.shape and q.dim() == 3 and q.shape[2] == 128, "q, k, v [H, T, 128]")
+    _need(q.is_contiguous() and k.is_contiguous() and v.is_contiguous(), "contiguous q, k, v")
+    h, t, _ = q.shape
+    out = torch.empty(t, h * d, dtype=BF16, device=q.device)
+    call("ffb_attention_full", ptr(q), ptr(k), ptr(v), ptr(out), t, h, int(d), float(scale), stream_ptr(q.device))
+    return out

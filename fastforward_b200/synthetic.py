@@ -60,3 +60,19 @@ def make_request(dims, layout, seed=1, device="cpu", deepstack=True):
             for _ in range(dims.deepstack)] if deepstack else []
     return dict(ids=ids.to(device), visual=visual.to(device), deep=[x.to(device) for x in deep],
                 pick=layout.pick, k=layout.k, image_start=layout.image_start)
+
+
+def make_vision_bf16(vdims, seed=0, device="cpu", std=0.02):
+    """Seeded bf16 vision-tower parameters by checkpoint name (without `model.visual.`), in
+    the order of `checkpoint.vision_param_shapes`: linear and patch-embedding weights,
+    biases and the position table N(0, std); LayerNorm weights 1 + N(0, 0.1) and biases
+    N(0, std), so that every term of the norms is exercised."""
+    from .checkpoint import vision_param_shapes
+    g = torch.Generator(device=device).manual_seed(seed)
+    out = {}
+    for name, shape in vision_param_shapes(vdims).items():
+        if name.endswith("norm1.weight") or name.endswith("norm2.weight") or name.endswith("norm.weight"):
+            out[name] = (1.0 + torch.randn(shape, generator=g, device=device) * 0.1).to(BF16)
+        else:
+            out[name] = _randn(shape, g, device, std)
+    return out

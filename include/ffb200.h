@@ -44,6 +44,12 @@ extern "C" {
 #define FFB_EPI_F32_PARTIAL 1  /* ws[split][m][n] = acc * sa * sw (fp32), reduced by the consumer */
 #define FFB_EPI_SWIGLU 2       /* gate/up rows interleaved per 128; out[m,c] = bf16(bf16(silu(g)) * u) */
 
+/* Epilogues of the bf16 linear (ffb_bf16_gemm); v = fp32(acc + bias[n]) (bias NULL: 0). */
+#define FFB_EPI_BIAS 10            /* out = bf16(v)                                        */
+#define FFB_EPI_BIAS_RES 11        /* out = bf16(res + bf16(v)) (res may alias out)        */
+#define FFB_EPI_BIAS_GELU_TANH 12  /* out = bf16(gelu_tanh(bf16(v)))                       */
+#define FFB_EPI_BIAS_GELU_ERF 13   /* out = bf16(gelu_erf(bf16(v)))                        */
+
 /* Library identification: returns a static string ("ffb200 <version> sm_100a"). */
 const char* ffb_version(void);
 
@@ -328,6 +334,58 @@ int ffb_pack_rgb(const uint8_t* rgb, uint16_t* pixels, int height, int width, vo
  * patch rows at rows [i*P, (i+1)*P); n * height * width <= 2^30. */
 int ffb_pack_rgb_batch(const uint8_t* rgb, uint16_t* pixels, int n, int height, int width,
                        void* stream);
+
+/* ---------------------------------------------------------------- vision tower
+ * The kernels of the Qwen3-VL vision tower in front of the language path (patch embedding,
+ * ViT blocks, deepstack and final mergers).  The reference runs it as HF modules plus its
+ * Triton vision RoPE (_legacy/vision_graph_runtime.py:16-27, `VisionGraph.core`;
+ * scaled_qwen_runtime.py:42-55, `NativeNormVision.core`). */
+
+/* bf16 linear on tcgen05 (kind::f16): out[m,n] = epilogue(sum_k a[m,k] * w[n,k] + bias[n]).
+ * Replaces the blocks' and mergers' nn.Linear calls and the patch embedding's Conv3d (as a
+ * [P, 1536] x [C, 1536]^T product); the epilogues fold in the residual add that follows
+ * attn.proj / mlp.linear_fc2 (and the position embedding after the patch embedding), and the
+ * GELU after linear_fc1 (tanh form in the blocks, erf form in the mergers; own polynomial
+ * tanh and Abramowitz-Stegun 7.1.26 erf, within 2e-7 of the exact functions).
+ * a [M,K], w [N,K] (K-major, as nn.Linear stores it), bias [N] or NULL, res [M,N]
+ * (FFB_EPI_BIAS_RES), out [M,N], all bf16 and 16-byte aligned; K and N multiples of 8.
+ * feature_tile 64 / 128 / 256 (0 = automatic, see ffb_bf16_gemm_feature_tile). */
+int ffb_bf16_gemm(const uint16_t* a, const uint16_t* w, const uint16_t* bias, const uint16_t* res,
+                  int epilogue, uint16_t* out, int feature_tile, int M, int N, int K, void* stream);
+
+/* The feature tile ffb_bf16_gemm picks for M x N on the current device (no reference
+ * counterpart; a host-side query). */
+int ffb_bf16_gemm_feature_tile(int M, int N);
+
+/* LayerNorm over rows of C: y = bf16(((x - mean) * rstd) * w + b), mean and variance from
+ * float64 sums, rstd = 1 / sqrt(var + eps).  Replaces the vision blocks' norm1 / norm2 and
+ * the mergers' norm (nn.LayerNorm, _legacy/vision_graph_runtime.py:16-27; the add + LayerNorm
+ * of _legacy/lower_kernels.py:115-136 with the add done by the producing linear).
+ * x, y [rows, C], w, b [C] bf16, 16-byte aligned; C a multiple of 8, at most 8192. */
+int ffb_layernorm(const uint16_t* x, const uint16_t* w, const uint16_t* b, float eps, uint16_t* y,
+                  int rows, int C, void* stream);
+
+/* Add + LayerNorm: residual = bf16(a + add), y = LayerNorm(residual) as ffb_layernorm.
+ * Replaces `add_layernorm` (_legacy/lower_kernels.py:115-136).  With add == NULL it is
+ * ffb_layernorm (residual unused).  a, add, residual, y [rows, C]; w, b [C]; bf16. */
+int ffb_add_layernorm(const uint16_t* a, const uint16_t* add, const uint16_t* w, const uint16_t* b,
+                      float eps, uint16_t* residual, uint16_t* y, int rows, int C, void* stream);
+
+/* 2-D vision rotary on the qkv projection, and the head-major layout of the attention
+ * kernel.  Replaces `_vision_rope` (_legacy/search_kernels.py:111-125): for q and k,
+ * y[c] = x[c] * cos[c] + r[c] * sin[c] with r = rotate_half(x) (each product and the sum
+ * rounded to fp32, then bf16).  qkv [P, 3*H*d] bf16 (patch rows [q | k | v], heads of d);
+ * cos, sin [P, d] fp32; q, k, v [H, P, dp] bf16 with columns d..dp-1 zero (dp >= d). */
+int ffb_vision_rope(const uint16_t* qkv, const float* cos, const float* sin, int P, int H, int d,
+                    int dp, uint16_t* q, uint16_t* k, uint16_t* v, void* stream);
+
+/* Non-causal multi-head attention over the T patches of one image (every query sees every
+ * key), the arithmetic of ffb_attention otherwise.  Replaces the vision blocks' SDPA
+ * (_legacy/vision_graph_runtime.py:16-27, one image per sequence).  q, k, v [H, T, 128]
+ * bf16 with the head dimension d zero-padded to 128 (as ffb_vision_rope writes them with
+ * dp = 128); out [T, H*d] bf16 (d a multiple of 8, at most 128). */
+int ffb_attention_full(const uint16_t* q, const uint16_t* k, const uint16_t* v, uint16_t* out,
+                       int T, int H, int d, float scale, void* stream);
 
 #ifdef __cplusplus
 }

@@ -1,5 +1,6 @@
-"""Loader of the oracle's C models: tensor-core accumulation (oracle/tcgemm.c) and the
-attention kernel's softmax arithmetic (oracle/attn.c).
+"""Loader of the oracle's C models: tensor-core accumulation (oracle/tcgemm.c), the
+attention kernel's softmax arithmetic (oracle/attn.c) and the bf16 linear's GELU
+epilogues (oracle/act.c).
 TEST INFRASTRUCTURE ONLY.  Built by `make -C oracle` (run here on first use if missing)."""
 import ctypes
 import subprocess
@@ -32,6 +33,8 @@ def lib():
                                             ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
         _lib.attn_fold.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int]
         _lib.attn_finish.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p]
+        for name in ("ffo_gelu_tanh_array", "ffo_gelu_erf_array"):
+            getattr(_lib, name).argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_long]
     return _lib
 
 
@@ -73,6 +76,15 @@ def exp2(x):
     x = x.float().contiguous()
     y = torch.empty_like(x)
     lib().ffo_exp2_array(x.data_ptr(), y.data_ptr(), x.numel())
+    return y
+
+
+def gelu(x, form):
+    """The bf16 linear epilogue's GELU of fp32 values, form "tanh" or "erf" (oracle/act.c)."""
+    x = x.float().contiguous()
+    y = torch.empty_like(x)
+    fn = lib().ffo_gelu_tanh_array if form == "tanh" else lib().ffo_gelu_erf_array
+    fn(x.data_ptr(), y.data_ptr(), x.numel())
     return y
 
 

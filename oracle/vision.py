@@ -30,7 +30,8 @@ import math
 import torch
 
 __all__ = ["vision_geometry", "vision_pos_embed", "vision_rot_cos_sin", "vision_rope", "vision_tower",
-           "vision_params_from_state_dict", "VisionDims"]
+           "vision_params_from_state_dict", "VisionDims", "layer_norm_k", "linear_k", "attention_full_k",
+           "vision_tower_k"]
 
 
 class VisionDims:
@@ -183,3 +184,112 @@ def vision_tower(p, dims, pixels, grid_h, grid_w, dtype=torch.float32):
 def vision_params_from_state_dict(sd, prefix="model.visual."):
     """The vision tower's parameters out of a full-model state dict (checkpoint names)."""
     return {k[len(prefix):]: v for k, v in sd.items() if k.startswith(prefix)}
+
+
+# ----------------------------------------------------------------------------- kernel arithmetic
+# The same forward with the rounding points and operation orders of the CUDA kernels
+# (fastforward_b200/csrc/gemm_bf16.cu, vision.cu, attention_tc.cu), for bit-exact checks of
+# the GPU path: every linear accumulates as the tensor core does (`_tc.acc_bf16`, kind::f16)
+# and rounds its bf16 output once after the bias add; the residual adds, LayerNorms and GELUs
+# are the kernels' own (below); the attention is the language path's kernel arithmetic with
+# every key visible.  It differs from `vision_tower` (the HF modules' semantics) only by
+# rounding.
+
+def layer_norm_k(x, w, b, eps, add=None):
+    """LayerNorm of the kernel `ffb_layernorm`: float64 sums S1 = sum x, S2 = sum x^2;
+    mean = fp32(S1 / C), rstd = fp32(1 / sqrt(max(S2 / C - (S1 / C)^2, 0) + eps)) in float64;
+    y = bf16(((x - mean) * rstd) * w + b) in fp32 operations.  x [R, C] bf16.  With `add`
+    (`ffb_add_layernorm`, the reference's `add_layernorm`, `_legacy/lower_kernels.py:115-136`)
+    the row is x = bf16(x + add) first."""
+    if add is not None:
+        x = (x.float() + add.float()).to(torch.bfloat16)
+    xf = x.float()
+    xd = xf.double()
+    c = x.shape[-1]
+    mean_d = xd.sum(-1) / c
+    var_d = ((xd * xd).sum(-1) / c - mean_d * mean_d).clamp(min=0.0)
+    mean = mean_d.float()
+    eps_d = float(torch.tensor(eps, dtype=torch.float32))
+    rstd = (1.0 / torch.sqrt(var_d + eps_d)).float()
+    y = ((xf - mean[:, None]) * rstd[:, None]) * w.float() + b.float()
+    return y.to(torch.bfloat16)
+
+
+def linear_k(x, w, b, epilogue="bias", res=None):
+    """The bf16 linear `ffb_bf16_gemm`: v = fp32(acc + b) with acc the tensor core's fp32
+    accumulator of x [M, K] . w [N, K]^T; epilogue "bias": bf16(v); "res": bf16(res +
+    bf16(v)); "gelu_tanh" / "gelu_erf": bf16(gelu(bf16(v))) with the kernel's GELU
+    (oracle/act.c).  bf16 in, bf16 out."""
+    from . import _tc
+    acc = _tc.acc_bf16(x, w, 0, x.shape[1])
+    v = acc + (b.float() if b is not None else 0.0)
+    if epilogue == "bias":
+        y = v
+    elif epilogue == "res":
+        y = res.float() + v.to(torch.bfloat16).float()
+    elif epilogue in ("gelu_tanh", "gelu_erf"):
+        y = _tc.gelu(v.to(torch.bfloat16).float(), epilogue[5:])
+    else:
+        raise ValueError(epilogue)
+    return y.to(torch.bfloat16)
+
+
+def attention_full_k(q, k, v, d, scale):
+    """Non-causal attention of `ffb_attention_full`: q, k, v [H, T, 128] bf16 (head dim d
+    zero-padded to 128); returns [T, H * d] bf16."""
+    from .qwen_path import attention_tc
+    h, t, _ = q.shape
+    out = attention_tc(q, k, v, scale, positions=torch.full((t,), t - 1, dtype=torch.long))
+    return out[:, :, :d].reshape(t, h * d)
+
+
+def _rope_heads(qkv, cos, sin, heads, d, dp=128):
+    """Rotary on q, k of qkv [P, 3 H d] and the head-major zero-padded layout [H, P, dp]
+    (`ffb_vision_rope`)."""
+    p_n = qkv.shape[0]
+    x = qkv.reshape(p_n, 3, heads, d)
+    q, k = vision_rope(x[:, 0], x[:, 1], cos, sin)
+    out = []
+    for t in (q, k, x[:, 2]):
+        z = torch.zeros(heads, p_n, dp, dtype=torch.bfloat16)
+        z[:, :, :d] = t.transpose(0, 1)
+        out.append(z)
+    return out
+
+
+def _merger_k(p, prefix, h, dims, post_shuffle):
+    c4 = dims.hidden * dims.merge * dims.merge
+    if post_shuffle:
+        x = layer_norm_k(h.reshape(-1, c4), p[prefix + "norm.weight"], p[prefix + "norm.bias"], dims.eps)
+    else:
+        x = layer_norm_k(h, p[prefix + "norm.weight"], p[prefix + "norm.bias"], dims.eps).reshape(-1, c4)
+    x = linear_k(x, p[prefix + "linear_fc1.weight"], p[prefix + "linear_fc1.bias"], "gelu_erf")
+    return linear_k(x, p[prefix + "linear_fc2.weight"], p[prefix + "linear_fc2.bias"])
+
+
+def vision_tower_k(p, dims, pixels, grid_h, grid_w):
+    """`vision_tower` with the CUDA kernels' arithmetic (bf16 activations between kernels).
+    p: bf16 parameters by checkpoint name (without `model.visual.`); pixels [P, 1536] bf16.
+    Returns (merged [P/4, out_hidden], [deepstack features]) bf16."""
+    p = {k: v.to(torch.bfloat16) for k, v in p.items()}
+    n_p = grid_h * grid_w
+    heads, d = dims.heads, dims.head_dim
+    pos, cos, sin = vision_geometry(p["pos_embed.weight"], grid_h, grid_w, d, dims.theta, dims.merge)
+    act = "gelu_tanh" if dims.act == "gelu_pytorch_tanh" else "gelu_erf"
+    h = linear_k(pixels.to(torch.bfloat16), p["patch_embed.proj.weight"].reshape(dims.hidden, -1),
+                 p["patch_embed.proj.bias"], "res", pos)
+    deep = []
+    for j in range(dims.depth):
+        b = f"blocks.{j}."
+        x = layer_norm_k(h, p[b + "norm1.weight"], p[b + "norm1.bias"], dims.eps)
+        qkv = linear_k(x, p[b + "attn.qkv.weight"], p[b + "attn.qkv.bias"])
+        q, k, v = _rope_heads(qkv, cos, sin, heads, d)
+        o = attention_full_k(q, k, v, d, d ** -0.5)
+        h = linear_k(o, p[b + "attn.proj.weight"], p[b + "attn.proj.bias"], "res", h)
+        x = layer_norm_k(h, p[b + "norm2.weight"], p[b + "norm2.bias"], dims.eps)
+        x = linear_k(x, p[b + "mlp.linear_fc1.weight"], p[b + "mlp.linear_fc1.bias"], act)
+        h = linear_k(x, p[b + "mlp.linear_fc2.weight"], p[b + "mlp.linear_fc2.bias"], "res", h)
+        if j in dims.deepstack:
+            i = dims.deepstack.index(j)
+            deep.append(_merger_k(p, f"deepstack_merger_list.{i}.", h, dims, post_shuffle=True))
+    return _merger_k(p, "merger.", h, dims, post_shuffle=False), deep

@@ -1,0 +1,110 @@
+"""Host side of the vision tower (no GPU): the product's geometry tables equal the oracle's
+(which is pinned to transformers' own vision code), the synthetic parameters have the
+checkpoint shapes, the GELU restatement of the linear's epilogue is accurate, the oracle's
+kernel-arithmetic tower agrees with its module-semantics tower, and the C ABI rejects bad
+vision arguments before any CUDA call."""
+import pytest
+import torch
+
+import oracle
+from oracle import _tc
+from fastforward_b200 import _lib as L
+from fastforward_b200.checkpoint import vision_param_shapes
+from fastforward_b200.config import VISION_MODELS, VisionDims
+from fastforward_b200.synthetic import make_vision_bf16
+from fastforward_b200.vision import VisionTower, position_table, rotary_cos_sin
+
+BF16 = torch.bfloat16
+
+
+@pytest.mark.parametrize("grid", [(32, 32), (16, 24), (8, 64), (2, 2)])
+def test_geometry_equals_oracle(grid):
+    gh, gw = grid
+    table = (torch.randn(2304, 64) * 0.02).to(BF16)
+    pos = position_table(table, gh, gw)
+    ref_pos = oracle.vision_pos_embed(table, gh, gw)
+    assert torch.equal(pos.view(torch.int16), ref_pos.view(torch.int16))
+    for d in (64, 72):
+        cos, sin = rotary_cos_sin(gh, gw, d)
+        rc, rs = oracle.vision_rot_cos_sin(gh, gw, d)
+        assert torch.equal(cos, rc) and torch.equal(sin, rs)
+
+
+def test_synthetic_vision_parameters_have_checkpoint_shapes():
+    v = VisionDims(64, 2, 128, 96, 2, (0,), num_pos=16)
+    p = make_vision_bf16(v, seed=3)
+    shapes = vision_param_shapes(v)
+    assert set(p) == set(shapes)
+    for name, shape in shapes.items():
+        assert tuple(p[name].shape) == tuple(shape) and p[name].dtype == BF16, name
+    assert torch.equal(make_vision_bf16(v, seed=3)["blocks.1.attn.qkv.weight"], p["blocks.1.attn.qkv.weight"])
+
+
+def test_launch_count():
+    assert VisionTower.launches(VISION_MODELS["4B"]) == 1 + 8 * 24 + 3 * 4
+
+
+@pytest.mark.parametrize("form,approx", [("tanh", "tanh"), ("erf", "none")])
+def test_gelu_epilogue_accuracy(form, approx):
+    """The epilogue's GELU (own tanh / Abramowitz-Stegun erf over exp2_poly) rounds to the
+    same bf16 as the exact function on every bf16 input of |x| < 3, and stays within 5e-7
+    absolute everywhere."""
+    x = torch.arange(-32768, 32768, dtype=torch.int32).to(torch.int16).view(BF16).float()
+    x = x[torch.isfinite(x) & (x.abs() < 64)]
+    y = _tc.gelu(x, form)
+    exact = torch.nn.functional.gelu(x.double(), approximate=approx)
+    assert (y.double() - exact).abs().max().item() < 5e-7
+    small = x.abs() < 3
+    assert torch.equal(y[small].to(BF16), exact[small].to(BF16))
+
+
+def test_layer_norm_restatement_matches_float64():
+    g = torch.Generator().manual_seed(0)
+    x = (torch.randn(7, 1152, generator=g) * 3 + 0.5).to(BF16)
+    w = (1 + torch.randn(1152, generator=g) * 0.1).to(BF16)
+    b = (torch.randn(1152, generator=g) * 0.02).to(BF16)
+    y = oracle.layer_norm_k(x, w, b, 1e-6)
+    ref = torch.nn.functional.layer_norm(x.double(), (1152,), w.double(), b.double(), 1e-6)
+    assert (y.double() - ref).abs().max().item() <= 2 ** -7 * ref.abs().max().item()
+
+
+def test_kernel_arithmetic_tower_close_to_module_semantics():
+    """`vision_tower_k` (the kernels' rounding points) against `vision_tower` in fp32 (the HF
+    modules' semantics) on a small two-block tower: the bf16 roundings between kernels
+    move the outputs by a few bf16 ulps only."""
+    v = VisionDims(128, 2, 256, 128, 2, (0,), num_pos=64)
+    p = make_vision_bf16(v, seed=1)
+    g = torch.Generator().manual_seed(2)
+    pixels = (torch.rand(64, 1536, generator=g) * 2 - 1).to(BF16)
+    mk, dk = oracle.vision_tower_k(p, v, pixels, 8, 8)
+    mf, df = oracle.vision_tower({k: t.float() for k, t in p.items()}, v, pixels.float(), 8, 8)
+    for a, b in [(mk, mf)] + list(zip(dk, df)):
+        err = (a.float() - b).abs().max().item()
+        assert err <= 0.02 * b.abs().max().item(), err
+
+
+def test_vision_entries_reject_bad_arguments():
+    with pytest.raises(ValueError, match="multiples of 8"):
+        L.call("ffb_bf16_gemm", 16, 16, None, None, L.EPI_BIAS, 16, 0, 16, 20, 64, None)
+    with pytest.raises(ValueError, match="epilogue"):
+        L.call("ffb_bf16_gemm", 16, 16, None, None, 99, 16, 0, 16, 16, 64, None)
+    with pytest.raises(ValueError, match="BIAS_RES"):
+        L.call("ffb_bf16_gemm", 16, 16, None, None, L.EPI_BIAS_RES, 16, 0, 16, 16, 64, None)
+    with pytest.raises(ValueError, match="feature tile"):
+        L.call("ffb_bf16_gemm", 16, 16, None, None, L.EPI_BIAS, 16, 96, 16, 16, 64, None)
+    with pytest.raises(ValueError, match="head dim"):
+        L.call("ffb_attention_full", 16, 16, 16, 16, 64, 4, 12, 0.1, None)
+    with pytest.raises(ValueError, match="multiple of 8"):
+        L.call("ffb_layernorm", 16, 16, 16, 1e-6, 16, 4, 100, None)
+    with pytest.raises(ValueError, match="residual"):
+        L.call("ffb_add_layernorm", 16, 16, 16, 16, 1e-6, None, 16, 4, 128, None)
+    with pytest.raises(ValueError, match="bad shape"):
+        L.call("ffb_vision_rope", 16, 16, 16, 4, 2, 9, 128, 16, 16, 16, None)
+
+
+def test_feature_tile_choice():
+    """The automatic feature tile fills the machine: 1024 patches x 1024 features -> 64-wide
+    tiles (128 tiles), 1024 x 4096 -> 256-wide (128 tiles)."""
+    assert L.lib().ffb_bf16_gemm_feature_tile(1024, 1024) == 64
+    assert L.lib().ffb_bf16_gemm_feature_tile(1024, 4096) == 256
+    assert L.lib().ffb_bf16_gemm_feature_tile(0, 4096) == 0
