@@ -266,6 +266,8 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll 1
       for (int c = half * (BN / 2); c < (half + 1) * (BN / 2); c += 32) {
         const int n = ft * BN + c;  // first output feature of the chunk
+        // chunks wholly past N or past M store nothing (warp-uniform: n and q are)
+        if (n >= args.N || tt * BM + q * 32 >= args.M) continue;
         uint32_t r0[16], r1[16];
         tmem_ld16_async(acc + (uint32_t)c, r0);
         tmem_ld16_async(acc + (uint32_t)(c + 16), r1);
