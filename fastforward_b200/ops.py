@@ -373,8 +373,8 @@ def vision_rope(q, k, cos, sin, block=512):
     yq = torch.empty(h, n, d, dtype=BF16, device=q.device)
     yk = torch.empty_like(yq)
     yv = torch.empty_like(yq)
-    call("ffb_vision_rope", ptr(qkv), ptr(cos.float().contiguous()), ptr(sin.float().contiguous()), n, h, d, d,
-         ptr(yq), ptr(yk), ptr(yv), stream_ptr(q.device))
+    cos, sin = cos.float().contiguous(), sin.float().contiguous()  # held until the launch is enqueued
+    call("ffb_vision_rope", ptr(qkv), ptr(cos), ptr(sin), n, h, d, d, ptr(yq), ptr(yk), ptr(yv), stream_ptr(q.device))
     return yq.transpose(0, 1).contiguous(), yk.transpose(0, 1).contiguous()
 
 

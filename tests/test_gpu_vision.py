@@ -106,8 +106,9 @@ def test_vision_rope_heads_layout(n_p, heads, d):
     gh, gw = (side, side) if side else (10, 10)
     cos, sin = rotary_cos_sin(gh, gw, d)
     out = [torch.full((heads, n_p, 128), 7.0, dtype=BF16, device=DEV) for _ in range(3)]
-    L.call("ffb_vision_rope", L.ptr(qkv.to(DEV)), L.ptr(cos.to(DEV)), L.ptr(sin.to(DEV)), n_p, heads, d, 128,
-           *[L.ptr(t) for t in out], L.stream_ptr())
+    qkv_d, cos_d, sin_d = qkv.to(DEV), cos.to(DEV), sin.to(DEV)  # alive until the kernel has run
+    L.call("ffb_vision_rope", L.ptr(qkv_d), L.ptr(cos_d), L.ptr(sin_d), n_p, heads, d, 128, *[L.ptr(t) for t in out],
+           L.stream_ptr())
     torch.cuda.synchronize()
     ref = oracle.vision._rope_heads(qkv, cos, sin, heads, d)
     for a, b in zip(out, ref):
