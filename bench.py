@@ -69,6 +69,8 @@ def parse():
                         "--workload 2B-layer-T512) instead of whole requests")
     p.add_argument("--layers", type=int, default=None,
                    help="build only this many decoder layers (same shapes; for small profiler captures)")
+    p.add_argument("--vision-ncu", action="store_true",
+                   help="run only the 4B vision tower and replay one forward inside a profiler range")
     p.add_argument("--ncu-range", action="store_true",
                    help="after set-up, replay one forward inside a cudaProfilerStart/Stop range and exit "
                         "(for `ncu --profile-from-start off`); prints no bench line")
@@ -532,6 +534,9 @@ def run_ours(args):
     clk_sum = clk.summary()
     launches = eng.launches_per_forward() * args.steps
     extra = {}
+    if world == 1 and args.workload == "4B-fp8-T320" and not args.no_extra:
+        # the image side of the request: the 4B vision tower on the headline's 512 x 512 canvas
+        extra["vision_4b"] = vision_measure(args, dev, peaks)
     if world > 1 and args.workload == "4B-fp8-T320" and not args.no_extra:
         # the multi-GPU configurations besides the headline's replicas, in the same line:
         # the 8B request stream served by N replicas (C4) and the 32B model tensor-parallel
@@ -569,6 +574,79 @@ def run_ours(args):
             del entry
             eng.graphs.clear()
         dist.destroy_process_group()
+
+
+def vision_flops(v, n_p):
+    """Useful FLOPs of one vision-tower forward over n_p patches (head dim unpadded)."""
+    c, i, m2 = v.hidden, v.inter, v.merge * v.merge
+    per_block = 2 * n_p * (c * 3 * c + c * c + 2 * c * i) + 4 * n_p * n_p * c
+    merger = 2 * (n_p // m2) * (c * m2 * c * m2 + c * m2 * v.out_hidden)
+    return 2 * n_p * 3 * v.temporal * v.patch * v.patch * c + v.depth * per_block + (len(v.deepstack) + 1) * merger
+
+
+def vision_measure(args, dev, peaks, name="4B", side=512):
+    """The vision tower in front of the language path (C1-C4's image side): seeded
+    synthetic weights of the family's published vision config, a side x side canvas per
+    image (32 x 32 patches -> the 256 visual rows of the headline layout).  Each step packs
+    one canvas already in HBM (ffb_pack_rgb) and replays the tower's CUDA graph; device
+    time with CUDA events; the 600 MB of weights exceed L2, so every step streams them."""
+    import torch
+    from fastforward_b200.config import VISION_MODELS
+    from fastforward_b200.ops import pack_rectangle
+    from fastforward_b200.synthetic import make_vision_bf16
+    from fastforward_b200.vision import VisionTower
+    v = VISION_MODELS[name]
+    vt = VisionTower(v, make_vision_bf16(v, seed=0, device=dev), device=dev)
+    grid = side // v.patch
+    n_p = grid * grid
+    g = torch.Generator().manual_seed(7)
+    canvases = [torch.randint(0, 256, (side, side, 3), generator=g, dtype=torch.uint8).to(dev) for _ in range(4)]
+    graph = vt.capture(grid, grid)
+    buf = vt.bufs[n_p]
+    for i in range(max(args.warmup, 3)):
+        pack_rectangle(canvases[i % 4], pixels=buf.pixels)
+        graph.replay()
+    torch.cuda.synchronize()
+    if getattr(args, "vision_ncu", False):
+        torch.cuda.profiler.start()
+        pack_rectangle(canvases[0], pixels=buf.pixels)
+        graph.replay()
+        torch.cuda.synchronize()
+        torch.cuda.profiler.stop()
+        return dict(ncu_range="one vision forward", launches=1 + VisionTower.launches(v))
+    steps = max(min(args.steps, 50), 5)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    for i in range(steps):
+        ev[i][0].record()
+        pack_rectangle(canvases[i % 4], pixels=buf.pixels)
+        graph.replay()
+        ev[i][1].record()
+    torch.cuda.synchronize()
+    ms = sorted(a.elapsed_time(b) for a, b in ev)
+    p50 = ms[len(ms) // 2]
+    flops = vision_flops(v, n_p)
+    # end to end: a host canvas (pinned) to the merged rows in host memory
+    host = [c.cpu().pin_memory() for c in canvases]
+    out = torch.empty(buf.merged.shape, dtype=buf.merged.dtype).pin_memory()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(steps):
+        canvases[i % 4].copy_(host[i % 4], non_blocking=True)
+        pack_rectangle(canvases[i % 4], pixels=buf.pixels)
+        graph.replay()
+        out.copy_(buf.merged, non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / steps
+    tflops = flops / (p50 * 1e-3) / 1e12
+    return dict(model=f"{name} vision tower ({v.depth} blocks, hidden {v.hidden}, deepstack {list(v.deepstack)})",
+                canvas=f"{side}x{side}", patches=n_p, merged_rows=n_p // 4, steps=steps, ms_per_image_p50=p50,
+                images_per_s=1e3 / p50, tflops=tflops, frac_of_bf16_peak=tflops / peaks["bf16"],
+                peak_note=f"{peaks['bf16']} TFLOP/s bf16 ({peaks['src']}, burst)", flops_per_image=flops,
+                gpu_launches_per_image=1 + VisionTower.launches(v),
+                e2e=dict(ms_per_image=e2e_ms, h2d_bytes=side * side * 3, d2h_bytes=out.numel() * 2,
+                         api="VisionTower graph: pinned canvas -> pack_rgb -> tower -> merged rows to host"))
 
 
 def _summarise_stream(line):
@@ -1066,6 +1144,11 @@ def main():
     from fastforward_b200.config import STREAMS
     if args.workload in PACK_WORKLOADS:
         return run_pack_reference(args) if args.impl == "reference" else run_pack(args)
+    if args.vision_ncu:
+        import torch
+        torch.cuda.set_device(0)
+        print(json.dumps(vision_measure(args, torch.device("cuda", 0), read_peaks())), flush=True)
+        return
     if args.impl == "reference":
         if args.workload in STREAMS:
             print(json.dumps(dict(impl="reference", unavailable="the CPU reference arm times the fixed-geometry "

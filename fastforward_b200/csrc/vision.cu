@@ -96,32 +96,50 @@ __global__ void __launch_bounds__(1024) layernorm_kernel(const uint16_t* __restr
   *reinterpret_cast<uint4*>(y + off) = make_uint4(o[0], o[1], o[2], o[3]);
 }
 
-// One CTA per patch.  qkv row p = [q (H x d) | k (H x d) | v (H x d)]; cos / sin [P, d]
-// fp32.  q, k: y[c] = x[c] cos[c] + r[c] sin[c] with r = (-x[c + d/2] for c < d/2,
-// x[c - d/2] otherwise), both products and the sum IEEE fp32 operations, then bf16; v
-// copied.  Outputs [H, P, dp] with columns d..dp-1 zero.
+// One CTA per (patch, part of q / k / v), one thread per 8 output columns of a head: the
+// part's H x d row is staged in shared memory (16-byte loads), then each thread writes 16
+// bytes of the head-major output.  qkv row p = [q (H x d) | k (H x d) | v (H x d)];
+// cos / sin [P, d] fp32.  q, k: y[c] = x[c] cos[c] + r[c] sin[c] with r = (-x[c + d/2] for
+// c < d/2, x[c - d/2] otherwise), both products and the sum IEEE fp32 operations, then
+// bf16; v copied.  Outputs [H, P, dp] with columns d..dp-1 zero.
 __global__ void vision_rope_kernel(const uint16_t* __restrict__ qkv, const float* __restrict__ cs,
                                    const float* __restrict__ sn, int P, int H, int d, int dp, uint16_t* q,
                                    uint16_t* k, uint16_t* v) {
+  extern __shared__ uint16_t srow[];  // [H * d]
   pdl_wait();
   pdl_launch();
-  const int p = blockIdx.x, half = d / 2, hd = H * dp;
-  const uint16_t* src = qkv + (size_t)p * 3 * H * d;
-  for (int idx = threadIdx.x; idx < 3 * hd; idx += blockDim.x) {
-    const int part = idx / hd, rem = idx - part * hd, h = rem / dp, c = rem - h * dp;
-    float out = 0.f;
-    if (c < d) {
-      const uint16_t* row = src + (size_t)part * H * d + (size_t)h * d;
-      const float xv = bf2f(row[c]);
-      if (part == 2) {
-        out = xv;
-      } else {
-        const float rv = c < half ? -bf2f(row[c + half]) : bf2f(row[c - half]);
-        out = __fadd_rn(__fmul_rn(xv, cs[(size_t)p * d + c]), __fmul_rn(rv, sn[(size_t)p * d + c]));
+  const int p = blockIdx.x, part = blockIdx.y, half = d / 2, hd = H * d;
+  const uint16_t* src = qkv + (size_t)p * 3 * hd + (size_t)part * hd;
+  for (int i = threadIdx.x; i < hd / 8; i += blockDim.x)
+    reinterpret_cast<uint4*>(srow)[i] = reinterpret_cast<const uint4*>(src)[i];
+  __syncthreads();
+  const int cpr = dp / 8;  // 16-byte chunks per output row
+  uint16_t* dst = part == 0 ? q : (part == 1 ? k : v);
+  for (int t = threadIdx.x; t < H * cpr; t += blockDim.x) {
+    const int h = t / cpr, c0 = (t - h * cpr) * 8;
+    const uint16_t* row = srow + h * d;
+    uint32_t w[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      float y[2];
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const int c = c0 + 2 * e + j;
+        float out = 0.f;
+        if (c < d) {
+          const float xv = bf2f(row[c]);
+          if (part == 2) {
+            out = xv;
+          } else {
+            const float rv = c < half ? -bf2f(row[c + half]) : bf2f(row[c - half]);
+            out = __fadd_rn(__fmul_rn(xv, __ldg(cs + (size_t)p * d + c)), __fmul_rn(rv, __ldg(sn + (size_t)p * d + c)));
+          }
+        }
+        y[j] = out;
       }
+      w[e] = (uint32_t)f2bf(y[0]) | ((uint32_t)f2bf(y[1]) << 16);
     }
-    uint16_t* dst = part == 0 ? q : (part == 1 ? k : v);
-    dst[((size_t)h * P + p) * dp + c] = f2bf(out);
+    *reinterpret_cast<uint4*>(dst + ((size_t)h * P + p) * dp + c0) = make_uint4(w[0], w[1], w[2], w[3]);
   }
 }
 
@@ -151,10 +169,13 @@ extern "C" int ffb_layernorm(const uint16_t* x, const uint16_t* w, const uint16_
 extern "C" int ffb_vision_rope(const uint16_t* qkv, const float* cos, const float* sin, int P, int H, int d, int dp,
                                uint16_t* q, uint16_t* k, uint16_t* v, void* stream) {
   FFB_REQUIRE(qkv && cos && sin && q && k && v, "ffb_vision_rope: NULL pointer");
-  FFB_REQUIRE(P > 0 && H > 0 && d > 0 && d % 2 == 0 && dp >= d && dp <= 256,
-              "ffb_vision_rope: bad shape P=%d H=%d d=%d dp=%d", P, H, d, dp);
-  cudaError_t e = ffb::launch(vision_rope_kernel, dim3(P), dim3(256), 0, (cudaStream_t)stream, qkv, cos, sin, P, H, d,
-                              dp, q, k, v);
+  FFB_REQUIRE(P > 0 && H > 0 && d > 0 && d % 8 == 0 && dp >= d && dp % 8 == 0 && dp <= 256 && H * d <= 16384,
+              "ffb_vision_rope: bad shape P=%d H=%d d=%d dp=%d (d, dp multiples of 8)", P, H, d, dp);
+  FFB_REQUIRE(ffb::aligned(qkv, 16) && ffb::aligned(q, 16) && ffb::aligned(k, 16) && ffb::aligned(v, 16),
+              "ffb_vision_rope: qkv, q, k, v must be 16-byte aligned");
+  const int threads = H * (dp / 8) < 1024 ? (H * (dp / 8) + 31) / 32 * 32 : 1024;
+  cudaError_t e = ffb::launch(vision_rope_kernel, dim3(P, 3), dim3(threads), (size_t)H * d * 2, (cudaStream_t)stream,
+                              qkv, cos, sin, P, H, d, dp, q, k, v);
   if (e != cudaSuccess) return ffb::fail(FFB_ECUDA, "ffb_vision_rope: launch: %s", cudaGetErrorString(e));
   return FFB_OK;
 }
