@@ -7,15 +7,19 @@
 files, RuntimeError for device problems and non-finite outputs; one RLock per instance
 serialises calls).  Behind them the B200 engine runs the prefill + scoring path.
 
-What lies before the path in the reference -- image decode, resize, vision tower,
-tokenizer (`_family/depth_runtime.py:54-82`) -- is outside this package: `predict` takes
-it from an `encoder(image, question, candidates) -> Request` callable.  Checkpoint bundles
-(the reference's `configs/*.json`: `model` = a Hugging Face Qwen3-VL directory, the recovery
-`checkpoint`, the calibration `profile_path`) load the language decoder's weights from the
-safetensors files (`fastforward_b200.checkpoint`); bundles with a `synthetic` block (seeded
-random weights, no checkpoint files) get a deterministic synthetic encoder so the whole
-surface runs without model assets.  `prefill_score` is the
-internal entry that `predict` calls after the encoder; benchmarks call it directly.
+Before the path, the reference decodes and resizes the image, runs the vision tower and
+tokenizes the prompt (`_family/depth_runtime.py:54-82`).  Here the vision tower runs on this
+package's kernels (`fastforward_b200.vision`: a pre-sized uint8 canvas -> patch rows ->
+tower graph -> visual and deepstack rows); decode / resize and the tokenizer are outside it
+(a `tokenizer(question, candidates) -> (prefix ids, suffix ids)` callable is passed in, or a
+whole `encoder(image, question, candidates) -> Request`).  Checkpoint bundles (the
+reference's `configs/*.json`: `model` = a Hugging Face Qwen3-VL directory, the recovery
+`checkpoint`, the calibration `profile_path`) load the weights from the safetensors files
+(`fastforward_b200.checkpoint`); bundles with a `synthetic` block (seeded random weights, no
+checkpoint files) get a deterministic synthetic encoder -- with `"vision": true` the seeded
+vision tower on the image canvas and synthetic text ids -- so the whole surface runs
+without model assets.  `prefill_score` is the internal entry that `predict` calls after the
+encoder; benchmarks call it directly.
 """
 import hashlib
 import json
@@ -105,7 +109,7 @@ class Accelerator:
     graph buffers are private to the instance.
     """
 
-    def __init__(self, bundle, *, backend="fast", device=None, encoder=None):
+    def __init__(self, bundle, *, backend="fast", device=None, encoder=None, tokenizer=None):
         self.bundle = Path(bundle).resolve()
         c = json.loads(self.bundle.read_text())
         if c.get("schema_version") != 1 or c.get("task") != "visual_choice":
@@ -159,10 +163,48 @@ class Accelerator:
             del src
             torch.cuda.empty_cache()
             self.engine = Engine(self.model)
+        self.vision = None
+        if encoder is None:
+            encoder = self._vision_encoder(c, synthetic, tokenizer)
         if encoder is None and synthetic is not None:
             encoder = SyntheticEncoder(self.dims, self.layout)
         self.encoder = encoder
         self._staging = {}
+
+    def _vision_encoder(self, c, synthetic, tokenizer):
+        """The image side of `predict` on this package's vision kernels, or None.
+
+        Synthetic bundles opt in with `"vision": true` (or an object with `seed`, `depth`:
+        a tower of fewer blocks, deepstack taken at its first blocks): a seeded tower of the
+        family's published vision config, text ids from the synthetic stand-in unless a
+        `tokenizer` is given.  Checkpoint bundles use the checkpoint's own vision tower
+        when a `tokenizer(question, candidates) -> (prefix ids, suffix ids)` is given (no
+        tokenizer ships with this package)."""
+        import torch
+        from .vision import VisionEncoder, VisionTower
+        if synthetic is not None:
+            spec = synthetic.get("vision")
+            if not spec:
+                return None
+            spec = spec if isinstance(spec, dict) else {}
+            from dataclasses import replace
+            from .config import VISION_MODELS
+            from .synthetic import make_vision_bf16
+            v = VISION_MODELS[synthetic["model"]]
+            if spec.get("depth"):
+                depth = int(spec["depth"])
+                v = replace(v, depth=depth, deepstack=tuple(min(i, depth - 1) for i in range(len(v.deepstack))))
+            with torch.cuda.device(self.device):
+                params = make_vision_bf16(v, seed=int(spec.get("seed", 0)), device=self.device)
+                self.vision = VisionTower(v, params, device=self.device)
+            lay = self.layout
+            return VisionEncoder(self.vision, self.dims.vocab, tokenizer, n_prefix=lay.image_start, n_suffix=lay.n_text)
+        if tokenizer is None:
+            return None
+        from .checkpoint import load_vision_tower
+        v, params = load_vision_tower(c["model"], device=self.device)
+        self.vision = VisionTower(v, params, device=self.device)
+        return VisionEncoder(self.vision, self.dims.vocab, tokenizer)
 
     # ------------------------------------------------------------------ checkpoint bundles
     @staticmethod
@@ -365,8 +407,9 @@ class Accelerator:
         if mode not in BACKENDS:
             raise ValueError("Unknown backend")
         if self.encoder is None:
-            raise RuntimeError("No encoder: the vision tower and tokenizer are outside this package; construct the "
-                               "Accelerator with encoder=callable(image, question, candidates) -> Request")
+            raise RuntimeError("No encoder: no tokenizer ships with this package; construct the Accelerator with "
+                               "tokenizer=callable(question, candidates) -> (prefix ids, suffix ids) to run the "
+                               "checkpoint's vision tower, or encoder=callable(image, question, candidates) -> Request")
         with self.lock:
             r = self.encoder(str(image), question, list(candidates))
             z, lp = self.prefill_score(r.ids, r.visual, r.deep, len(candidates), r.image_start, r.grid_h,

@@ -12,17 +12,19 @@
 // Tile = 128 tokens (UMMA M) x BN output features (UMMA N = 64, 128 or 256), 64 K
 // elements (one 128-byte swizzle row of bf16) per stage.  Persistent kernel, one CTA per
 // SM, tiles round-robin with the token tile fastest (CTAs that run at the same time share
-// weight tiles in L2).  Roles (320 threads):
+// weight tiles in L2).  Roles (64 + 32 x EW threads; EW = 16 epilogue warps for BN >= 128,
+// 8 for BN = 64):
 //   warp 0      TMA producer: activation tile [128 x 64] and weight tile [BN x 64], both
 //               K-major with the 128-byte swizzle, into a ring of STAGES slots; the first
 //               ring pass of weight tiles is requested before the wait on the previous
 //               kernel (weights do not depend on it);
 //   warp 1      TMEM allocator + single-thread MMA issuer (4 x K16 per stage) into one of
 //               two accumulators, so the epilogue of tile i overlaps the mainloop of i+1;
-//   warps 2..9  epilogue: lane quarter (warp % 4) x half of the tile's columns; 32
+//   warps 2..   epilogue: lane quarter (warp % 4) x one of EW / 4 column groups; 32
 //               columns at a time: fp32 accumulator + bias, the epilogue's operation,
 //               bf16, staged in shared memory and written by TMA store (rows past M and
-//               columns past N are clipped by the store).
+//               columns past N are clipped by the store).  With one or two tiles per CTA
+//               the last tile's epilogue is exposed, so the GELU epilogues get 16 warps.
 // K past the end of the operands is zero-filled by TMA (adds nothing), so K need not be
 // a multiple of 64.  Every wait is bounded; a timeout sets the abort flag and the device
 // error word, and TMEM is released.
@@ -35,15 +37,16 @@ constexpr int BM = 128;
 constexpr int BKE = 64;
 constexpr int UMMA_K = 16;
 constexpr int A_BYTES = BM * BKE * 2;  // 16 KB
-constexpr int EPI_WARPS = 8;
-constexpr int THREADS = 64 + EPI_WARPS * 32;
 constexpr int SMEM_LIMIT = 232448;
 
 template <int BN>
 struct BCfg {
+  static constexpr int EW = BN >= 128 ? 16 : 8;  // epilogue warps
+  static constexpr int NSTG = EW == 16 ? 1 : 2;  // 2 KB staging buffers per epilogue warp
+  static constexpr int THREADS = 64 + EW * 32;
   static constexpr int W_BYTES = BN * BKE * 2;
   static constexpr int STAGE_BYTES = A_BYTES + W_BYTES;
-  static constexpr int STG_BYTES = EPI_WARPS * 2 * 2048;
+  static constexpr int STG_BYTES = EW * NSTG * 2048;
   static constexpr int FIXED = STG_BYTES + 512 + 1024;
   static constexpr int FIT = (SMEM_LIMIT - FIXED) / STAGE_BYTES;
   static constexpr int STAGES = FIT > 8 ? 8 : FIT;
@@ -116,7 +119,7 @@ __device__ __forceinline__ float epilogue_op(float acc, float b, float r) {
 }
 
 template <int BN, int EPI>
-__global__ void __launch_bounds__(THREADS, 1)
+__global__ void __launch_bounds__(BCfg<BN>::THREADS, 1)
     bf16_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_w,
                      const __grid_constant__ CUtensorMap tmap_o, const BArgs args) {
   using C = BCfg<BN>;
@@ -140,7 +143,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], EPI_WARPS);
+      mbar_init(&tempty[b], C::EW);
     }
     *abort_flag = 0;
     fence_mbar_init();
@@ -250,7 +253,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     pdl_wait();
     if (warp == 2 && lane == 0) pdl_launch();
     const int q = warp & 3;             // TMEM lane quarter = this warp's 32 tokens
-    const int half = (warp - 2) >> 2;  // which half of the tile's columns
+    constexpr int GROUP = BN / (C::EW / 4);  // columns per column group
+    const int cg = (warp - 2) >> 2;          // this warp's column group
     int lt = 0;
     uint32_t sc = 0;
     for (int t = blockIdx.x; t < args.n_tiles; t += gridDim.x, ++lt) {
@@ -264,7 +268,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       const uint32_t acc = tmem + (uint32_t)(buf * BN) + ((uint32_t)(q * 32) << 16);
       const int row = tt * BM + q * 32 + lane;  // this thread's token
 #pragma unroll 1
-      for (int c = half * (BN / 2); c < (half + 1) * (BN / 2); c += 32) {
+      for (int c = cg * GROUP; c < (cg + 1) * GROUP; c += 32) {
         const int n = ft * BN + c;  // first output feature of the chunk
         // chunks wholly past N or past M store nothing (warp-uniform: n and q are)
         if (n >= args.N || tt * BM + q * 32 >= args.M) continue;
@@ -293,9 +297,9 @@ __global__ void __launch_bounds__(THREADS, 1)
           o[8 + (j >> 1)] = pack2(epilogue_op<EPI>(__uint_as_float(r1[j]), bv[16 + j], rv[16 + j]),
                                   epilogue_op<EPI>(__uint_as_float(r1[j + 1]), bv[17 + j], rv[17 + j]));
         }
-        // 32 rows x 64 bytes, 64-byte swizzle (make_tmap_out), double-buffered per warp
-        uint8_t* sb = stg_all + ((warp - 2) * 2 + (int)(sc & 1)) * 2048;
-        if (lane == 0) bulk_wait_read<1>();
+        // 32 rows x 64 bytes, 64-byte swizzle (make_tmap_out), NSTG buffers per warp
+        uint8_t* sb = stg_all + ((warp - 2) * C::NSTG + (int)(sc % C::NSTG)) * 2048;
+        if (lane == 0) bulk_wait_read<C::NSTG - 1>();  // the store that last used this buffer has read it
         __syncwarp();
 #pragma unroll
         for (int k = 0; k < 4; ++k)
@@ -339,7 +343,7 @@ cudaError_t launch_instance(const CUtensorMap& ta, const CUtensorMap& tw, const 
   using C = BCfg<BN>;
   cudaError_t e = ffb::set_smem_attr(reinterpret_cast<const void*>(bf16_gemm_kernel<BN, EPI>), C::SMEM);
   if (e != cudaSuccess) return e;
-  return ffb::launch(bf16_gemm_kernel<BN, EPI>, dim3(grid), dim3(THREADS), C::SMEM, stream, ta, tw, to, ba);
+  return ffb::launch(bf16_gemm_kernel<BN, EPI>, dim3(grid), dim3(C::THREADS), C::SMEM, stream, ta, tw, to, ba);
 }
 
 template <int BN>

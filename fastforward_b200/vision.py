@@ -268,3 +268,90 @@ class VisionTower:
             pack_rectangle(rgb, pixels=buf.pixels)
             g.replay()
             return buf.merged, list(buf.deep)
+
+
+# ---------------------------------------------------------------------------- request encoder
+
+def read_canvas(image):
+    """uint8 [H, W, 3] canvas from an array or tensor, a `.npy` file, or a binary PPM (P6,
+    maxval 255) file.  Canvas sides must already be multiples of 32: decoding compressed
+    formats and resizing into the canvas (the reference's cv2 step, `_family/depth_runtime.py:
+    54-76`) happen before this package."""
+    import numpy as np
+    from pathlib import Path
+    if isinstance(image, torch.Tensor):
+        a = image
+    elif isinstance(image, np.ndarray):
+        a = torch.from_numpy(np.ascontiguousarray(image))
+    else:
+        path = Path(image)
+        raw = path.read_bytes()
+        if raw[:6] == b"\x93NUMPY":
+            a = torch.from_numpy(np.ascontiguousarray(np.load(path, allow_pickle=False)))
+        elif raw[:2] == b"P6":
+            fields, pos = [], 2
+            while len(fields) < 3:  # width, height, maxval; whitespace and '#' comments between
+                while raw[pos:pos + 1].isspace():
+                    pos += 1
+                if raw[pos:pos + 1] == b"#":
+                    pos = raw.index(b"\n", pos) + 1
+                    continue
+                end = pos
+                while not raw[end:end + 1].isspace():
+                    end += 1
+                fields.append(int(raw[pos:end]))
+                pos = end
+            w, h, maxval = fields
+            if maxval != 255:
+                raise ValueError(f"PPM maxval {maxval}: only 8-bit canvases are supported")
+            pos += 1
+            a = torch.frombuffer(bytearray(raw[pos:pos + h * w * 3]), dtype=torch.uint8).reshape(h, w, 3)
+        else:
+            raise ValueError(f"{path.name}: expected an uint8 canvas as .npy or binary PPM (P6)")
+    if a.dtype != torch.uint8 or a.dim() != 3 or a.shape[2] != 3:
+        raise ValueError(f"canvas must be uint8 [H, W, 3], got {tuple(a.shape)} {a.dtype}")
+    if a.shape[0] % 32 or a.shape[1] % 32:
+        raise ValueError(f"canvas {a.shape[0]}x{a.shape[1]}: sides must be multiples of 32")
+    return a.contiguous()
+
+
+def synthetic_text_ids(question, candidates, n_prefix, n_suffix, vocab):
+    """Deterministic stand-in for the tokenizer (absent here): prefix and suffix ids drawn
+    from a generator seeded by the question and choices."""
+    import hashlib
+    h = hashlib.sha256(question.encode() + b"\x00" + "\x00".join(candidates).encode()).digest()
+    g = torch.Generator().manual_seed(int.from_bytes(h[:8], "little") & ((1 << 62) - 1))
+    ids = torch.randint(0, vocab, (n_prefix + n_suffix,), generator=g)
+    return ids[:n_prefix], ids[n_prefix:]
+
+
+class VisionEncoder:
+    """image canvas + question + choices -> `api.Request` through this package's vision
+    tower: the canvas is packed into patch rows and run through the tower's CUDA graph;
+    the merged rows are the request's visual rows and the deepstack mergers' outputs its
+    deepstack rows.  Text ids come from `tokenize(question, candidates) -> (prefix ids,
+    suffix ids)`; without one (no tokenizer ships with this package) they are the
+    deterministic synthetic ids of the bundle's layout (`n_prefix` before the image,
+    `n_suffix` after it)."""
+
+    def __init__(self, tower, vocab, tokenize=None, n_prefix=0, n_suffix=64):
+        self.tower = tower
+        self.vocab = vocab
+        self.tokenize = tokenize
+        self.n_prefix, self.n_suffix = n_prefix, n_suffix
+
+    def __call__(self, image, question, candidates):
+        from .api import Request
+        rgb = read_canvas(image).to(self.tower.device)
+        merged, deep = self.tower.encode(rgb)
+        grid_h, grid_w = rgb.shape[0] // self.tower.v.patch, rgb.shape[1] // self.tower.v.patch
+        if self.tokenize is not None:
+            pre, suf = self.tokenize(question, list(candidates))
+            pre, suf = torch.as_tensor(pre, dtype=torch.long), torch.as_tensor(suf, dtype=torch.long)
+        else:
+            pre, suf = synthetic_text_ids(question, list(candidates), self.n_prefix, self.n_suffix, self.vocab)
+        nv = merged.shape[0]
+        ids = torch.cat([pre, torch.zeros(nv, dtype=torch.long), suf])
+        # the tower's buffers are reused by its next image: the request keeps copies
+        return Request(ids=ids, visual=merged.clone(), deep=[d.clone() for d in deep], image_start=int(pre.shape[0]),
+                       grid_h=grid_h, grid_w=grid_w, k=len(candidates))

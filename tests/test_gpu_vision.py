@@ -196,3 +196,53 @@ def test_vision_tower_encodes_a_canvas():
     torch.cuda.synchronize()
     rm, rd = oracle.vision_tower_k(p, v, oracle.pack_rgb(rgb), 16, 24)
     assert _bits_equal(merged, rm) and _bits_equal(deep[0], rd[0])
+
+
+# ---------------------------------------------------------------------------- predict
+
+def test_predict_runs_the_vision_tower_end_to_end(tmp_path):
+    """`Accelerator.predict(canvas, question, choices)` on a synthetic bundle with the
+    vision tower on: canvas -> ffb_pack_rgb -> the tower's graph -> the language prefill +
+    scoring graph.  The logits equal, bit for bit, the oracle's vision tower (kernel
+    arithmetic) feeding the oracle's language path on the same ids."""
+    import json
+    import numpy as np
+    from dataclasses import replace
+    from fastforward_b200.api import Accelerator
+    from fastforward_b200.config import MODELS
+    from fastforward_b200.mrope import position_ids
+    from fastforward_b200.synthetic import make_model_bf16
+    g = torch.Generator().manual_seed(21)
+    rgb = torch.randint(0, 256, (256, 256, 3), generator=g, dtype=torch.uint8)
+    img = tmp_path / "canvas.npy"
+    np.save(img, rgb.numpy())
+    syn = dict(model="2B", layers=2, seed=3, vision=dict(seed=5, depth=3),
+               layout=dict(image_start=4, grid_h=16, grid_w=16, n_text=32))
+    bundle = tmp_path / "bundle.json"
+    bundle.write_text(json.dumps(dict(schema_version=1, task="visual_choice", architecture="qwen3_vl_family",
+                                      synthetic=syn)))
+    acc = Accelerator(bundle)
+    cands = ["cat", "dog", "bird", "fish"]
+    out = acc.predict(img, "What is shown?", cands)
+    r = acc.encoder(str(img), "What is shown?", cands)
+    assert r.visual.shape == (64, 2048) and len(r.deep) == 3 and r.image_start == 4
+
+    v = acc.vision.v
+    p = make_vision_bf16(v, seed=5, device=DEV)
+    p = {k: t.cpu() for k, t in p.items()}
+    merged, deep = oracle.vision_tower_k(p, v, oracle.pack_rgb(rgb), 16, 16)
+    assert _bits_equal(r.visual, merged) and all(_bits_equal(a, b) for a, b in zip(r.deep, deep))
+    dims = MODELS["2B"]
+    src = make_model_bf16(dims, seed=3, device=DEV, layers=2)
+    src = {k: ([{n: t.cpu() for n, t in lay.items()} for lay in src[k]] if k == "layers" else src[k].cpu())
+           for k in src}
+    T = next(b for b in acc.buckets if b >= r.ids.shape[0])
+    splits = {k: pl.splits for k, pl in acc.engine.plans[T].items()}
+    om = oracle.quantized_model(dims, src, "rowwise", splits=splits)
+    ids = torch.zeros(T, dtype=torch.long)
+    ids[:r.ids.shape[0]] = r.ids
+    pos = position_ids(T, r.image_start, 16, 16)
+    zr, _ = oracle.prefill_score(om, ids, merged, deep, pos, r.ids.shape[0] - 1, 4, image_start=r.image_start)
+    assert torch.equal(torch.tensor(out["logits"], dtype=torch.float32).view(torch.int32), zr.view(torch.int32)), \
+        (out["logits"], zr)
+    assert out["answer"]["text"] == cands[int(torch.argmax(zr))]

@@ -108,3 +108,23 @@ def test_feature_tile_choice():
     assert L.lib().ffb_bf16_gemm_feature_tile(1024, 1024) == 64
     assert L.lib().ffb_bf16_gemm_feature_tile(1024, 4096) == 256
     assert L.lib().ffb_bf16_gemm_feature_tile(0, 4096) == 0
+
+
+def test_read_canvas_formats(tmp_path):
+    """Canvases come as arrays, .npy files or binary PPM (P6) files; anything else, or sides
+    that are not multiples of 32, is rejected."""
+    import numpy as np
+    from fastforward_b200.vision import read_canvas, synthetic_text_ids
+    a = np.random.default_rng(0).integers(0, 256, (64, 96, 3), dtype=np.uint8)
+    np.save(tmp_path / "c.npy", a)
+    (tmp_path / "c.ppm").write_bytes(b"P6\n# comment\n96 64\n255\n" + a.tobytes())
+    for src in (a, torch.from_numpy(a), tmp_path / "c.npy", tmp_path / "c.ppm"):
+        assert torch.equal(read_canvas(src), torch.from_numpy(a))
+    (tmp_path / "x.png").write_bytes(b"\x89PNG not decoded here")
+    with pytest.raises(ValueError, match="npy or binary PPM"):
+        read_canvas(tmp_path / "x.png")
+    with pytest.raises(ValueError, match="multiples of 32"):
+        read_canvas(a[:48])
+    p1, s1 = synthetic_text_ids("q", ["a", "b"], 4, 8, 1000)
+    p2, s2 = synthetic_text_ids("q", ["a", "b"], 4, 8, 1000)
+    assert torch.equal(p1, p2) and torch.equal(s1, s2) and p1.shape == (4,) and s1.shape == (8,)
