@@ -58,8 +58,8 @@ SIGNATURES = {
     "ffb_w4a16_gemm": [P, P, P, I, P, P, I, I, I, I, I, P],
     "ffb_pack_rgb": [P, P, I, I, P],
     "ffb_pack_rgb_batch": [P, P, I, I, I, P],
-    "ffb_bf16_gemm": [P, P, P, P, I, P, I, I, I, I, P],
-    "ffb_bf16_gemm_feature_tile": [I, I],
+    "ffb_bf16_gemm": [P, P, P, P, I, P, I, I, P, P, I, I, I, P],
+    "ffb_bf16_gemm_plan": [I, I, I, P],
     "ffb_layernorm": [P, P, P, F, P, I, I, P],
     "ffb_add_layernorm": [P, P, P, P, F, P, P, I, I, P],
     "ffb_vision_rope": [P, P, P, I, I, I, I, P, P, P, P],
@@ -138,6 +138,13 @@ def stream_ctas(m, n, k, epilogue, splits=1):
     """CTAs of ffb_fp8_gemm's weight-stationary schedule for this GEMM, 0 if it does not
     apply (host query)."""
     return int(lib().ffb_fp8_gemm_stream_ctas(int(m), int(n), int(k), int(epilogue), int(splits)))
+
+
+def bf16_gemm_plan(m, n, k):
+    """(feature tile, K splits, counters needed) that ffb_bf16_gemm plans for m x n x k."""
+    plan = (ctypes.c_int * 3)()
+    call("ffb_bf16_gemm_plan", int(m), int(n), int(k), ctypes.addressof(plan))
+    return plan[0], plan[1], plan[2]
 
 
 def set_pdl(enable):

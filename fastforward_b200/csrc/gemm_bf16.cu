@@ -59,8 +59,21 @@ struct BCfg {
 struct BArgs {
   const uint16_t* bias;  // [N] bf16 or NULL (no bias)
   const uint16_t* res;   // [M][N] bf16 (FFB_EPI_BIAS_RES)
-  int M, N, K, n_ttiles, n_tiles;
+  float* ws;             // split-K: [splits][M][N] fp32 partial planes
+  uint32_t* counters;    // split-K: arrivals per output tile (zero between launches)
+  int M, N, K, n_ttiles, n_tiles, splits;
 };
+
+// Tile t -> token tile (fastest), K split, feature tile; the split's K blocks [kb0, kb1).
+__device__ __forceinline__ void tile_coords(const BArgs& a, int t, int nkb, int& tt, int& ks, int& ft, int& kb0,
+                                            int& kb1) {
+  tt = t % a.n_ttiles;
+  const int r = t / a.n_ttiles;
+  ks = r % a.splits;
+  ft = r / a.splits;
+  kb0 = (int)((long long)ks * nkb / a.splits);
+  kb1 = (int)((long long)(ks + 1) * nkb / a.splits);
+}
 
 // Both GELU forms are (x / 2) s with s = 1 + tanh(u) or 1 + erf(z), and s is evaluated
 // without the cancellation of 1 + (a value near -1): for u, z < 0 it is the small
@@ -132,6 +145,7 @@ __global__ void __launch_bounds__(BCfg<BN>::THREADS, 1)
   uint64_t* tempty = tfull + 2;         // [2]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* last_flag = abort_flag + 1;  // split-K: the epilogue warps' shared verdict per tile
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int nkb = (args.K + BKE - 1) / BKE;
@@ -166,21 +180,23 @@ __global__ void __launch_bounds__(BCfg<BN>::THREADS, 1)
     // ------------------------------------------------------------------ TMA producer
     if (lane == 0) {
       const uint64_t pol_w = policy_evict_first(), pol_a = policy_evict_last();
-      int pre = 0;
+      int pre = 0, tt0 = 0, kb00 = 0;
       if ((int)blockIdx.x < args.n_tiles) {  // weights do not depend on the previous kernel
-        const int ft = (int)blockIdx.x / args.n_ttiles;
-        pre = nkb < C::STAGES ? nkb : C::STAGES;
+        int ks, ft, kb1;
+        tile_coords(args, blockIdx.x, nkb, tt0, ks, ft, kb00, kb1);
+        pre = kb1 - kb00 < C::STAGES ? kb1 - kb00 : C::STAGES;
         for (int i = 0; i < pre; ++i) {
           mbar_arrive_expect_tx(&full[i], C::STAGE_BYTES);
-          tma_load_2d(smem + i * C::STAGE_BYTES + A_BYTES, &tmap_w, &full[i], i * BKE, ft * BN, pol_w);
+          tma_load_2d(smem + i * C::STAGE_BYTES + A_BYTES, &tmap_w, &full[i], (kb00 + i) * BKE, ft * BN, pol_w);
         }
       }
       pdl_wait();
       int it = 0, s = 0;
       uint32_t ph = 0;
       for (int t = blockIdx.x; t < args.n_tiles && !*abort_flag; t += gridDim.x) {
-        const int tt = t % args.n_ttiles, ft = t / args.n_ttiles;
-        for (int kb = 0; kb < nkb; ++kb, ++it) {
+        int tt, ks, ft, kb0, kb1;
+        tile_coords(args, t, nkb, tt, ks, ft, kb0, kb1);
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
           uint8_t* st = smem + s * C::STAGE_BYTES;
           if (it >= pre) {
             if (!mbar_wait_bounded(&empty[s], ph ^ 1u, abort_flag)) {
@@ -200,8 +216,7 @@ __global__ void __launch_bounds__(BCfg<BN>::THREADS, 1)
       if (*abort_flag) {  // every slot whose copy was issued must land before the CTA exits
         volatile int never = 0;
         for (int j = it; j < pre; ++j)  // requested before the wait, never given their activations
-          tma_load_2d(smem + j * C::STAGE_BYTES, &tmap_a, &full[j], j * BKE,
-                      ((int)blockIdx.x % args.n_ttiles) * BM, pol_a);
+          tma_load_2d(smem + j * C::STAGE_BYTES, &tmap_a, &full[j], (kb00 + j) * BKE, tt0 * BM, pol_a);
         const int issued = it > pre ? it : pre;
         for (int j = (issued > C::STAGES ? issued - C::STAGES : 0); j < issued; ++j)
           mbar_wait_bounded(&full[j % C::STAGES], (uint32_t)(j / C::STAGES) & 1u, &never, 200000000ull);
@@ -226,7 +241,9 @@ __global__ void __launch_bounds__(BCfg<BN>::THREADS, 1)
         }
         tc_fence_after();
         const uint32_t acc = tmem + (uint32_t)(buf * BN);
-        for (int kb = 0; kb < nkb; ++kb) {
+        int tt, ks, ft, kb0, kb1;
+        tile_coords(args, t, nkb, tt, ks, ft, kb0, kb1);
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait_bounded(&full[s], ph, abort_flag)) {
             ok = false;
             break;
@@ -237,7 +254,7 @@ __global__ void __launch_bounds__(BCfg<BN>::THREADS, 1)
           const uint64_t dw = umma_desc_sw128(base + A_BYTES);
 #pragma unroll
           for (int kk = 0; kk < BKE / UMMA_K; ++kk)  // +32 bytes per K step = +2 encoded
-            umma_f16(acc, da + 2 * kk, dw + 2 * kk, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+            umma_f16(acc, da + 2 * kk, dw + 2 * kk, idesc, (kb > kb0 || kk > 0) ? 1u : 0u);
           umma_commit(&empty[s]);
           if (++s == C::STAGES) {
             s = 0;
@@ -258,20 +275,72 @@ __global__ void __launch_bounds__(BCfg<BN>::THREADS, 1)
     int lt = 0;
     uint32_t sc = 0;
     for (int t = blockIdx.x; t < args.n_tiles; t += gridDim.x, ++lt) {
-      const int tt = t % args.n_ttiles, ft = t / args.n_ttiles;
+      int tt, ks, ft, kb0, kb1;
+      tile_coords(args, t, nkb, tt, ks, ft, kb0, kb1);
       const int buf = lt & 1;
-      if (!(mbar_wait_bounded(&tfull[buf], (uint32_t)(lt >> 1) & 1u, abort_flag) && !*abort_flag)) {
-        *abort_flag = 1;
-        break;
-      }
+      const bool got = mbar_wait_bounded(&tfull[buf], (uint32_t)(lt >> 1) & 1u, abort_flag) && !*abort_flag;
+      if (!got) *abort_flag = 1;
       tc_fence_after();
       const uint32_t acc = tmem + (uint32_t)(buf * BN) + ((uint32_t)(q * 32) << 16);
       const int row = tt * BM + q * 32 + lane;  // this thread's token
+      const bool rows_in = tt * BM + q * 32 < args.M;  // warp-uniform
+      if (args.splits > 1) {
+        // split-K: every split writes its fp32 partial plane; the split that arrives last
+        // at the tile's counter sums the planes in split order and runs the epilogue.  All
+        // epilogue warps take both named barriers on every tile (also after a failed wait)
+        // and leave together on the verdict thread 0 of warp 2 publishes between them.
+        if (got && rows_in) {
+#pragma unroll 1
+          for (int c = cg * GROUP; c < (cg + 1) * GROUP; c += 32) {
+            const int n = ft * BN + c;
+            if (n >= args.N) continue;
+            uint32_t r[32];
+            tmem_ld16_async(acc + (uint32_t)c, *reinterpret_cast<uint32_t(*)[16]>(r));
+            tmem_ld16_async(acc + (uint32_t)(c + 16), *reinterpret_cast<uint32_t(*)[16]>(r + 16));
+            tmem_wait_ld();
+            reg_fence(r);
+            if (row < args.M) {
+              float* dst = args.ws + ((size_t)ks * args.M + row) * args.N + n;
+#pragma unroll
+              for (int g = 0; g < 4; ++g)
+                if (n + 8 * g < args.N) {
+                  reinterpret_cast<uint4*>(dst + 8 * g)[0] = make_uint4(r[8 * g], r[8 * g + 1], r[8 * g + 2], r[8 * g + 3]);
+                  reinterpret_cast<uint4*>(dst + 8 * g)[1] =
+                      make_uint4(r[8 * g + 4], r[8 * g + 5], r[8 * g + 6], r[8 * g + 7]);
+                }
+            }
+          }
+        }
+        __threadfence();
+        named_barrier(1, C::EW * 32);
+        if (warp == 2 && lane == 0) {
+          int verdict = -1;  // -1: stop (a wait gave up somewhere); 0: not last; 1: last
+          if (!*abort_flag) {
+            const int tile_out = tt + args.n_ttiles * ft;
+            const uint32_t old = atomicAdd(args.counters + tile_out, 1u);
+            verdict = old == (uint32_t)(args.splits - 1) ? 1 : 0;
+            if (verdict) args.counters[tile_out] = 0;  // every split has arrived: ready for the next launch
+          }
+          *last_flag = verdict;
+        }
+        named_barrier(1, C::EW * 32);
+        const int verdict = *last_flag;
+        if (verdict < 0) break;
+        if (verdict == 0) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&tempty[buf]);
+          continue;
+        }
+        __threadfence();  // the other splits' planes, published before their arrivals
+      } else if (!got) {
+        break;
+      }
 #pragma unroll 1
       for (int c = cg * GROUP; c < (cg + 1) * GROUP; c += 32) {
         const int n = ft * BN + c;  // first output feature of the chunk
         // chunks wholly past N or past M store nothing (warp-uniform: n and q are)
-        if (n >= args.N || tt * BM + q * 32 >= args.M) continue;
+        if (n >= args.N || !rows_in) continue;
         uint32_t r0[16], r1[16];
         tmem_ld16_async(acc + (uint32_t)c, r0);
         tmem_ld16_async(acc + (uint32_t)(c + 16), r1);
@@ -289,6 +358,36 @@ __global__ void __launch_bounds__(BCfg<BN>::THREADS, 1)
         tmem_wait_ld();
         reg_fence(r0);
         reg_fence(r1);
+        if (args.splits > 1 && row < args.M) {
+          // total = ((p0 + p1) + p2) + ...: this split's own partial from TMEM, the others'
+          // from their planes (L2, bypassing L1); four columns at a time
+          const float* srcp = args.ws + (size_t)row * args.N + n;
+          const size_t plane = (size_t)args.M * args.N;
+#pragma unroll
+          for (int g = 0; g < 8; ++g) {
+            uint32_t* rg = g < 4 ? r0 + 4 * g : r1 + 4 * (g - 4);
+            if (n + 4 * g >= args.N) continue;
+            float4 t4 = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 1
+            for (int j = 0; j < args.splits; ++j) {
+              const float4 p4 = j == ks ? make_float4(__uint_as_float(rg[0]), __uint_as_float(rg[1]),
+                                                      __uint_as_float(rg[2]), __uint_as_float(rg[3]))
+                                        : __ldcg(reinterpret_cast<const float4*>(srcp + j * plane) + g);
+              if (j == 0) {
+                t4 = p4;
+              } else {
+                t4.x = __fadd_rn(t4.x, p4.x);
+                t4.y = __fadd_rn(t4.y, p4.y);
+                t4.z = __fadd_rn(t4.z, p4.z);
+                t4.w = __fadd_rn(t4.w, p4.w);
+              }
+            }
+            rg[0] = __float_as_uint(t4.x);
+            rg[1] = __float_as_uint(t4.y);
+            rg[2] = __float_as_uint(t4.z);
+            rg[3] = __float_as_uint(t4.w);
+          }
+        }
         uint32_t o[16];
 #pragma unroll
         for (int j = 0; j < 16; j += 2) {
@@ -357,34 +456,42 @@ cudaError_t launch_epi(int epilogue, const CUtensorMap& ta, const CUtensorMap& t
   }
 }
 
-// Feature tile of the smallest cost: waves of the persistent grid x bytes each CTA receives
-// per 64-element K block (16 KB of activations + 128 bytes per feature).
-int auto_feature_tile(int M, int N) {
+// Plan of the smallest cost: waves of the persistent grid x bytes each CTA receives --
+// per 64-element K block 16 KB of activations + 128 bytes per feature, and with a K split
+// about one fp32 [128 x BN] plane per split for the partials written and read back.
+void auto_plan(int M, int N, int K, int& bn_out, int& splits_out) {
   const int sms = ffb::sm_count();
-  const int ttiles = (M + BM - 1) / BM;
-  int best = 256;
+  const long long ttiles = (M + BM - 1) / BM, nkb = (K + BKE - 1) / BKE;
   long long best_cost = -1;
-  for (int bn : {256, 128, 64}) {
-    const long long tiles = (long long)ttiles * ((N + bn - 1) / bn);
-    const long long waves = (tiles + sms - 1) / sms;
-    const long long cost = waves * (A_BYTES + 128LL * bn);
-    if (best_cost < 0 || cost < best_cost) {
-      best = bn;
-      best_cost = cost;
+  bn_out = 256;
+  splits_out = 1;
+  for (int sp = 1; sp <= 4 && sp <= nkb; ++sp)
+    for (int bn : {256, 128, 64}) {
+      const long long tiles = ttiles * ((N + bn - 1) / bn) * sp;
+      const long long waves = (tiles + sms - 1) / sms;
+      const long long per_cta = ((nkb + sp - 1) / sp) * (A_BYTES + 128LL * bn) + (sp > 1 ? 512LL * bn * sp : 0);
+      const long long cost = waves * per_cta;
+      if (best_cost < 0 || cost < best_cost) {
+        best_cost = cost;
+        bn_out = bn;
+        splits_out = sp;
+      }
     }
-  }
-  return best;
 }
 
 }  // namespace
 
-extern "C" int ffb_bf16_gemm_feature_tile(int M, int N) {
-  if (M <= 0 || N <= 0) return 0;
-  return auto_feature_tile(M, N);
+extern "C" int ffb_bf16_gemm_plan(int M, int N, int K, int* plan) {
+  FFB_REQUIRE(plan != nullptr, "ffb_bf16_gemm_plan: NULL plan");
+  FFB_REQUIRE(M > 0 && N > 0 && K > 0, "ffb_bf16_gemm_plan: bad shape M=%d N=%d K=%d", M, N, K);
+  auto_plan(M, N, K, plan[0], plan[1]);
+  plan[2] = ((M + BM - 1) / BM) * ((N + plan[0] - 1) / plan[0]);
+  return FFB_OK;
 }
 
 extern "C" int ffb_bf16_gemm(const uint16_t* a, const uint16_t* w, const uint16_t* bias, const uint16_t* res,
-                             int epilogue, uint16_t* out, int feature_tile, int M, int N, int K, void* stream) {
+                             int epilogue, uint16_t* out, int feature_tile, int splits, float* ws, uint32_t* counters,
+                             int M, int N, int K, void* stream) {
   FFB_REQUIRE(a && w && out, "ffb_bf16_gemm: NULL operand");
   FFB_REQUIRE(M > 0 && N > 0 && K > 0, "ffb_bf16_gemm: bad shape M=%d N=%d K=%d", M, N, K);
   FFB_REQUIRE(K % 8 == 0 && N % 8 == 0, "ffb_bf16_gemm: K=%d and N=%d must be multiples of 8", K, N);
@@ -395,7 +502,16 @@ extern "C" int ffb_bf16_gemm(const uint16_t* a, const uint16_t* w, const uint16_
                   epilogue == FFB_EPI_BIAS_GELU_ERF,
               "ffb_bf16_gemm: unknown epilogue %d", epilogue);
   FFB_REQUIRE(epilogue != FFB_EPI_BIAS_RES || res != nullptr, "ffb_bf16_gemm: BIAS_RES needs res");
-  const int bn = feature_tile > 0 ? feature_tile : auto_feature_tile(M, N);
+  const int nkb = (K + BKE - 1) / BKE;
+  FFB_REQUIRE(splits >= 1 && splits <= 16 && splits <= nkb, "ffb_bf16_gemm: splits=%d outside [1, %d]", splits,
+              nkb < 16 ? nkb : 16);
+  FFB_REQUIRE(splits == 1 || (ws && counters && ffb::aligned(ws, 16) && ffb::aligned(counters, 4)),
+              "ffb_bf16_gemm: splits > 1 needs ws (16-byte aligned) and counters");
+  int bn = feature_tile;
+  if (bn <= 0) {
+    int sp;
+    auto_plan(M, N, K, bn, sp);
+  }
   FFB_REQUIRE(bn == 64 || bn == 128 || bn == 256, "ffb_bf16_gemm: feature tile %d (64, 128 or 256)", bn);
   CUtensorMap ta, tw, to;
   int rc = ffb::make_tmap_2d(&ta, a, (uint64_t)M, (uint64_t)K, (uint64_t)K * 2, BM, BKE, 2);
@@ -405,11 +521,14 @@ extern "C" int ffb_bf16_gemm(const uint16_t* a, const uint16_t* w, const uint16_
   BArgs ba = {};
   ba.bias = bias;
   ba.res = res;
+  ba.ws = ws;
+  ba.counters = counters;
+  ba.splits = splits;
   ba.M = M;
   ba.N = N;
   ba.K = K;
   ba.n_ttiles = (M + BM - 1) / BM;
-  ba.n_tiles = ba.n_ttiles * ((N + bn - 1) / bn);
+  ba.n_tiles = ba.n_ttiles * ((N + bn - 1) / bn) * splits;
   const int sms = ffb::sm_count();
   const int grid = ba.n_tiles < sms ? ba.n_tiles : sms;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);

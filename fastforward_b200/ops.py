@@ -326,10 +326,11 @@ _VISION_EPI = {"bias": L.EPI_BIAS, "res": L.EPI_BIAS_RES, "gelu_tanh": L.EPI_BIA
                "gelu_erf": L.EPI_BIAS_GELU_ERF}
 
 
-def vision_linear(x, weight, bias=None, epilogue="bias", res=None, out=None, feature_tile=0):
+def vision_linear(x, weight, bias=None, epilogue="bias", res=None, out=None, feature_tile=0, splits=None):
     """bf16 linear of the vision tower on tcgen05: epilogue "bias" = bf16(x W^T + b), "res" =
     bf16(res + that), "gelu_tanh" / "gelu_erf" = bf16(gelu(that)) (nn.Linear + the residual
-    add or activation that follows it in the HF vision blocks and mergers)."""
+    add or activation that follows it in the HF vision blocks and mergers).  feature_tile /
+    splits: 0 / None = the library's plan."""
     _need(epilogue in _VISION_EPI, f"unknown epilogue {epilogue!r}")
     _bf16_cuda(x, weight)
     _need(x.dim() == 2 and weight.dim() == 2 and x.shape[1] == weight.shape[1], "x [M, K], weight [N, K]")
@@ -343,8 +344,15 @@ def vision_linear(x, weight, bias=None, epilogue="bias", res=None, out=None, fea
         _need(res is not None and res.shape == (m, n) and res.is_contiguous(), "res [M, N] contiguous")
         _bf16_cuda(res)
     out = torch.empty(m, n, dtype=BF16, device=x.device) if out is None else out
-    call("ffb_bf16_gemm", ptr(x), ptr(weight), ptr(bias), ptr(res), _VISION_EPI[epilogue], ptr(out),
-         int(feature_tile), m, n, k, stream_ptr(x.device))
+    tile, plan_splits, _ = L.bf16_gemm_plan(m, n, k)
+    tile = int(feature_tile) or tile
+    splits = plan_splits if splits is None else int(splits)
+    ws = counters = None
+    if splits > 1:
+        ws = torch.empty(splits, m, n, dtype=torch.float32, device=x.device)
+        counters = torch.zeros(-(-m // 128) * -(-n // tile), dtype=torch.int32, device=x.device)
+    call("ffb_bf16_gemm", ptr(x), ptr(weight), ptr(bias), ptr(res), _VISION_EPI[epilogue], ptr(out), tile, splits,
+         ptr(ws), ptr(counters), m, n, k, stream_ptr(x.device))
     return out
 
 

@@ -97,6 +97,16 @@ class _Buffers:
         self.mfc = z(n_p // m2, c * m2)
         self.merged = z(n_p // m2, v.out_hidden)
         self.deep = [z(n_p // m2, v.out_hidden) for _ in v.deepstack]
+        # the linears' plans (feature tile, K splits) and one split-K scratch for all of them
+        # (they run one after another on the stream; each leaves its counters zero)
+        g = n_p // m2
+        shapes = [(n_p, c, 3 * v.temporal * v.patch * v.patch), (n_p, 3 * c, c), (n_p, c, c), (n_p, v.inter, c),
+                  (n_p, c, v.inter), (g, c * m2, c * m2), (g, v.out_hidden, c * m2)]
+        self.plans = {sh: L.bf16_gemm_plan(*sh) for sh in shapes}
+        ws = max((sp * m * n for (m, n, _), (_, sp, _) in self.plans.items() if sp > 1), default=4)
+        cnt = max((c_n for (_, sp, c_n) in self.plans.values() if sp > 1), default=1)
+        self.ws = torch.zeros(ws, dtype=torch.float32, device=device)
+        self.counters = torch.zeros(cnt, dtype=torch.int32, device=device)
 
 
 class VisionTower:
@@ -167,7 +177,10 @@ class VisionTower:
     def _linear(self, x, wt, bias, epi, out, res=None):
         m, k = x.shape
         n = wt.shape[0]
-        call("ffb_bf16_gemm", ptr(x), ptr(wt), ptr(bias), ptr(res), epi, ptr(out), 0, m, n, k, self._s)
+        buf = self.bufs[self._n_p]
+        tile, splits, _ = buf.plans[(m, n, k)]
+        call("ffb_bf16_gemm", ptr(x), ptr(wt), ptr(bias), ptr(res), epi, ptr(out), tile, splits, ptr(buf.ws),
+             ptr(buf.counters), m, n, k, self._s)
 
     def _norm(self, x, wt, bias, out, rows, c):
         call("ffb_layernorm", ptr(x), ptr(wt), ptr(bias), float(self.v.eps), ptr(out), rows, c, self._s)
@@ -190,6 +203,7 @@ class VisionTower:
         pos, cos, sin = self.geometry(grid_h, grid_w)
         buf = self.buffers(n_p)
         self._s = stream_ptr(self.device)
+        self._n_p = n_p
         c, d, heads = v.hidden, v.head_dim, v.heads
         act = L.EPI_BIAS_GELU_TANH if self.act == "gelu_tanh" else L.EPI_BIAS_GELU_ERF
         self._linear(buf.pixels, self.patch_w, self.patch_b, L.EPI_BIAS_RES, buf.h, res=pos)

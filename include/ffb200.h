@@ -346,16 +346,22 @@ int ffb_pack_rgb_batch(const uint8_t* rgb, uint16_t* pixels, int n, int height, 
  * [P, 1536] x [C, 1536]^T product); the epilogues fold in the residual add that follows
  * attn.proj / mlp.linear_fc2 (and the position embedding after the patch embedding), and the
  * GELU after linear_fc1 (tanh form in the blocks, erf form in the mergers; own polynomial
- * tanh and Abramowitz-Stegun 7.1.26 erf, within 2e-7 of the exact functions).
+ * tanh and Abramowitz-Stegun 7.1.26 erf, within 5e-7 of the exact functions).
  * a [M,K], w [N,K] (K-major, as nn.Linear stores it), bias [N] or NULL, res [M,N]
- * (FFB_EPI_BIAS_RES), out [M,N], all bf16 and 16-byte aligned; K and N multiples of 8.
- * feature_tile 64 / 128 / 256 (0 = automatic, see ffb_bf16_gemm_feature_tile). */
+ * (FFB_EPI_BIAS_RES, may alias out), out [M,N], all bf16 and 16-byte aligned; K and N
+ * multiples of 8.  feature_tile 64 / 128 / 256 (0 = the plan's).  splits > 1 splits K: each
+ * split writes an fp32 partial plane to ws [splits][M][N] (16-byte aligned) and the split
+ * that finishes last sums the planes in split order ((p0 + p1) + p2 ...) and runs the
+ * epilogue; counters [ceil(M/128) * ceil(N/feature_tile)] uint32 must be zero before the
+ * first call and are left zero by every call that completes. */
 int ffb_bf16_gemm(const uint16_t* a, const uint16_t* w, const uint16_t* bias, const uint16_t* res,
-                  int epilogue, uint16_t* out, int feature_tile, int M, int N, int K, void* stream);
+                  int epilogue, uint16_t* out, int feature_tile, int splits, float* ws,
+                  uint32_t* counters, int M, int N, int K, void* stream);
 
-/* The feature tile ffb_bf16_gemm picks for M x N on the current device (no reference
- * counterpart; a host-side query). */
-int ffb_bf16_gemm_feature_tile(int M, int N);
+/* The plan ffb_bf16_gemm uses for M x N x K on the current device: plan[0] = feature tile,
+ * plan[1] = K splits, plan[2] = counters that plan needs (no reference counterpart; a
+ * host-side query). */
+int ffb_bf16_gemm_plan(int M, int N, int K, int* plan);
 
 /* LayerNorm over rows of C: y = bf16(((x - mean) * rstd) * w + b), mean and variance from
  * float64 sums, rstd = 1 / sqrt(var + eps).  Replaces the vision blocks' norm1 / norm2 and

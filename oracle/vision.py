@@ -215,13 +215,20 @@ def layer_norm_k(x, w, b, eps, add=None):
     return y.to(torch.bfloat16)
 
 
-def linear_k(x, w, b, epilogue="bias", res=None):
+def linear_k(x, w, b, epilogue="bias", res=None, splits=1):
     """The bf16 linear `ffb_bf16_gemm`: v = fp32(acc + b) with acc the tensor core's fp32
-    accumulator of x [M, K] . w [N, K]^T; epilogue "bias": bf16(v); "res": bf16(res +
-    bf16(v)); "gelu_tanh" / "gelu_erf": bf16(gelu(bf16(v))) with the kernel's GELU
-    (oracle/act.c).  bf16 in, bf16 out."""
+    accumulator of x [M, K] . w [N, K]^T -- with a K split, the splits' accumulators over
+    their ranges of 64-element K blocks summed in split order -- ; epilogue "bias": bf16(v);
+    "res": bf16(res + bf16(v)); "gelu_tanh" / "gelu_erf": bf16(gelu(bf16(v))) with the
+    kernel's GELU (oracle/act.c).  bf16 in, bf16 out."""
     from . import _tc
-    acc = _tc.acc_bf16(x, w, 0, x.shape[1])
+    k = x.shape[1]
+    nkb = -(-k // 64)
+    acc = None
+    for j in range(splits):
+        k0, k1 = j * nkb // splits * 64, min((j + 1) * nkb // splits * 64, k)
+        part = _tc.acc_bf16(x, w, k0, k1)
+        acc = part if acc is None else acc + part
     v = acc + (b.float() if b is not None else 0.0)
     if epilogue == "bias":
         y = v
@@ -257,39 +264,50 @@ def _rope_heads(qkv, cos, sin, heads, d, dp=128):
     return out
 
 
-def _merger_k(p, prefix, h, dims, post_shuffle):
+def _merger_k(p, prefix, h, dims, post_shuffle, sp):
     c4 = dims.hidden * dims.merge * dims.merge
     if post_shuffle:
         x = layer_norm_k(h.reshape(-1, c4), p[prefix + "norm.weight"], p[prefix + "norm.bias"], dims.eps)
     else:
         x = layer_norm_k(h, p[prefix + "norm.weight"], p[prefix + "norm.bias"], dims.eps).reshape(-1, c4)
-    x = linear_k(x, p[prefix + "linear_fc1.weight"], p[prefix + "linear_fc1.bias"], "gelu_erf")
-    return linear_k(x, p[prefix + "linear_fc2.weight"], p[prefix + "linear_fc2.bias"])
+    w1, w2 = p[prefix + "linear_fc1.weight"], p[prefix + "linear_fc2.weight"]
+    x = linear_k(x, w1, p[prefix + "linear_fc1.bias"], "gelu_erf", splits=sp(x, w1))
+    return linear_k(x, w2, p[prefix + "linear_fc2.bias"], splits=sp(x, w2))
 
 
-def vision_tower_k(p, dims, pixels, grid_h, grid_w):
+def vision_tower_k(p, dims, pixels, grid_h, grid_w, splits=None):
     """`vision_tower` with the CUDA kernels' arithmetic (bf16 activations between kernels).
-    p: bf16 parameters by checkpoint name (without `model.visual.`); pixels [P, 1536] bf16.
+    p: bf16 parameters by checkpoint name (without `model.visual.`); pixels [P, 1536] bf16;
+    splits: {(M, N, K): K splits} of the linears (the GPU's plans; default none split).
     Returns (merged [P/4, out_hidden], [deepstack features]) bf16."""
     p = {k: v.to(torch.bfloat16) for k, v in p.items()}
+    plan = splits or {}
+
+    def sp(x, w):
+        return plan.get((x.shape[0], w.shape[0], x.shape[1]), 1)
     n_p = grid_h * grid_w
     heads, d = dims.heads, dims.head_dim
     pos, cos, sin = vision_geometry(p["pos_embed.weight"], grid_h, grid_w, d, dims.theta, dims.merge)
     act = "gelu_tanh" if dims.act == "gelu_pytorch_tanh" else "gelu_erf"
-    h = linear_k(pixels.to(torch.bfloat16), p["patch_embed.proj.weight"].reshape(dims.hidden, -1),
-                 p["patch_embed.proj.bias"], "res", pos)
+    pixels = pixels.to(torch.bfloat16)
+    w_pe = p["patch_embed.proj.weight"].reshape(dims.hidden, -1)
+    h = linear_k(pixels, w_pe, p["patch_embed.proj.bias"], "res", pos, splits=sp(pixels, w_pe))
     deep = []
     for j in range(dims.depth):
         b = f"blocks.{j}."
         x = layer_norm_k(h, p[b + "norm1.weight"], p[b + "norm1.bias"], dims.eps)
-        qkv = linear_k(x, p[b + "attn.qkv.weight"], p[b + "attn.qkv.bias"])
+        w = p[b + "attn.qkv.weight"]
+        qkv = linear_k(x, w, p[b + "attn.qkv.bias"], splits=sp(x, w))
         q, k, v = _rope_heads(qkv, cos, sin, heads, d)
         o = attention_full_k(q, k, v, d, d ** -0.5)
-        h = linear_k(o, p[b + "attn.proj.weight"], p[b + "attn.proj.bias"], "res", h)
+        w = p[b + "attn.proj.weight"]
+        h = linear_k(o, w, p[b + "attn.proj.bias"], "res", h, splits=sp(o, w))
         x = layer_norm_k(h, p[b + "norm2.weight"], p[b + "norm2.bias"], dims.eps)
-        x = linear_k(x, p[b + "mlp.linear_fc1.weight"], p[b + "mlp.linear_fc1.bias"], act)
-        h = linear_k(x, p[b + "mlp.linear_fc2.weight"], p[b + "mlp.linear_fc2.bias"], "res", h)
+        w = p[b + "mlp.linear_fc1.weight"]
+        x = linear_k(x, w, p[b + "mlp.linear_fc1.bias"], act, splits=sp(x, w))
+        w = p[b + "mlp.linear_fc2.weight"]
+        h = linear_k(x, w, p[b + "mlp.linear_fc2.bias"], "res", h, splits=sp(x, w))
         if j in dims.deepstack:
             i = dims.deepstack.index(j)
-            deep.append(_merger_k(p, f"deepstack_merger_list.{i}.", h, dims, post_shuffle=True))
-    return _merger_k(p, "merger.", h, dims, post_shuffle=False), deep
+            deep.append(_merger_k(p, f"deepstack_merger_list.{i}.", h, dims, True, sp))
+    return _merger_k(p, "merger.", h, dims, False, sp), deep

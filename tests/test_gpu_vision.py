@@ -34,19 +34,22 @@ def _rand(shape, g, std=1.0):
 # ---------------------------------------------------------------------------- linear
 
 @pytest.mark.parametrize("epilogue", ["bias", "res", "gelu_tanh", "gelu_erf"])
-@pytest.mark.parametrize("m,n,k,tile", [(300, 136, 200, 0), (128, 256, 64, 256), (1, 64, 1536, 64),
-                                        (517, 1152, 1152, 128), (256, 4304, 72, 0)])
-def test_bf16_linear_bit_exact(epilogue, m, n, k, tile):
+@pytest.mark.parametrize("m,n,k,tile,splits", [(300, 136, 200, 0, 1), (128, 256, 64, 256, 1), (1, 64, 1536, 64, 1),
+                                               (517, 1152, 1152, 128, 1), (256, 4304, 72, 0, 1),
+                                               (300, 136, 1000, 64, 3), (1024, 1024, 4096, 128, 2),
+                                               (200, 520, 4304, 256, 4)])
+def test_bf16_linear_bit_exact(epilogue, m, n, k, tile, splits):
     """Every epilogue, ragged M / N / K (zero-filled K tail, clipped stores), each feature
-    tile: identical bytes to the tensor-core accumulation model + the restated epilogue."""
+    tile, K splits (last-arriver reduction in split order): identical bytes to the
+    tensor-core accumulation model + the restated epilogue."""
     g = torch.Generator().manual_seed(m * 7 + n + k)
     x, w = _rand((m, k), g), _rand((n, k), g, k ** -0.5)
     b = _rand((n,), g, 0.5)
     res = _rand((m, n), g) if epilogue == "res" else None
     out = ops.vision_linear(x.to(DEV), w.to(DEV), b.to(DEV), epilogue, res.to(DEV) if res is not None else None,
-                            feature_tile=tile)
+                            feature_tile=tile, splits=splits)
     torch.cuda.synchronize()
-    ref = oracle.linear_k(x, w, b, epilogue, res)
+    ref = oracle.linear_k(x, w, b, epilogue, res, splits=splits)
     assert _bits_equal(out, ref), (out.cpu().float() - ref.float()).abs().max()
 
 
@@ -55,15 +58,19 @@ def test_bf16_linear_residual_in_place_and_no_bias():
     g = torch.Generator().manual_seed(5)
     x, w, h = _rand((384, 512), g), _rand((1024, 512), g, 0.05), _rand((384, 1024), g)
     hd = h.to(DEV)
-    ops.vision_linear(x.to(DEV), w.to(DEV), None, "res", hd, out=hd)
+    ops.vision_linear(x.to(DEV), w.to(DEV), None, "res", hd, out=hd, splits=1)
     torch.cuda.synchronize()
     assert _bits_equal(hd, oracle.linear_k(x, w, None, "res", h))
+    hd = h.to(DEV)
+    ops.vision_linear(x.to(DEV), w.to(DEV), None, "res", hd, out=hd, splits=2)
+    torch.cuda.synchronize()
+    assert _bits_equal(hd, oracle.linear_k(x, w, None, "res", h, splits=2))
 
 
 def test_bf16_linear_tile_choice_does_not_change_bytes():
     g = torch.Generator().manual_seed(6)
     x, w, b = _rand((700, 1024), g), _rand((3072, 1024), g, 0.03), _rand((3072,), g)
-    outs = [ops.vision_linear(x.to(DEV), w.to(DEV), b.to(DEV), "bias", feature_tile=t) for t in (64, 128, 256)]
+    outs = [ops.vision_linear(x.to(DEV), w.to(DEV), b.to(DEV), "bias", feature_tile=t, splits=1) for t in (64, 128, 256)]
     torch.cuda.synchronize()
     assert _bits_equal(outs[0], outs[1]) and _bits_equal(outs[0], outs[2])
 
@@ -143,12 +150,16 @@ def _tower_case(vdims, grid, seed=0):
     return p, pixels
 
 
+def _splits(vt, grid):
+    return {sh: sp for sh, (_, sp, _) in vt.bufs[grid[0] * grid[1]].plans.items()}
+
+
 def _check_tower(vt, p, vdims, pixels, grid, graph):
     run = vt.replay if graph else vt.forward
     merged, deep = run(pixels.to(DEV), *grid)
     torch.cuda.synchronize()
     merged, deep = merged.cpu().clone(), [d.cpu().clone() for d in deep]
-    rm, rd = oracle.vision_tower_k(p, vdims, pixels, *grid)
+    rm, rd = oracle.vision_tower_k(p, vdims, pixels, *grid, splits=_splits(vt, grid))
     assert len(deep) == len(rd) == len(vdims.deepstack)
     assert _bits_equal(merged, rm), (merged.float() - rm.float()).abs().max()
     for a, b in zip(deep, rd):
@@ -194,7 +205,7 @@ def test_vision_tower_encodes_a_canvas():
     vt = VisionTower(v, p, device=DEV)
     merged, deep = vt.encode(rgb.to(DEV))
     torch.cuda.synchronize()
-    rm, rd = oracle.vision_tower_k(p, v, oracle.pack_rgb(rgb), 16, 24)
+    rm, rd = oracle.vision_tower_k(p, v, oracle.pack_rgb(rgb), 16, 24, splits=_splits(vt, (16, 24)))
     assert _bits_equal(merged, rm) and _bits_equal(deep[0], rd[0])
 
 
@@ -230,7 +241,7 @@ def test_predict_runs_the_vision_tower_end_to_end(tmp_path):
     v = acc.vision.v
     p = make_vision_bf16(v, seed=5, device=DEV)
     p = {k: t.cpu() for k, t in p.items()}
-    merged, deep = oracle.vision_tower_k(p, v, oracle.pack_rgb(rgb), 16, 16)
+    merged, deep = oracle.vision_tower_k(p, v, oracle.pack_rgb(rgb), 16, 16, splits=_splits(acc.vision, (16, 16)))
     assert _bits_equal(r.visual, merged) and all(_bits_equal(a, b) for a, b in zip(r.deep, deep))
     dims = MODELS["2B"]
     src = make_model_bf16(dims, seed=3, device=DEV, layers=2)

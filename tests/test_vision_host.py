@@ -85,13 +85,17 @@ def test_kernel_arithmetic_tower_close_to_module_semantics():
 
 def test_vision_entries_reject_bad_arguments():
     with pytest.raises(ValueError, match="multiples of 8"):
-        L.call("ffb_bf16_gemm", 16, 16, None, None, L.EPI_BIAS, 16, 0, 16, 20, 64, None)
+        L.call("ffb_bf16_gemm", 16, 16, None, None, L.EPI_BIAS, 16, 0, 1, None, None, 16, 20, 64, None)
     with pytest.raises(ValueError, match="epilogue"):
-        L.call("ffb_bf16_gemm", 16, 16, None, None, 99, 16, 0, 16, 16, 64, None)
+        L.call("ffb_bf16_gemm", 16, 16, None, None, 99, 16, 0, 1, None, None, 16, 16, 64, None)
     with pytest.raises(ValueError, match="BIAS_RES"):
-        L.call("ffb_bf16_gemm", 16, 16, None, None, L.EPI_BIAS_RES, 16, 0, 16, 16, 64, None)
+        L.call("ffb_bf16_gemm", 16, 16, None, None, L.EPI_BIAS_RES, 16, 0, 1, None, None, 16, 16, 64, None)
     with pytest.raises(ValueError, match="feature tile"):
-        L.call("ffb_bf16_gemm", 16, 16, None, None, L.EPI_BIAS, 16, 96, 16, 16, 64, None)
+        L.call("ffb_bf16_gemm", 16, 16, None, None, L.EPI_BIAS, 16, 96, 1, None, None, 16, 16, 64, None)
+    with pytest.raises(ValueError, match="splits"):
+        L.call("ffb_bf16_gemm", 16, 16, None, None, L.EPI_BIAS, 16, 0, 2, None, None, 16, 16, 640, None)
+    with pytest.raises(ValueError, match="splits"):
+        L.call("ffb_bf16_gemm", 16, 16, None, None, L.EPI_BIAS, 16, 0, 3, None, None, 16, 16, 128, None)
     with pytest.raises(ValueError, match="head dim"):
         L.call("ffb_attention_full", 16, 16, 16, 16, 64, 4, 12, 0.1, None)
     with pytest.raises(ValueError, match="multiple of 8"):
@@ -102,12 +106,16 @@ def test_vision_entries_reject_bad_arguments():
         L.call("ffb_vision_rope", 16, 16, 16, 4, 2, 9, 128, 16, 16, 16, None)
 
 
-def test_feature_tile_choice():
-    """The automatic feature tile fills the machine: 1024 patches x 1024 features -> 64-wide
-    tiles (128 tiles), 1024 x 4096 -> 256-wide (128 tiles)."""
-    assert L.lib().ffb_bf16_gemm_feature_tile(1024, 1024) == 64
-    assert L.lib().ffb_bf16_gemm_feature_tile(1024, 4096) == 256
-    assert L.lib().ffb_bf16_gemm_feature_tile(0, 4096) == 0
+def test_linear_plans():
+    """The plan fills the machine in one wave with the fewest bytes per CTA (no GPU here: the
+    library assumes 148 SMs): qkv / fc1 256-wide tiles, proj 64-wide, fc2 (K = 4096)
+    128-wide with a 2-way K split; the counters match the plan's output tiles."""
+    assert L.bf16_gemm_plan(1024, 3072, 1024) == (256, 1, 96)
+    assert L.bf16_gemm_plan(1024, 4096, 1024) == (256, 1, 128)
+    assert L.bf16_gemm_plan(1024, 1024, 1024)[:2] == (64, 1)
+    assert L.bf16_gemm_plan(1024, 1024, 4096) == (128, 2, 64)
+    with pytest.raises(ValueError, match="bad shape"):
+        L.bf16_gemm_plan(0, 4096, 64)
 
 
 def test_read_canvas_formats(tmp_path):
