@@ -456,27 +456,27 @@ cudaError_t launch_epi(int epilogue, const CUtensorMap& ta, const CUtensorMap& t
   }
 }
 
-// Plan of the smallest cost: waves of the persistent grid x bytes each CTA receives --
-// per 64-element K block 16 KB of activations + 128 bytes per feature, and with a K split
-// about one fp32 [128 x BN] plane per split for the partials written and read back.
+// Plan of the smallest cost: waves of the persistent grid x bytes each CTA receives per
+// 64-element K block (16 KB of activations + 128 bytes per feature).  The plan never splits
+// K: measured at the vision tower's shapes (CUDA-graph replays, B200), every split plan was
+// slower than the best unsplit one -- a CTA's mainloop runs ~0.3 us per K block almost
+// independently of the tile width, and the partial planes' write / fence / read-back cost
+// more than the shorter K range saves.  Splits stay available by argument.
 void auto_plan(int M, int N, int K, int& bn_out, int& splits_out) {
   const int sms = ffb::sm_count();
   const long long ttiles = (M + BM - 1) / BM, nkb = (K + BKE - 1) / BKE;
   long long best_cost = -1;
   bn_out = 256;
   splits_out = 1;
-  for (int sp = 1; sp <= 4 && sp <= nkb; ++sp)
-    for (int bn : {256, 128, 64}) {
-      const long long tiles = ttiles * ((N + bn - 1) / bn) * sp;
-      const long long waves = (tiles + sms - 1) / sms;
-      const long long per_cta = ((nkb + sp - 1) / sp) * (A_BYTES + 128LL * bn) + (sp > 1 ? 512LL * bn * sp : 0);
-      const long long cost = waves * per_cta;
-      if (best_cost < 0 || cost < best_cost) {
-        best_cost = cost;
-        bn_out = bn;
-        splits_out = sp;
-      }
+  for (int bn : {256, 128, 64}) {
+    const long long tiles = ttiles * ((N + bn - 1) / bn);
+    const long long waves = (tiles + sms - 1) / sms;
+    const long long cost = waves * nkb * (A_BYTES + 128LL * bn);
+    if (best_cost < 0 || cost < best_cost) {
+      best_cost = cost;
+      bn_out = bn;
     }
+  }
 }
 
 }  // namespace

@@ -108,12 +108,12 @@ def test_vision_entries_reject_bad_arguments():
 
 def test_linear_plans():
     """The plan fills the machine in one wave with the fewest bytes per CTA (no GPU here: the
-    library assumes 148 SMs): qkv / fc1 256-wide tiles, proj 64-wide, fc2 (K = 4096)
-    128-wide with a 2-way K split; the counters match the plan's output tiles."""
+    library assumes 148 SMs): qkv / fc1 256-wide tiles, proj / fc2 64-wide, no K split; the
+    counters match the plan's output tiles."""
     assert L.bf16_gemm_plan(1024, 3072, 1024) == (256, 1, 96)
     assert L.bf16_gemm_plan(1024, 4096, 1024) == (256, 1, 128)
-    assert L.bf16_gemm_plan(1024, 1024, 1024)[:2] == (64, 1)
-    assert L.bf16_gemm_plan(1024, 1024, 4096) == (128, 2, 64)
+    assert L.bf16_gemm_plan(1024, 1024, 1024) == (64, 1, 128)
+    assert L.bf16_gemm_plan(1024, 1024, 4096) == (64, 1, 128)
     with pytest.raises(ValueError, match="bad shape"):
         L.bf16_gemm_plan(0, 4096, 64)
 
