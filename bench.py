@@ -411,7 +411,7 @@ def run_ours(args):
             torch.cuda.profiler.stop()
             if rank == 0:
                 print(json.dumps(dict(ncu_range="one graph replay", workload=args.workload, layers=pm.depth,
-                                      launches=eng.launches_per_forward())), flush=True)
+                                      launches=eng.launches_per_forward(T))), flush=True)
             return
         s = torch.cuda.current_stream()
         starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
@@ -532,7 +532,7 @@ def run_ours(args):
                               f"{dims.layers - 1} layers + tail; fp32 GEMMs of the quantised weights")
 
     clk_sum = clk.summary()
-    launches = eng.launches_per_forward() * args.steps
+    launches = eng.launches_per_forward(T) * args.steps
     extra = {}
     if world == 1 and args.workload == "4B-fp8-T320" and not args.no_extra:
         # the image side of the request: the 4B vision tower on the headline's 512 x 512 canvas
@@ -899,7 +899,8 @@ def stream_measure(args, workload, world, rank, local, dev, n_req=None):
                     e2e=dict(value=world * n_req / e2e_s, unit="req/s", h2d_bytes_per_step=h2d,
                              d2h_bytes_per_step=d2h, api="Accelerator.prefill_score",
                              host_latency_ms=dict(p50=pct(host_lat, 0.5), p99=pct(host_lat, 0.99))),
-                    gpu_launches=sum(eng.launches_per_forward() for _ in reqs), clocks=clk_sum, cpu_baseline=None)
+                    gpu_launches=sum(eng.launches_per_forward(r["lay"].bucket) for r in reqs), clocks=clk_sum,
+                    cpu_baseline=None)
     entries.clear()
     eng.graphs.clear()
     del eng, pm, reqs, dev_reqs

@@ -13,7 +13,7 @@
 
 int ffb_attention_tc(const uint16_t* q, const uint16_t* k, const uint16_t* v, const int64_t* sel, int q_gather,
                      int S, const int* key_lo, void* out, int T, int HQ, int HK, float scale, float out_inv,
-                     int causal, int out_cols, cudaStream_t stream);
+                     int causal, int out_cols, void* rq_sync, float* qscale, cudaStream_t stream);
 
 extern "C" int ffb_attention_segmented(const uint16_t* q, const uint16_t* k, const uint16_t* v,
                                        const int64_t* positions, int q_gather, const int* key_lo, uint16_t* out, int S,
@@ -27,8 +27,8 @@ extern "C" int ffb_attention_segmented(const uint16_t* q, const uint16_t* k, con
               "ffb_attention: q, k, v and out must be 16-byte aligned");
   FFB_REQUIRE(!key_lo || ffb::aligned(key_lo, 4), "ffb_attention: key_lo alignment");
   FFB_REQUIRE(!positions || ffb::aligned(positions, 8), "ffb_attention: positions alignment");
-  return ffb_attention_tc(q, k, v, positions, q_gather, S, key_lo, out, T, HQ, HK, scale, 0.f, 1, 0,
-                          (cudaStream_t)stream);
+  return ffb_attention_tc(q, k, v, positions, q_gather, S, key_lo, out, T, HQ, HK, scale, 0.f, 1, 0, nullptr,
+                          nullptr, (cudaStream_t)stream);
 }
 
 extern "C" int ffb_attention_fp8(const uint16_t* q, const uint16_t* k, const uint16_t* v, const int* key_lo,
@@ -39,7 +39,7 @@ extern "C" int ffb_attention_fp8(const uint16_t* q, const uint16_t* k, const uin
   FFB_REQUIRE(ffb::aligned(q, 16) && ffb::aligned(k, 16) && ffb::aligned(v, 16) && ffb::aligned(out8, 16),
               "ffb_attention_fp8: alignment");
   FFB_REQUIRE(!key_lo || ffb::aligned(key_lo, 4), "ffb_attention_fp8: key_lo alignment");
-  return ffb_attention_tc(q, k, v, nullptr, 0, T, key_lo, out8, T, HQ, HK, scale, out_inv, 1, 0,
+  return ffb_attention_tc(q, k, v, nullptr, 0, T, key_lo, out8, T, HQ, HK, scale, out_inv, 1, 0, nullptr, nullptr,
                           (cudaStream_t)stream);
 }
 
@@ -55,5 +55,25 @@ extern "C" int ffb_attention_full(const uint16_t* q, const uint16_t* k, const ui
   FFB_REQUIRE(d > 0 && d <= 128 && d % 8 == 0, "ffb_attention_full: head dim %d (8..128, a multiple of 8)", d);
   FFB_REQUIRE(ffb::aligned(q, 16) && ffb::aligned(k, 16) && ffb::aligned(v, 16) && ffb::aligned(out, 16),
               "ffb_attention_full: q, k, v and out must be 16-byte aligned");
-  return ffb_attention_tc(q, k, v, nullptr, 0, T, nullptr, out, T, H, H, scale, 0.f, 0, d, (cudaStream_t)stream);
+  return ffb_attention_tc(q, k, v, nullptr, 0, T, nullptr, out, T, H, H, scale, 0.f, 0, d, nullptr, nullptr,
+                          (cudaStream_t)stream);
+}
+
+extern "C" int ffb_attention_rowwise_sync_bytes(int T) { return T > 0 ? 8 * T + 4 * ((T + 127) / 128) : 0; }
+
+extern "C" int ffb_attention_rowwise(const uint16_t* q, const uint16_t* k, const uint16_t* v, uint8_t* out8,
+                                     float* qscale, void* sync, int T, int HQ, int HK, float scale, void* stream) {
+  FFB_REQUIRE(q && k && v && out8 && qscale && sync, "ffb_attention_rowwise: NULL pointer");
+  FFB_REQUIRE(T > 0 && HQ > 0 && HK > 0 && HQ % HK == 0, "ffb_attention_rowwise: bad shape T=%d HQ=%d HK=%d", T, HQ,
+              HK);
+  FFB_REQUIRE(ffb::aligned(q, 16) && ffb::aligned(k, 16) && ffb::aligned(v, 16) && ffb::aligned(out8, 16) &&
+                  ffb::aligned(sync, 16) && ffb::aligned(qscale, 4),
+              "ffb_attention_rowwise: alignment");
+  const long long ctas = (long long)((T + 127) / 128) * HQ;
+  if (ctas > ffb::sm_count())
+    return ffb::fail(FFB_EUNSUPPORTED,
+                     "ffb_attention_rowwise: %lld CTAs exceed the %d SMs (the row maxima need every CTA resident)",
+                     ctas, ffb::sm_count());
+  return ffb_attention_tc(q, k, v, nullptr, 0, T, nullptr, out8, T, HQ, HK, scale, 0.f, 1, 0, sync, qscale,
+                          (cudaStream_t)stream);
 }

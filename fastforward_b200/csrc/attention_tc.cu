@@ -87,7 +87,20 @@ struct TcArgs {
   // > 0: the first out_cols columns of each head's output (the rest is zero padding of the
   // head dimension) go to out[row, h * out_cols + c] by plain stores; 0: TMA tile stores
   int out_cols;
+  // Rowwise FP8 output (causal prefill, every CTA resident at once): e4m3(bf16 output / s)
+  // with s = max(max|row|, 1e-12) / 448 over the row's HQ heads.  rowmax[T] holds
+  // (generation << 32 | max bits) per row, tile_count[T / 128] the arrivals per query tile
+  // (HQ per launch, never reset: the generation is the count / HQ); qscale[T] gets s.
+  unsigned long long* rowmax;
+  uint32_t* tile_count;
+  float* qscale;
 };
+
+__device__ __forceinline__ uint32_t ld_acquire_u32(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
 
 __global__ void __launch_bounds__(THREADS, 1)
     attention_tc_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_k,
@@ -354,8 +367,65 @@ __global__ void __launch_bounds__(THREADS, 1)
     // Output tile [128 rows x 128 columns] bf16 staged as two 128-byte-swizzled [128 x 64]
     // boxes in the P tiles (every P.V has completed: the last fold waited for it), then TMA
     // stores; rows past T are clipped by the store.
-    const bool stage = ok && !*abort_flag;
+    bool stage = ok && !*abort_flag;
     const bool fp8_out = args.out_inv > 0.f;
+    float rscale = 0.f;  // rowwise FP8: this row's scale
+    if (args.rowmax != nullptr) {
+      // Rowwise FP8 output.  o <- the bf16 output values; the row's maximum over this head
+      // (four parts) goes into rowmax tagged with this launch's generation; once every
+      // head's CTA of the query tile has arrived (a bounded wait: the host launches this
+      // only when every CTA of the grid is resident), the row's maximum over all heads gives
+      // the scale -- the bytes of ffb_quantize_fp8 (ROWWISE) on the bf16 output.
+      const int row = q0 + r, tile = q0 / BM;
+      float amax = 0.f;
+      if (stage) {
+        const float rl = __frcp_rn(l);
+#pragma unroll
+        for (int i = 0; i < D / 4; ++i) {
+          o[i] = bf2f(bf16_quotient(o[i], l, rl));
+          amax = fmaxf(amax, fabsf(o[i]));
+        }
+      }
+      float parts[4];
+      const bool xok = exchange(amax, parts);
+      amax = fmaxf(fmaxf(parts[0], parts[1]), fmaxf(parts[2], parts[3]));
+      const uint32_t gen = ld_acquire_u32(args.tile_count + tile) / (uint32_t)args.HQ;
+      if (stage && xok && part == 0 && row < args.T)
+        atomicMax(args.rowmax + row, ((unsigned long long)gen << 32) | __float_as_uint(amax));
+      __threadfence();
+      named_barrier(2, SOFTMAX_WARPS * 32);
+      volatile int* verdict = reinterpret_cast<volatile int*>(xch);  // the exchange buffers are free now
+      if (warp == 2 && lane == 0) {
+        int v = 0;
+        if (stage && xok && !*abort_flag) {
+          const uint32_t old = atomicAdd(args.tile_count + tile, 1u);
+          const uint32_t target = (old / (uint32_t)args.HQ + 1u) * (uint32_t)args.HQ;
+          const uint64_t t0 = global_timer_ns();
+          v = 1;
+          uint32_t polls = 0;
+          while ((int)(ld_acquire_u32(args.tile_count + tile) - target) < 0) {
+            if ((++polls & 63u) == 0 && global_timer_ns() - t0 > 2000000000ull) {
+              v = 0;
+              break;
+            }
+          }
+        }
+        *verdict = v;
+      }
+      named_barrier(2, SOFTMAX_WARPS * 32);
+      if (!*verdict) {
+        *abort_flag = 1;
+        stage = false;
+      } else if (row < args.T) {
+        const unsigned long long m = __ldcg(args.rowmax + row);
+        if ((uint32_t)(m >> 32) != gen) {
+          *abort_flag = 1;
+          stage = false;
+        }
+        rscale = __fdiv_rn(fmaxf(__uint_as_float((uint32_t)m), 1e-12f), 448.f);
+        if (h == 0 && part == 0) args.qscale[row] = rscale;
+      }
+    }
     if (rows_mode) {
       // only the tile's first row is the selected query: its four threads (row 0 of lane
       // quarter 0) store their 32 output columns of output row x with plain stores
@@ -391,6 +461,24 @@ __global__ void __launch_bounds__(THREADS, 1)
           *reinterpret_cast<uint4*>(dst + col) = make_uint4(w[0], w[1], w[2], w[3]);
         }
       }
+    } else if (stage && args.rowmax != nullptr) {
+      // one 128-byte-swizzled [128 rows x 128 B] box of e4m3 in P tile 0, as the static path
+      uint8_t* orow = sp + r * 128;
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        uint32_t w[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          uint32_t word = 0;
+#pragma unroll
+          for (int b = 0; b < 4; ++b)
+            word |= (uint32_t)f2e4m3(clamp448(__fdiv_rn(o[16 * c + 4 * e + b], rscale))) << (8 * b);
+          w[e] = word;
+        }
+        const int chunk = 2 * part + c;
+        *reinterpret_cast<uint4*>(orow + ((chunk ^ (r & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+      fence_proxy_async_smem();
     } else if (stage && fp8_out) {
       // the static FP8 quantisation of the o projection's input, applied to the bf16 output:
       // one 128-byte-swizzled [128 rows x 128 B] box in P tile 0, this part's 32 columns
@@ -465,10 +553,13 @@ __global__ void __launch_bounds__(THREADS, 1)
 // else rows x of a [HQ, S, 128] q), out [S, HQ*128] bf16.  key_lo: per output row.
 // Called by the host entries of attention.cu after their argument checks.
 // causal == 0: every row sees all T keys (sel must be NULL); out_cols > 0: out [T, HQ *
-// out_cols] bf16 holds the first out_cols columns of each head (plain stores).
+// out_cols] bf16 holds the first out_cols columns of each head (plain stores); rq_sync !=
+// NULL: rowwise FP8 output out [T, HQ*128] e4m3 with scales qscale [T], rq_sync the
+// [T] u64 row maxima followed by [ceil(T/128)] u32 tile counters (the caller checked that
+// the grid is resident at once).
 int ffb_attention_tc(const uint16_t* q, const uint16_t* k, const uint16_t* v, const int64_t* sel, int q_gather,
                      int S, const int* key_lo, void* out, int T, int HQ, int HK, float scale, float out_inv,
-                     int causal, int out_cols, cudaStream_t stream) {
+                     int causal, int out_cols, void* rq_sync, float* qscale, cudaStream_t stream) {
   CUtensorMap tq, tk, tv, to;
   const uint64_t q_rows = (sel && !q_gather) ? (uint64_t)S : (uint64_t)T;
   int rc = ffb::make_tmap_3d_bf16(&tq, q, D, q_rows, (uint64_t)HQ, 64, BM);
@@ -478,7 +569,7 @@ int ffb_attention_tc(const uint16_t* q, const uint16_t* k, const uint16_t* v, co
   // (selected rows: plain stores, the map is not used)
   if (sel || out_cols > 0)
     memset(&to, 0, sizeof(to));
-  else if (!rc && out_inv > 0.f)
+  else if (!rc && (out_inv > 0.f || rq_sync))
     rc = ffb::make_tmap_2d(&to, out, (uint64_t)T, (uint64_t)HQ * D, (uint64_t)HQ * D, BM, 128, 1);
   else if (!rc)
     rc = ffb::make_tmap_2d(&to, out, (uint64_t)T, (uint64_t)HQ * D, (uint64_t)HQ * D * 2, BM, 64, 2);
@@ -486,7 +577,8 @@ int ffb_attention_tc(const uint16_t* q, const uint16_t* k, const uint16_t* v, co
   cudaError_t e = ffb::set_smem_attr(reinterpret_cast<const void*>(attention_tc_kernel), SMEM);
   if (e != cudaSuccess) return ffb::fail(FFB_ECUDA, "ffb_attention: %s", cudaGetErrorString(e));
   TcArgs a = {static_cast<uint16_t*>(out), key_lo, sel, q_gather, T, HQ, HK, scale * 1.4426950408889634f, out_inv,
-              causal, out_cols};
+              causal, out_cols, static_cast<unsigned long long*>(rq_sync),
+              rq_sync ? reinterpret_cast<uint32_t*>(static_cast<unsigned long long*>(rq_sync) + T) : nullptr, qscale};
   const dim3 grid(sel ? S : (T + BM - 1) / BM, HQ);
   e = ffb::launch(attention_tc_kernel, grid, dim3(THREADS), SMEM, stream, tq, tk, tv, to, a);
   if (e != cudaSuccess) return ffb::fail(FFB_ECUDA, "ffb_attention: %s", cudaGetErrorString(e));

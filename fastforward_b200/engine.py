@@ -259,6 +259,8 @@ class Buffers:
         self.attn = z(T, hq * d)
         self.o8 = z(T, hq * d, dt=E4M3)
         self.os = z(T, dt=torch.float32)
+        # ffb_attention_rowwise's row maxima + tile counters (zero once; they carry over)
+        self.qsync = z((L.lib().ffb_attention_rowwise_sync_bytes(T) + 7) // 8, dt=torch.int64)
         self.lin_out = z(T, h)
         self.post8 = z(T, h, dt=E4M3)
         self.posts = z(T, dt=torch.float32)
@@ -301,7 +303,8 @@ class BatchBuffers(Buffers):
 class Engine:
     """Runs prefill + choice scoring for one packed model on one device."""
 
-    def __init__(self, model: PackedModel, pdl=True, autotune=True, tp_group=None, fuse="tail", stream_od=True):
+    def __init__(self, model: PackedModel, pdl=True, autotune=True, tp_group=None, fuse="tail", stream_od=True,
+                 attn_q8=True):
         """tp_group: the torch.distributed (NCCL) group of a tensor-parallel model
         (`PackedModel(tp=...)`); o_proj and down_proj partial sums are all-reduced in it.
         fuse (FP8 modes): where an activation quantiser or an add+RMSNorm runs as the fused
@@ -311,7 +314,9 @@ class Engine:
         launches per layer instead of nine; "none" (or False): nowhere.  Every choice
         computes the same bytes.  At T = 320 the separate row kernels are faster than the
         prologues (which run the same row work on fewer warps per row, then meet at a grid
-        barrier), hence the default."""
+        barrier), hence the default.  attn_q8 (per-token scales): the attention kernel writes
+        the o projection's FP8 input and scales itself (`ffb_attention_rowwise`) whenever its
+        grid is resident at once -- the same bytes as attention + `ffb_quantize_fp8`."""
         L.require_cuda()
         self.m = model
         self.d = model.dims
@@ -336,6 +341,11 @@ class Engine:
         # linear after them (`ffb_attention_fp8`, `ffb_fp8_gemm_swiglu_fp8`), so neither
         # activation quantiser has a launch of its own
         self.static_q8 = model.mode == "static" and self.fuse != "none"
+        # per-token scales: attention writes the o projection's FP8 input and scales itself
+        # (`ffb_attention_rowwise`) when its grid fits the SMs at once (single GPU: with tensor
+        # parallelism the scale is a maximum over the ranks)
+        self.attn_q8 = attn_q8 and model.mode == "rowwise" and self.world == 1 and self.fuse != "all"
+        self.sms = torch.cuda.get_device_properties(model.device).multi_processor_count
         # o_proj / down_proj on the weight-stationary schedule (K splits chosen by its cost
         # model, measured 1% faster per 4B request than token-major split-K tiles)
         self.stream_od = stream_od
@@ -593,8 +603,12 @@ class Engine:
             nxt = m.layers[j + 1]
             # ---- attention block
             self._qkv(pl[("full", "qkv")], b, lay, cos, sin, T, int4, rowwise)
+            attn_q8 = self.attn_uses_q8(T)
             if self.static_q8:  # attention writes the o projection's FP8 input itself
                 call("ffb_attention_fp8", ptr(b.yq), ptr(b.yk), ptr(b.yv), None, float(lay.inv["o"]), ptr(b.o8),
+                     T, HQ, HK, scale, self._s)
+            elif attn_q8:  # ... with per-token scales
+                call("ffb_attention_rowwise", ptr(b.yq), ptr(b.yk), ptr(b.yv), ptr(b.o8), ptr(b.os), ptr(b.qsync),
                      T, HQ, HK, scale, self._s)
             else:
                 call("ffb_attention", ptr(b.yq), ptr(b.yk), ptr(b.yv), None, 0, ptr(b.attn), T, T, HQ, HK, scale,
@@ -604,7 +618,8 @@ class Engine:
                 self._w4(p, b.attn, lay.lin["o"], b.lin_out, b.ws)
             else:
                 if not self.static_q8:
-                    self._quant_in(b.attn, qmode, lay.inv["o"], b.o8, b.os, T, HQ * D)
+                    if not attn_q8:
+                        self._quant_in(b.attn, qmode, lay.inv["o"], b.o8, b.os, T, HQ * D)
                     obs(j, "o", b.os, T)
                 self._gemm(p, b.o8, sa(lay, "o", b.os), lay.lin["o"], b.lin_out, b.ws, rowwise)
             self._tp_reduce(p, b.ws)
@@ -934,12 +949,19 @@ class Engine:
         per_layer = 7 if self.static_q8 else 9
         return R + 1 + per_layer * (self.m.depth - 1) + 1 + 1 + 2 + 1 + 1 + 2 + R
 
-    def launches_per_forward(self):
-        """Kernel launches `enqueue` issues (for the bench's gpu_launches count)."""
+    def attn_uses_q8(self, T):
+        """Whether the T-row forward's attention writes the o projection's rowwise FP8 input
+        (`ffb_attention_rowwise`: its ceil(T/128) x HQ CTAs must fit the SMs at once)."""
+        return self.attn_q8 and -(-T // 128) * self.d.hq <= self.sms
+
+    def launches_per_forward(self, T=None):
+        """Kernel launches `enqueue` issues for T rows (for the bench's gpu_launches count)."""
         tail = 6 if self.fuse != "none" else 9  # attention, (quant,) o, gather, (add+norm,) gate/up, (quant,) down, readout
         if self.fuse == "all":  # embed, 5 per layer, the last layer's qkv, tail
             return 1 + 5 * (self.m.depth - 1) + 1 + tail
         per_layer = 7 if self.static_q8 else (9 if self.m.mode != "int4" else 8)
+        if T is not None and not self.static_q8 and self.attn_uses_q8(T):
+            per_layer -= 1
         if self.m.mode == "int4":
             tail = 8
         return 2 + per_layer * (self.m.depth - 1) + 1 + tail

@@ -322,6 +322,44 @@ def test_attention_fp8_is_attention_then_static_quant(T, HQ, HK, segments):
         call("ffb_attention_fp8", ptr(q), ptr(k), ptr(v), None, 0.0, ptr(got8), T, HQ, HK, 128 ** -0.5, _sp())
 
 
+@pytest.mark.parametrize("T,HQ,HK", [(320, 32, 8), (100, 16, 8), (576, 16, 8), (1, 8, 2)])
+def test_attention_rowwise_is_attention_then_rowwise_quant(T, HQ, HK):
+    """`ffb_attention_rowwise` writes exactly the bytes (e4m3 rows and per-row scales) of the
+    causal attention followed by `ffb_quantize_fp8` (ROWWISE): each row's maximum is combined
+    over its HQ head CTAs in-kernel.  Three calls on one sync buffer (its counters carry the
+    generation over), different inputs each time."""
+    g = _g(43)
+    sync = torch.zeros((L.lib().ffb_attention_rowwise_sync_bytes(T) + 15) // 16 * 2, device=DEV, dtype=torch.int64)
+    for rep in range(3):
+        q = (torch.randn((HQ, T, 128), generator=g) * (1 + rep)).to(BF16).to(DEV)
+        k = torch.randn((HK, T, 128), generator=g).to(BF16).to(DEV)
+        v = (torch.randn((HK, T, 128), generator=g) * (3 - rep)).to(BF16).to(DEV)
+        out = torch.empty((T, HQ * 128), device=DEV, dtype=BF16)
+        call("ffb_attention", ptr(q), ptr(k), ptr(v), None, 0, ptr(out), T, T, HQ, HK, 128 ** -0.5, _sp())
+        want8 = torch.empty((T, HQ * 128), device=DEV, dtype=E4M3)
+        want_s = torch.empty(T, device=DEV, dtype=torch.float32)
+        call("ffb_quantize_fp8", ptr(out), L.QUANT_ROWWISE, 0.0, ptr(want8), ptr(want_s), T, HQ * 128, _sp())
+        got8 = torch.full((T + 1, HQ * 128), 0x7F, device=DEV, dtype=torch.uint8)
+        got_s = torch.full((T + 1,), -1.0, device=DEV, dtype=torch.float32)
+        call("ffb_attention_rowwise", ptr(q), ptr(k), ptr(v), ptr(got8), ptr(got_s), ptr(sync), T, HQ, HK,
+             128 ** -0.5, _sp())
+        torch.cuda.synchronize()
+        assert_bytes_equal(got8[:T], want8, "fused attention + rowwise quant")
+        assert torch.equal(got_s[:T], want_s), "row scales"
+        assert bool((got8[T] == 0x7F).all()) and got_s[T].item() == -1.0, "wrote past the last row"
+        assert L.device_error() == 0
+
+
+def test_attention_rowwise_refuses_grids_larger_than_the_sms():
+    """The row maxima meet across the CTAs of a query tile, so the whole grid must be resident:
+    more CTAs than SMs is refused before any launch."""
+    T, HQ = 2048, 32
+    sync = torch.zeros(T * 2, device=DEV, dtype=torch.int64)
+    x = torch.zeros((HQ, T, 128), device=DEV, dtype=BF16)
+    with pytest.raises(L.FFBUnsupported, match="resident"):
+        call("ffb_attention_rowwise", ptr(x), ptr(x), ptr(x), ptr(x), ptr(sync), ptr(sync), T, HQ, 8, 0.1, _sp())
+
+
 def test_swiglu_epilogue_every_bf16_gate():
     """The SwiGLU epilogues look the activation bf16(g / (1 + exp(-g))) up by the bf16 gate's
     bits; the table must equal the formula evaluated on the device (the standalone swiglu
