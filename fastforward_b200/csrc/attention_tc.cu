@@ -518,7 +518,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     named_barrier(1, SOFTMAX_WARPS * 32);
     if (!rows_mode && args.out_cols == 0 && warp == 2 && lane == 0 && !*abort_flag) {
-      if (fp8_out) {
+      if (fp8_out || args.rowmax != nullptr) {  // one [128 x 128 B] e4m3 box
         tma_store_2d(&tmap_o, sp, h * D, q0);
       } else {
         tma_store_2d(&tmap_o, sp, h * D, q0);
