@@ -118,8 +118,10 @@ def test_layer_ops_teacher_forced(name, mode):
     dims, src, req, layout = small_case(MODELS[name], 2, vocab=4096)
     prof = _profile(dims, src, req, layout) if mode == "static" else None
     # unfused launches, so every intermediate buffer still holds layer 0's values when the
-    # hook for layer 1 runs (the fused forward is bit-identical: tests/test_gpu_fused.py)
-    eng = Engine(PackedModel(dims, src, mode=mode, device=DEV, profile=prof), autotune=False, fuse=False)
+    # hook for layer 1 runs (the fused forward is bit-identical: tests/test_gpu_fused.py;
+    # the attention with its own rowwise FP8 output: tests/test_gpu_kernels.py)
+    eng = Engine(PackedModel(dims, src, mode=mode, device=DEV, profile=prof), autotune=False, fuse=False,
+                 attn_q8=False)
     T = layout.bucket
     eng.buffers_for(T)
     for key, p in eng.plans[T].items():          # keep every GEMM output in its bf16 buffer
