@@ -389,10 +389,16 @@ __global__ void __launch_bounds__(THREADS, 1)
       float parts[4];
       const bool xok = exchange(amax, parts);
       amax = fmaxf(fmaxf(parts[0], parts[1]), fmaxf(parts[2], parts[3]));
-      const uint32_t gen = ld_acquire_u32(args.tile_count + tile) / (uint32_t)args.HQ;
-      if (stage && xok && part == 0 && row < args.T)
-        atomicMax(args.rowmax + row, ((unsigned long long)gen << 32) | __float_as_uint(amax));
-      __threadfence();
+      // this launch's generation: the tile's count before this CTA's arrival lies in
+      // [gen * HQ, (gen + 1) * HQ) (the next launch cannot start before this one ends)
+      uint32_t gen = 0;
+      if (part == 0) {
+        gen = *reinterpret_cast<volatile const uint32_t*>(args.tile_count + tile) / (uint32_t)args.HQ;
+        if (stage && xok && row < args.T) {
+          atomicMax(args.rowmax + row, ((unsigned long long)gen << 32) | __float_as_uint(amax));
+          __threadfence();  // the maximum is visible before this CTA's arrival
+        }
+      }
       named_barrier(2, SOFTMAX_WARPS * 32);
       volatile int* verdict = reinterpret_cast<volatile int*>(xch);  // the exchange buffers are free now
       if (warp == 2 && lane == 0) {
@@ -404,15 +410,18 @@ __global__ void __launch_bounds__(THREADS, 1)
           v = 1;
           uint32_t polls = 0;
           while ((int)(ld_acquire_u32(args.tile_count + tile) - target) < 0) {
+            __nanosleep(64);
             if ((++polls & 63u) == 0 && global_timer_ns() - t0 > 2000000000ull) {
               v = 0;
               break;
             }
           }
+          v = v ? (int)(old / (uint32_t)args.HQ) + 1 : 0;  // the generation + 1 (0: failed)
         }
         *verdict = v;
       }
       named_barrier(2, SOFTMAX_WARPS * 32);
+      gen = (uint32_t)(*verdict - 1);
       if (!*verdict) {
         *abort_flag = 1;
         stage = false;
