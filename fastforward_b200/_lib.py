@@ -42,7 +42,7 @@ SIGNATURES = {
     "ffb_attention_segmented": [P, P, P, P, I, P, P, I, I, I, I, F, P],
     "ffb_attention_fp8": [P, P, P, P, F, P, I, I, I, F, P],
     "ffb_attention_rowwise": [P, P, P, P, P, P, I, I, I, F, P],
-    "ffb_attention_rowwise_sync_bytes": [I],
+    "ffb_attention_rowwise_sync_bytes": [I, I],
     "ffb_gather_rows": [P, P, P, I, I, P],
     "ffb_quantize_fp8": [P, I, F, P, P, I, I, P],
     "ffb_quantize_weight_fp8": [P, I, P, P, P, I, I, P],

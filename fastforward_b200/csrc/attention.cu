@@ -59,13 +59,15 @@ extern "C" int ffb_attention_full(const uint16_t* q, const uint16_t* k, const ui
                           (cudaStream_t)stream);
 }
 
-extern "C" int ffb_attention_rowwise_sync_bytes(int T) { return T > 0 ? 8 * T + 4 * ((T + 127) / 128) : 0; }
+extern "C" int ffb_attention_rowwise_sync_bytes(int T, int HQ) {
+  return T > 0 && HQ > 0 ? 4 * T * HQ + 4 * ((T + 127) / 128) : 0;
+}
 
 extern "C" int ffb_attention_rowwise(const uint16_t* q, const uint16_t* k, const uint16_t* v, uint8_t* out8,
                                      float* qscale, void* sync, int T, int HQ, int HK, float scale, void* stream) {
   FFB_REQUIRE(q && k && v && out8 && qscale && sync, "ffb_attention_rowwise: NULL pointer");
-  FFB_REQUIRE(T > 0 && HQ > 0 && HK > 0 && HQ % HK == 0, "ffb_attention_rowwise: bad shape T=%d HQ=%d HK=%d", T, HQ,
-              HK);
+  FFB_REQUIRE(T > 0 && HQ > 0 && HK > 0 && HQ % HK == 0 && HQ % 4 == 0,
+              "ffb_attention_rowwise: bad shape T=%d HQ=%d HK=%d (HQ a multiple of 4)", T, HQ, HK);
   FFB_REQUIRE(ffb::aligned(q, 16) && ffb::aligned(k, 16) && ffb::aligned(v, 16) && ffb::aligned(out8, 16) &&
                   ffb::aligned(sync, 16) && ffb::aligned(qscale, 4),
               "ffb_attention_rowwise: alignment");

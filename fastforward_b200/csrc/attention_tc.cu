@@ -88,10 +88,10 @@ struct TcArgs {
   // head dimension) go to out[row, h * out_cols + c] by plain stores; 0: TMA tile stores
   int out_cols;
   // Rowwise FP8 output (causal prefill, every CTA resident at once): e4m3(bf16 output / s)
-  // with s = max(max|row|, 1e-12) / 448 over the row's HQ heads.  rowmax[T] holds
-  // (generation << 32 | max bits) per row, tile_count[T / 128] the arrivals per query tile
-  // (HQ per launch, never reset: the generation is the count / HQ); qscale[T] gets s.
-  unsigned long long* rowmax;
+  // with s = max(max|row|, 1e-12) / 448 over the row's HQ heads.  headmax[T][HQ] gets each
+  // head's maximum of the row, tile_count[T / 128] counts the arrivals per query tile (HQ
+  // per launch, never reset: a CTA waits for the next multiple of HQ); qscale[T] gets s.
+  float* headmax;
   uint32_t* tile_count;
   float* qscale;
 };
@@ -370,12 +370,12 @@ __global__ void __launch_bounds__(THREADS, 1)
     bool stage = ok && !*abort_flag;
     const bool fp8_out = args.out_inv > 0.f;
     float rscale = 0.f;  // rowwise FP8: this row's scale
-    if (args.rowmax != nullptr) {
-      // Rowwise FP8 output.  o <- the bf16 output values; the row's maximum over this head
-      // (four parts) goes into rowmax tagged with this launch's generation; once every
-      // head's CTA of the query tile has arrived (a bounded wait: the host launches this
-      // only when every CTA of the grid is resident), the row's maximum over all heads gives
-      // the scale -- the bytes of ffb_quantize_fp8 (ROWWISE) on the bf16 output.
+    if (args.headmax != nullptr) {
+      // Rowwise FP8 output.  o <- the bf16 output values; each head's maximum of the row
+      // (over its four parts) goes to headmax; once every head's CTA of the query tile has
+      // arrived (a bounded wait: the host launches this only when every CTA of the grid is
+      // resident), the maximum over the HQ heads gives the row's scale -- the bytes of
+      // ffb_quantize_fp8 (ROWWISE) on the bf16 output.
       const int row = q0 + r, tile = q0 / BM;
       float amax = 0.f;
       if (stage) {
@@ -389,15 +389,9 @@ __global__ void __launch_bounds__(THREADS, 1)
       float parts[4];
       const bool xok = exchange(amax, parts);
       amax = fmaxf(fmaxf(parts[0], parts[1]), fmaxf(parts[2], parts[3]));
-      // this launch's generation: the tile's count before this CTA's arrival lies in
-      // [gen * HQ, (gen + 1) * HQ) (the next launch cannot start before this one ends)
-      uint32_t gen = 0;
-      if (part == 0) {
-        gen = *reinterpret_cast<volatile const uint32_t*>(args.tile_count + tile) / (uint32_t)args.HQ;
-        if (stage && xok && row < args.T) {
-          atomicMax(args.rowmax + row, ((unsigned long long)gen << 32) | __float_as_uint(amax));
-          __threadfence();  // the maximum is visible before this CTA's arrival
-        }
+      if (part == 0 && stage && xok && row < args.T) {
+        args.headmax[(size_t)row * args.HQ + h] = amax;
+        __threadfence();  // visible before this CTA's arrival
       }
       named_barrier(2, SOFTMAX_WARPS * 32);
       volatile int* verdict = reinterpret_cast<volatile int*>(xch);  // the exchange buffers are free now
@@ -410,28 +404,28 @@ __global__ void __launch_bounds__(THREADS, 1)
           v = 1;
           uint32_t polls = 0;
           while ((int)(ld_acquire_u32(args.tile_count + tile) - target) < 0) {
-            __nanosleep(64);
+            __nanosleep(32);
             if ((++polls & 63u) == 0 && global_timer_ns() - t0 > 2000000000ull) {
               v = 0;
               break;
             }
           }
-          v = v ? (int)(old / (uint32_t)args.HQ) + 1 : 0;  // the generation + 1 (0: failed)
         }
         *verdict = v;
       }
       named_barrier(2, SOFTMAX_WARPS * 32);
-      gen = (uint32_t)(*verdict - 1);
       if (!*verdict) {
         *abort_flag = 1;
         stage = false;
       } else if (row < args.T) {
-        const unsigned long long m = __ldcg(args.rowmax + row);
-        if ((uint32_t)(m >> 32) != gen) {
-          *abort_flag = 1;
-          stage = false;
+        // the row's HQ head maxima (L2, bypassing L1), four at a time
+        const float* hm = args.headmax + (size_t)row * args.HQ;
+        float m = 0.f;
+        for (int i = 0; i < args.HQ; i += 4) {
+          const float4 f4 = __ldcg(reinterpret_cast<const float4*>(hm + i));
+          m = fmaxf(m, fmaxf(fmaxf(f4.x, f4.y), fmaxf(f4.z, f4.w)));
         }
-        rscale = __fdiv_rn(fmaxf(__uint_as_float((uint32_t)m), 1e-12f), 448.f);
+        rscale = __fdiv_rn(fmaxf(m, 1e-12f), 448.f);
         if (h == 0 && part == 0) args.qscale[row] = rscale;
       }
     }
@@ -470,7 +464,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           *reinterpret_cast<uint4*>(dst + col) = make_uint4(w[0], w[1], w[2], w[3]);
         }
       }
-    } else if (stage && args.rowmax != nullptr) {
+    } else if (stage && args.headmax != nullptr) {
       // one 128-byte-swizzled [128 rows x 128 B] box of e4m3 in P tile 0, as the static path
       uint8_t* orow = sp + r * 128;
 #pragma unroll
@@ -527,7 +521,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     named_barrier(1, SOFTMAX_WARPS * 32);
     if (!rows_mode && args.out_cols == 0 && warp == 2 && lane == 0 && !*abort_flag) {
-      if (fp8_out || args.rowmax != nullptr) {  // one [128 x 128 B] e4m3 box
+      if (fp8_out || args.headmax != nullptr) {  // one [128 x 128 B] e4m3 box
         tma_store_2d(&tmap_o, sp, h * D, q0);
       } else {
         tma_store_2d(&tmap_o, sp, h * D, q0);
@@ -564,8 +558,8 @@ __global__ void __launch_bounds__(THREADS, 1)
 // causal == 0: every row sees all T keys (sel must be NULL); out_cols > 0: out [T, HQ *
 // out_cols] bf16 holds the first out_cols columns of each head (plain stores); rq_sync !=
 // NULL: rowwise FP8 output out [T, HQ*128] e4m3 with scales qscale [T], rq_sync the
-// [T] u64 row maxima followed by [ceil(T/128)] u32 tile counters (the caller checked that
-// the grid is resident at once).
+// [T][HQ] fp32 head maxima followed by [ceil(T/128)] u32 tile counters (the caller checked
+// that the grid is resident at once; HQ a multiple of 4).
 int ffb_attention_tc(const uint16_t* q, const uint16_t* k, const uint16_t* v, const int64_t* sel, int q_gather,
                      int S, const int* key_lo, void* out, int T, int HQ, int HK, float scale, float out_inv,
                      int causal, int out_cols, void* rq_sync, float* qscale, cudaStream_t stream) {
@@ -586,8 +580,8 @@ int ffb_attention_tc(const uint16_t* q, const uint16_t* k, const uint16_t* v, co
   cudaError_t e = ffb::set_smem_attr(reinterpret_cast<const void*>(attention_tc_kernel), SMEM);
   if (e != cudaSuccess) return ffb::fail(FFB_ECUDA, "ffb_attention: %s", cudaGetErrorString(e));
   TcArgs a = {static_cast<uint16_t*>(out), key_lo, sel, q_gather, T, HQ, HK, scale * 1.4426950408889634f, out_inv,
-              causal, out_cols, static_cast<unsigned long long*>(rq_sync),
-              rq_sync ? reinterpret_cast<uint32_t*>(static_cast<unsigned long long*>(rq_sync) + T) : nullptr, qscale};
+              causal, out_cols, static_cast<float*>(rq_sync),
+              rq_sync ? reinterpret_cast<uint32_t*>(static_cast<float*>(rq_sync) + (size_t)T * HQ) : nullptr, qscale};
   const dim3 grid(sel ? S : (T + BM - 1) / BM, HQ);
   e = ffb::launch(attention_tc_kernel, grid, dim3(THREADS), SMEM, stream, tq, tk, tv, to, a);
   if (e != cudaSuccess) return ffb::fail(FFB_ECUDA, "ffb_attention: %s", cudaGetErrorString(e));

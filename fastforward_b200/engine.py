@@ -260,7 +260,7 @@ class Buffers:
         self.o8 = z(T, hq * d, dt=E4M3)
         self.os = z(T, dt=torch.float32)
         # ffb_attention_rowwise's row maxima + tile counters (zero once; they carry over)
-        self.qsync = z((L.lib().ffb_attention_rowwise_sync_bytes(T) + 7) // 8, dt=torch.int64)
+        self.qsync = z((L.lib().ffb_attention_rowwise_sync_bytes(T, hq) + 7) // 8, dt=torch.int64)
         self.lin_out = z(T, h)
         self.post8 = z(T, h, dt=E4M3)
         self.posts = z(T, dt=torch.float32)

@@ -140,17 +140,19 @@ int ffb_attention_fp8(const uint16_t* q, const uint16_t* k, const uint16_t* v, c
  * identical to ffb_attention followed by ffb_quantize_fp8 (FFB_QUANT_ROWWISE).  Replaces
  * `attention_direct` (_legacy/limit_kernels.py:36-45) plus `quantize_rows`
  * (_legacy/fp8_private.py:11-18) on the per-token-scale path.  Each row's maximum over its
- * HQ heads is combined across the CTAs of its 128-row query tile (device-scope atomics and
- * a bounded wait), so every CTA of the grid, ceil(T/128) * HQ, must be resident at once:
- * FFB_EUNSUPPORTED when that exceeds the SM count.  sync: ffb_attention_rowwise_sync_bytes(T)
- * bytes, 16-byte aligned, zero before the first call and not touched by the caller between
- * calls (its counters carry over from call to call; zero it again after a device error).
- * Calls sharing one sync must run in stream order. */
+ * HQ heads is combined across the CTAs of its 128-row query tile (per-head maxima in the
+ * scratch, an arrival counter and a bounded wait), so every CTA of the grid,
+ * ceil(T/128) * HQ, must be resident at once: FFB_EUNSUPPORTED when that exceeds the SM
+ * count.  HQ a multiple of 4.  sync: ffb_attention_rowwise_sync_bytes(T, HQ) bytes, 16-byte
+ * aligned, zero before the first call and not touched by the caller between calls (its
+ * counters carry over from call to call; zero it again after a device error).  Calls
+ * sharing one sync must run in stream order. */
 int ffb_attention_rowwise(const uint16_t* q, const uint16_t* k, const uint16_t* v, uint8_t* out8,
                           float* qscale, void* sync, int T, int HQ, int HK, float scale, void* stream);
 
-/* Scratch bytes ffb_attention_rowwise needs for T rows (no reference counterpart). */
-int ffb_attention_rowwise_sync_bytes(int T);
+/* Scratch bytes ffb_attention_rowwise needs for T rows and HQ heads (no reference
+ * counterpart). */
+int ffb_attention_rowwise_sync_bytes(int T, int HQ);
 
 /* Copies rows index[i] of src [*, row_bytes] to dst [n, row_bytes] (index on device;
  * the tail's `h.index_select(1, pick)`, _family/night_runtime.py:103). */

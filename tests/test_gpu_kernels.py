@@ -329,7 +329,8 @@ def test_attention_rowwise_is_attention_then_rowwise_quant(T, HQ, HK):
     over its HQ head CTAs in-kernel.  Three calls on one sync buffer (its counters carry the
     generation over), different inputs each time."""
     g = _g(43)
-    sync = torch.zeros((L.lib().ffb_attention_rowwise_sync_bytes(T) + 15) // 16 * 2, device=DEV, dtype=torch.int64)
+    sync = torch.zeros((L.lib().ffb_attention_rowwise_sync_bytes(T, HQ) + 15) // 16 * 2, device=DEV,
+                       dtype=torch.int64)
     for rep in range(3):
         q = (torch.randn((HQ, T, 128), generator=g) * (1 + rep)).to(BF16).to(DEV)
         k = torch.randn((HK, T, 128), generator=g).to(BF16).to(DEV)
@@ -354,7 +355,7 @@ def test_attention_rowwise_refuses_grids_larger_than_the_sms():
     """The row maxima meet across the CTAs of a query tile, so the whole grid must be resident:
     more CTAs than SMs is refused before any launch."""
     T, HQ = 2048, 32
-    sync = torch.zeros(T * 2, device=DEV, dtype=torch.int64)
+    sync = torch.zeros(T * HQ, device=DEV, dtype=torch.int64)
     x = torch.zeros((HQ, T, 128), device=DEV, dtype=BF16)
     with pytest.raises(L.FFBUnsupported, match="resident"):
         call("ffb_attention_rowwise", ptr(x), ptr(x), ptr(x), ptr(x), ptr(sync), ptr(sync), T, HQ, 8, 0.1, _sp())
