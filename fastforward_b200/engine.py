@@ -304,7 +304,7 @@ class Engine:
     """Runs prefill + choice scoring for one packed model on one device."""
 
     def __init__(self, model: PackedModel, pdl=True, autotune=True, tp_group=None, fuse="tail", stream_od=True,
-                 attn_q8=True):
+                 attn_q8=False):
         """tp_group: the torch.distributed (NCCL) group of a tensor-parallel model
         (`PackedModel(tp=...)`); o_proj and down_proj partial sums are all-reduced in it.
         fuse (FP8 modes): where an activation quantiser or an add+RMSNorm runs as the fused
@@ -316,7 +316,11 @@ class Engine:
         prologues (which run the same row work on fewer warps per row, then meet at a grid
         barrier), hence the default.  attn_q8 (per-token scales): the attention kernel writes
         the o projection's FP8 input and scales itself (`ffb_attention_rowwise`) whenever its
-        grid is resident at once -- the same bytes as attention + `ffb_quantize_fp8`."""
+        grid is resident at once -- the same bytes as attention + `ffb_quantize_fp8`.  Off by
+        default: measured in CUDA-graph chains on a B200 (4B, T = 320) it takes 22.5 us where
+        attention + the separate quantiser take 19.2 us, because every head CTA of a query
+        tile must stay resident until the tile's last head arrives, which holds back the
+        next kernel's CTAs; the whole request went from 3.45 to 3.58 ms with it on."""
         L.require_cuda()
         self.m = model
         self.d = model.dims

@@ -310,3 +310,25 @@ def test_accelerator_static_calibrated_bundle(tmp_path):
                                  variant="v")))
     r2 = Accelerator(p).predict(img, "What is shown?", ["cat", "dog", "bird", "fish"])
     assert r2["logits"] == r1["logits"]
+
+
+def test_engine_attention_rowwise_output_is_bit_identical():
+    """Engine(attn_q8=True): the attention writes the o projection's rowwise FP8 input itself
+    (`ffb_attention_rowwise`), one launch per layer fewer; the logits equal the default
+    forward's (attention + `ffb_quantize_fp8`) bit for bit, eager and through the graph."""
+    dims, src, req, layout = small_case(MODELS["4B"], 3, vocab=4096)
+    pm = PackedModel(dims, src, device=DEV)
+    T = layout.bucket
+    out = []
+    for flag in (False, True):
+        eng = Engine(pm, attn_q8=flag)
+        assert eng.attn_uses_q8(T) == flag
+        assert eng.launches_per_forward(T) == Engine(pm).launches_per_forward(T) - (2 if flag else 0)
+        ids, vis, deep = req["ids"][:T].to(DEV), req["visual"].to(DEV), [x.to(DEV) for x in req["deep"]]
+        z, _ = eng.forward(ids, vis, deep, req["pick"], req["k"], layout.image_start, layout.grid_h, layout.grid_w,
+                           T=T)
+        entry = eng.capture(T, layout.image_start, layout.nv, layout.grid_h, layout.grid_w, req["k"], len(deep))
+        zg, _ = eng.replay(entry, req["ids"][:layout.n_tokens].to(DEV), vis, deep, req["pick"])
+        out.append((z.cpu().clone(), zg.cpu().clone()))
+    assert torch.equal(out[0][0].view(torch.int32), out[1][0].view(torch.int32))
+    assert torch.equal(out[0][1].view(torch.int32), out[1][1].view(torch.int32))
