@@ -19,6 +19,7 @@ restatement of the reference path (the reference itself is Triton/CUDA-only and 
 CPU path), a bounded sample of whole decoder layers scaled to the full model.
 """
 import argparse
+import contextlib
 import json
 import os
 import statistics
@@ -573,6 +574,7 @@ def run_ours(args):
         if not extra:
             del entry
             eng.graphs.clear()
+            eng.close_peers()
         dist.destroy_process_group()
 
 
@@ -680,30 +682,47 @@ def tp32b_measure(args, world, rank, local, dev):
         pm = PackedModel(dims, src, mode=mode, device=dev, free_source=True, tp=(rank, world))
         del src
         torch.cuda.empty_cache()
-        eng = Engine(pm, tp_group=dist.group.WORLD)
         req = make_request(dims, layout, seed=1, device=dev)
-        entry = eng.capture(T, layout.image_start, layout.nv, layout.grid_h, layout.grid_w, layout.k, len(req["deep"]))
         ids = req["ids"][:layout.n_tokens]
-        for _ in range(3):
-            eng.replay(entry, ids, req["visual"], req["deep"], req["pick"])
-        torch.cuda.synchronize()
-        dist.barrier()
         steps = max(5, min(args.steps, 20))
-        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
-        with Clocks(local) as clk:
-            t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            t0.record(s)
-            for a, b in evs:
-                a.record(s)
-                entry["graph"].replay()
-                b.record(s)
-            t1.record(s)
+
+        def time_engine(peer, clocks):
+            """(seconds for `steps` replays max over ranks, sorted latencies, logits, engine's
+            reduction path) of one engine's graph."""
+            eng = Engine(pm, tp_group=dist.group.WORLD, peer=peer)
+            entry = eng.capture(T, layout.image_start, layout.nv, layout.grid_h, layout.grid_w, layout.k,
+                                len(req["deep"]))
+            for _ in range(3):
+                eng.replay(entry, ids, req["visual"], req["deep"], req["pick"])
             torch.cuda.synchronize()
-        total = torch.tensor([t0.elapsed_time(t1) * 1e-3], device=dev)
-        dist.all_reduce(total, op=dist.ReduceOp.MAX)
-        lat = sorted(a.elapsed_time(b) for a, b in evs)
+            dist.barrier()
+            evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+            with (clocks if clocks is not None else contextlib.nullcontext()):
+                t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                t0.record(s)
+                for a, b in evs:
+                    a.record(s)
+                    entry["graph"].replay()
+                    b.record(s)
+                t1.record(s)
+                torch.cuda.synchronize()
+            tot = torch.tensor([t0.elapsed_time(t1) * 1e-3], device=dev)
+            dist.all_reduce(tot, op=dist.ReduceOp.MAX)
+            lat_ = sorted(a.elapsed_time(b) for a, b in evs)
+            zz = entry["buffers"].logits[:layout.k].float().cpu().tolist()
+            path = "peer" if eng.peer is not None else "nccl"
+            del entry
+            eng.graphs.clear()
+            eng.close_peers()
+            del eng
+            torch.cuda.empty_cache()
+            dist.barrier()
+            return tot.item(), lat_, zz, path
+
+        clk = Clocks(local)
+        total, lat, z, path = time_engine(True, clk)
+        total_nccl, lat_nccl, z_nccl, _ = time_engine(False, None)
         p50 = lat[len(lat) // 2]
-        z = entry["buffers"].logits[:layout.k].float().cpu().tolist()
 
         def coll_us(numel, op):  # one collective alone, device-timed, median of 20, max over ranks
             buf = torch.zeros(numel, device=dev)
@@ -722,21 +741,26 @@ def tp32b_measure(args, world, rank, local, dev):
             return t.item()
         ar_us = coll_us(T * dims.hidden, dist.ReduceOp.SUM)
         scale_us = coll_us(T, dist.ReduceOp.MAX)
-        del entry
-        eng.graphs.clear()
-        del eng, pm
+        del pm
         torch.cuda.empty_cache()
         dist.barrier()
     if rank != 0:
         return None
-    per_req = total.item() / steps
+    per_req = total / steps
+    per_req_nccl = total_nccl / steps
     n_ar = 2 * (dims.layers - 1) + 2
-    return dict(workload=wl, parallelism=f"tp{world}", ms_per_request=per_req * 1e3,
+    return dict(workload=wl, parallelism=f"tp{world}", reductions=path, ms_per_request=per_req * 1e3,
                 latency_ms=dict(p50=p50, p99=lat[-1]), tok_per_s=T / per_req, requests_per_s=1.0 / per_req,
+                nccl_reductions=dict(ms_per_request=per_req_nccl * 1e3, p50=lat_nccl[len(lat_nccl) // 2],
+                                     logits_equal=z == z_nccl,
+                                     note="the same model and graph with every reduction an NCCL collective"),
                 allreduce=dict(per_call_us=ar_us, bytes_per_call=T * dims.hidden * 4, calls_per_request=n_ar,
                                busbw_gbs=2 * (world - 1) / world * T * dims.hidden * 4 / (ar_us * 1e-6) / 1e9,
-                               share_of_request=n_ar * ar_us * 1e-3 / (per_req * 1e3),
-                               scale_max_us=scale_us, scale_calls_per_request=n_ar),
+                               share_of_request_nccl=n_ar * ar_us * 1e-3 / (per_req_nccl * 1e3),
+                               scale_max_us=scale_us, scale_calls_per_request=n_ar,
+                               note="NCCL all-reduce of one fp32 [T, H] partial / of the [T] scales, timed alone; "
+                                    "with reductions='peer' the full layers read the partials and maxima from "
+                                    "peer memory inside ffb_add_rmsnorm_peers / ffb_quantize_fp8_peers"),
                 logits=z, clocks=clk.summary())
 
 

@@ -27,6 +27,14 @@ class Prologue(ctypes.Structure):
                 ("sync", c_void_p)]
 
 P, I, F = c_void_p, c_int, c_float
+MAX_PEERS = 8
+
+
+class PeerSync(ctypes.Structure):
+    """`ffb_peer_sync` (include/ffb200.h): a rank's cross-GPU handshake state."""
+    _fields_ = [("flags", c_void_p * MAX_PEERS), ("local", c_void_p), ("rank", c_int), ("world", c_int),
+                ("nslots", c_int)]
+
 
 # name -> argtypes, in the order of include/ffb200.h
 SIGNATURES = {
@@ -60,6 +68,12 @@ SIGNATURES = {
     "ffb_w4a16_gemm": [P, P, P, I, P, P, I, I, I, I, I, P],
     "ffb_pack_rgb": [P, P, I, I, P],
     "ffb_pack_rgb_batch": [P, P, I, I, I, P],
+    "ffb_peer_alloc": [c_size_t, P, P],
+    "ffb_peer_open": [P, P],
+    "ffb_peer_close": [P],
+    "ffb_peer_free": [P],
+    "ffb_add_rmsnorm_peers": [P, P, P, P, I, I, P, F, P, P, I, F, P, P, I, I, P],
+    "ffb_quantize_fp8_peers": [P, P, P, P, P, I, I, P],
     "ffb_bf16_gemm": [P, P, P, P, I, P, I, I, P, P, I, I, I, P],
     "ffb_bf16_gemm_plan": [I, I, I, P],
     "ffb_layernorm": [P, P, P, F, P, I, I, P],

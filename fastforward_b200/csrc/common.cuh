@@ -49,6 +49,7 @@ enum : uint32_t {
   ERR_W4_TIMEOUT = 1u << 1,
   ERR_ATTN_TIMEOUT = 1u << 2,
   ERR_GRID_SYNC_TIMEOUT = 1u << 3,
+  ERR_PEER_TIMEOUT = 1u << 4,
 };
 
 // Fills ffb_silu_table on this device once (stream-ordered, before the caller's next

@@ -11,6 +11,7 @@
 // HBM traffic per row: read a, b (or the split-K partials), w; write residual, out, q8.
 #include "common.cuh"
 #include "pdl.cuh"
+#include "peer.cuh"
 
 namespace {
 
@@ -73,11 +74,16 @@ struct NormArgs {
   float* qscale;
   int T, H;
   int add;  // 0: plain RMSNorm of a
+  // tensor-parallel ranks' partial planes (S == -2): planes[r] summed in rank order after
+  // the row's handshake
+  const float* planes[FFB_MAX_PEERS];
+  ffb_peer_sync ps;
 };
 
 // S >= 1: b is the sum of S fp32 split-K partial planes (all loads issued before the first
 // add, summed in plane order); S == 0: b is bf16 (or there is no add); S == -1: any number
-// of planes, loaded plane by plane.
+// of planes, loaded plane by plane; S == -2: the tensor-parallel ranks' planes (peer
+// memory), summed in rank order once the row's CTA has handshaken with every rank.
 template <int V, int S>
 __global__ void __launch_bounds__(MAXT) add_rmsnorm_kernel(const NormArgs p) {
   __shared__ float red[MAXT / 32];
@@ -95,6 +101,15 @@ __global__ void __launch_bounds__(MAXT) add_rmsnorm_kernel(const NormArgs p) {
   }
   pdl_wait();
   pdl_launch();
+  if constexpr (S == -2) {
+    __shared__ int hs_ok;
+    if (threadIdx.x == 0) {
+      hs_ok = peer_handshake(p.ps, row);
+      if (!hs_ok) atomicOr(&ffb_device_error_word, ffb::ERR_PEER_TIMEOUT);
+    }
+    __syncthreads();
+    if (!hs_ok) return;
+  }
   const bool deep_row = p.deep && row >= p.start && row < p.start + p.nv;
   float x[V][8], b[V][8];
   constexpr int SP = S > 0 ? S : 1;
@@ -135,6 +150,11 @@ __global__ void __launch_bounds__(MAXT) add_rmsnorm_kernel(const NormArgs p) {
           if constexpr (S > 0) {
 #pragma unroll
             for (int s = 0; s < S; ++s) add_plane(part[i][s][0], part[i][s][1]);
+          } else if constexpr (S == -2) {
+            for (int r = 0; r < p.ps.world; ++r) {
+              const float4* src = reinterpret_cast<const float4*>(p.planes[r] + base + v * 8);
+              add_plane(__ldcg(src), __ldcg(src + 1));
+            }
           } else {
             for (int s = 0; s < p.splits; ++s) {
               const float4* src = reinterpret_cast<const float4*>(p.b32 + (size_t)s * p.T * p.H + base + v * 8);
@@ -213,7 +233,8 @@ int run(const NormArgs& p, const char* who, void* stream) {
   const bool planes = p.add && !p.b;
   const int sp = planes ? p.splits : 0;
   auto kernel = add_rmsnorm_kernel<MAXV, -1>;
-  switch (sp) {
+  switch (p.ps.world > 0 ? -2 : sp) {
+    case -2: kernel = add_rmsnorm_kernel<MAXV, -2>; break;
     case 0: kernel = add_rmsnorm_kernel<MAXV, 0>; break;
     case 1: kernel = add_rmsnorm_kernel<MAXV, 1>; break;
     case 2: kernel = add_rmsnorm_kernel<MAXV, 2>; break;
@@ -275,4 +296,41 @@ extern "C" int ffb_add_rmsnorm(const uint16_t* a, const uint16_t* b, const float
   p.H = H;
   p.add = 1;
   return run(p, "ffb_add_rmsnorm", stream);
+}
+
+extern "C" int ffb_add_rmsnorm_peers(const uint16_t* a, const float* const* planes, const ffb_peer_sync* sync,
+                                     const uint16_t* deep, int start, int nv, const uint16_t* w, float eps,
+                                     uint16_t* residual, uint16_t* out, int quant_mode, float inv_scale, uint8_t* q8,
+                                     float* qscale, int T, int H, void* stream) {
+  FFB_REQUIRE(planes && sync, "ffb_add_rmsnorm_peers: NULL planes / sync");
+  FFB_REQUIRE(sync->world >= 1 && sync->world <= FFB_MAX_PEERS && sync->rank >= 0 && sync->rank < sync->world,
+              "ffb_add_rmsnorm_peers: rank %d of %d (at most %d ranks)", sync->rank, sync->world, FFB_MAX_PEERS);
+  FFB_REQUIRE(sync->local && T <= sync->nslots, "ffb_add_rmsnorm_peers: %d rows need %d slots (have %d)", T, T,
+              sync->nslots);
+  for (int r = 0; r < sync->world; ++r)
+    FFB_REQUIRE(planes[r] && sync->flags[r] && ffb::aligned(planes[r], 16),
+                "ffb_add_rmsnorm_peers: rank %d's plane / flags missing or unaligned", r);
+  FFB_REQUIRE(!deep || (start >= 0 && nv >= 0 && start + nv <= T && ffb::aligned(deep, 16)),
+              "ffb_add_rmsnorm_peers: bad deepstack window start=%d nv=%d T=%d", start, nv, T);
+  FFB_REQUIRE(residual != nullptr, "ffb_add_rmsnorm_peers: residual is NULL");
+  NormArgs p = {};
+  p.a = a;
+  p.splits = 1;
+  p.deep = deep;
+  p.start = start;
+  p.nv = deep ? nv : 0;
+  p.w = w;
+  p.eps = eps;
+  p.residual = residual;
+  p.out = out;
+  p.quant_mode = quant_mode;
+  p.inv_scale = inv_scale;
+  p.q8 = q8;
+  p.qscale = qscale;
+  p.T = T;
+  p.H = H;
+  p.add = 1;
+  for (int r = 0; r < sync->world; ++r) p.planes[r] = planes[r];
+  p.ps = *sync;
+  return run(p, "ffb_add_rmsnorm_peers", stream);
 }

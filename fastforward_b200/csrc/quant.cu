@@ -10,6 +10,7 @@
 // are reproducible on any IEEE implementation.
 #include "common.cuh"
 #include "pdl.cuh"
+#include "peer.cuh"
 
 #include <atomic>
 
@@ -91,6 +92,67 @@ __global__ void __launch_bounds__(1024) quant_rows_vec_kernel(const uint16_t* __
       for (int e = 0; e < 8; ++e) {
         const float qv = divide ? __fdiv_rn(v[i][e], scale) : v[i][e] * inv;
         const uint32_t b = f2e4m3(clamp448(qv));
+        if (e < 4) lo |= b << (8 * e);
+        else hi |= b << (8 * (e - 4));
+      }
+      *reinterpret_cast<uint2*>(qr + vi * 8) = make_uint2(lo, hi);
+    }
+  }
+}
+
+// Rowwise quantiser of a row split over the tensor-parallel ranks: the slice maximum goes
+// to every rank's amax[p][rank][row] (peer stores), the row's CTA handshakes slot `row`
+// with every rank, and the scale is max(max over the ranks' maxima, 1e-12) / 448.
+struct PeerAmax {
+  float* amax[FFB_MAX_PEERS];  // rank p's [world][M] buffer, as mapped here
+};
+__global__ void __launch_bounds__(1024) quant_rows_peer_kernel(const uint16_t* __restrict__ x, PeerAmax pa,
+                                                              ffb_peer_sync ps, uint8_t* __restrict__ q8,
+                                                              float* __restrict__ qscale, int M, int K) {
+  __shared__ float red[32];
+  __shared__ int hs_ok;
+  pdl_wait();
+  pdl_launch();
+  const int row = blockIdx.x, nvec = K / 8;
+  const uint16_t* xr = x + (size_t)row * K;
+  uint8_t* qr = q8 + (size_t)row * K;
+  float v[QV][8];
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < QV; ++i) {
+    const int vi = threadIdx.x + i * blockDim.x;
+    if (vi < nvec) {
+      const uint4 u = *reinterpret_cast<const uint4*>(xr + vi * 8);
+      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        v[i][2 * e] = __uint_as_float(w[e] << 16);
+        v[i][2 * e + 1] = __uint_as_float(w[e] & 0xffff0000u);
+      }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) amax = fmaxf(amax, fabsf(v[i][e]));
+    }
+  }
+  amax = block_max_any(amax, red);
+  if (threadIdx.x == 0) {
+    for (int p = 0; p < ps.world; ++p) pa.amax[p][(size_t)ps.rank * M + row] = amax;
+    hs_ok = peer_handshake(ps, row);  // fences the stores above before its signals
+    if (!hs_ok) atomicOr(&ffb_device_error_word, ffb::ERR_PEER_TIMEOUT);
+  }
+  __syncthreads();
+  if (!hs_ok) return;
+  float m = 0.f;
+  for (int q = 0; q < ps.world; ++q) m = fmaxf(m, __ldcg(pa.amax[ps.rank] + (size_t)q * M + row));
+  const float scale = fmaxf(m, 1e-12f) / 448.f;
+  if (threadIdx.x == 0) qscale[row] = scale;
+#pragma unroll
+  for (int i = 0; i < QV; ++i) {
+    const int vi = threadIdx.x + i * blockDim.x;
+    if (vi < nvec) {
+      uint32_t lo = 0, hi = 0;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const uint32_t b = f2e4m3(clamp448(__fdiv_rn(v[i][e], scale)));
         if (e < 4) lo |= b << (8 * e);
         else hi |= b << (8 * (e - 4));
       }
@@ -280,5 +342,27 @@ extern "C" int ffb_pack_gateup(const void* src, void* dst, int I, int K, int ele
   cudaError_t e = ffb::launch(pack_gateup_kernel, dim3(2 * I), dim3(128), 0, (cudaStream_t)stream,
                               (const uint8_t*)src, (uint8_t*)dst, I, row_bytes);
   if (e != cudaSuccess) return ffb::fail(FFB_ECUDA, "ffb_pack_gateup: %s", cudaGetErrorString(e));
+  return FFB_OK;
+}
+
+extern "C" int ffb_quantize_fp8_peers(const uint16_t* x, float* const* amax, const ffb_peer_sync* sync, uint8_t* q8,
+                                      float* qscale, int M, int K, void* stream) {
+  FFB_REQUIRE(x && amax && sync && q8 && qscale, "ffb_quantize_fp8_peers: NULL pointer");
+  FFB_REQUIRE(M > 0 && K > 0 && K % 8 == 0 && K / 8 <= 1024 * QV, "ffb_quantize_fp8_peers: bad shape M=%d K=%d", M, K);
+  FFB_REQUIRE(ffb::aligned(x, 16) && ffb::aligned(q8, 8), "ffb_quantize_fp8_peers: alignment");
+  FFB_REQUIRE(sync->world >= 1 && sync->world <= FFB_MAX_PEERS && sync->rank >= 0 && sync->rank < sync->world,
+              "ffb_quantize_fp8_peers: rank %d of %d (at most %d ranks)", sync->rank, sync->world, FFB_MAX_PEERS);
+  FFB_REQUIRE(sync->local && M <= sync->nslots, "ffb_quantize_fp8_peers: %d rows need %d slots (have %d)", M, M,
+              sync->nslots);
+  PeerAmax pa = {};
+  for (int r = 0; r < sync->world; ++r) {
+    FFB_REQUIRE(amax[r] && sync->flags[r], "ffb_quantize_fp8_peers: rank %d's amax / flags missing", r);
+    pa.amax[r] = amax[r];
+  }
+  int nt = (K / 8 + QV - 1) / QV;
+  nt = (nt + 31) / 32 * 32;
+  cudaError_t e = ffb::launch(quant_rows_peer_kernel, dim3(M), dim3(nt), 0, (cudaStream_t)stream, x, pa, *sync, q8,
+                              qscale, M, K);
+  if (e != cudaSuccess) return ffb::fail(FFB_ECUDA, "ffb_quantize_fp8_peers: %s", cudaGetErrorString(e));
   return FFB_OK;
 }

@@ -304,7 +304,7 @@ class Engine:
     """Runs prefill + choice scoring for one packed model on one device."""
 
     def __init__(self, model: PackedModel, pdl=True, autotune=True, tp_group=None, fuse="tail", stream_od=True,
-                 attn_q8=False):
+                 attn_q8=False, peer=True):
         """tp_group: the torch.distributed (NCCL) group of a tensor-parallel model
         (`PackedModel(tp=...)`); o_proj and down_proj partial sums are all-reduced in it.
         fuse (FP8 modes): where an activation quantiser or an add+RMSNorm runs as the fused
@@ -350,10 +350,61 @@ class Engine:
         # parallelism the scale is a maximum over the ranks)
         self.attn_q8 = attn_q8 and model.mode == "rowwise" and self.world == 1 and self.fuse != "all"
         self.sms = torch.cuda.get_device_properties(model.device).multi_processor_count
+        # tensor parallel: the full layers' reductions read the ranks' partials and activation
+        # maxima from peer memory inside the consuming kernel (`ffb_add_rmsnorm_peers`,
+        # `ffb_quantize_fp8_peers`) when every rank could map every other's buffers; else NCCL
+        self.peer = self._open_peers() if (peer and self.world > 1) else None
         # o_proj / down_proj on the weight-stationary schedule (K splits chosen by its cost
         # model, measured 1% faster per 4B request than token-major split-K tiles)
         self.stream_od = stream_od
         L.set_pdl(pdl)
+
+    def _open_peers(self):
+        """PeerBuffers for the group, or None on every rank when any rank cannot map them
+        (the decision is collective, so the ranks never mix the two reduction paths)."""
+        import torch.distributed as dist
+        from .config import BUCKETS
+        from .peer import PeerBuffers
+        pb, ok = None, 1
+        try:
+            pb = PeerBuffers(self.group, self.m.tp[0], self.world, max(BUCKETS), self.d.hidden, self.device)
+        except Exception:
+            ok = 0
+        flag = torch.tensor([ok], dtype=torch.int32, device=self.device)
+        dist.all_reduce(flag, op=dist.ReduceOp.MIN, group=self.group)
+        if int(flag.item()) == 0:
+            if pb is not None:
+                pb.close()
+            return None
+        return pb
+
+    def close_peers(self):
+        """Releases the peer mappings (call on every rank before destroying the group)."""
+        if self.peer is not None:
+            self.peer.close()
+            self.peer = None
+
+    def _red_target(self, b):
+        """Where the next row-parallel GEMM writes its fp32 partial: this rank's peer plane
+        (alternating between two) or the NCCL workspace."""
+        if self.peer is None:
+            return b.ws
+        from .peer import DevicePtr
+        return DevicePtr(self.peer.own_plane[self._pc & 1])
+
+    def _add_rmsnorm_reduced(self, plan, b, ws, a, deep, start, nv, w, eps, residual, out, qmode, inv, q8, qs, T, H):
+        """residual = a + (the ranks' summed partial), out / q8 = its RMSNorm: through peer
+        memory in one kernel, or NCCL all-reduce + ffb_add_rmsnorm."""
+        if self.peer is not None:
+            call("ffb_add_rmsnorm_peers", ptr(a), ctypes.addressof(self.peer.planes[self._pc & 1]),
+                 ctypes.addressof(self.peer.sync), ptr(deep), start, nv, ptr(w), eps, ptr(residual), ptr(out), qmode,
+                 inv, ptr(q8), ptr(qs), T, H, self._s)
+            self._pc += 1
+            return
+        self._tp_reduce(plan, ws)
+        xb, x32, xs = self._split_args(plan, None, ws)
+        call("ffb_add_rmsnorm", ptr(a), xb, x32, xs, ptr(deep), start, nv, ptr(w), eps, ptr(residual), ptr(out),
+             qmode, inv, ptr(q8), ptr(qs), T, H, self._s)
 
     # ------------------------------------------------------------------ plans / buffers
     def _plans(self, T):
@@ -532,10 +583,14 @@ class Engine:
         dist.all_reduce(qs[:rows], op=dist.ReduceOp.MAX, group=self.group)
         call("ffb_quantize_fp8", ptr(x), L.QUANT_ROWSCALE, 0.0, ptr(q8), ptr(qs), rows, K, self._s)
 
-    def _quant_in(self, x, qmode, inv, q8, qs, rows, K):
+    def _quant_in(self, x, qmode, inv, q8, qs, rows, K, full=False):
         """The activation quantiser in front of o_proj / down_proj (rank-complete rows under
-        tensor parallelism)."""
-        if self.world > 1 and qmode == L.QUANT_ROWWISE:
+        tensor parallelism: in the full layers through peer memory when available)."""
+        if self.world > 1 and qmode == L.QUANT_ROWWISE and full and self.peer is not None:
+            call("ffb_quantize_fp8_peers", ptr(x), ctypes.addressof(self.peer.amax[self._qc & 1]),
+                 ctypes.addressof(self.peer.sync), ptr(q8), ptr(qs), rows, K, self._s)
+            self._qc += 1
+        elif self.world > 1 and qmode == L.QUANT_ROWWISE:
             self._quant_rows_tp(x, q8, qs, rows, K)
         else:
             call("ffb_quantize_fp8", ptr(x), qmode, inv, ptr(q8), ptr(qs), rows, K, self._s)
@@ -570,6 +625,7 @@ class Engine:
         b = b or self.buffers_for(T)
         pl = self._plans(T)
         self._s = torch.cuda.current_stream(self.device).cuda_stream
+        self._pc = self._qc = 0  # peer planes / maxima: each forward starts on buffer 0 (an even count of uses)
         cos, sin = self.rope_tables(T, image_start, grid_h, grid_w)
         H, D, HQ, HK, I = d.hidden, d.d, d.hq, d.hk, d.inter
         eps = float(d.eps)
@@ -618,23 +674,32 @@ class Engine:
                 call("ffb_attention", ptr(b.yq), ptr(b.yk), ptr(b.yv), None, 0, ptr(b.attn), T, T, HQ, HK, scale,
                      self._s)
             p = pl[("full", "o")]
+            red = self._red_target(b) if self.world > 1 else b.ws  # the fp32 partial's home
             if int4:
-                self._w4(p, b.attn, lay.lin["o"], b.lin_out, b.ws)
+                self._w4(p, b.attn, lay.lin["o"], b.lin_out, red)
             else:
                 if not self.static_q8:
                     if not attn_q8:
-                        self._quant_in(b.attn, qmode, lay.inv["o"], b.o8, b.os, T, HQ * D)
+                        self._quant_in(b.attn, qmode, lay.inv["o"], b.o8, b.os, T, HQ * D, full=True)
                     obs(j, "o", b.os, T)
-                self._gemm(p, b.o8, sa(lay, "o", b.os), lay.lin["o"], b.lin_out, b.ws, rowwise)
-            self._tp_reduce(p, b.ws)
-            ob, o32, os_ = self._split_args(p, b.lin_out, b.ws)
-            if int4:
-                call("ffb_add_rmsnorm", ptr(h_cur), ob, o32, os_, None, 0, 0, ptr(lay.post_norm), eps, ptr(h_mid),
-                     ptr(b.postb), L.QUANT_NONE, 0.0, None, None, T, H, self._s)
+                self._gemm(p, b.o8, sa(lay, "o", b.os), lay.lin["o"], b.lin_out, red, rowwise)
+            if self.world > 1:
+                if int4:
+                    self._add_rmsnorm_reduced(p, b, red, h_cur, None, 0, 0, lay.post_norm, eps, h_mid, b.postb,
+                                              L.QUANT_NONE, 0.0, None, None, T, H)
+                else:
+                    self._add_rmsnorm_reduced(p, b, red, h_cur, None, 0, 0, lay.post_norm, eps, h_mid, None, qmode,
+                                              lay.inv["gateup"], b.post8, b.posts, T, H)
+                    obs(j, "gateup", b.posts, T)
             else:
-                call("ffb_add_rmsnorm", ptr(h_cur), ob, o32, os_, None, 0, 0, ptr(lay.post_norm), eps, ptr(h_mid),
-                     None, qmode, lay.inv["gateup"], ptr(b.post8), ptr(b.posts), T, H, self._s)
-                obs(j, "gateup", b.posts, T)
+                ob, o32, os_ = self._split_args(p, b.lin_out, b.ws)
+                if int4:
+                    call("ffb_add_rmsnorm", ptr(h_cur), ob, o32, os_, None, 0, 0, ptr(lay.post_norm), eps, ptr(h_mid),
+                         ptr(b.postb), L.QUANT_NONE, 0.0, None, None, T, H, self._s)
+                else:
+                    call("ffb_add_rmsnorm", ptr(h_cur), ob, o32, os_, None, 0, 0, ptr(lay.post_norm), eps, ptr(h_mid),
+                         None, qmode, lay.inv["gateup"], ptr(b.post8), ptr(b.posts), T, H, self._s)
+                    obs(j, "gateup", b.posts, T)
             # ---- MLP block
             p = pl[("full", "gateup")]
             if int4:
@@ -645,24 +710,33 @@ class Engine:
             else:
                 self._gemm(p, b.post8, sa(lay, "gateup", b.posts), lay.lin["gateup"], b.act, b.ws, rowwise)
             p = pl[("full", "down")]
+            red = self._red_target(b) if self.world > 1 else b.ws
             if int4:
-                self._w4(p, b.act, lay.lin["down"], b.lin_out, b.ws)
+                self._w4(p, b.act, lay.lin["down"], b.lin_out, red)
             else:
                 if not self.static_q8:
-                    self._quant_in(b.act, qmode, lay.inv["down"], b.act8, b.acts, T, I)
+                    self._quant_in(b.act, qmode, lay.inv["down"], b.act8, b.acts, T, I, full=True)
                     obs(j, "down", b.acts, T)
-                self._gemm(p, b.act8, sa(lay, "down", b.acts), lay.lin["down"], b.lin_out, b.ws, rowwise)
-            self._tp_reduce(p, b.ws)
-            db, d32, ds = self._split_args(p, b.lin_out, b.ws)
+                self._gemm(p, b.act8, sa(lay, "down", b.acts), lay.lin["down"], b.lin_out, red, rowwise)
             dp = deep[j] if (deep is not None and j < len(deep)) else None
-            if int4:
-                call("ffb_add_rmsnorm", ptr(h_mid), db, d32, ds, ptr(dp), image_start, nv if dp is not None else 0,
-                     ptr(nxt.in_norm), eps, ptr(h_cur), ptr(b.xb), L.QUANT_NONE, 0.0, None, None, T, H, self._s)
+            dnv = nv if dp is not None else 0
+            if self.world > 1:
+                if int4:
+                    self._add_rmsnorm_reduced(p, b, red, h_mid, dp, image_start, dnv, nxt.in_norm, eps, h_cur, b.xb,
+                                              L.QUANT_NONE, 0.0, None, None, T, H)
+                else:
+                    self._add_rmsnorm_reduced(p, b, red, h_mid, dp, image_start, dnv, nxt.in_norm, eps, h_cur, None,
+                                              qmode, nxt.inv["qkv"], b.x8, b.xs, T, H)
+                    obs(j + 1, "qkv", b.xs, T)
             else:
-                call("ffb_add_rmsnorm", ptr(h_mid), db, d32, ds, ptr(dp), image_start, nv if dp is not None else 0,
-                     ptr(nxt.in_norm), eps, ptr(h_cur), None, qmode, nxt.inv["qkv"], ptr(b.x8), ptr(b.xs), T, H,
-                     self._s)
-                obs(j + 1, "qkv", b.xs, T)
+                db, d32, ds = self._split_args(p, b.lin_out, b.ws)
+                if int4:
+                    call("ffb_add_rmsnorm", ptr(h_mid), db, d32, ds, ptr(dp), image_start, dnv, ptr(nxt.in_norm), eps,
+                         ptr(h_cur), ptr(b.xb), L.QUANT_NONE, 0.0, None, None, T, H, self._s)
+                else:
+                    call("ffb_add_rmsnorm", ptr(h_mid), db, d32, ds, ptr(dp), image_start, dnv, ptr(nxt.in_norm), eps,
+                         ptr(h_cur), None, qmode, nxt.inv["qkv"], ptr(b.x8), ptr(b.xs), T, H, self._s)
+                    obs(j + 1, "qkv", b.xs, T)
         # ---- tail: last layer on the pick row (night_runtime.py:92-105)
         if on_layer is not None:
             on_layer(depth - 1, h_cur)
@@ -1104,5 +1178,6 @@ def calibrate_profile(dims, bf16_model, requests, margin=1.5, device="cuda", tp=
     try:
         return eng.calibrate(requests, margin)
     finally:
+        eng.close_peers()
         del eng, pm
         torch.cuda.empty_cache()

@@ -354,6 +354,52 @@ int ffb_pack_rgb(const uint8_t* rgb, uint16_t* pixels, int height, int width, vo
 int ffb_pack_rgb_batch(const uint8_t* rgb, uint16_t* pixels, int n, int height, int width,
                        void* stream);
 
+/* ---------------------------------------------------------------- tensor parallel, peer memory
+ * One process per GPU.  The o_proj / down_proj partial sums and the per-token activation
+ * maxima of the tensor-parallel ranks are read straight from each other's memory over
+ * NVLink (CUDA IPC mappings; plain loads, stores and atomics, no multicast), by the kernel
+ * that consumes them, instead of after an NCCL collective.  No reference counterpart (the
+ * reference runs on one GPU, api.py:56-57). */
+
+#define FFB_MAX_PEERS 8
+
+/* Handshake state of one rank: flags[p] is rank p's [world][nslots] uint32 array (for
+ * p == rank this process's own, else the IPC mapping of rank p's); local is this rank's
+ * [nslots] uint32 call counts.  Both zero before the first call of any rank.  Slot i is
+ * used by row i's CTA; every rank must make the same sequence of calls. */
+typedef struct ffb_peer_sync {
+  uint32_t* flags[FFB_MAX_PEERS];
+  uint32_t* local;
+  int rank, world, nslots;
+} ffb_peer_sync;
+
+/* Device allocation of `bytes` (zeroed) with its 64-byte CUDA IPC handle, and the mapping
+ * of another process's allocation from its handle (peer access enabled lazily). */
+int ffb_peer_alloc(size_t bytes, void** dptr, void* handle);
+int ffb_peer_open(const void* handle, void** dptr);
+int ffb_peer_close(void* dptr);
+int ffb_peer_free(void* dptr);
+
+/* ffb_add_rmsnorm whose b is the sum of the ranks' fp32 partial planes: planes[r] (host
+ * array of `world` device pointers; rank r's [T, H] plane, peer-mapped) are summed in rank
+ * order ((p0 + p1) + p2 ...), then rounded to bf16 as the linear's output.  Replaces the
+ * NCCL all-reduce of the row-parallel o_proj / down_proj partials plus the residual add +
+ * RMSNorm (_legacy/lower_kernels.py:7-32) of a tensor-parallel layer.  Row t's CTA
+ * handshakes slot t with every rank before reading the planes (its own rank's producer has
+ * finished by stream order); a wait that gives up after 2 s sets the device error word. */
+int ffb_add_rmsnorm_peers(const uint16_t* a, const float* const* planes, const ffb_peer_sync* sync,
+                          const uint16_t* deep, int start, int nv, const uint16_t* w, float eps,
+                          uint16_t* residual, uint16_t* out, int quant_mode, float inv_scale,
+                          uint8_t* q8, float* qscale, int T, int H, void* stream);
+
+/* ffb_quantize_fp8 (ROWWISE) of a row split over the tensor-parallel ranks (x is this
+ * rank's [M, K] slice): each row's slice maximum is written into every rank's amax[p]
+ * ([world][M] fp32, host array of device pointers), the ranks handshake the row's slot, and
+ * the scale is max(max over ranks, 1e-12) / 448 -- the unsharded row's scale, as
+ * ffb_quantize_fp8 ROWWISE + an all-reduce (MAX) of the scales + FFB_QUANT_ROWSCALE. */
+int ffb_quantize_fp8_peers(const uint16_t* x, float* const* amax, const ffb_peer_sync* sync,
+                           uint8_t* q8, float* qscale, int M, int K, void* stream);
+
 /* ---------------------------------------------------------------- vision tower
  * The kernels of the Qwen3-VL vision tower in front of the language path (patch embedding,
  * ViT blocks, deepstack and final mergers).  The reference runs it as HF modules plus its

@@ -1,9 +1,11 @@
-"""Tensor-parallel engine on 2 GPUs (NCCL): a 32B-shaped model of two layers (one full
-layer and the pick-row tail) sharded over two ranks.  The logits must equal, bit for bit,
-the oracle's tensor-parallel path (whole-row activation scales, fp32 partials summed across
-ranks -- for two ranks the unsharded linear with a two-way K split), and the CUDA-graph
-replay -- which holds the NCCL all-reduces -- must equal the eager forward bit for bit.
-Skipped with fewer than two GPUs."""
+"""Tensor-parallel engine on 2 GPUs: a 32B-shaped model of two layers (one full layer and
+the pick-row tail) sharded over two ranks, once with the full layers' reductions read from
+peer memory inside the consuming kernels (`ffb_add_rmsnorm_peers`, `ffb_quantize_fp8_peers`)
+and once through NCCL.  The logits must equal, bit for bit, the oracle's tensor-parallel
+path (whole-row activation scales, fp32 partials summed across ranks -- for two ranks the
+unsharded linear with a two-way K split), both reduction paths must agree, and the
+CUDA-graph replays -- which hold the handshakes or the NCCL calls -- must equal the eager
+forwards bit for bit.  Skipped with fewer than two GPUs."""
 import os
 import socket
 
@@ -29,6 +31,7 @@ def _rank_main(rank, world, port, out):
     from datetime import timedelta
     import torch.distributed as dist
     from fastforward_b200.engine import Engine, PackedModel
+    from fastforward_b200 import _lib as L
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     torch.cuda.set_device(rank)
     dev = torch.device("cuda", rank)
@@ -37,25 +40,38 @@ def _rank_main(rank, world, port, out):
     try:
         dims, src, req, layout = _case()
         pm = PackedModel(dims, src, device=dev, tp=(rank, world))
-        eng = Engine(pm, tp_group=dist.group.WORLD)
         T = layout.bucket
         ids, vis = req["ids"][:T].to(dev), req["visual"].to(dev)
         deep = [x.to(dev) for x in req["deep"]]
-        z, _ = eng.forward(ids, vis, deep, req["pick"], req["k"], layout.image_start, layout.grid_h, layout.grid_w, T=T)
-        z = z.cpu().clone()
-        entry = eng.capture(T, layout.image_start, layout.nv, layout.grid_h, layout.grid_w, req["k"], len(deep))
-        zg, _ = eng.replay(entry, req["ids"][:layout.n_tokens].to(dev), vis, deep, req["pick"])
-        zg = zg.cpu().clone()
-        torch.cuda.synchronize()
-        splits = {k: p.splits for k, p in eng.plans[T].items()}
+        res = {}
+        for peer in (True, False):  # reductions through peer memory, then through NCCL
+            eng = Engine(pm, tp_group=dist.group.WORLD, peer=peer)
+            assert (eng.peer is not None) == peer, "peer mappings unavailable"
+            z, _ = eng.forward(ids, vis, deep, req["pick"], req["k"], layout.image_start, layout.grid_h,
+                               layout.grid_w, T=T)
+            z = z.cpu().clone()
+            entry = eng.capture(T, layout.image_start, layout.nv, layout.grid_h, layout.grid_w, req["k"], len(deep))
+            zg, _ = eng.replay(entry, req["ids"][:layout.n_tokens].to(dev), vis, deep, req["pick"])
+            zg = zg.cpu().clone()
+            torch.cuda.synchronize()
+            res["peer" if peer else "nccl"] = dict(z=z, zg=zg)
+            res["splits"] = {k: p.splits for k, p in eng.plans[T].items()}
+            res["error_word"] = L.device_error()
+            dist.barrier()
+            del entry
+            entry = None
+            eng.graphs.clear()
+            eng.close_peers()
+            eng = None
         if rank == 0:
-            torch.save(dict(z=z, zg=zg, splits=splits), out)
+            torch.save(res, out)
         dist.barrier()
     finally:
         if entry is not None:  # graphs holding NCCL work go before the process group
             del entry
         if eng is not None:
             eng.graphs.clear()
+            eng.close_peers()
         dist.destroy_process_group()
 
 
@@ -66,8 +82,12 @@ def test_tp2_engine_matches_oracle(tmp_path):
     from fastforward_b200.mrope import position_ids
     out = str(tmp_path / "tp2.pt")
     mp.start_processes(_rank_main, args=(2, _free_port(), out), nprocs=2, start_method="spawn")
-    r = torch.load(out)
-    assert torch.equal(r["z"], r["zg"]), "graph replay (with the NCCL all-reduces) must equal the eager forward"
+    res = torch.load(out)
+    assert res["error_word"] == 0
+    r = dict(res["peer"], splits=res["splits"])
+    assert torch.equal(r["z"], r["zg"]), "graph replay (with the peer reductions) must equal the eager forward"
+    assert torch.equal(res["nccl"]["z"], res["nccl"]["zg"]), "graph replay (with the NCCL all-reduces) == eager"
+    assert torch.equal(r["z"].view(torch.int32), res["nccl"]["z"].view(torch.int32)), "peer and NCCL reductions"
     dims, src, req, layout = _case()
     T = layout.bucket
     pos = position_ids(T, layout.image_start, layout.grid_h, layout.grid_w)
