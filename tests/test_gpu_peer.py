@@ -109,7 +109,9 @@ def test_quantize_peers_takes_the_maximum_over_ranks():
          L.stream_ptr())
     torch.cuda.synchronize()
     own_max = x.float().abs().amax(1)
-    want_s = torch.maximum(own_max, peer_max).clamp(min=1e-12) / 448.0
+    # the IEEE fp32 quotient (float64 then rounded; torch's CUDA scalar division multiplies
+    # by the reciprocal)
+    want_s = (torch.maximum(own_max, peer_max).clamp(min=1e-12).double() / 448.0).float()
     assert torch.equal(qs, want_s)
     want8 = torch.empty(M, K, dtype=torch.uint8, device=DEV)
     call("ffb_quantize_fp8", ptr(x), L.QUANT_ROWSCALE, 0.0, ptr(want8), ptr(want_s), M, K, L.stream_ptr())
