@@ -89,9 +89,7 @@ __global__ void __launch_bounds__(MAXT) add_rmsnorm_kernel(const NormArgs p) {
   __shared__ float red[MAXT / 32];
   __shared__ double redd[MAXT / 32];
   const int NT = blockDim.x;
-  const int row = blockIdx.x;
   const int nvec = p.H / 8;
-  const size_t base = (size_t)row * p.H;
   // the norm weight does not depend on the previous kernel: fetch it before waiting
   float w[V][8];
 #pragma unroll
@@ -101,117 +99,121 @@ __global__ void __launch_bounds__(MAXT) add_rmsnorm_kernel(const NormArgs p) {
   }
   pdl_wait();
   pdl_launch();
-  if constexpr (S == -2) {
+  if constexpr (S == -2) {  // one handshake per CTA (slot = CTA), then its rows
     __shared__ int hs_ok;
     if (threadIdx.x == 0) {
-      hs_ok = peer_handshake(p.ps, row);
+      hs_ok = peer_handshake(p.ps, blockIdx.x);
       if (!hs_ok) atomicOr(&ffb_device_error_word, ffb::ERR_PEER_TIMEOUT);
     }
     __syncthreads();
     if (!hs_ok) return;
   }
-  const bool deep_row = p.deep && row >= p.start && row < p.start + p.nv;
-  float x[V][8], b[V][8];
-  constexpr int SP = S > 0 ? S : 1;
-  float4 part[V][SP][2];
-  // every load of the row in flight before the first use
+  // one row per CTA (the peer variant's smaller grid strides over the rows)
+  for (int row = blockIdx.x; row < p.T; row += gridDim.x) {
+    const size_t base = (size_t)row * p.H;
+    const bool deep_row = p.deep && row >= p.start && row < p.start + p.nv;
+    float x[V][8], b[V][8];
+    constexpr int SP = S > 0 ? S : 1;
+    float4 part[V][SP][2];
+    // every load of the row in flight before the first use
 #pragma unroll
-  for (int i = 0; i < V; ++i) {
-    const int v = threadIdx.x + i * NT;
-    if (v < nvec) {
-      load8(p.a + base + v * 8, x[i]);
-      if (p.add) {
-        if constexpr (S == 0) {
-          load8(p.b + base + v * 8, b[i]);
-        } else if constexpr (S > 0) {
+    for (int i = 0; i < V; ++i) {
+      const int v = threadIdx.x + i * NT;
+      if (v < nvec) {
+        load8(p.a + base + v * 8, x[i]);
+        if (p.add) {
+          if constexpr (S == 0) {
+            load8(p.b + base + v * 8, b[i]);
+          } else if constexpr (S > 0) {
 #pragma unroll
-          for (int s = 0; s < S; ++s) {
-            const float4* src = reinterpret_cast<const float4*>(p.b32 + (size_t)s * p.T * p.H + base + v * 8);
-            part[i][s][0] = src[0];
-            part[i][s][1] = src[1];
-          }
-        }
-      }
-    }
-  }
-  double ss = 0.0;
-#pragma unroll
-  for (int i = 0; i < V; ++i) {
-    const int v = threadIdx.x + i * NT;
-    if (v < nvec) {
-      if (p.add) {
-        if constexpr (S != 0) {
-#pragma unroll
-          for (int e = 0; e < 8; ++e) b[i][e] = 0.f;
-          auto add_plane = [&](const float4 lo, const float4 hi) {
-            b[i][0] += lo.x; b[i][1] += lo.y; b[i][2] += lo.z; b[i][3] += lo.w;
-            b[i][4] += hi.x; b[i][5] += hi.y; b[i][6] += hi.z; b[i][7] += hi.w;
-          };
-          if constexpr (S > 0) {
-#pragma unroll
-            for (int s = 0; s < S; ++s) add_plane(part[i][s][0], part[i][s][1]);
-          } else if constexpr (S == -2) {
-            for (int r = 0; r < p.ps.world; ++r) {
-              const float4* src = reinterpret_cast<const float4*>(p.planes[r] + base + v * 8);
-              add_plane(__ldcg(src), __ldcg(src + 1));
-            }
-          } else {
-            for (int s = 0; s < p.splits; ++s) {
+            for (int s = 0; s < S; ++s) {
               const float4* src = reinterpret_cast<const float4*>(p.b32 + (size_t)s * p.T * p.H + base + v * 8);
-              add_plane(src[0], src[1]);
+              part[i][s][0] = src[0];
+              part[i][s][1] = src[1];
             }
           }
+        }
+      }
+    }
+    double ss = 0.0;
 #pragma unroll
-          for (int e = 0; e < 8; ++e) b[i][e] = round_bf(b[i][e]);  // the linear's bf16 output
+    for (int i = 0; i < V; ++i) {
+      const int v = threadIdx.x + i * NT;
+      if (v < nvec) {
+        if (p.add) {
+          if constexpr (S != 0) {
+#pragma unroll
+            for (int e = 0; e < 8; ++e) b[i][e] = 0.f;
+            auto add_plane = [&](const float4 lo, const float4 hi) {
+              b[i][0] += lo.x; b[i][1] += lo.y; b[i][2] += lo.z; b[i][3] += lo.w;
+              b[i][4] += hi.x; b[i][5] += hi.y; b[i][6] += hi.z; b[i][7] += hi.w;
+            };
+            if constexpr (S > 0) {
+#pragma unroll
+              for (int s = 0; s < S; ++s) add_plane(part[i][s][0], part[i][s][1]);
+            } else if constexpr (S == -2) {
+              for (int r = 0; r < p.ps.world; ++r) {
+                const float4* src = reinterpret_cast<const float4*>(p.planes[r] + base + v * 8);
+                add_plane(__ldcg(src), __ldcg(src + 1));
+              }
+            } else {
+              for (int s = 0; s < p.splits; ++s) {
+                const float4* src = reinterpret_cast<const float4*>(p.b32 + (size_t)s * p.T * p.H + base + v * 8);
+                add_plane(src[0], src[1]);
+              }
+            }
+#pragma unroll
+            for (int e = 0; e < 8; ++e) b[i][e] = round_bf(b[i][e]);  // the linear's bf16 output
+          }
+#pragma unroll
+          for (int e = 0; e < 8; ++e) x[i][e] = round_bf(x[i][e] + b[i][e]);
+          if (deep_row) {
+            float d[8];
+            load8(p.deep + (size_t)(row - p.start) * p.H + v * 8, d);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) x[i][e] = round_bf(x[i][e] + d[e]);
+          }
+          if (p.residual) store8(p.residual + base + v * 8, x[i]);
         }
 #pragma unroll
-        for (int e = 0; e < 8; ++e) x[i][e] = round_bf(x[i][e] + b[i][e]);
-        if (deep_row) {
-          float d[8];
-          load8(p.deep + (size_t)(row - p.start) * p.H + v * 8, d);
+        for (int e = 0; e < 8; ++e) ss += (double)(x[i][e] * x[i][e]);  // x*x exact in fp32
+      }
+    }
+    const float inv = inv_rms_from_ss(block_sum_d(ss, redd), p.H, p.eps);
+    float amax = 0.f;
 #pragma unroll
-          for (int e = 0; e < 8; ++e) x[i][e] = round_bf(x[i][e] + d[e]);
+    for (int i = 0; i < V; ++i) {
+      const int v = threadIdx.x + i * NT;
+      if (v < nvec) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          x[i][e] = round_bf(round_bf(x[i][e] * inv) * w[i][e]);
+          amax = fmaxf(amax, fabsf(x[i][e]));
         }
-        if (p.residual) store8(p.residual + base + v * 8, x[i]);
+        if (p.out) store8(p.out + base + v * 8, x[i]);
       }
-#pragma unroll
-      for (int e = 0; e < 8; ++e) ss += (double)(x[i][e] * x[i][e]);  // x*x exact in fp32
     }
-  }
-  const float inv = inv_rms_from_ss(block_sum_d(ss, redd), p.H, p.eps);
-  float amax = 0.f;
-#pragma unroll
-  for (int i = 0; i < V; ++i) {
-    const int v = threadIdx.x + i * NT;
-    if (v < nvec) {
-#pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        x[i][e] = round_bf(round_bf(x[i][e] * inv) * w[i][e]);
-        amax = fmaxf(amax, fabsf(x[i][e]));
-      }
-      if (p.out) store8(p.out + base + v * 8, x[i]);
+    if (p.quant_mode == FFB_QUANT_NONE) continue;
+    float mul = p.inv_scale, scale = 0.f;
+    if (p.quant_mode == FFB_QUANT_ROWWISE) {
+      amax = block_max(amax, red);
+      scale = fmaxf(amax, 1e-12f) / 448.f;
+      if (threadIdx.x == 0) p.qscale[row] = scale;
     }
-  }
-    if (p.quant_mode == FFB_QUANT_NONE) return;
-  float mul = p.inv_scale, scale = 0.f;
-  if (p.quant_mode == FFB_QUANT_ROWWISE) {
-    amax = block_max(amax, red);
-    scale = fmaxf(amax, 1e-12f) / 448.f;
-    if (threadIdx.x == 0) p.qscale[row] = scale;
-  }
 #pragma unroll
-  for (int i = 0; i < V; ++i) {
-    const int v = threadIdx.x + i * NT;
-    if (v < nvec) {
-      uint32_t lo = 0, hi = 0;
+    for (int i = 0; i < V; ++i) {
+      const int v = threadIdx.x + i * NT;
+      if (v < nvec) {
+        uint32_t lo = 0, hi = 0;
 #pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        const float qv = p.quant_mode == FFB_QUANT_ROWWISE ? __fdiv_rn(x[i][e], scale) : x[i][e] * mul;
-        const uint32_t b = f2e4m3(clamp448(qv));
-        if (e < 4) lo |= b << (8 * e);
-        else hi |= b << (8 * (e - 4));
+        for (int e = 0; e < 8; ++e) {
+          const float qv = p.quant_mode == FFB_QUANT_ROWWISE ? __fdiv_rn(x[i][e], scale) : x[i][e] * mul;
+          const uint32_t b = f2e4m3(clamp448(qv));
+          if (e < 4) lo |= b << (8 * e);
+          else hi |= b << (8 * (e - 4));
+        }
+        *reinterpret_cast<uint2*>(p.q8 + base + v * 8) = make_uint2(lo, hi);
       }
-      *reinterpret_cast<uint2*>(p.q8 + base + v * 8) = make_uint2(lo, hi);
     }
   }
 }
@@ -242,7 +244,11 @@ int run(const NormArgs& p, const char* who, void* stream) {
     case 4: kernel = add_rmsnorm_kernel<MAXV, 4>; break;
     default: break;
   }
-  cudaError_t e = ffb::launch(kernel, dim3(p.T), dim3(nt), 0, (cudaStream_t)stream, p);
+  // the peer variant handshakes once per CTA: a grid of at most two CTAs per SM strides
+  // over the rows
+  const int sms2 = 2 * ffb::sm_count();
+  const int grid = p.ps.world > 0 && p.T > sms2 ? sms2 : p.T;
+  cudaError_t e = ffb::launch(kernel, dim3(grid), dim3(nt), 0, (cudaStream_t)stream, p);
   if (e != cudaSuccess) return ffb::fail(FFB_ECUDA, "%s: launch: %s", who, cudaGetErrorString(e));
   return FFB_OK;
 }

@@ -4,33 +4,39 @@
 #pragma once
 #include "common.cuh"
 
-// Slot `slot` of every rank: rank `rank` adds 1 to flags[p][rank][slot] on every rank p
-// (release atomics at system scope), then waits until its own flags[rank][q][slot] has
-// reached the number of its own calls for this slot, for every rank q.  Every rank makes
-// the same sequence of calls per slot, so the counts advance in lockstep and need no reset.
-// One thread per CTA calls it (the CTA's writes it publishes are fenced before); false when
-// the bounded wait (2 s) gave up.
-__device__ __forceinline__ void red_release_sys_add(uint32_t* p, uint32_t v) {
-  asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+// Slot `slot` of every rank: rank `rank` adds 1 to flags[p][rank][slot] on every rank p,
+// then waits until its own flags[rank][q][slot] has reached the number of its own calls for
+// this slot, for every rank q.  Every rank makes the same sequence of calls per slot, so the
+// counts advance in lockstep and need no reset.  Release pattern: a system-scope fence, then
+// relaxed adds; acquire pattern: relaxed polling, then a system-scope fence.  One thread per
+// CTA calls it, after the CTA's writes to publish (ordered before it by a CTA barrier);
+// false when the bounded wait (2 s) gave up.
+__device__ __forceinline__ void red_relaxed_sys_add(uint32_t* p, uint32_t v) {
+  asm volatile("red.relaxed.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
-__device__ __forceinline__ uint32_t ld_acquire_sys_u32(const uint32_t* p) {
+__device__ __forceinline__ uint32_t ld_relaxed_sys_u32(const uint32_t* p) {
   uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
 __device__ __forceinline__ bool peer_handshake(const ffb_peer_sync& s, int slot) {
   const uint32_t n = s.local[slot] + 1u;  // only this CTA's one thread touches its slot
   s.local[slot] = n;
   __threadfence_system();
-  for (int p = 0; p < s.world; ++p) red_release_sys_add(s.flags[p] + (size_t)s.rank * s.nslots + slot, 1u);
+  for (int p = 0; p < s.world; ++p) red_relaxed_sys_add(s.flags[p] + (size_t)s.rank * s.nslots + slot, 1u);
   const uint64_t t0 = global_timer_ns();
-  for (int q = 0; q < s.world; ++q) {
+  bool ok = true;
+  for (int q = 0; q < s.world && ok; ++q) {
     const uint32_t* f = s.flags[s.rank] + (size_t)q * s.nslots + slot;
     uint32_t polls = 0;
-    while ((int)(ld_acquire_sys_u32(f) - n) < 0) {
-      __nanosleep(64);
-      if ((++polls & 31u) == 0 && global_timer_ns() - t0 > 2000000000ull) return false;
+    while ((int)(ld_relaxed_sys_u32(f) - n) < 0) {
+      __nanosleep(32);
+      if ((++polls & 31u) == 0 && global_timer_ns() - t0 > 2000000000ull) {
+        ok = false;
+        break;
+      }
     }
   }
-  return true;
+  __threadfence_system();
+  return ok;
 }

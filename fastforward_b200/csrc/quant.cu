@@ -100,12 +100,23 @@ __global__ void __launch_bounds__(1024) quant_rows_vec_kernel(const uint16_t* __
   }
 }
 
-// Rowwise quantiser of a row split over the tensor-parallel ranks: the slice maximum goes
-// to every rank's amax[p][rank][row] (peer stores), the row's CTA handshakes slot `row`
-// with every rank, and the scale is max(max over the ranks' maxima, 1e-12) / 448.
+// Rowwise quantiser of rows split over the tensor-parallel ranks.  A grid of at most two
+// CTAs per SM strides over the rows twice: first each row's slice maximum goes to every
+// rank's amax[p][rank][row] (peer stores); then the CTA handshakes its slot with every rank
+// (one handshake per CTA), and each row is quantised with max(max over the ranks' maxima,
+// 1e-12) / 448 as its scale.
 struct PeerAmax {
   float* amax[FFB_MAX_PEERS];  // rank p's [world][M] buffer, as mapped here
 };
+__device__ __forceinline__ void load_row8(const uint16_t* xr, int vi, float (&v)[8]) {
+  const uint4 u = *reinterpret_cast<const uint4*>(xr + vi * 8);
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    v[2 * e] = __uint_as_float(w[e] << 16);
+    v[2 * e + 1] = __uint_as_float(w[e] & 0xffff0000u);
+  }
+}
 __global__ void __launch_bounds__(1024) quant_rows_peer_kernel(const uint16_t* __restrict__ x, PeerAmax pa,
                                                               ffb_peer_sync ps, uint8_t* __restrict__ q8,
                                                               float* __restrict__ qscale, int M, int K) {
@@ -113,50 +124,55 @@ __global__ void __launch_bounds__(1024) quant_rows_peer_kernel(const uint16_t* _
   __shared__ int hs_ok;
   pdl_wait();
   pdl_launch();
-  const int row = blockIdx.x, nvec = K / 8;
-  const uint16_t* xr = x + (size_t)row * K;
-  uint8_t* qr = q8 + (size_t)row * K;
-  float v[QV][8];
-  float amax = 0.f;
+  const int nvec = K / 8;
+  for (int row = blockIdx.x; row < M; row += gridDim.x) {
+    const uint16_t* xr = x + (size_t)row * K;
+    float amax = 0.f;
 #pragma unroll
-  for (int i = 0; i < QV; ++i) {
-    const int vi = threadIdx.x + i * blockDim.x;
-    if (vi < nvec) {
-      const uint4 u = *reinterpret_cast<const uint4*>(xr + vi * 8);
-      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+    for (int i = 0; i < QV; ++i) {
+      const int vi = threadIdx.x + i * blockDim.x;
+      if (vi < nvec) {
+        float v[8];
+        load_row8(xr, vi, v);
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        v[i][2 * e] = __uint_as_float(w[e] << 16);
-        v[i][2 * e + 1] = __uint_as_float(w[e] & 0xffff0000u);
+        for (int e = 0; e < 8; ++e) amax = fmaxf(amax, fabsf(v[e]));
       }
-#pragma unroll
-      for (int e = 0; e < 8; ++e) amax = fmaxf(amax, fabsf(v[i][e]));
+    }
+    amax = block_max_any(amax, red);
+    if (threadIdx.x < ps.world) {
+      pa.amax[threadIdx.x][(size_t)ps.rank * M + row] = amax;
+      __threadfence_system();
     }
   }
-  amax = block_max_any(amax, red);
+  __syncthreads();
   if (threadIdx.x == 0) {
-    for (int p = 0; p < ps.world; ++p) pa.amax[p][(size_t)ps.rank * M + row] = amax;
-    hs_ok = peer_handshake(ps, row);  // fences the stores above before its signals
+    hs_ok = peer_handshake(ps, blockIdx.x);  // fences the maxima above before its signals
     if (!hs_ok) atomicOr(&ffb_device_error_word, ffb::ERR_PEER_TIMEOUT);
   }
   __syncthreads();
   if (!hs_ok) return;
-  float m = 0.f;
-  for (int q = 0; q < ps.world; ++q) m = fmaxf(m, __ldcg(pa.amax[ps.rank] + (size_t)q * M + row));
-  const float scale = fmaxf(m, 1e-12f) / 448.f;
-  if (threadIdx.x == 0) qscale[row] = scale;
+  for (int row = blockIdx.x; row < M; row += gridDim.x) {
+    const uint16_t* xr = x + (size_t)row * K;
+    uint8_t* qr = q8 + (size_t)row * K;
+    float m = 0.f;
+    for (int q = 0; q < ps.world; ++q) m = fmaxf(m, __ldcg(pa.amax[ps.rank] + (size_t)q * M + row));
+    const float scale = fmaxf(m, 1e-12f) / 448.f;
+    if (threadIdx.x == 0) qscale[row] = scale;
 #pragma unroll
-  for (int i = 0; i < QV; ++i) {
-    const int vi = threadIdx.x + i * blockDim.x;
-    if (vi < nvec) {
-      uint32_t lo = 0, hi = 0;
+    for (int i = 0; i < QV; ++i) {
+      const int vi = threadIdx.x + i * blockDim.x;
+      if (vi < nvec) {
+        float v[8];
+        load_row8(xr, vi, v);
+        uint32_t lo = 0, hi = 0;
 #pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        const uint32_t b = f2e4m3(clamp448(__fdiv_rn(v[i][e], scale)));
-        if (e < 4) lo |= b << (8 * e);
-        else hi |= b << (8 * (e - 4));
+        for (int e = 0; e < 8; ++e) {
+          const uint32_t b = f2e4m3(clamp448(__fdiv_rn(v[e], scale)));
+          if (e < 4) lo |= b << (8 * e);
+          else hi |= b << (8 * (e - 4));
+        }
+        *reinterpret_cast<uint2*>(qr + vi * 8) = make_uint2(lo, hi);
       }
-      *reinterpret_cast<uint2*>(qr + vi * 8) = make_uint2(lo, hi);
     }
   }
 }
@@ -361,8 +377,9 @@ extern "C" int ffb_quantize_fp8_peers(const uint16_t* x, float* const* amax, con
   }
   int nt = (K / 8 + QV - 1) / QV;
   nt = (nt + 31) / 32 * 32;
-  cudaError_t e = ffb::launch(quant_rows_peer_kernel, dim3(M), dim3(nt), 0, (cudaStream_t)stream, x, pa, *sync, q8,
-                              qscale, M, K);
+  const int grid = M < 2 * ffb::sm_count() ? M : 2 * ffb::sm_count();
+  cudaError_t e = ffb::launch(quant_rows_peer_kernel, dim3(grid), dim3(nt), 0, (cudaStream_t)stream, x, pa, *sync,
+                              q8, qscale, M, K);
   if (e != cudaSuccess) return ffb::fail(FFB_ECUDA, "ffb_quantize_fp8_peers: %s", cudaGetErrorString(e));
   return FFB_OK;
 }

@@ -366,7 +366,7 @@ int ffb_pack_rgb_batch(const uint8_t* rgb, uint16_t* pixels, int n, int height, 
 /* Handshake state of one rank: flags[p] is rank p's [world][nslots] uint32 array (for
  * p == rank this process's own, else the IPC mapping of rank p's); local is this rank's
  * [nslots] uint32 call counts.  Both zero before the first call of any rank.  Slot i is
- * used by row i's CTA; every rank must make the same sequence of calls. */
+ * used by CTA i of a call; every rank must make the same sequence of calls. */
 typedef struct ffb_peer_sync {
   uint32_t* flags[FFB_MAX_PEERS];
   uint32_t* local;
@@ -384,9 +384,10 @@ int ffb_peer_free(void* dptr);
  * array of `world` device pointers; rank r's [T, H] plane, peer-mapped) are summed in rank
  * order ((p0 + p1) + p2 ...), then rounded to bf16 as the linear's output.  Replaces the
  * NCCL all-reduce of the row-parallel o_proj / down_proj partials plus the residual add +
- * RMSNorm (_legacy/lower_kernels.py:7-32) of a tensor-parallel layer.  Row t's CTA
- * handshakes slot t with every rank before reading the planes (its own rank's producer has
- * finished by stream order); a wait that gives up after 2 s sets the device error word. */
+ * RMSNorm (_legacy/lower_kernels.py:7-32) of a tensor-parallel layer.  A grid of at most two
+ * CTAs per SM strides over the rows; CTA i handshakes slot i with every rank once before
+ * reading the planes (its own rank's producer has finished by stream order); a wait that
+ * gives up after 2 s sets the device error word.  Slots used: min(T, 2 x SMs). */
 int ffb_add_rmsnorm_peers(const uint16_t* a, const float* const* planes, const ffb_peer_sync* sync,
                           const uint16_t* deep, int start, int nv, const uint16_t* w, float eps,
                           uint16_t* residual, uint16_t* out, int quant_mode, float inv_scale,
