@@ -244,10 +244,10 @@ int run(const NormArgs& p, const char* who, void* stream) {
     case 4: kernel = add_rmsnorm_kernel<MAXV, 4>; break;
     default: break;
   }
-  // the peer variant handshakes once per CTA: a grid of at most two CTAs per SM strides
+  // the peer variant handshakes once per CTA: a grid of at most four CTAs per SM strides
   // over the rows
-  const int sms2 = 2 * ffb::sm_count();
-  const int grid = p.ps.world > 0 && p.T > sms2 ? sms2 : p.T;
+  const int sms4 = 4 * ffb::sm_count();
+  const int grid = p.ps.world > 0 && p.T > sms4 ? sms4 : p.T;
   cudaError_t e = ffb::launch(kernel, dim3(grid), dim3(nt), 0, (cudaStream_t)stream, p);
   if (e != cudaSuccess) return ffb::fail(FFB_ECUDA, "%s: launch: %s", who, cudaGetErrorString(e));
   return FFB_OK;

@@ -100,7 +100,7 @@ __global__ void __launch_bounds__(1024) quant_rows_vec_kernel(const uint16_t* __
   }
 }
 
-// Rowwise quantiser of rows split over the tensor-parallel ranks.  A grid of at most two
+// Rowwise quantiser of rows split over the tensor-parallel ranks.  A grid of at most four
 // CTAs per SM strides over the rows twice: first each row's slice maximum goes to every
 // rank's amax[p][rank][row] (peer stores); then the CTA handshakes its slot with every rank
 // (one handshake per CTA), and each row is quantised with max(max over the ranks' maxima,
@@ -141,7 +141,7 @@ __global__ void __launch_bounds__(1024) quant_rows_peer_kernel(const uint16_t* _
     amax = block_max_any(amax, red);
     if (threadIdx.x < ps.world) {
       pa.amax[threadIdx.x][(size_t)ps.rank * M + row] = amax;
-      __threadfence_system();
+      fence_acq_rel_sys();
     }
   }
   __syncthreads();
@@ -377,7 +377,7 @@ extern "C" int ffb_quantize_fp8_peers(const uint16_t* x, float* const* amax, con
   }
   int nt = (K / 8 + QV - 1) / QV;
   nt = (nt + 31) / 32 * 32;
-  const int grid = M < 2 * ffb::sm_count() ? M : 2 * ffb::sm_count();
+  const int grid = M < 4 * ffb::sm_count() ? M : 4 * ffb::sm_count();
   cudaError_t e = ffb::launch(quant_rows_peer_kernel, dim3(grid), dim3(nt), 0, (cudaStream_t)stream, x, pa, *sync,
                               q8, qscale, M, K);
   if (e != cudaSuccess) return ffb::fail(FFB_ECUDA, "ffb_quantize_fp8_peers: %s", cudaGetErrorString(e));

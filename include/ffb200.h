@@ -384,10 +384,10 @@ int ffb_peer_free(void* dptr);
  * array of `world` device pointers; rank r's [T, H] plane, peer-mapped) are summed in rank
  * order ((p0 + p1) + p2 ...), then rounded to bf16 as the linear's output.  Replaces the
  * NCCL all-reduce of the row-parallel o_proj / down_proj partials plus the residual add +
- * RMSNorm (_legacy/lower_kernels.py:7-32) of a tensor-parallel layer.  A grid of at most two
+ * RMSNorm (_legacy/lower_kernels.py:7-32) of a tensor-parallel layer.  A grid of at most four
  * CTAs per SM strides over the rows; CTA i handshakes slot i with every rank once before
  * reading the planes (its own rank's producer has finished by stream order); a wait that
- * gives up after 2 s sets the device error word.  Slots used: min(T, 2 x SMs). */
+ * gives up after 2 s sets the device error word.  Slots used: min(T, 4 x SMs). */
 int ffb_add_rmsnorm_peers(const uint16_t* a, const float* const* planes, const ffb_peer_sync* sync,
                           const uint16_t* deep, int start, int nv, const uint16_t* w, float eps,
                           uint16_t* residual, uint16_t* out, int quant_mode, float inv_scale,
