@@ -720,8 +720,8 @@ def tp32b_measure(args, world, rank, local, dev):
             return tot.item(), lat_, zz, path
 
         clk = Clocks(local)
-        total, lat, z, path = time_engine(True, clk)
-        total_nccl, lat_nccl, z_nccl, _ = time_engine(False, None)
+        total, lat, z, path = time_engine(False, clk)  # the default: NCCL collectives
+        total_peer, lat_peer, z_peer, peer_path = time_engine(True, None)
         p50 = lat[len(lat) // 2]
 
         def coll_us(numel, op):  # one collective alone, device-timed, median of 20, max over ranks
@@ -747,20 +747,19 @@ def tp32b_measure(args, world, rank, local, dev):
     if rank != 0:
         return None
     per_req = total / steps
-    per_req_nccl = total_nccl / steps
+    per_req_peer = total_peer / steps
     n_ar = 2 * (dims.layers - 1) + 2
     return dict(workload=wl, parallelism=f"tp{world}", reductions=path, ms_per_request=per_req * 1e3,
                 latency_ms=dict(p50=p50, p99=lat[-1]), tok_per_s=T / per_req, requests_per_s=1.0 / per_req,
-                nccl_reductions=dict(ms_per_request=per_req_nccl * 1e3, p50=lat_nccl[len(lat_nccl) // 2],
-                                     logits_equal=z == z_nccl,
-                                     note="the same model and graph with every reduction an NCCL collective"),
+                peer_reductions=dict(ms_per_request=per_req_peer * 1e3, p50=lat_peer[len(lat_peer) // 2],
+                                     path=peer_path, logits_equal=z == z_peer,
+                                     note="Engine(peer=True): the full layers' reductions read from peer memory "
+                                          "inside ffb_add_rmsnorm_peers / ffb_quantize_fp8_peers"),
                 allreduce=dict(per_call_us=ar_us, bytes_per_call=T * dims.hidden * 4, calls_per_request=n_ar,
                                busbw_gbs=2 * (world - 1) / world * T * dims.hidden * 4 / (ar_us * 1e-6) / 1e9,
-                               share_of_request_nccl=n_ar * ar_us * 1e-3 / (per_req_nccl * 1e3),
+                               share_of_request=n_ar * ar_us * 1e-3 / (per_req * 1e3),
                                scale_max_us=scale_us, scale_calls_per_request=n_ar,
-                               note="NCCL all-reduce of one fp32 [T, H] partial / of the [T] scales, timed alone; "
-                                    "with reductions='peer' the full layers read the partials and maxima from "
-                                    "peer memory inside ffb_add_rmsnorm_peers / ffb_quantize_fp8_peers"),
+                               note="NCCL all-reduce of one fp32 [T, H] partial / of the [T] scales, timed alone"),
                 logits=z, clocks=clk.summary())
 
 
