@@ -406,9 +406,9 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
       named_barrier(2, SOFTMAX_WARPS * 32);
       volatile int* verdict = reinterpret_cast<volatile int*>(xch);  // the exchange buffers are free now
-      if (warp == 2 && lane == 0) {
+      if (warp == 2 && lane == 0) {  // (warp 2's own rows may all be dropped: `ok`, not `stage`)
         int v = 0;
-        if (stage && xok && !*abort_flag) {
+        if (ok && xok && !*abort_flag) {
           const uint32_t old = atomicAdd(args.tile_count + tile, 1u);
           const uint32_t target = (old / (uint32_t)args.HQ + 1u) * (uint32_t)args.HQ;
           const uint64_t t0 = global_timer_ns();
