@@ -247,11 +247,6 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int r = quarter * 32 + lane;  // this thread's query row in the tile
     // selected rows: every row of the tile masks as row 0; non-causal: as the last row
     const int qpos = !args.causal ? args.T - 1 : rows_mode ? spos : q0 + r;
-    // whether any of this warp's 32 rows is kept (selected rows: only row 0 of the tile;
-    // otherwise rows below T).  The other warps skip the math of every block -- their rows'
-    // results are dropped -- and only keep the barriers' arrival counts, so the warps that
-    // matter get the issue slots (the last, partial query tile is the heaviest one).
-    const bool live = rows_mode ? quarter == 0 : q0 + quarter * 32 < args.T;
     const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
     float o[D / 4];
 #pragma unroll
@@ -300,18 +295,12 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
       tc_fence_after();
       uint32_t sr[16];
-      if (live) {
-        tmem_ld16_async(tmem + lane_addr + 64 * b + 16 * part, sr);
-        tmem_wait_ld();
-        reg_fence(sr);
-      }
+      tmem_ld16_async(tmem + lane_addr + 64 * b + 16 * part, sr);
+      tmem_wait_ld();
+      reg_fence(sr);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&s_free[b]);  // the MMA warp may overwrite S[b]
-      if (!live) {  // no row of this warp is kept: its P rows stay as they are (their O rows are dropped)
-        if (lane == 0) mbar_arrive(&p_full[b]);
-        continue;
-      }
       // mask (blocks reaching past the tile's first row or past T, or below a row's first
       // visible key) + scale into base 2, in place
       float bmax = -INFINITY;
@@ -368,8 +357,8 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (j > 0) ok = fold(j - 1, alpha_prev);  // block j-1's P.V ran while this softmax did
       alpha_prev = alpha;
     }
-    if (ok && nit > 0 && live) ok = fold(nit - 1, alpha_prev);
-    if (ok && live) {
+    if (ok && nit > 0) ok = fold(nit - 1, alpha_prev);
+    if (ok) {
       float parts[4];
       ok = exchange(l, parts) && !*abort_flag;
       l = __fadd_rn(__fadd_rn(__fadd_rn(parts[0], parts[1]), parts[2]), parts[3]);  // the four parts, in order
@@ -378,7 +367,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     // Output tile [128 rows x 128 columns] bf16 staged as two 128-byte-swizzled [128 x 64]
     // boxes in the P tiles (every P.V has completed: the last fold waited for it), then TMA
     // stores; rows past T are clipped by the store.
-    bool stage = ok && live && !*abort_flag;
+    bool stage = ok && !*abort_flag;
     const bool fp8_out = args.out_inv > 0.f;
     float rscale = 0.f;  // rowwise FP8: this row's scale
     if (args.headmax != nullptr) {
@@ -406,7 +395,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
       named_barrier(2, SOFTMAX_WARPS * 32);
       volatile int* verdict = reinterpret_cast<volatile int*>(xch);  // the exchange buffers are free now
-      if (warp == 2 && lane == 0) {  // (warp 2's own rows may all be dropped: `ok`, not `stage`)
+      if (warp == 2 && lane == 0) {
         int v = 0;
         if (ok && xok && !*abort_flag) {
           const uint32_t old = atomicAdd(args.tile_count + tile, 1u);
