@@ -70,6 +70,9 @@ def parse():
                         "--workload 2B-layer-T512) instead of whole requests")
     p.add_argument("--layers", type=int, default=None,
                    help="build only this many decoder layers (same shapes; for small profiler captures)")
+    p.add_argument("--tp-peer", action="store_true",
+                   help="N > 1: also time the 32B tensor-parallel model with its reductions through peer memory "
+                        "(Engine(peer=True)) beside the NCCL default")
     p.add_argument("--vision-ncu", action="store_true",
                    help="run only the 4B vision tower and replay one forward inside a profiler range")
     p.add_argument("--ncu-range", action="store_true",
@@ -721,7 +724,8 @@ def tp32b_measure(args, world, rank, local, dev):
 
         clk = Clocks(local)
         total, lat, z, path = time_engine(False, clk)  # the default: NCCL collectives
-        total_peer, lat_peer, z_peer, peer_path = time_engine(True, None)
+        if args.tp_peer:
+            total_peer, lat_peer, z_peer, peer_path = time_engine(True, None)
         p50 = lat[len(lat) // 2]
 
         def coll_us(numel, op):  # one collective alone, device-timed, median of 20, max over ranks
@@ -747,14 +751,14 @@ def tp32b_measure(args, world, rank, local, dev):
     if rank != 0:
         return None
     per_req = total / steps
-    per_req_peer = total_peer / steps
     n_ar = 2 * (dims.layers - 1) + 2
     return dict(workload=wl, parallelism=f"tp{world}", reductions=path, ms_per_request=per_req * 1e3,
                 latency_ms=dict(p50=p50, p99=lat[-1]), tok_per_s=T / per_req, requests_per_s=1.0 / per_req,
-                peer_reductions=dict(ms_per_request=per_req_peer * 1e3, p50=lat_peer[len(lat_peer) // 2],
-                                     path=peer_path, logits_equal=z == z_peer,
-                                     note="Engine(peer=True): the full layers' reductions read from peer memory "
-                                          "inside ffb_add_rmsnorm_peers / ffb_quantize_fp8_peers"),
+                peer_reductions=(dict(ms_per_request=total_peer / steps * 1e3, p50=lat_peer[len(lat_peer) // 2],
+                                      path=peer_path, logits_equal=z == z_peer,
+                                      note="Engine(peer=True): the full layers' reductions read from peer memory "
+                                           "inside ffb_add_rmsnorm_peers / ffb_quantize_fp8_peers")
+                                 if args.tp_peer else None),
                 allreduce=dict(per_call_us=ar_us, bytes_per_call=T * dims.hidden * 4, calls_per_request=n_ar,
                                busbw_gbs=2 * (world - 1) / world * T * dims.hidden * 4 / (ar_us * 1e-6) / 1e9,
                                share_of_request=n_ar * ar_us * 1e-3 / (per_req * 1e3),
