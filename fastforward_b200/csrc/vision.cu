@@ -97,21 +97,30 @@ __global__ void __launch_bounds__(1024) layernorm_kernel(const uint16_t* __restr
 }
 
 // One CTA per (patch, part of q / k / v), one thread per 8 output columns of a head: the
-// part's H x d row is staged in shared memory (16-byte loads), then each thread writes 16
-// bytes of the head-major output.  qkv row p = [q (H x d) | k (H x d) | v (H x d)];
-// cos / sin [P, d] fp32.  q, k: y[c] = x[c] cos[c] + r[c] sin[c] with r = (-x[c + d/2] for
-// c < d/2, x[c - d/2] otherwise), both products and the sum IEEE fp32 operations, then
-// bf16; v copied.  Outputs [H, P, dp] with columns d..dp-1 zero.
+// part's H x d row (and for q / k the patch's cos / sin rows) is staged in shared memory
+// with 16-byte loads, then each thread writes 16 bytes of the head-major output.  qkv row
+// p = [q (H x d) | k (H x d) | v (H x d)]; cos / sin [P, d] fp32.  q, k: y[c] = x[c] cos[c] +
+// r[c] sin[c] with r = (-x[c + d/2] for c < d/2, x[c - d/2] otherwise), both products and
+// the sum IEEE fp32 operations, then bf16; v copied.  Outputs [H, P, dp] with columns
+// d..dp-1 zero.
 __global__ void vision_rope_kernel(const uint16_t* __restrict__ qkv, const float* __restrict__ cs,
                                    const float* __restrict__ sn, int P, int H, int d, int dp, uint16_t* q,
                                    uint16_t* k, uint16_t* v) {
-  extern __shared__ uint16_t srow[];  // [H * d]
+  extern __shared__ __align__(16) uint8_t vr_smem[];
+  uint16_t* srow = reinterpret_cast<uint16_t*>(vr_smem);   // [H * d]
+  float* scos = reinterpret_cast<float*>(vr_smem + ((size_t)H * d * 2 + 15) / 16 * 16);  // [d]
+  float* ssin = scos + d;                                                              // [d]
   pdl_wait();
   pdl_launch();
   const int p = blockIdx.x, part = blockIdx.y, half = d / 2, hd = H * d;
   const uint16_t* src = qkv + (size_t)p * 3 * hd + (size_t)part * hd;
   for (int i = threadIdx.x; i < hd / 8; i += blockDim.x)
     reinterpret_cast<uint4*>(srow)[i] = reinterpret_cast<const uint4*>(src)[i];
+  if (part < 2)
+    for (int i = threadIdx.x; i < d / 4; i += blockDim.x) {  // d is a multiple of 8
+      reinterpret_cast<float4*>(scos)[i] = __ldg(reinterpret_cast<const float4*>(cs + (size_t)p * d) + i);
+      reinterpret_cast<float4*>(ssin)[i] = __ldg(reinterpret_cast<const float4*>(sn + (size_t)p * d) + i);
+    }
   __syncthreads();
   const int cpr = dp / 8;  // 16-byte chunks per output row
   uint16_t* dst = part == 0 ? q : (part == 1 ? k : v);
@@ -132,7 +141,7 @@ __global__ void vision_rope_kernel(const uint16_t* __restrict__ qkv, const float
             out = xv;
           } else {
             const float rv = c < half ? -bf2f(row[c + half]) : bf2f(row[c - half]);
-            out = __fadd_rn(__fmul_rn(xv, __ldg(cs + (size_t)p * d + c)), __fmul_rn(rv, __ldg(sn + (size_t)p * d + c)));
+            out = __fadd_rn(__fmul_rn(xv, scos[c]), __fmul_rn(rv, ssin[c]));
           }
         }
         y[j] = out;
@@ -174,8 +183,10 @@ extern "C" int ffb_vision_rope(const uint16_t* qkv, const float* cos, const floa
   FFB_REQUIRE(ffb::aligned(qkv, 16) && ffb::aligned(q, 16) && ffb::aligned(k, 16) && ffb::aligned(v, 16),
               "ffb_vision_rope: qkv, q, k, v must be 16-byte aligned");
   const int threads = H * (dp / 8) < 1024 ? (H * (dp / 8) + 31) / 32 * 32 : 1024;
-  cudaError_t e = ffb::launch(vision_rope_kernel, dim3(P, 3), dim3(threads), (size_t)H * d * 2, (cudaStream_t)stream,
-                              qkv, cos, sin, P, H, d, dp, q, k, v);
+  FFB_REQUIRE(ffb::aligned(cos, 16) && ffb::aligned(sin, 16), "ffb_vision_rope: cos and sin must be 16-byte aligned");
+  const size_t smem = ((size_t)H * d * 2 + 15) / 16 * 16 + (size_t)2 * d * 4;
+  cudaError_t e = ffb::launch(vision_rope_kernel, dim3(P, 3), dim3(threads), smem, (cudaStream_t)stream, qkv, cos, sin,
+                              P, H, d, dp, q, k, v);
   if (e != cudaSuccess) return ffb::fail(FFB_ECUDA, "ffb_vision_rope: launch: %s", cudaGetErrorString(e));
   return FFB_OK;
 }

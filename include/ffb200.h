@@ -448,7 +448,7 @@ int ffb_add_layernorm(const uint16_t* a, const uint16_t* add, const uint16_t* w,
  * y[c] = x[c] * cos[c] + r[c] * sin[c] with r = rotate_half(x) (each product and the sum
  * rounded to fp32, then bf16).  qkv [P, 3*H*d] bf16 (patch rows [q | k | v], heads of d);
  * cos, sin [P, d] fp32; q, k, v [H, P, dp] bf16 with columns d..dp-1 zero (dp >= d; d and
- * dp multiples of 8, H * d <= 16384; qkv, q, k, v 16-byte aligned). */
+ * dp multiples of 8, H * d <= 16384; qkv, q, k, v, cos, sin 16-byte aligned). */
 int ffb_vision_rope(const uint16_t* qkv, const float* cos, const float* sin, int P, int H, int d,
                     int dp, uint16_t* q, uint16_t* k, uint16_t* v, void* stream);
 
