@@ -96,37 +96,36 @@ __global__ void __launch_bounds__(1024) layernorm_kernel(const uint16_t* __restr
   *reinterpret_cast<uint4*>(y + off) = make_uint4(o[0], o[1], o[2], o[3]);
 }
 
-// One CTA per (patch, part of q / k / v), one thread per 8 output columns of a head: the
-// part's H x d row (and for q / k the patch's cos / sin rows) is staged in shared memory
-// with 16-byte loads, then each thread writes 16 bytes of the head-major output.  qkv row
-// p = [q (H x d) | k (H x d) | v (H x d)]; cos / sin [P, d] fp32.  q, k: y[c] = x[c] cos[c] +
-// r[c] sin[c] with r = (-x[c + d/2] for c < d/2, x[c - d/2] otherwise), both products and
-// the sum IEEE fp32 operations, then bf16; v copied.  Outputs [H, P, dp] with columns
-// d..dp-1 zero.
+// One CTA per patch, one thread per 8 columns of a head of q, k or v: the patch's qkv row
+// (and its cos / sin rows) staged in shared memory with 16-byte loads, then each thread
+// writes 16 bytes of the head-major output.  qkv row p = [q (H x d) | k (H x d) |
+// v (H x d)]; cos / sin [P, d] fp32.  q, k: y[c] = x[c] cos[c] + r[c] sin[c] with
+// r = (-x[c + d/2] for c < d/2, x[c - d/2] otherwise), both products and the sum IEEE fp32
+// operations, then bf16; v copied.  Outputs [H, P, dp]: columns [0, d) written, columns
+// [d, dp) (the attention kernel's zero padding) left as they are.
 __global__ void vision_rope_kernel(const uint16_t* __restrict__ qkv, const float* __restrict__ cs,
                                    const float* __restrict__ sn, int P, int H, int d, int dp, uint16_t* q,
                                    uint16_t* k, uint16_t* v) {
   extern __shared__ __align__(16) uint8_t vr_smem[];
-  uint16_t* srow = reinterpret_cast<uint16_t*>(vr_smem);   // [H * d]
-  float* scos = reinterpret_cast<float*>(vr_smem + ((size_t)H * d * 2 + 15) / 16 * 16);  // [d]
-  float* ssin = scos + d;                                                              // [d]
+  const int hd = H * d;
+  uint16_t* srow = reinterpret_cast<uint16_t*>(vr_smem);                             // [3 * H * d]
+  float* scos = reinterpret_cast<float*>(vr_smem + ((size_t)3 * hd * 2 + 15) / 16 * 16);  // [d]
+  float* ssin = scos + d;                                                               // [d]
   pdl_wait();
   pdl_launch();
-  const int p = blockIdx.x, part = blockIdx.y, half = d / 2, hd = H * d;
-  const uint16_t* src = qkv + (size_t)p * 3 * hd + (size_t)part * hd;
-  for (int i = threadIdx.x; i < hd / 8; i += blockDim.x)
+  const int p = blockIdx.x, half = d / 2;
+  const uint16_t* src = qkv + (size_t)p * 3 * hd;
+  for (int i = threadIdx.x; i < 3 * hd / 8; i += blockDim.x)
     reinterpret_cast<uint4*>(srow)[i] = reinterpret_cast<const uint4*>(src)[i];
-  if (part < 2)
-    for (int i = threadIdx.x; i < d / 4; i += blockDim.x) {  // d is a multiple of 8
-      reinterpret_cast<float4*>(scos)[i] = __ldg(reinterpret_cast<const float4*>(cs + (size_t)p * d) + i);
-      reinterpret_cast<float4*>(ssin)[i] = __ldg(reinterpret_cast<const float4*>(sn + (size_t)p * d) + i);
-    }
+  for (int i = threadIdx.x; i < d / 4; i += blockDim.x) {  // d is a multiple of 8
+    reinterpret_cast<float4*>(scos)[i] = __ldg(reinterpret_cast<const float4*>(cs + (size_t)p * d) + i);
+    reinterpret_cast<float4*>(ssin)[i] = __ldg(reinterpret_cast<const float4*>(sn + (size_t)p * d) + i);
+  }
   __syncthreads();
-  const int cpr = dp / 8;  // 16-byte chunks per output row
-  uint16_t* dst = part == 0 ? q : (part == 1 ? k : v);
-  for (int t = threadIdx.x; t < H * cpr; t += blockDim.x) {
-    const int h = t / cpr, c0 = (t - h * cpr) * 8;
-    const uint16_t* row = srow + h * d;
+  const int cpr = d / 8;  // 16-byte chunks per head row
+  for (int t = threadIdx.x; t < 3 * H * cpr; t += blockDim.x) {
+    const int part = t / (H * cpr), rem = t - part * H * cpr, h = rem / cpr, c0 = (rem - h * cpr) * 8;
+    const uint16_t* row = srow + (size_t)part * hd + h * d;
     uint32_t w[4];
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
@@ -134,20 +133,17 @@ __global__ void vision_rope_kernel(const uint16_t* __restrict__ qkv, const float
 #pragma unroll
       for (int j = 0; j < 2; ++j) {
         const int c = c0 + 2 * e + j;
-        float out = 0.f;
-        if (c < d) {
-          const float xv = bf2f(row[c]);
-          if (part == 2) {
-            out = xv;
-          } else {
-            const float rv = c < half ? -bf2f(row[c + half]) : bf2f(row[c - half]);
-            out = __fadd_rn(__fmul_rn(xv, scos[c]), __fmul_rn(rv, ssin[c]));
-          }
+        const float xv = bf2f(row[c]);
+        if (part == 2) {
+          y[j] = xv;
+        } else {
+          const float rv = c < half ? -bf2f(row[c + half]) : bf2f(row[c - half]);
+          y[j] = __fadd_rn(__fmul_rn(xv, scos[c]), __fmul_rn(rv, ssin[c]));
         }
-        y[j] = out;
       }
       w[e] = (uint32_t)f2bf(y[0]) | ((uint32_t)f2bf(y[1]) << 16);
     }
+    uint16_t* dst = part == 0 ? q : (part == 1 ? k : v);
     *reinterpret_cast<uint4*>(dst + ((size_t)h * P + p) * dp + c0) = make_uint4(w[0], w[1], w[2], w[3]);
   }
 }
@@ -178,15 +174,16 @@ extern "C" int ffb_layernorm(const uint16_t* x, const uint16_t* w, const uint16_
 extern "C" int ffb_vision_rope(const uint16_t* qkv, const float* cos, const float* sin, int P, int H, int d, int dp,
                                uint16_t* q, uint16_t* k, uint16_t* v, void* stream) {
   FFB_REQUIRE(qkv && cos && sin && q && k && v, "ffb_vision_rope: NULL pointer");
-  FFB_REQUIRE(P > 0 && H > 0 && d > 0 && d % 8 == 0 && dp >= d && dp % 8 == 0 && dp <= 256 && H * d <= 16384,
+  FFB_REQUIRE(P > 0 && H > 0 && d > 0 && d % 8 == 0 && dp >= d && dp % 8 == 0 && dp <= 256 && H * d <= 7680,
               "ffb_vision_rope: bad shape P=%d H=%d d=%d dp=%d (d, dp multiples of 8)", P, H, d, dp);
   FFB_REQUIRE(ffb::aligned(qkv, 16) && ffb::aligned(q, 16) && ffb::aligned(k, 16) && ffb::aligned(v, 16),
               "ffb_vision_rope: qkv, q, k, v must be 16-byte aligned");
-  const int threads = H * (dp / 8) < 1024 ? (H * (dp / 8) + 31) / 32 * 32 : 1024;
+  const int work = 3 * H * (d / 8);
+  const int threads = work < 1024 ? (work + 31) / 32 * 32 : 1024;
   FFB_REQUIRE(ffb::aligned(cos, 16) && ffb::aligned(sin, 16), "ffb_vision_rope: cos and sin must be 16-byte aligned");
-  const size_t smem = ((size_t)H * d * 2 + 15) / 16 * 16 + (size_t)2 * d * 4;
-  cudaError_t e = ffb::launch(vision_rope_kernel, dim3(P, 3), dim3(threads), smem, (cudaStream_t)stream, qkv, cos, sin,
-                              P, H, d, dp, q, k, v);
+  const size_t smem = ((size_t)3 * H * d * 2 + 15) / 16 * 16 + (size_t)2 * d * 4;
+  cudaError_t e = ffb::launch(vision_rope_kernel, dim3(P), dim3(threads), smem, (cudaStream_t)stream, qkv, cos, sin, P,
+                              H, d, dp, q, k, v);
   if (e != cudaSuccess) return ffb::fail(FFB_ECUDA, "ffb_vision_rope: launch: %s", cudaGetErrorString(e));
   return FFB_OK;
 }

@@ -447,8 +447,9 @@ int ffb_add_layernorm(const uint16_t* a, const uint16_t* add, const uint16_t* w,
  * kernel.  Replaces `_vision_rope` (_legacy/search_kernels.py:111-125): for q and k,
  * y[c] = x[c] * cos[c] + r[c] * sin[c] with r = rotate_half(x) (each product and the sum
  * rounded to fp32, then bf16).  qkv [P, 3*H*d] bf16 (patch rows [q | k | v], heads of d);
- * cos, sin [P, d] fp32; q, k, v [H, P, dp] bf16 with columns d..dp-1 zero (dp >= d; d and
- * dp multiples of 8, H * d <= 16384; qkv, q, k, v, cos, sin 16-byte aligned). */
+ * cos, sin [P, d] fp32; q, k, v [H, P, dp] bf16: columns [0, d) written, columns [d, dp)
+ * left untouched (the attention's zero padding: zero them once) (dp >= d; d and dp
+ * multiples of 8, H * d <= 7680; qkv, q, k, v, cos, sin 16-byte aligned). */
 int ffb_vision_rope(const uint16_t* qkv, const float* cos, const float* sin, int P, int H, int d,
                     int dp, uint16_t* q, uint16_t* k, uint16_t* v, void* stream);
 
