@@ -185,6 +185,16 @@ def test_vision_tower_two_blocks_bit_exact(name):
     assert (m_graph.float() - mf).abs().max().item() <= 0.03 * mf.abs().max().item()
 
 
+@pytest.mark.parametrize("grid", [(4, 4), (2, 8), (6, 2)])
+def test_vision_tower_tiny_canvases(grid):
+    """Canvases of a few patches (16, 16 and 12 patch rows: 4, 4 and 3 merged rows): every
+    kernel runs with far fewer rows than one 128-row tile, bit-identical to the oracle."""
+    v = VisionDims(1024, 16, 4096, 2560, 2, (0, 1))
+    p, pixels = _tower_case(v, grid, seed=11)
+    vt = VisionTower(v, p, device=DEV)
+    _check_tower(vt, p, v, pixels, grid, graph=True)
+
+
 def test_vision_tower_full_depth_4b_bit_exact():
     """The 4B vision tower at full depth (24 blocks, deepstack at 5 / 11 / 17) on the
     benchmarked 32 x 32 patch grid (a 512 x 512 canvas, 256 merged rows), through the CUDA
