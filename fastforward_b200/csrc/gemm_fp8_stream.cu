@@ -4,9 +4,10 @@
 //
 // Why: at M = 320 tokens a token-major tile (128 tokens x 256 features) leaves the third
 // token tile half empty, 228 tiles on 148 SMs make a second, one-third-full wave, and a
-// split-K plan re-reads every weight tile once per token tile.  The mainloop of these
-// GEMMs is bound by the bytes each SM must receive per 128-byte K block (the weight tile
-// dominates), so here each CTA gets one item: weight tile f (P = 2 tiles, gate and up, for
+// split-K plan re-reads every weight tile once per token tile.  A CTA's mainloop costs
+// ~70 ns per tcgen05.mma of its accumulator chain (measured on B200: nearly independent of
+// N up to 256, and of the bytes per stage), i.e. ~0.28 us per 128-byte K block, so the
+// plan wants one wave with the K blocks spread evenly; here each CTA gets one item: weight tile f (P = 2 tiles, gate and up, for
 // SwiGLU), a range of 16-token units [u0, u0 + n) of the tile's tokens (C ranges per tile,
 // n <= 16, so N = 16 n <= 256) and a range of K blocks (S splits; S > 1 writes fp32
 // partial planes that the consumer sums).  G = tiles x C x S <= SMs: one wave, no CTA
@@ -20,7 +21,10 @@
 // Epilogues (the codes of gemm_fp8.cu): bf16 out [M, N]; fp32 split-K partial planes
 // [S][M][N]; SwiGLU (out [M, N/2] bf16, or with static scales e4m3 bytes for the down
 // projection); qkv + per-head QK RMSNorm + rotate-half M-RoPE (one head per weight tile)
-// through a shared-memory transpose.
+// through a shared-memory transpose.  The epilogue is latency-bound (a few units of 16
+// tokens per warp), so everything it reads that does not depend on the accumulators (the
+// per-token scales, the norm weights, the rotary rows) is requested before it waits, and
+// the bf16 / fp32 outputs leave as direct row-segment stores (no staging round trip).
 //
 // Roles (576 threads): warp 0 TMA producer (the weight tile(s) + one [16 n x 128 B] token
 // box per stage; the weight half of the first stages is requested before the programmatic-
@@ -77,6 +81,7 @@ struct StreamArgs {
   int stages;
   uint32_t tmem_cols;
   float out_inv;  // E_SWIGLU_Q8: static inverse scale of the next linear's input
+  void* out;      // E_BF16 / E_F32: the output (stored directly, one 128 / 64-byte row segment per warp store)
   StreamRope rope;
 };
 
@@ -133,7 +138,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmap_a);
     tma_prefetch_desc(&tmap_w);
-    if (EPI != E_QKROPE) tma_prefetch_desc(&tmap_o);
+    if (EPI == E_SWIGLU || EPI == E_SWIGLU_Q8) tma_prefetch_desc(&tmap_o);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, args.tmem_cols);
@@ -247,17 +252,36 @@ __global__ void __launch_bounds__(THREADS, 1)
     } else {
       sw0 = sw1 = __ldg(args.w_scale);
     }
+    // this warp's activation scales, requested while the MMAs run: unit share + 4 i (i < 4,
+    // n <= 16), token j of it sits in lane 16 (i & 1) + j of sreg[i >> 1]; tokens past M
+    // get 0
+    float sreg[2] = {0.f, 0.f};
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int u = share + 4 * (2 * h + (lane >> 4)), t = (item.u0 + u) * UN + (lane & 15);
+      if (!args.a_per_row)
+        sreg[h] = __ldg(args.a_scale);
+      else if (u < n && t < args.M)
+        sreg[h] = __ldg(args.a_scale + t);
+    }
+    // qkv: the RMSNorm weights of this thread's 8 + 8 elements (part lane & 7 of every token)
+    uint4 wn0 = make_uint4(0u, 0u, 0u, 0u), wn1 = wn0;
+    if constexpr (EPI == E_QKROPE) {
+      if (f < args.rope.HQ + args.rope.HK) {
+        const uint16_t* wn = f < args.rope.HQ ? args.rope.q_norm : args.rope.k_norm;
+        wn0 = __ldg(reinterpret_cast<const uint4*>(wn + 8 * (lane & 7)));
+        wn1 = __ldg(reinterpret_cast<const uint4*>(wn + 64 + 8 * (lane & 7)));
+      }
+    }
     if (!mbar_wait_bounded(tfull, 0u, abort_flag)) ok = false;
     tc_fence_after();
     const uint32_t acc = tmem + ((uint32_t)(q * 32) << 16);
-    for (int u = share; u < n && ok; u += 4) {
+    for (int u = share, i = 0; u < n && ok; u += 4, ++i) {
       const int t0 = (item.u0 + u) * UN;  // first token of the unit
       float sa[UN];
+      const float sv = (i >> 1) ? sreg[1] : sreg[0];
 #pragma unroll
-      for (int j = 0; j < UN; ++j) {
-        const int t = t0 + j;
-        sa[j] = args.a_per_row ? (t < args.M ? __ldg(args.a_scale + t) : 0.f) : __ldg(args.a_scale);
-      }
+      for (int j = 0; j < UN; ++j) sa[j] = __shfl_sync(0xffffffffu, sv, ((i & 1) << 4) + j);
       uint32_t r0[16];
       tmem_ld16_async(acc + (uint32_t)(u * UN), r0);
       if constexpr (P == 2) {
@@ -287,41 +311,36 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         ++sc;
       } else if constexpr (EPI == E_BF16) {
+        // one 64-byte row segment (32 features) per token and store
         tmem_wait_ld();
         reg_fence(r0);
-        uint8_t* sb = stg + ((warp - 2) * 2 + (int)(sc & 1)) * 1024;
-        if (lane == 0) bulk_wait_read<1>();
-        __syncwarp();
+        uint16_t* dst = reinterpret_cast<uint16_t*>(args.out) + (size_t)t0 * args.N + f * FT + fl;
 #pragma unroll
         for (int j = 0; j < UN; ++j)
-          *reinterpret_cast<uint16_t*>(sb + j * 64 + lane * 2) = f2bf(__uint_as_float(r0[j]) * sa[j] * sw0);
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) {
-          tma_store_2d(&tmap_o, sb, 2 * (f * FT + q * 32), t0);
-          bulk_commit();
-        }
-        ++sc;
+          if (t0 + j < args.M) dst[(size_t)j * args.N] = f2bf(__uint_as_float(r0[j]) * sa[j] * sw0);
       } else if constexpr (EPI == E_F32) {
-        // this K split's fp32 partial (acc * sa * sw), plane ks of [S][M][N]
+        // this K split's fp32 partial (acc * sa * sw), plane ks of [S][M][N]: one 128-byte
+        // row segment per token and store
         tmem_wait_ld();
         reg_fence(r0);
-        uint8_t* sb = stg + (warp - 2) * 2048;  // [16 tokens x 32 features] fp32, single-buffered
-        if (lane == 0) bulk_wait_read<0>();
-        __syncwarp();
+        float* dst = reinterpret_cast<float*>(args.out) + ((size_t)ks * args.M + t0) * args.N + f * FT + fl;
 #pragma unroll
         for (int j = 0; j < UN; ++j)
-          *reinterpret_cast<float*>(sb + j * 128 + lane * 4) = __uint_as_float(r0[j]) * sa[j] * sw0;
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) {
-          tma_store_3d(&tmap_o, sb, 4 * (f * FT + q * 32), t0, ks);
-          bulk_commit();
-        }
+          if (t0 + j < args.M) dst[(size_t)j * args.N] = __uint_as_float(r0[j]) * sa[j] * sw0;
       } else {
         // qkv: (1) the 4 warps of this share write the unit's bf16 head rows into a
         // [16 tokens x 128 features] tile; (2) the same 128 threads, 8 per token, each
-        // normalise and rotate 8 elements and their rotate-half partners (+64).
+        // normalise and rotate 8 elements and their rotate-half partners (+64).  The
+        // rotary rows of step (2) are requested first, so they arrive during step (1).
+        const StreamRope& r = args.rope;
+        const int idx = q * 32 + lane, jt = idx >> 3, pp = idx & 7;  // token jt of the unit, part pp
+        const int t = t0 + jt;
+        const bool qk_row = f < r.HQ + r.HK && t < args.M;
+        uint4 c0 = make_uint4(0u, 0u, 0u, 0u), s0 = c0;
+        if (qk_row) {
+          c0 = __ldg(reinterpret_cast<const uint4*>(r.cos + (size_t)t * 128 + 8 * pp));
+          s0 = __ldg(reinterpret_cast<const uint4*>(r.sin + (size_t)t * 128 + 8 * pp));
+        }
         tmem_wait_ld();
         reg_fence(r0);
         uint8_t* xt = stg + (share * 2 + (xu & 1)) * 4096;
@@ -335,11 +354,8 @@ __global__ void __launch_bounds__(THREADS, 1)
           break;
         }
         ++xu;
-        const int idx = q * 32 + lane, j = idx >> 3, pp = idx & 7;  // token j of the unit, part pp
-        const int t = t0 + j;
-        const StreamRope& r = args.rope;
-        const uint4 xa = *reinterpret_cast<const uint4*>(xt + j * 256 + pp * 16);        // elements 8pp..
-        const uint4 xb = *reinterpret_cast<const uint4*>(xt + j * 256 + 128 + pp * 16);  // elements 64+8pp..
+        const uint4 xa = *reinterpret_cast<const uint4*>(xt + jt * 256 + pp * 16);        // elements 8pp..
+        const uint4 xb = *reinterpret_cast<const uint4*>(xt + jt * 256 + 128 + pp * 16);  // elements 64+8pp..
         const uint32_t wa[4] = {xa.x, xa.y, xa.z, xa.w}, wb[4] = {xb.x, xb.y, xb.z, xb.w};
         const size_t T = (size_t)args.M;
         if (f >= r.HQ + r.HK) {  // v heads: copied through
@@ -358,16 +374,11 @@ __global__ void __launch_bounds__(THREADS, 1)
           ss += __shfl_xor_sync(0xffffffffu, ss, 1);
           ss += __shfl_xor_sync(0xffffffffu, ss, 2);
           ss += __shfl_xor_sync(0xffffffffu, ss, 4);
-          if (t < args.M) {
+          if (qk_row) {
             const bool is_q = f < r.HQ;
-            const uint16_t* wn = is_q ? r.q_norm : r.k_norm;
             uint16_t* dst = is_q ? r.yq + ((size_t)f * T + t) * 128 : r.yk + ((size_t)(f - r.HQ) * T + t) * 128;
             const float inv = inv_rms_from_ss(ss, 128, r.eps);
-            const uint4 w0 = __ldg(reinterpret_cast<const uint4*>(wn + 8 * pp));
-            const uint4 w1 = __ldg(reinterpret_cast<const uint4*>(wn + 64 + 8 * pp));
-            const uint4 c0 = __ldg(reinterpret_cast<const uint4*>(r.cos + (size_t)t * 128 + 8 * pp));
-            const uint4 s0 = __ldg(reinterpret_cast<const uint4*>(r.sin + (size_t)t * 128 + 8 * pp));
-            const uint32_t wna[4] = {w0.x, w0.y, w0.z, w0.w}, wnb[4] = {w1.x, w1.y, w1.z, w1.w};
+            const uint32_t wna[4] = {wn0.x, wn0.y, wn0.z, wn0.w}, wnb[4] = {wn1.x, wn1.y, wn1.z, wn1.w};
             const uint32_t ca[4] = {c0.x, c0.y, c0.z, c0.w}, sa4[4] = {s0.x, s0.y, s0.z, s0.w};
             auto b2 = [](uint32_t w) { return *reinterpret_cast<const __nv_bfloat162*>(&w); };
             auto u32 = [](__nv_bfloat162 v) { return *reinterpret_cast<const uint32_t*>(&v); };
@@ -501,18 +512,13 @@ int stream_gemm(const uint8_t* a8, const float* a_scale, int a_per_row, const ui
   a.K = K;
   a.P = P;
   a.out_inv = out_inv;
+  a.out = out;
   if (rope_side) memcpy(&a.rope, rope_side, sizeof(StreamRope));
   CUtensorMap ta, tw, to;
   memset(&to, 0, sizeof(to));
   int rc = make_tmap_2d(&ta, a8, (uint64_t)M, (uint64_t)K, (uint64_t)K, (uint32_t)(a.b_bytes / BK), BK, 1);
   if (!rc) rc = make_tmap_2d(&tw, w8, (uint64_t)N, (uint64_t)K, (uint64_t)K, FT, BK, 1);
-  // outputs through unswizzled [16 rows x 64 B] (bf16), [16 x 32 B] (e4m3) or
-  // [16 x 128 B] x one plane (fp32) boxes
-  if (!rc && epilogue == E_BF16)
-    rc = make_tmap_2d_bytes(&to, out, (uint64_t)M, (uint64_t)N * 2, (uint64_t)N * 2, UN, 64);
-  if (!rc && epilogue == E_F32)
-    rc = make_tmap_3d_bytes(&to, out, (uint64_t)N * 4, (uint64_t)M, (uint64_t)splits, (uint64_t)N * 4,
-                            (uint64_t)N * 4 * M, 128, UN);
+  // SwiGLU outputs through unswizzled [16 rows x 64 B] (bf16) or [16 x 32 B] (e4m3) boxes
   if (!rc && epilogue == E_SWIGLU)
     rc = make_tmap_2d_bytes(&to, out, (uint64_t)M, (uint64_t)N, (uint64_t)N, UN, 64);
   if (!rc && epilogue == E_SWIGLU_Q8)
