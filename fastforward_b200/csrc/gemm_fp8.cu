@@ -369,10 +369,10 @@ __device__ void prologue_rows(const GemmArgs& g, uint8_t* scratch, F&& issue_pre
         unpack8(xv[j], x);
         uint32_t lo = 0, hi = 0;
         if (rowwise) {
-          const float sc = stat[rr];
+          const float sc = stat[rr], rcp = __frcp_rn(sc);
 #pragma unroll
           for (int e = 0; e < 8; ++e) {
-            const uint32_t bq = f2e4m3(clamp448(__fdiv_rn(x[e], sc)));
+            const uint32_t bq = e4m3_quotient(x[e], sc, rcp);
             if (e < 4) lo |= bq << (8 * e);
             else hi |= bq << (8 * (e - 4));
           }

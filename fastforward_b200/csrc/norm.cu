@@ -194,10 +194,11 @@ __global__ void __launch_bounds__(MAXT) add_rmsnorm_kernel(const NormArgs p) {
       }
     }
     if (p.quant_mode == FFB_QUANT_NONE) continue;
-    float mul = p.inv_scale, scale = 0.f;
+    float mul = p.inv_scale, scale = 0.f, rcp = 0.f;
     if (p.quant_mode == FFB_QUANT_ROWWISE) {
       amax = block_max(amax, red);
       scale = fmaxf(amax, 1e-12f) / 448.f;
+      rcp = __frcp_rn(scale);
       if (threadIdx.x == 0) p.qscale[row] = scale;
     }
 #pragma unroll
@@ -207,8 +208,8 @@ __global__ void __launch_bounds__(MAXT) add_rmsnorm_kernel(const NormArgs p) {
         uint32_t lo = 0, hi = 0;
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
-          const float qv = p.quant_mode == FFB_QUANT_ROWWISE ? __fdiv_rn(x[i][e], scale) : x[i][e] * mul;
-          const uint32_t b = f2e4m3(clamp448(qv));
+          const uint32_t b = p.quant_mode == FFB_QUANT_ROWWISE ? e4m3_quotient(x[i][e], scale, rcp)
+                                                               : f2e4m3(clamp448(x[i][e] * mul));
           if (e < 4) lo |= b << (8 * e);
           else hi |= b << (8 * (e - 4));
         }

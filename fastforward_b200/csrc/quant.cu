@@ -82,7 +82,7 @@ __global__ void __launch_bounds__(1024) quant_rows_vec_kernel(const uint16_t* __
   } else if (mode == FFB_QUANT_ROWSCALE) {
     scale = qscale[row];
   }
-  const bool divide = mode != FFB_QUANT_STATIC;
+  const float rcp = __frcp_rn(scale);
 #pragma unroll
   for (int i = 0; i < QV; ++i) {
     const int vi = threadIdx.x + i * blockDim.x;
@@ -90,8 +90,10 @@ __global__ void __launch_bounds__(1024) quant_rows_vec_kernel(const uint16_t* __
       uint32_t lo = 0, hi = 0;
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
-        const float qv = divide ? __fdiv_rn(v[i][e], scale) : v[i][e] * inv;
-        const uint32_t b = f2e4m3(clamp448(qv));
+        // ROWSCALE's given scale is outside e4m3_quotient's checked domain: IEEE divide
+        const uint32_t b = mode == FFB_QUANT_ROWWISE   ? e4m3_quotient(v[i][e], scale, rcp)
+                           : mode == FFB_QUANT_STATIC ? f2e4m3(clamp448(v[i][e] * inv))
+                                                      : f2e4m3(clamp448(__fdiv_rn(v[i][e], scale)));
         if (e < 4) lo |= b << (8 * e);
         else hi |= b << (8 * (e - 4));
       }
@@ -156,7 +158,7 @@ __global__ void __launch_bounds__(1024) quant_rows_peer_kernel(const uint16_t* _
     uint8_t* qr = q8 + (size_t)row * K;
     float m = 0.f;
     for (int q = 0; q < ps.world; ++q) m = fmaxf(m, __ldcg(pa.amax[ps.rank] + (size_t)q * M + row));
-    const float scale = fmaxf(m, 1e-12f) / 448.f;
+    const float scale = fmaxf(m, 1e-12f) / 448.f, rcp = __frcp_rn(scale);
     if (threadIdx.x == 0) qscale[row] = scale;
 #pragma unroll
     for (int i = 0; i < QV; ++i) {
@@ -167,7 +169,7 @@ __global__ void __launch_bounds__(1024) quant_rows_peer_kernel(const uint16_t* _
         uint32_t lo = 0, hi = 0;
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
-          const uint32_t b = f2e4m3(clamp448(__fdiv_rn(v[e], scale)));
+          const uint32_t b = e4m3_quotient(v[e], scale, rcp);
           if (e < 4) lo |= b << (8 * e);
           else hi |= b << (8 * (e - 4));
         }
@@ -197,10 +199,12 @@ __global__ void __launch_bounds__(NT) quant_rows_kernel(const uint16_t* __restri
   } else if (mode == FFB_QUANT_ROWSCALE) {
     scale = qscale[row];
   }
+  const float rcp = __frcp_rn(scale);
   for (int k = threadIdx.x; k < K; k += NT) {
     const float v = bf2f(xr[k]);
-    const float qv = mode != FFB_QUANT_STATIC ? __fdiv_rn(v, scale) : v * inv;
-    qr[k] = f2e4m3(clamp448(qv));
+    qr[k] = mode == FFB_QUANT_ROWWISE   ? e4m3_quotient(v, scale, rcp)
+            : mode == FFB_QUANT_STATIC ? f2e4m3(clamp448(v * inv))
+                                       : f2e4m3(clamp448(__fdiv_rn(v, scale)));
   }
 }
 

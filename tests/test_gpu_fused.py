@@ -295,3 +295,35 @@ def test_rowwise_quant_exhaustive_bf16(rows_amax):
     assert_bytes_equal(sa, s[:M], "row scales")
     assert_bytes_equal(a8, q[:M].view(torch.uint8), "e4m3 bytes")
     assert L.device_error() == 0
+
+
+@pytest.mark.parametrize("amax", [3.71875, 0.0123, 448.0, 1.0, 97.5, 2.0 ** -10, 0.00549, 200.0])
+def test_quantizer_rowwise_exhaustive_bf16(amax):
+    """ffb_quantize_fp8 (ROWWISE) over every bf16 value up to a row maximum: the vectorised
+    kernel (K = 8192, each row = the maximum + a slice of the values) and the scalar one
+    (one row of all of them) give the oracle's IEEE-division bytes."""
+    import oracle
+    vals = _all_bf16_upto(amax)
+    K = 8192
+    per = K - 1
+    nrows = (vals.numel() + per - 1) // per
+    x = torch.zeros((nrows, K))
+    for i in range(nrows):
+        part = vals[i * per:(i + 1) * per]
+        x[i, 0] = amax
+        x[i, 1:1 + part.numel()] = part
+    K1 = (vals.numel() + 127) // 128 * 128
+    x1 = torch.zeros((1, K1))
+    x1[0, :vals.numel()] = vals
+    for xx in (x, x1):
+        xx = xx.to(BF16)
+        M, Kx = xx.shape
+        xd = xx.to(DEV)
+        q8 = torch.zeros((M, Kx), dtype=torch.uint8, device=DEV)
+        qs = torch.zeros(M, device=DEV)
+        call("ffb_quantize_fp8", ptr(xd), L.QUANT_ROWWISE, 0.0, ptr(q8), ptr(qs), M, Kx, _s())
+        torch.cuda.synchronize()
+        q, s = oracle.quantize_rows(xx)
+        assert_bytes_equal(qs, s[:M], f"row scales (K={Kx})")  # the oracle pads the rows
+        assert_bytes_equal(q8, q[:M].view(torch.uint8), f"e4m3 bytes (K={Kx})")
+    assert L.device_error() == 0
