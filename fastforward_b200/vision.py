@@ -97,14 +97,16 @@ class _Buffers:
         self.mfc = z(n_p // m2, c * m2)
         self.merged = z(n_p // m2, v.out_hidden)
         self.deep = [z(n_p // m2, v.out_hidden) for _ in v.deepstack]
-        # the linears' plans (feature tile, K splits) and one split-K scratch for all of them
-        # (they run one after another on the stream; each leaves its counters zero)
+        # the linears' plans (feature tile, K splits, counters) and one split-K scratch for the
+        # plans that reduce through fp32 planes (they run one after another on the stream; each
+        # leaves its counters zero); the cluster split-K plans (counters 0) need none
         g = n_p // m2
         shapes = [(n_p, c, 3 * v.temporal * v.patch * v.patch), (n_p, 3 * c, c), (n_p, c, c), (n_p, v.inter, c),
                   (n_p, c, v.inter), (g, c * m2, c * m2), (g, v.out_hidden, c * m2)]
         self.plans = {sh: L.bf16_gemm_plan(*sh) for sh in shapes}
-        ws = max((sp * m * n for (m, n, _), (_, sp, _) in self.plans.items() if sp > 1), default=4)
+        ws = max((sp * m * n for (m, n, _), (_, sp, c_n) in self.plans.items() if sp > 1 and c_n > 0), default=4)
         cnt = max((c_n for (_, sp, c_n) in self.plans.values() if sp > 1), default=1)
+        cnt = max(cnt, 1)
         self.ws = torch.zeros(ws, dtype=torch.float32, device=device)
         self.counters = torch.zeros(cnt, dtype=torch.int32, device=device)
 

@@ -415,18 +415,21 @@ int ffb_quantize_fp8_peers(const uint16_t* x, float* const* amax, const ffb_peer
  * tanh and Abramowitz-Stegun 7.1.26 erf, within 5e-7 of the exact functions).
  * a [M,K], w [N,K] (K-major, as nn.Linear stores it), bias [N] or NULL, res [M,N]
  * (FFB_EPI_BIAS_RES, may alias out), out [M,N], all bf16 and 16-byte aligned; K and N
- * multiples of 8.  feature_tile 64 / 128 / 256 (0 = the plan's).  splits > 1 splits K: each
+ * multiples of 8.  feature_tile 64 / 128 / 256 (0 = the plan's).  splits > 1 splits K, the
+ * partial sums added in split order ((p0 + p1) + p2 ...) before the epilogue.  A 256-wide
+ * tile split 2 or 4 ways runs as thread-block clusters (one CTA per split) that reduce over
+ * distributed shared memory: ws and counters are not used and may be NULL.  Every other
  * split writes an fp32 partial plane to ws [splits][M][N] (16-byte aligned) and the split
- * that finishes last sums the planes in split order ((p0 + p1) + p2 ...) and runs the
- * epilogue; counters [ceil(M/128) * ceil(N/feature_tile)] uint32 must be zero before the
- * first call and are left zero by every call that completes. */
+ * that finishes last sums the planes and runs the epilogue; counters
+ * [ceil(M/128) * ceil(N/feature_tile)] uint32 must be zero before the first call and are
+ * left zero by every call that completes. */
 int ffb_bf16_gemm(const uint16_t* a, const uint16_t* w, const uint16_t* bias, const uint16_t* res,
                   int epilogue, uint16_t* out, int feature_tile, int splits, float* ws,
                   uint32_t* counters, int M, int N, int K, void* stream);
 
 /* The plan ffb_bf16_gemm uses for M x N x K on the current device: plan[0] = feature tile,
- * plan[1] = K splits, plan[2] = counters that plan needs (no reference counterpart; a
- * host-side query). */
+ * plan[1] = K splits, plan[2] = counters that plan needs (0 when it needs no ws / counters;
+ * no reference counterpart; a host-side query). */
 int ffb_bf16_gemm_plan(int M, int N, int K, int* plan);
 
 /* LayerNorm over rows of C: y = bf16(((x - mean) * rstd) * w + b), mean and variance from

@@ -37,11 +37,14 @@ def _rand(shape, g, std=1.0):
 @pytest.mark.parametrize("m,n,k,tile,splits", [(300, 136, 200, 0, 1), (128, 256, 64, 256, 1), (1, 64, 1536, 64, 1),
                                                (517, 1152, 1152, 128, 1), (256, 4304, 72, 0, 1),
                                                (300, 136, 1000, 64, 3), (1024, 1024, 4096, 128, 2),
-                                               (200, 520, 4304, 256, 4)])
+                                               (200, 520, 4304, 256, 4), (1024, 1024, 4096, 256, 4),
+                                               (256, 2560, 4096, 256, 2), (1, 64, 1536, 256, 2),
+                                               (130, 264, 520, 256, 4)])
 def test_bf16_linear_bit_exact(epilogue, m, n, k, tile, splits):
     """Every epilogue, ragged M / N / K (zero-filled K tail, clipped stores), each feature
-    tile, K splits (last-arriver reduction in split order): identical bytes to the
-    tensor-core accumulation model + the restated epilogue."""
+    tile, K splits (last-arriver reduction in split order; 256-wide tiles split 2 or 4 ways
+    run as thread-block clusters reducing over distributed shared memory): identical bytes
+    to the tensor-core accumulation model + the restated epilogue."""
     g = torch.Generator().manual_seed(m * 7 + n + k)
     x, w = _rand((m, k), g), _rand((n, k), g, k ** -0.5)
     b = _rand((n,), g, 0.5)
@@ -65,6 +68,11 @@ def test_bf16_linear_residual_in_place_and_no_bias():
     ops.vision_linear(x.to(DEV), w.to(DEV), None, "res", hd, out=hd, splits=2)
     torch.cuda.synchronize()
     assert _bits_equal(hd, oracle.linear_k(x, w, None, "res", h, splits=2))
+    for sp in (2, 4):  # the cluster split-K kernel, in place
+        hd = h.to(DEV)
+        ops.vision_linear(x.to(DEV), w.to(DEV), None, "res", hd, out=hd, feature_tile=256, splits=sp)
+        torch.cuda.synchronize()
+        assert _bits_equal(hd, oracle.linear_k(x, w, None, "res", h, splits=sp))
 
 
 def test_bf16_linear_tile_choice_does_not_change_bytes():

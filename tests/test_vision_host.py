@@ -107,13 +107,16 @@ def test_vision_entries_reject_bad_arguments():
 
 
 def test_linear_plans():
-    """The plan fills the machine in one wave with the fewest bytes per CTA (no GPU here: the
-    library assumes 148 SMs): qkv / fc1 256-wide tiles, proj / fc2 64-wide, no K split; the
-    counters match the plan's output tiles."""
-    assert L.bf16_gemm_plan(1024, 3072, 1024) == (256, 1, 96)
-    assert L.bf16_gemm_plan(1024, 4096, 1024) == (256, 1, 128)
-    assert L.bf16_gemm_plan(1024, 1024, 1024) == (64, 1, 128)
-    assert L.bf16_gemm_plan(1024, 1024, 4096) == (64, 1, 128)
+    """The plan minimises the fitted time model (no GPU here: the library assumes 148 SMs):
+    qkv / fc1 unsplit 256-wide tiles; proj 256-wide split 2 ways, fc2 and the mergers' K=4096
+    linears split 4 ways (cluster split-K: no counters); a many-tile K=64 shape 128-wide."""
+    assert L.bf16_gemm_plan(1024, 3072, 1024) == (256, 1, 0)
+    assert L.bf16_gemm_plan(1024, 4096, 1024) == (256, 1, 0)
+    assert L.bf16_gemm_plan(1024, 1024, 1024) == (256, 2, 0)
+    assert L.bf16_gemm_plan(1024, 1024, 4096) == (256, 4, 0)
+    assert L.bf16_gemm_plan(256, 4096, 4096) == (256, 4, 0)
+    assert L.bf16_gemm_plan(256, 2560, 4096) == (256, 4, 0)
+    assert L.bf16_gemm_plan(4096, 4096, 64) == (128, 1, 0)
     with pytest.raises(ValueError, match="bad shape"):
         L.bf16_gemm_plan(0, 4096, 64)
 
