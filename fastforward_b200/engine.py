@@ -209,11 +209,14 @@ def plan_splits(m, n, k, bn=None, allow_split=True, sms=SMS):
 
 def weight_stationary_plan(m, n, k, swiglu=False, max_splits=MAX_PLAN_SPLITS):
     """(splits, epilogue) of the weight-stationary schedule (`ffb_fp8_gemm` feature_tile
-    TILE_STREAM) for an m x n x k GEMM, or None when it does not apply.  Its mainloop is
-    bound by the bytes each CTA receives per 128-byte K block (the 16 KB weight tile + 2 KB
-    per 16 tokens), so the cost model is K blocks per CTA x those bytes, plus a charge per
-    split for the fp32 partial planes the consumer sums.  A split plan writes fp32 partials
-    (EPI_F32_PARTIAL); one split writes bf16 (or SwiGLU) directly."""
+    TILE_STREAM) for an m x n x k GEMM, or None when it does not apply.  A CTA's mainloop
+    costs about the same per 128-byte K block whatever its token count (one tcgen05.mma
+    chain, ~70 ns per instruction, 4 per K block), so fewer K blocks per CTA is what counts;
+    the cost model -- K blocks per CTA x (16 KB weight tile + 2 KB per 16 tokens), plus a
+    charge per split for the fp32 partial planes the consumer sums -- ranks the feasible
+    plans of the 4B / 8B shapes the same way (o / down: 3 splits, the most that one wave of
+    <= 256-token CTAs allows).  A split plan writes fp32 partials (EPI_F32_PARTIAL); one
+    split writes bf16 (or SwiGLU) directly."""
     nkb = math.ceil(k / 128)
     units = math.ceil(m / 16)
     tiles = n // (256 if swiglu else 128)
