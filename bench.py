@@ -16,7 +16,8 @@ collective on the data path ("replicas only"; requests are independent).
 
 `--impl reference` times the reference's arithmetic on the host CPU: the oracle's
 restatement of the reference path (the reference itself is Triton/CUDA-only and has no
-CPU path), a bounded sample of whole decoder layers scaled to the full model.
+CPU path), every step one whole request (all layers + scoring).  The GPU arm's own
+`cpu_baseline` is a bounded sample of that: a few timed decoder layers scaled to the model.
 """
 import argparse
 import contextlib
